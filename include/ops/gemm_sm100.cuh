@@ -1,0 +1,325 @@
+#pragma once
+
+// Warp-specialised tcgen05 GEMM for sm_100a ("TN": both operands K-major).
+//
+//   out[split][tok][feat] = epi( sum_{k in split} A[feat][k] * B[tok][k] )
+//
+// A is the "feature" operand (weights [out_features, in_features] in the HF
+// layout, or B^T of ops::mat_mul) and fills the 128 TMEM lanes; B is the
+// "token" operand (activations [tokens, in_features]) and fills BN TMEM
+// columns. Putting features on lanes makes the epilogue store coalesced:
+// for each token column the 32 lanes of a warp write 32 consecutive floats.
+// Decode (few tokens) therefore runs the same kernel with a narrow N tile
+// (BN = 32) and split-K across CTAs; prefill uses BN = 256.
+//
+// Roles (192 threads): warp 0 = TMA producer (one elected lane), warp 1 =
+// TMEM allocator + single-thread MMA issuer, warps 2-5 = epilogue (warp w may
+// only read TMEM lanes 32*(w%4)..+31). A STAGES-deep ring of smem stages is
+// guarded by full/empty mbarriers; tcgen05.commit releases a stage when the
+// MMAs reading it complete, and a final commit hands the accumulator to the
+// epilogue.
+//
+// Precision kinds:
+//   kBF16   one kind::f16 MMA per 16-wide K step (bf16 x bf16 -> fp32)
+//   kTF32x3 split-precision fp32: operands pre-split into tf32 hi/lo parts,
+//           three kind::tf32 MMAs per K step (hi*hi + hi*lo + lo*hi) give
+//           ~fp32 accuracy on the tensor cores.
+
+#include <type_traits>
+#include <cuda_bf16.h>
+
+#include "detail/sm100.cuh"
+
+namespace opworks::sm100 {
+
+enum class GemmKind { kBF16, kTF32x3 };
+
+struct GemmParams {
+    float *out;           // [splits][m_tok][ldo]
+    int64_t ldo;          // row stride of out (elements)
+    int64_t split_stride; // elements between split slices
+    int n_feat;           // rows of A
+    int m_tok;            // rows of B
+    int num_kb;           // K blocks of 128 bytes
+    int splits;
+    int *err;             // error word (bounded wait ran out)
+};
+
+struct Identity {
+    __device__ __forceinline__ float operator()(float x) const { return x; }
+};
+
+// Epilogues are unary `float(float)` functors (the ops::mat_mul contract) or
+// position-aware `float(float, int tok, int feat)` functors (bias, fused
+// model epilogues).
+template <typename Epi>
+__device__ __forceinline__ float apply_epilogue(const Epi &epi, float v, int tok, int feat) {
+    if constexpr (std::is_invocable_v<const Epi &, float, int, int>)
+        return epi(v, tok, feat);
+    else
+        return epi(v);
+}
+
+template <GemmKind kKind, int BN> struct GemmShape {
+    static constexpr bool kSplit3 = kKind == GemmKind::kTF32x3;
+    static constexpr uint32_t kABytes = kUmmaM * kUmmaKBytes;
+    static constexpr uint32_t kBBytes = BN * kUmmaKBytes;
+    static constexpr uint32_t kStageBytes = (kABytes + kBBytes) * (kSplit3 ? 2u : 1u);
+    static constexpr int kBudget = 192 * 1024;
+    static constexpr int kStagesRaw = kBudget / static_cast<int>(kStageBytes);
+    static constexpr int kStages = kStagesRaw > 8 ? 8 : kStagesRaw;
+    static constexpr int kKElems = kSplit3 ? 32 : 64; // elements per 128-byte K block
+    static constexpr uint32_t kTmemCols = BN < 32 ? 32 : BN;
+    static constexpr size_t kSmemBytes = 1024 + static_cast<size_t>(kStages) * kStageBytes + 256;
+    static_assert(kStages >= 2, "GEMM tile does not fit two pipeline stages");
+    static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N must be a multiple of 16 in [16, 256]");
+};
+
+template <GemmKind kKind, int BN, typename Epi>
+__global__ void __launch_bounds__(192, 1)
+    umma_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const __grid_constant__ CUtensorMap tmA_lo, const __grid_constant__ CUtensorMap tmB_lo,
+                     GemmParams p, Epi epi) {
+    using S = GemmShape<kKind, BN>;
+    constexpr int kStages = S::kStages;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + kStages * S::kStageBytes);
+    uint64_t *empty = full + kStages;
+    uint64_t *accum = empty + kStages;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(accum + 1);
+
+    const int warp = threadIdx.x / kWarpSize;
+    const int lane = threadIdx.x % kWarpSize;
+    const int f0 = blockIdx.x * kUmmaM;
+    const int t0 = blockIdx.y * BN;
+    const int split = blockIdx.z;
+    const int kb_begin = static_cast<int>(static_cast<int64_t>(p.num_kb) * split / p.splits);
+    const int kb_end = static_cast<int>(static_cast<int64_t>(p.num_kb) * (split + 1) / p.splits);
+
+    if (warp == 0 && lane == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(accum, 1);
+        fence_mbarrier_init();
+        prefetch_tmap(&tmA);
+        prefetch_tmap(&tmB);
+        if constexpr (S::kSplit3) {
+            prefetch_tmap(&tmA_lo);
+            prefetch_tmap(&tmB_lo);
+        }
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, S::kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_d = *tmem_slot;
+    bool ok = true;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int it = 0;
+            for (int kb = kb_begin; kb < kb_end; ++kb, ++it) {
+                const int s = it % kStages;
+                const uint32_t ph = static_cast<uint32_t>(it / kStages) & 1u;
+                if (!mbar_wait(&empty[s], ph ^ 1u)) {
+                    ok = false;
+                    break;
+                }
+                uint8_t *st = smem + s * S::kStageBytes;
+                mbar_arrive_expect_tx(&full[s], S::kStageBytes);
+                const int kc = kb * S::kKElems;
+                tma_load_2d(st, &tmA, &full[s], kc, f0);
+                tma_load_2d(st + S::kABytes, &tmB, &full[s], kc, t0);
+                if constexpr (S::kSplit3) {
+                    tma_load_2d(st + S::kABytes + S::kBBytes, &tmA_lo, &full[s], kc, f0);
+                    tma_load_2d(st + 2 * S::kABytes + S::kBBytes, &tmB_lo, &full[s], kc, t0);
+                }
+            }
+            // never leave the CTA with copies in flight: the last issued
+            // phase of every slot must have landed (returns at once when the
+            // MMA warp already consumed it)
+            for (int j = (it > kStages ? it - kStages : 0); j < it; ++j)
+                if (!mbar_wait(&full[j % kStages], static_cast<uint32_t>(j / kStages) & 1u))
+                    ok = false;
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_make(S::kSplit3 ? kFmtTF32 : kFmtBF16, kUmmaM, BN);
+            int it = 0;
+            for (int kb = kb_begin; kb < kb_end; ++kb, ++it) {
+                const int s = it % kStages;
+                const uint32_t ph = static_cast<uint32_t>(it / kStages) & 1u;
+                if (!mbar_wait(&full[s], ph)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t a = smem_u32(smem + s * S::kStageBytes);
+                const uint32_t b = a + S::kABytes;
+#pragma unroll
+                for (int k = 0; k < 4; ++k) { // four 32-byte K steps per 128-byte block
+                    const uint32_t acc = (kb > kb_begin || k > 0) ? 1u : 0u;
+                    const uint64_t ad = sdesc_k128(a + 32 * k);
+                    const uint64_t bd = sdesc_k128(b + 32 * k);
+                    if constexpr (S::kSplit3) {
+                        const uint64_t ad_lo = sdesc_k128(a + S::kABytes + S::kBBytes + 32 * k);
+                        const uint64_t bd_lo = sdesc_k128(a + 2 * S::kABytes + S::kBBytes + 32 * k);
+                        umma_tf32(tmem_d, ad, bd_lo, idesc, acc);
+                        umma_tf32(tmem_d, ad_lo, bd, idesc, 1u);
+                        umma_tf32(tmem_d, ad, bd, idesc, 1u);
+                    } else {
+                        umma_bf16(tmem_d, ad, bd, idesc, acc);
+                    }
+                }
+                umma_commit(&empty[s]);
+            }
+            umma_commit(accum);
+        }
+    } else {
+        const int q = warp & 3; // TMEM lane quarter this warp may access
+        if (!mbar_wait(accum, 0)) {
+            ok = false;
+        }
+        tc_fence_after();
+        const int feat = f0 + q * 32 + lane;
+        float *out = p.out + static_cast<int64_t>(split) * p.split_stride;
+        const bool feat_ok = feat < p.n_feat;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 16) {
+            uint32_t r[16];
+            tmem_ld_32x16(tmem_d + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(c), r);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                const int tok = t0 + c + i;
+                if (feat_ok && tok < p.m_tok)
+                    out[static_cast<int64_t>(tok) * p.ldo + feat] =
+                        apply_epilogue(epi, __uint_as_float(r[i]), tok, feat);
+            }
+        }
+    }
+    if (!ok)
+        atomicExch(p.err, 1);
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_d, S::kTmemCols);
+    }
+}
+
+template <GemmKind kKind, int BN, typename Epi> inline void gemm_prepare_kernel() {
+    using S = GemmShape<kKind, BN>;
+    static thread_local int done_device = -1;
+    int dev = 0;
+    OPWORKS_CUDA_CHECK(cudaGetDevice(&dev));
+    if (done_device != dev) {
+        OPWORKS_CUDA_CHECK(cudaFuncSetAttribute(umma_gemm_kernel<kKind, BN, Epi>,
+                                                cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                static_cast<int>(S::kSmemBytes)));
+        done_device = dev;
+    }
+}
+
+template <GemmKind kKind, int BN, typename Epi>
+inline void gemm_launch(const CUtensorMap &a, const CUtensorMap &b, const CUtensorMap &a_lo,
+                        const CUtensorMap &b_lo, const GemmParams &p, const Epi &epi, cudaStream_t stream) {
+    using S = GemmShape<kKind, BN>;
+    gemm_prepare_kernel<kKind, BN, Epi>();
+    const dim3 grid((p.n_feat + kUmmaM - 1) / kUmmaM, (p.m_tok + BN - 1) / BN, p.splits);
+    detail::require(grid.y <= 65535 && grid.z <= 65535, "GEMM grid exceeds the CUDA limits");
+    umma_gemm_kernel<kKind, BN, Epi><<<grid, 192, S::kSmemBytes, stream>>>(a, b, a_lo, b_lo, p, epi);
+    OPWORKS_CUDA_CHECK(cudaGetLastError());
+}
+
+// Operand description for the host launcher.
+struct GemmOperand {
+    const void *hi;     // bf16 or fp32 (tf32 hi part)
+    const void *lo;     // tf32 lo part (kTF32x3 only)
+    int rows;
+    int64_t ld;         // row stride in elements; K extent is the GEMM's k
+};
+
+inline int gemm_pick_bn(GemmKind kind, int m_tok) {
+    if (m_tok <= 32)
+        return 32;
+    if (m_tok <= 64)
+        return 64;
+    if (m_tok <= 128 || kind == GemmKind::kTF32x3)
+        return 128;
+    return 256;
+}
+
+// Number of K splits that brings the CTA count near a multiple of the SM
+// count without making a split shorter than `min_kb` blocks.
+inline int gemm_pick_splits(int tiles, int num_kb, int sm_count, int min_kb = 4) {
+    if (tiles >= sm_count)
+        return 1;
+    int best = 1;
+    double best_eff = 0.0;
+    for (int s = 1; s <= 32 && s * min_kb <= num_kb; ++s) {
+        const int ctas = tiles * s;
+        const int waves = (ctas + sm_count - 1) / sm_count;
+        const double eff = static_cast<double>(ctas) / (static_cast<double>(waves) * sm_count);
+        if (eff > best_eff + 0.02) {
+            best_eff = eff;
+            best = s;
+        }
+    }
+    return best;
+}
+
+// out[split][tok][feat] = epi(sum_k A[feat][k] B[tok][k]); `k` is the logical
+// K extent. A K tail shorter than one 128-byte block is zero-filled by TMA,
+// so only the row strides need 16-byte alignment.
+template <GemmKind kKind, typename Epi = Identity>
+inline void gemm_tn(const GemmOperand &A, const GemmOperand &B, int k, float *out, int64_t ldo, int splits,
+                    int64_t split_stride, cudaStream_t stream, const Epi &epi = {}, int force_bn = 0) {
+    constexpr bool kBf16 = kKind == GemmKind::kBF16;
+    constexpr int kKElems = kBf16 ? 64 : 32;
+    detail::require(k > 0, "gemm_tn: K must be positive");
+    detail::require(A.rows > 0 && B.rows > 0, "gemm_tn: empty operand");
+    GemmParams p;
+    p.out = out;
+    p.ldo = ldo;
+    p.split_stride = split_stride;
+    p.n_feat = A.rows;
+    p.m_tok = B.rows;
+    p.num_kb = (k + kKElems - 1) / kKElems;
+    p.splits = splits < 1 ? 1 : (splits > p.num_kb ? p.num_kb : splits);
+    p.err = device_error_word();
+    int bn = force_bn ? force_bn : gemm_pick_bn(kKind, B.rows);
+    if (!force_bn && p.splits == 1) {
+        // narrow the token tile while the grid is under one wave
+        const int sms = detail::device_facts().sm_count;
+        const int ftiles = (A.rows + kUmmaM - 1) / kUmmaM;
+        while (bn > 32 && ftiles * ((B.rows + bn - 1) / bn) < sms)
+            bn /= 2;
+    }
+    const CUtensorMap ta = make_tmap_2d(A.hi, kBf16, static_cast<uint64_t>(k), A.rows, A.ld, kKElems, kUmmaM);
+    const CUtensorMap tb = make_tmap_2d(B.hi, kBf16, static_cast<uint64_t>(k), B.rows, B.ld, kKElems, bn);
+    CUtensorMap ta_lo = ta, tb_lo = tb;
+    if constexpr (!kBf16) {
+        ta_lo = make_tmap_2d(A.lo, false, static_cast<uint64_t>(k), A.rows, A.ld, kKElems, kUmmaM);
+        tb_lo = make_tmap_2d(B.lo, false, static_cast<uint64_t>(k), B.rows, B.ld, kKElems, bn);
+    }
+    switch (bn) {
+    case 32: gemm_launch<kKind, 32, Epi>(ta, tb, ta_lo, tb_lo, p, epi, stream); break;
+    case 64: gemm_launch<kKind, 64, Epi>(ta, tb, ta_lo, tb_lo, p, epi, stream); break;
+    case 128: gemm_launch<kKind, 128, Epi>(ta, tb, ta_lo, tb_lo, p, epi, stream); break;
+    default:
+        if constexpr (kBf16)
+            gemm_launch<kKind, 256, Epi>(ta, tb, ta_lo, tb_lo, p, epi, stream);
+        else
+            gemm_launch<kKind, 128, Epi>(ta, tb, ta_lo, tb_lo, p, epi, stream);
+        break;
+    }
+}
+
+} // namespace opworks::sm100

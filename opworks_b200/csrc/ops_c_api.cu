@@ -1,0 +1,257 @@
+// libopworks_ops.so: C ABI over the header-only operator layer, declared in
+// include/opworks_ops.h. Each entry point forwards to the C++ API and turns
+// std::exception into -1 plus a thread-local message.
+
+#include <opworks>
+
+#include <cstring>
+#include <string>
+
+#include "opworks_ops.h"
+#include "ops/add.cuh"
+#include "ops/argmax.cuh"
+#include "ops/attention_decode.cuh"
+#include "ops/attention_prefill.cuh"
+#include "ops/causal_scale.cuh"
+#include "ops/embedding.cuh"
+#include "ops/linear.cuh"
+#include "ops/linear_mma.cuh"
+#include "ops/rms_norm.cuh"
+#include "ops/rope.cuh"
+#include "ops/split_heads.cuh"
+#include "ops/swiglu.cuh"
+
+namespace {
+
+thread_local std::string g_error;
+
+template <typename F> int guarded(F &&f) {
+    try {
+        f();
+        return 0;
+    } catch (const std::exception &e) {
+        g_error = e.what();
+    } catch (...) {
+        g_error = "unknown C++ exception";
+    }
+    return -1;
+}
+
+cudaStream_t as_stream(void *s) { return static_cast<cudaStream_t>(s); }
+
+struct AddF {
+    __device__ float operator()(float a, float b) const { return a + b; }
+};
+struct ReluF {
+    __device__ float operator()(float x) const { return fmaxf(x, 0.f); }
+};
+struct ScaleF {
+    float factor;
+    __device__ float operator()(float x) const { return factor * x; }
+};
+struct SumF {
+    static __device__ float identity() { return 0.f; }
+    static __device__ float combine(float a, float b) { return a + b; }
+};
+struct MaxF {
+    static __device__ float identity() { return -INFINITY; }
+    static __device__ float combine(float a, float b) { return fmaxf(a, b); }
+};
+struct ProdF {
+    static __device__ float identity() { return 1.f; }
+    static __device__ float combine(float a, float b) { return a * b; }
+};
+
+template <typename Op>
+void reduce_with(const float *in, float *out, int n, float *ws, int ws_size, cudaStream_t s) {
+    if (ws == nullptr && ws_size == 0)
+        opworks::ops::reduce<Op>(in, out, n, s);
+    else
+        opworks::ops::reduce<Op>(in, out, n, opworks::DeviceSpan<float>(ws, ws_size), s);
+}
+
+const __nv_bfloat16 *as_bf16(const uint16_t *p) { return reinterpret_cast<const __nv_bfloat16 *>(p); }
+
+} // namespace
+
+extern "C" {
+
+const char *opw_ops_last_error(void) { return g_error.c_str(); }
+
+int opw_ops_sync(void *stream) {
+    OPWORKS_CUDA_CHECK(cudaStreamSynchronize(as_stream(stream)));
+    int *word = opworks::sm100::device_error_word();
+    int value = 0;
+    OPWORKS_CUDA_CHECK(cudaMemcpy(&value, word, sizeof(int), cudaMemcpyDeviceToHost));
+    if (value != 0) {
+        OPWORKS_CUDA_CHECK(cudaMemset(word, 0, sizeof(int)));
+        g_error = "a device-side wait timed out (error code " + std::to_string(value) + ")";
+        return -1;
+    }
+    return 0;
+}
+
+int opw_map_add(const float *a, const float *b, float *out, int n, void *stream) {
+    return guarded([&] { opworks::ops::map(a, b, out, n, AddF{}, as_stream(stream)); });
+}
+int opw_map_relu(const float *in, float *out, int n, void *stream) {
+    return guarded([&] { opworks::ops::map(in, out, n, ReluF{}, as_stream(stream)); });
+}
+int opw_map_scale(const float *in, float *out, int n, float factor, void *stream) {
+    return guarded([&] { opworks::ops::map(in, out, n, ScaleF{factor}, as_stream(stream)); });
+}
+
+int opw_reduction_workspace_size(int n) {
+    int r = -1;
+    guarded([&] { r = opworks::ops::reduction_workspace_size(n); });
+    return r;
+}
+
+int opw_reduce(int kind, const float *in, float *out, int n, float *workspace, int workspace_size, void *stream) {
+    return guarded([&] {
+        switch (kind) {
+        case 0: reduce_with<SumF>(in, out, n, workspace, workspace_size, as_stream(stream)); break;
+        case 1: reduce_with<MaxF>(in, out, n, workspace, workspace_size, as_stream(stream)); break;
+        case 2: reduce_with<ProdF>(in, out, n, workspace, workspace_size, as_stream(stream)); break;
+        default: throw std::invalid_argument("unknown reduction kind");
+        }
+    });
+}
+
+int opw_softmax(const float *in, float *out, int rows, int cols, void *stream) {
+    return guarded([&] { opworks::ops::softmax(in, out, rows, cols, as_stream(stream)); });
+}
+
+int opw_layer_norm(const float *in, float *out, const float *gamma, const float *beta, int rows, int cols, float eps,
+                   void *stream) {
+    return guarded([&] { opworks::ops::layer_norm(in, out, gamma, beta, rows, cols, eps, as_stream(stream)); });
+}
+
+int opw_mat_mul(const float *A, const float *B, float *C, int M, int N, int K, int epilogue, float param,
+                void *stream) {
+    return guarded([&] {
+        switch (epilogue) {
+        case 0: opworks::ops::mat_mul(A, B, C, M, N, K, opworks::ops::PassThrough{}, as_stream(stream)); break;
+        case 1: opworks::ops::mat_mul(A, B, C, M, N, K, ReluF{}, as_stream(stream)); break;
+        case 2: opworks::ops::mat_mul(A, B, C, M, N, K, ScaleF{param}, as_stream(stream)); break;
+        default: throw std::invalid_argument("unknown epilogue");
+        }
+    });
+}
+
+int opw_matmul_builder(const float *A, const float *B, float *C, int M, int N, int K, int transpose_a,
+                       int transpose_b, const float *bias, int activation, void *stream) {
+    return guarded([&] {
+        using namespace opworks;
+        MatmulBuilder g(DeviceSpan<const float>(A, M * N), DeviceSpan<const float>(B, N * K),
+                        DeviceSpan<float>(C, M * K), M, N, K, as_stream(stream));
+        g.transpose_a(transpose_a != 0).transpose_b(transpose_b != 0);
+        if (bias)
+            g.bias(DeviceSpan<const float>(bias, K));
+        g.activation(static_cast<MatmulActivation>(activation));
+        g.apply(ops::matmul_launcher{});
+    });
+}
+
+int opw_rowwise_builder(int op, const float *in, float *out, const float *param, const float *beta, int rows,
+                        int cols, float eps, void *stream) {
+    return guarded([&] {
+        using namespace opworks;
+        const DeviceSpan<const float> i(in, rows * cols);
+        const DeviceSpan<float> o(out, rows * cols);
+        if (op == 0)
+            RowwiseBuilder::softmax(i, o, rows, cols, as_stream(stream)).apply(ops::rowwise_launcher{});
+        else if (op == 1)
+            RowwiseBuilder::layer_norm(i, o, DeviceSpan<const float>(param, cols), DeviceSpan<const float>(beta, cols),
+                                       rows, cols, eps, as_stream(stream))
+                .apply(ops::rowwise_launcher{});
+        else if (op == 2)
+            RowwiseBuilder::rms_norm(i, o, DeviceSpan<const float>(param, cols), rows, cols, eps, as_stream(stream))
+                .apply(ops::rowwise_launcher{});
+        else
+            throw std::invalid_argument("unknown rowwise op");
+    });
+}
+
+int opw_rms_norm(const float *x, const float *weight, float *out, int rows, int cols, float eps, void *stream) {
+    return guarded([&] { opworks::ops::rms_norm(x, weight, out, rows, cols, eps, as_stream(stream)); });
+}
+
+int opw_linear_f32(const float *X, const float *W, float *Y, int rows, int in_features, int out_features,
+                   void *stream) {
+    return guarded([&] { opworks::ops::linear(X, W, Y, rows, in_features, out_features, as_stream(stream)); });
+}
+
+int opw_linear_bf16(const float *X, const uint16_t *W, float *Y, int rows, int in_features, int out_features,
+                    void *stream) {
+    return guarded(
+        [&] { opworks::ops::linear(X, as_bf16(W), Y, rows, in_features, out_features, as_stream(stream)); });
+}
+
+int opw_linear_mma_bf16(const float *X, const uint16_t *W, float *Y, int rows, int in_features, int out_features,
+                        void *stream) {
+    return guarded([&] {
+        opworks::ops::linear_mma_bf16(X, as_bf16(W), Y, rows, in_features, out_features, as_stream(stream));
+    });
+}
+
+int opw_embedding_f32(const float *table, const int32_t *ids, float *out, int n, int hidden, void *stream) {
+    return guarded([&] { opworks::ops::embedding(table, ids, out, n, hidden, as_stream(stream)); });
+}
+
+int opw_embedding_bf16(const uint16_t *table, const int32_t *ids, float *out, int n, int hidden, void *stream) {
+    return guarded([&] { opworks::ops::embedding(as_bf16(table), ids, out, n, hidden, as_stream(stream)); });
+}
+
+int opw_rope(float *x, const float *inv_freq, int rows, int heads, int head_dim, int pos_start, void *stream) {
+    return guarded([&] { opworks::ops::rope(x, inv_freq, rows, heads, head_dim, pos_start, as_stream(stream)); });
+}
+
+int opw_split_heads(const float *in, float *out, int rows, int heads, int head_dim, int out_row_stride,
+                    int out_row_offset, void *stream) {
+    return guarded([&] {
+        opworks::ops::split_heads(in, out, rows, heads, head_dim, out_row_stride, out_row_offset, as_stream(stream));
+    });
+}
+
+int opw_merge_heads(const float *in, float *out, int rows, int heads, int head_dim, int in_row_stride,
+                    int in_row_offset, void *stream) {
+    return guarded([&] {
+        opworks::ops::merge_heads(in, out, rows, heads, head_dim, in_row_stride, in_row_offset, as_stream(stream));
+    });
+}
+
+int opw_causal_scale(float *scores, int rows, int cols, float scale, void *stream) {
+    return guarded([&] { opworks::ops::causal_scale(scores, rows, cols, scale, as_stream(stream)); });
+}
+
+int opw_swiglu(const float *gate, const float *up, float *out, int64_t n, void *stream) {
+    return guarded([&] { opworks::ops::swiglu(gate, up, out, n, as_stream(stream)); });
+}
+
+int opw_add(const float *a, const float *b, float *out, int64_t n, void *stream) {
+    return guarded([&] { opworks::ops::add(a, b, out, n, as_stream(stream)); });
+}
+
+int opw_argmax(const float *x, int n, int32_t *out, void *stream) {
+    return guarded([&] { opworks::ops::argmax(x, n, out, as_stream(stream)); });
+}
+
+int opw_attention_decode(const float *q, const float *kcache, const float *vcache, float *out, int num_q_heads,
+                         int kv_rep, int head_dim, int len, int max_seq, void *stream) {
+    return guarded([&] {
+        opworks::ops::attention_decode(q, kcache, vcache, out, num_q_heads, kv_rep, head_dim, len, max_seq,
+                                       as_stream(stream));
+    });
+}
+
+int opw_attention_prefill_chunked(const float *q_heads, const float *kcache, const float *vcache, float *out, int T,
+                                  int S, int q_offset, int num_q_heads, int kv_rep, int head_dim, int cap,
+                                  void *stream) {
+    return guarded([&] {
+        opworks::ops::attention_prefill_chunked(q_heads, kcache, vcache, out, T, S, q_offset, num_q_heads, kv_rep,
+                                                head_dim, cap, as_stream(stream));
+    });
+}
+
+} // extern "C"
