@@ -69,7 +69,11 @@ template <GemmKind kKind, int BN> struct GemmShape {
     static constexpr int kStagesRaw = kBudget / static_cast<int>(kStageBytes);
     static constexpr int kStages = kStagesRaw > 8 ? 8 : kStagesRaw;
     static constexpr int kKElems = kSplit3 ? 32 : 64; // elements per 128-byte K block
-    static constexpr uint32_t kTmemCols = BN < 32 ? 32 : BN;
+    // split-precision path: two accumulators (double-buffered promotion)
+    static constexpr uint32_t kTmemCols = (BN < 32 ? 32 : BN) * (kSplit3 ? 2u : 1u);
+    // K blocks accumulated in TMEM before the epilogue promotes the partial
+    // sum into fp32 registers (split-precision path only)
+    static constexpr int kPromoteKb = 2;
     static constexpr size_t kSmemBytes = 1024 + static_cast<size_t>(kStages) * kStageBytes + 256;
     static_assert(kStages >= 2, "GEMM tile does not fit two pipeline stages");
     static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N must be a multiple of 16 in [16, 256]");
@@ -87,7 +91,9 @@ __global__ void __launch_bounds__(192, 1)
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + kStages * S::kStageBytes);
     uint64_t *empty = full + kStages;
     uint64_t *accum = empty + kStages;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(accum + 1);
+    uint64_t *ready = accum + 1;   // [2] promotion buffers filled (split path)
+    uint64_t *drained = ready + 2; // [2] promotion buffers read (split path)
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drained + 2);
 
     const int warp = threadIdx.x / kWarpSize;
     const int lane = threadIdx.x % kWarpSize;
@@ -103,6 +109,10 @@ __global__ void __launch_bounds__(192, 1)
             mbar_init(&empty[s], 1);
         }
         mbar_init(accum, 1);
+        mbar_init(&ready[0], 1);
+        mbar_init(&ready[1], 1);
+        mbar_init(&drained[0], 128);
+        mbar_init(&drained[1], 128);
         fence_mbarrier_init();
         prefetch_tmap(&tmA);
         prefetch_tmap(&tmB);
@@ -155,6 +165,17 @@ __global__ void __launch_bounds__(192, 1)
             for (int kb = kb_begin; kb < kb_end; ++kb, ++it) {
                 const int s = it % kStages;
                 const uint32_t ph = static_cast<uint32_t>(it / kStages) & 1u;
+                // split path: group of kPromoteKb blocks into TMEM buffer group & 1
+                const int group = it / S::kPromoteKb;
+                const bool first_in_group = !S::kSplit3 || it % S::kPromoteKb == 0;
+                const uint32_t dst = S::kSplit3 ? tmem_d + static_cast<uint32_t>((group & 1) * BN) : tmem_d;
+                if (S::kSplit3 && first_in_group && group >= 2) {
+                    if (!mbar_wait(&drained[group & 1], static_cast<uint32_t>((group - 2) >> 1) & 1u)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                }
                 if (!mbar_wait(&full[s], ph)) {
                     ok = false;
                     break;
@@ -164,36 +185,74 @@ __global__ void __launch_bounds__(192, 1)
                 const uint32_t b = a + S::kABytes;
 #pragma unroll
                 for (int k = 0; k < 4; ++k) { // four 32-byte K steps per 128-byte block
-                    const uint32_t acc = (kb > kb_begin || k > 0) ? 1u : 0u;
                     const uint64_t ad = sdesc_k128(a + 32 * k);
                     const uint64_t bd = sdesc_k128(b + 32 * k);
                     if constexpr (S::kSplit3) {
+                        const uint32_t acc = (first_in_group && k == 0) ? 0u : 1u;
                         const uint64_t ad_lo = sdesc_k128(a + S::kABytes + S::kBBytes + 32 * k);
                         const uint64_t bd_lo = sdesc_k128(a + 2 * S::kABytes + S::kBBytes + 32 * k);
-                        umma_tf32(tmem_d, ad, bd_lo, idesc, acc);
-                        umma_tf32(tmem_d, ad_lo, bd, idesc, 1u);
-                        umma_tf32(tmem_d, ad, bd, idesc, 1u);
+                        umma_tf32(dst, ad, bd_lo, idesc, acc);
+                        umma_tf32(dst, ad_lo, bd, idesc, 1u);
+                        umma_tf32(dst, ad, bd, idesc, 1u);
                     } else {
-                        umma_bf16(tmem_d, ad, bd, idesc, acc);
+                        const uint32_t acc = (kb > kb_begin || k > 0) ? 1u : 0u;
+                        umma_bf16(dst, ad, bd, idesc, acc);
                     }
                 }
                 umma_commit(&empty[s]);
+                if (S::kSplit3 && (it % S::kPromoteKb == S::kPromoteKb - 1 || kb == kb_end - 1))
+                    umma_commit(&ready[group & 1]);
             }
-            umma_commit(accum);
+            if (!S::kSplit3)
+                umma_commit(accum);
         }
     } else {
         const int q = warp & 3; // TMEM lane quarter this warp may access
+        const int feat = f0 + q * 32 + lane;
+        float *out = p.out + static_cast<int64_t>(split) * p.split_stride;
+        const bool feat_ok = feat < p.n_feat;
+        const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
+        if constexpr (S::kSplit3) {
+            // promote each group's TMEM partial into fp32 registers: the
+            // tensor core's accumulator only ever holds kPromoteKb blocks
+            float acc[BN];
+#pragma unroll
+            for (int i = 0; i < BN; ++i)
+                acc[i] = 0.f;
+            const int ngroups = (kb_end - kb_begin + S::kPromoteKb - 1) / S::kPromoteKb;
+            for (int g = 0; g < ngroups; ++g) {
+                if (!mbar_wait(&ready[g & 1], static_cast<uint32_t>(g >> 1) & 1u)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+#pragma unroll
+                for (int c = 0; c < BN; c += 16) {
+                    uint32_t r[16];
+                    tmem_ld_32x16(tmem_d + lane_base + static_cast<uint32_t>((g & 1) * BN + c), r);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 16; ++i)
+                        acc[c + i] += __uint_as_float(r[i]);
+                }
+                tc_fence_before();
+                mbar_arrive(&drained[g & 1]);
+            }
+#pragma unroll
+            for (int i = 0; i < BN; ++i) {
+                const int tok = t0 + i;
+                if (feat_ok && tok < p.m_tok)
+                    out[static_cast<int64_t>(tok) * p.ldo + feat] = apply_epilogue(epi, acc[i], tok, feat);
+            }
+        } else {
         if (!mbar_wait(accum, 0)) {
             ok = false;
         }
         tc_fence_after();
-        const int feat = f0 + q * 32 + lane;
-        float *out = p.out + static_cast<int64_t>(split) * p.split_stride;
-        const bool feat_ok = feat < p.n_feat;
 #pragma unroll 1
         for (int c = 0; c < BN; c += 16) {
             uint32_t r[16];
-            tmem_ld_32x16(tmem_d + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(c), r);
+            tmem_ld_32x16(tmem_d + lane_base + static_cast<uint32_t>(c), r);
             tmem_wait_ld();
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
@@ -202,6 +261,7 @@ __global__ void __launch_bounds__(192, 1)
                     out[static_cast<int64_t>(tok) * p.ldo + feat] =
                         apply_epilogue(epi, __uint_as_float(r[i]), tok, feat);
             }
+        }
         }
     }
     if (!ok)

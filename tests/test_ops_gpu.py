@@ -1,0 +1,460 @@
+"""GPU parity of the operator layer, called through libopworks_ops.so (the C
+ABI of include/opworks_ops.h), against the pinned CPU oracle and — where the
+reference was built from its own sources (oracle/_ref) — against the
+reference's CUDA kernels on the same inputs.
+
+Tolerances: fp32 element ops |a-e| <= 1e-5 (1 + |e|) (framework.cu:45-48);
+model ops abs <= 1e-5 + 1e-4 |e| (test_common.cuh:52-60); fp32 GEMMs (3xTF32)
+the fp32 element rule; bf16 GEMMs nrmse <= 1e-2 and cosine >= 0.999
+(ops_test.cu:85-117); integer results bit-exact."""
+
+import ctypes
+import math
+import os
+
+import numpy as np
+import pytest
+
+import inputs
+import oracle
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+REF_OPS = os.path.join(ROOT, "oracle", "_ref", "libopworks_ops_ref.so")
+GOLD = os.path.join(ROOT, "tests", "golden")
+
+
+@pytest.fixture(scope="module")
+def ops():
+    import opworks_b200
+
+    return opworks_b200.ops_lib()
+
+
+@pytest.fixture(scope="module")
+def ref():
+    if not os.path.exists(REF_OPS):
+        pytest.skip("reference operators were not built (oracle/_ref)")
+    return ctypes.CDLL(REF_OPS)
+
+
+def dev(a, dtype=None):
+    t = torch.from_numpy(np.ascontiguousarray(a))
+    if dtype is not None:
+        t = t.to(dtype)
+    return t.cuda()
+
+
+def host(t):
+    torch.cuda.synchronize()
+    return t.cpu().numpy()
+
+
+def sync(ops):
+    ops.ops_sync(0)
+
+
+def close(a, e, tol=1e-5):
+    a, e = np.asarray(a, np.float64), np.asarray(e, np.float64)
+    assert a.shape == e.shape
+    assert np.all(np.isfinite(a))
+    rel = np.abs(a - e) / (1 + np.abs(e))
+    assert np.all(rel <= tol), f"max rel err {rel.max():.3g} at {np.unravel_index(rel.argmax(), rel.shape)}"
+
+
+def model_close(a, e):
+    a, e = np.asarray(a, np.float64), np.asarray(e, np.float64)
+    err = np.abs(a - e)
+    assert np.all(err <= 1e-5 + 1e-4 * np.abs(e)), f"max abs err {err.max():.3g}"
+
+
+def stats(a, e):
+    a, e = np.asarray(a, np.float64).ravel(), np.asarray(e, np.float64).ravel()
+    nrmse = np.sqrt(np.mean((a - e) ** 2)) / max(np.sqrt(np.mean(e**2)), 1e-6)
+    cos = a @ e / max(np.linalg.norm(a) * np.linalg.norm(e), 1e-30)
+    return nrmse, cos
+
+
+def bf16_bits(x):
+    return torch.from_numpy(np.ascontiguousarray(x, np.float32)).to(torch.bfloat16).view(torch.int16).numpy().view(
+        np.uint16)
+
+
+# ------------------------------------------------------------------ matmul
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 1, 1), (3, 5, 7), (37, 100, 129), (130, 257, 200), (64, 2048, 96),
+                                   (1024, 2048, 1024)])
+def test_mat_mul_3xtf32_vs_oracle(ops, M, N, K):
+    rng = np.random.default_rng(M * 7 + N * 13 + K)
+    a = (rng.standard_normal((M, N)) / math.sqrt(max(N, 1))).astype(np.float32)
+    b = (rng.standard_normal((N, K)) / math.sqrt(max(N, 1))).astype(np.float32)
+    da, db, dc = dev(a), dev(b), torch.empty(M, K, device="cuda")
+    ops.mat_mul(da, db, dc, M, N, K, 1, 0.0, 0)  # ReLU epilogue
+    sync(ops)
+    close(host(dc), oracle.mat_mul(a, b, epilogue=1))
+
+
+def test_mat_mul_framework_cases(ops):
+    a = np.array([i % 7 - 3 for i in range(15)], np.float32).reshape(3, 5)
+    b = np.array([i % 5 - 2 for i in range(35)], np.float32).reshape(5, 7)
+    c = torch.empty(3, 7, device="cuda")
+    ops.mat_mul(dev(a), dev(b), c, 3, 5, 7, 2, 2.0, 0)
+    close(host(c), 2 * (a.astype(np.float64) @ b))
+    c.fill_(123.0)
+    ops.mat_mul(0, 0, c, 3, 0, 7, 0, 0.0, 0)  # empty contraction writes epilogue(0)
+    close(host(c), np.zeros((3, 7)))
+    ops.mat_mul(0, 0, 0, 0, 4, 5, 0, 0.0, 0)  # empty output: no-op
+    with pytest.raises(ValueError):
+        ops.mat_mul(0, 0, 0, 2, 2, 2, 0, 0.0, 0)
+
+
+@pytest.mark.parametrize("ta,tb,act,bias", [(0, 0, 0, False), (1, 0, 1, True), (0, 1, 2, True), (1, 1, 0, True)])
+def test_matmul_builder_launcher(ops, ta, tb, act, bias):
+    M, N, K = 45, 70, 33
+    rng = np.random.default_rng(5)
+    a = rng.standard_normal((M, N)).astype(np.float32)
+    b = rng.standard_normal((N, K)).astype(np.float32)
+    bv = rng.standard_normal(K).astype(np.float32)
+    a_st = a.T.copy() if ta else a
+    b_st = b.T.copy() if tb else b
+    c = torch.empty(M, K, device="cuda")
+    ops.matmul_builder(dev(a_st), dev(b_st), c, M, N, K, ta, tb, dev(bv) if bias else 0, act, 0)
+    e = a.astype(np.float64) @ b + (bv if bias else 0)
+    if act == 1:
+        e = np.maximum(e, 0)
+    elif act == 2:
+        e = 0.5 * e * (1 + np.vectorize(math.erf)(e / math.sqrt(2)))
+    close(host(c), e, 2e-5)
+
+
+@pytest.mark.parametrize("rows", [2, 3, 16, 32, 33, 64, 100, 128, 256, 300])
+def test_linear_bf16_tensor_cores(ops, rows):
+    rng = np.random.default_rng(rows)
+    x = rng.standard_normal((rows, 2048)).astype(np.float32)
+    w = (rng.standard_normal((512, 2048)) / math.sqrt(2048)).astype(np.float32)
+    wb = bf16_bits(w)
+    y = torch.empty(rows, 512, device="cuda")
+    ops.linear_mma_bf16(dev(x), dev(wb.view(np.int16)), y, rows, 2048, 512, 0)
+    got = host(y)
+    want = oracle.linear_bf16(x, wb)
+    nrmse, cos = stats(got, want)
+    assert nrmse <= 1e-2 and cos >= 0.999, (nrmse, cos)
+    # bf16 rounding of X is the only difference: compare with X rounded too
+    xr = torch.from_numpy(x).to(torch.bfloat16).float().numpy()
+    model_close(got, oracle.linear_bf16(xr, wb))
+
+
+def test_linear_fixture_paths(ops):
+    g = np.load(os.path.join(GOLD, "ops_golden.npz"))
+    x = inputs.op_inputs()
+    y = torch.empty(3, 512, device="cuda")
+    ops.linear_f32(dev(x["lin.x"]), dev(x["lin.w"]), y, 3, 2048, 512, 0)
+    model_close(host(y), g["lin.out"])
+    y1 = torch.empty(1, 8192, device="cuda")
+    ops.linear_f32(dev(x["gemv.x"]), dev(x["gemv.w"]), y1, 1, 2048, 8192, 0)
+    model_close(host(y1), g["gemv.out"])
+    wb = bf16_bits(x["gemv.w"])
+    ops.linear_bf16(dev(x["gemv.x"]), dev(wb.view(np.int16)), y1, 1, 2048, 8192, 0)
+    nrmse, cos = stats(host(y1), g["gemv.out"])
+    assert nrmse <= 1e-2 and cos >= 0.999
+    model_close(host(y1), oracle.linear_bf16(x["gemv.x"], wb))
+
+
+@pytest.mark.parametrize("in_f,out_f", [(7, 5), (33, 129), (2048, 2048), (8192, 2048)])
+def test_gemv_shapes(ops, in_f, out_f):
+    rng = np.random.default_rng(in_f + out_f)
+    x = rng.standard_normal((1, in_f)).astype(np.float32)
+    w = rng.standard_normal((out_f, in_f)).astype(np.float32)
+    y = torch.empty(1, out_f, device="cuda")
+    ops.linear_f32(dev(x), dev(w), y, 1, in_f, out_f, 0)
+    model_close(host(y), oracle.linear(x, w))
+
+
+# ----------------------------------------------------------- element / row
+
+
+def test_map_boundaries_and_inplace(ops):
+    for n in (1, 2, 3, 4, 5, 31, 32, 33, 255, 256, 257, 1025):
+        for off in (0, 1):
+            h = np.arange(n + off, dtype=np.float32) - 10
+            a, b, out = dev(h), dev(h), torch.zeros(n + off, device="cuda")
+            pa, pb, po = a.data_ptr() + 4 * off, b.data_ptr() + 4 * off, out.data_ptr() + 4 * off
+            ops.map_add(pa, pb, po, n, 0)
+            close(host(out)[off:], 2 * h[off:])
+            ops.map_scale(pa, pa, n, 3.0, 0)
+            close(host(a)[off:], 3 * h[off:])
+    x = np.random.default_rng(1).standard_normal(1 << 20).astype(np.float32)
+    y = torch.empty(1 << 20, device="cuda")
+    ops.map_relu(dev(x), y, 1 << 20, 0)
+    close(host(y), np.maximum(x, 0))
+    with pytest.raises(ValueError):
+        ops.map_relu(0, 0, 1, 0)
+    ops.map_relu(0, 0, 0, 0)
+
+
+@pytest.mark.parametrize("kind", [0, 1, 2])
+def test_reduce(ops, kind):
+    ones = dev(np.ones(4099, np.float32))
+    out = torch.empty(1, device="cuda")
+    ws_n = ops.raw("reduction_workspace_size")(4099)
+    ws = torch.empty(max(ws_n, 1), device="cuda")
+    for n in (0, 1, 31, 32, 33, 255, 256, 257, 4099):
+        for use_ws in (True, False):
+            if use_ws:
+                ops.reduce(kind, ones, out, n, ws, ws_n, 0)
+            else:
+                ops.reduce(kind, ones, out, n, 0, 0, 0)
+            want = {0: float(n), 1: (1.0 if n else -math.inf), 2: 1.0}[kind]
+            assert host(out)[0] == want
+    with pytest.raises(ValueError):
+        ops.reduce(0, ones, out, 4099, 0, 1, 0)  # workspace too small
+
+
+def test_reduce_sum_c1(ops):
+    x = np.random.default_rng(4).uniform(-1, 1, 1 << 24).astype(np.float32)
+    out = torch.empty(1, device="cuda")
+    ws_n = ops.raw("reduction_workspace_size")(1 << 24)
+    ws = torch.empty(ws_n, device="cuda")
+    ops.reduce(0, dev(x), out, 1 << 24, ws, ws_n, 0)
+    want = oracle.reduce_sum(x)
+    # fp32 accumulation over 2^24 terms: relative to the sum of magnitudes
+    assert abs(host(out)[0] - want) <= 1e-5 * (1 + np.abs(x).sum() / 1000)
+
+
+@pytest.mark.parametrize("rows,cols,off", [(2, 5, 0), (4096, 1024, 0), (3, 1, 0), (7, 31, 1), (5, 1025, 0),
+                                           (3, 2048, 1), (4, 5000, 0), (2, 8192, 0), (2, 10000, 0), (2, 40000, 0)])
+def test_softmax(ops, rows, cols, off):
+    x = (np.random.default_rng(rows * cols).standard_normal(rows * cols + off) * 4).astype(np.float32)
+    dx, dy = dev(x), torch.empty(rows * cols + off, device="cuda")
+    ops.softmax(dx.data_ptr() + 4 * off, dy.data_ptr() + 4 * off, rows, cols, 0)
+    close(host(dy)[off:].reshape(rows, cols), oracle.softmax(x[off:].reshape(rows, cols)))
+
+
+@pytest.mark.parametrize("rows,cols", [(2, 5), (4096, 2048), (3, 7), (5, 1025), (2, 12000), (2, 40000)])
+def test_layer_norm(ops, rows, cols):
+    rng = np.random.default_rng(2)
+    x = rng.standard_normal((rows, cols)).astype(np.float32)
+    g = rng.uniform(0.5, 1.5, cols).astype(np.float32)
+    b = (rng.standard_normal(cols) * 0.1).astype(np.float32)
+    y = torch.empty(rows, cols, device="cuda")
+    ops.layer_norm(dev(x), y, dev(g), dev(b), rows, cols, 1e-5, 0)
+    close(host(y), oracle.layer_norm(x, g, b, 1e-5))
+    with pytest.raises(ValueError):
+        ops.layer_norm(0, 0, 0, 0, 0, 3, 0.0, 0)
+
+
+def test_rowwise_builder_and_rms_norm(ops):
+    g = np.load(os.path.join(GOLD, "ops_golden.npz"))
+    x = inputs.op_inputs()
+    y = torch.empty(5, 2048, device="cuda")
+    ops.rms_norm(dev(x["rms.x"]), dev(x["rms.w"]), y, 5, 2048, inputs.EPS, 0)
+    model_close(host(y), g["rms.out"])
+    y.zero_()
+    ops.rowwise_builder(2, dev(x["rms.x"]), y, dev(x["rms.w"]), 0, 5, 2048, inputs.EPS, 0)
+    model_close(host(y), g["rms.out"])
+    for cols in (3, 100, 5000, 9000):
+        xr = np.random.default_rng(cols).standard_normal((3, cols)).astype(np.float32)
+        w = np.random.default_rng(cols + 1).standard_normal(cols).astype(np.float32)
+        yr = torch.empty(3, cols, device="cuda")
+        ops.rms_norm(dev(xr), dev(w), yr, 3, cols, 1e-5, 0)
+        model_close(host(yr), oracle.rms_norm(xr, w, 1e-5))
+
+
+# ------------------------------------------------------------- model ops
+
+
+def test_embedding(ops):
+    rng = np.random.default_rng(3)
+    table = (rng.standard_normal((1000, 2048)) * 0.02).astype(np.float32)
+    ids = np.array([0, 5, 999, 128, 0], np.int32)
+    out = torch.empty(5, 2048, device="cuda")
+    ops.embedding_f32(dev(table), dev(ids), out, 5, 2048, 0)
+    assert np.array_equal(host(out), table[ids])
+    tb = bf16_bits(table)
+    ops.embedding_bf16(dev(tb.view(np.int16)), dev(ids), out, 5, 2048, 0)
+    want = torch.from_numpy(tb.view(np.int16)).view(torch.bfloat16).float().numpy()[ids]
+    assert np.array_equal(host(out), want)
+
+
+def test_rope_fixture(ops):
+    g = np.load(os.path.join(GOLD, "ops_golden.npz"))
+    x = inputs.op_inputs()
+    inv = dev(g["rope.inv_freq"])
+    q = dev(x["rope.q"])
+    ops.rope(q, inv, 17, inputs.QH, inputs.D, 29, 0)
+    model_close(host(q), g["rope.q_out"])
+    k = dev(x["rope.k"])
+    ops.rope(k, inv, 17, inputs.KVH, inputs.D, 29, 0)
+    model_close(host(k), g["rope.k_out"])
+
+
+def test_swiglu_add_split_merge_causal(ops):
+    g = np.load(os.path.join(GOLD, "ops_golden.npz"))
+    x = inputs.op_inputs()
+    out = torch.empty(4, 8192, device="cuda")
+    ops.swiglu(dev(x["swiglu.g"]), dev(x["swiglu.u"]), out, 4 * 8192, 0)
+    model_close(host(out), g["swiglu.out"])
+    a = dev(x["swiglu.g"])
+    ops.add(a, dev(x["swiglu.u"]), a, 4 * 8192, 0)
+    close(host(a), x["swiglu.g"] + x["swiglu.u"])
+    packed = np.random.default_rng(9).standard_normal((5, 3 * 64)).astype(np.float32)
+    slabs = torch.zeros(3, 9, 64, device="cuda")
+    ops.split_heads(dev(packed), slabs, 5, 3, 64, 9, 2, 0)
+    s = host(slabs)
+    assert np.array_equal(s[:, 2:7, :], packed.reshape(5, 3, 64).transpose(1, 0, 2))
+    back = torch.empty(5, 3 * 64, device="cuda")
+    ops.merge_heads(slabs, back, 5, 3, 64, 9, 2, 0)
+    assert np.array_equal(host(back), packed)
+    sc = np.random.default_rng(1).standard_normal((4, 9)).astype(np.float32)
+    dsc = dev(sc)
+    ops.causal_scale(dsc, 4, 9, 0.5, 0)
+    want = np.where(np.arange(9)[None, :] <= (5 + np.arange(4))[:, None], sc * 0.5, -np.inf)
+    assert np.array_equal(host(dsc), want.astype(np.float32))
+
+
+def test_argmax_exact(ops):
+    g = np.load(os.path.join(GOLD, "ops_golden.npz"))
+    x = inputs.op_inputs()["argmax.x"]
+    out = torch.empty(1, dtype=torch.int32, device="cuda")
+    ops.argmax(dev(x), x.size, out, 0)
+    assert int(host(out)[0]) == int(g["argmax.out"][0])
+    ties = np.zeros(128256, np.float32)
+    ties[[77, 5000, 128255]] = 3.0
+    ops.argmax(dev(ties), ties.size, out, 0)
+    assert int(host(out)[0]) == 77
+
+
+def test_attention_fixtures(ops):
+    g = np.load(os.path.join(GOLD, "ops_golden.npz"))
+    x = inputs.op_inputs()
+    T, QH, KVH, D = 37, inputs.QH, inputs.KVH, inputs.D
+    slab = lambda a: np.ascontiguousarray(a.transpose(1, 0, 2))  # [T, h, D] -> [h, T, D]
+    q, k, v = dev(slab(x["attn.q"])), dev(slab(x["attn.k"])), dev(slab(x["attn.v"]))
+    out = torch.empty(QH, T, D, device="cuda")
+    ops.attention_prefill_chunked(q, k, v, out, T, T, 0, QH, QH // KVH, D, T, 0)
+    model_close(host(out), slab(g["attn.out"]))
+    od = torch.empty(QH, D, device="cuda")
+    ops.attention_decode(dev(x["attn.qd"][0]), k, v, od, QH, QH // KVH, D, T, T, 0)
+    model_close(host(od), g["attn.out_decode"][0])
+
+
+@pytest.mark.parametrize("L,rep", [(1, 4), (64, 4), (65, 4), (2500, 4), (300, 1), (300, 8), (9000, 4)])
+def test_attention_decode_lengths(ops, L, rep):
+    QH = 32
+    KVH = QH // rep
+    rng = np.random.default_rng(L + rep)
+    cap = L + 7
+    k = rng.uniform(-1.5, 1.5, (KVH, cap, 64)).astype(np.float32)
+    v = rng.uniform(-1.5, 1.5, (KVH, cap, 64)).astype(np.float32)
+    q = rng.uniform(-1.5, 1.5, (QH, 64)).astype(np.float32)
+    out = torch.empty(QH, 64, device="cuda")
+    ops.attention_decode(dev(q), dev(k), dev(v), out, QH, rep, 64, L, cap, 0)
+    want = oracle.attention(q[None], k[:, :L].transpose(1, 0, 2), v[:, :L].transpose(1, 0, 2))[0]
+    model_close(host(out), want)
+
+
+def test_attention_prefill_long_vs_oracle(ops):
+    # the reference's chunked-vs-explicit check (ops_test.cu:315-354) uses an
+    # LCG-seeded 2500-token case; same length here, compared with the oracle
+    T, QH, KVH = 2500, 32, 8
+    state = [42]
+
+    def lcg(n):
+        out = np.empty(n, np.float32)
+        s = state[0]
+        for i in range(n):
+            s = (s * 6364136223846793005 + 1442695040888963407) & ((1 << 64) - 1)
+            out[i] = ((s >> 33) & 0xFFFFFF) / 8388608.0 - 1.5
+        state[0] = s
+        return out
+
+    q = lcg(QH * T * 64).reshape(QH, T, 64)
+    k = lcg(KVH * T * 64).reshape(KVH, T, 64)
+    v = lcg(KVH * T * 64).reshape(KVH, T, 64)
+    out = torch.empty(QH, T, 64, device="cuda")
+    ops.attention_prefill_chunked(dev(q), dev(k), dev(v), out, T, T, 0, QH, 4, 64, T, 0)
+    got = host(out)
+    rows = np.r_[0:40, 1000:1010, T - 40:T]  # oracle on a subset of query rows
+    want = np.empty((QH, rows.size, 64), np.float32)
+    for j, t in enumerate(rows):
+        want[:, j] = oracle.attention(q[:, t:t + 1].transpose(1, 0, 2), k[:, :t + 1].transpose(1, 0, 2),
+                                      v[:, :t + 1].transpose(1, 0, 2))[0]
+    nrmse, _ = stats(got[:, rows], want)
+    assert nrmse <= 1e-5, nrmse
+    model_close(got[:, rows], want)
+
+
+def test_graph_capture_replay(ops):
+    # tests/unit/framework.cu:154-169: map + reduce(workspace) captured once,
+    # replayed twice: 2 * 4099 = 8198, then 16396
+    x = dev(np.ones(4099, np.float32))
+    out = torch.empty(1, device="cuda")
+    ws_n = ops.raw("reduction_workspace_size")(4099)
+    ws = torch.empty(ws_n, device="cuda")
+    ops.reduce(0, x, out, 4099, ws, ws_n, 0)  # warm (module load) outside capture
+    ops.map_scale(x, x, 4099, 1.0, 0)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        s = torch.cuda.current_stream().cuda_stream
+        ops.map_scale(x, x, 4099, 2.0, s)
+        ops.reduce(0, x, out, 4099, ws, ws_n, s)
+    torch.cuda.synchronize()
+    x.fill_(1.0)
+    g.replay()
+    assert host(out)[0] == 8198
+    g.replay()
+    assert host(out)[0] == 16396
+
+
+# ------------------------------------------------- vs the reference kernels
+
+
+def _f(lib, name, *types):
+    fn = getattr(lib, name)
+    fn.argtypes = list(types)
+    fn.restype = None
+    return fn
+
+
+def test_against_reference_cuda_kernels(ops, ref):
+    P, I, F = ctypes.c_void_p, ctypes.c_int, ctypes.c_float
+    rng = np.random.default_rng(11)
+    # softmax 4096 x 1024 (C1)
+    x = (rng.standard_normal((4096, 1024)) * 4).astype(np.float32)
+    a, b = torch.empty(4096, 1024, device="cuda"), torch.empty(4096, 1024, device="cuda")
+    ops.softmax(dev(x), a, 4096, 1024, 0)
+    _f(ref, "ref_softmax", P, P, I, I)(dev(x).data_ptr(), b.data_ptr(), 4096, 1024)
+    close(host(a), host(b))
+    # layer_norm 4096 x 2048 (C1)
+    x = rng.standard_normal((4096, 2048)).astype(np.float32)
+    gm = rng.uniform(0.5, 1.5, 2048).astype(np.float32)
+    bt = (rng.standard_normal(2048) * 0.1).astype(np.float32)
+    a, b = torch.empty(4096, 2048, device="cuda"), torch.empty(4096, 2048, device="cuda")
+    dx, dg, db = dev(x), dev(gm), dev(bt)
+    ops.layer_norm(dx, a, dg, db, 4096, 2048, 1e-5, 0)
+    _f(ref, "ref_layer_norm", P, P, P, P, I, I, F)(dx.data_ptr(), b.data_ptr(), dg.data_ptr(), db.data_ptr(), 4096,
+                                                    2048, 1e-5)
+    close(host(a), host(b))
+    # mat_mul + ReLU 1024x2048 @ 2048x1024 (C1)
+    A = (rng.standard_normal((1024, 2048)) / math.sqrt(2048)).astype(np.float32)
+    B = (rng.standard_normal((2048, 1024)) / math.sqrt(2048)).astype(np.float32)
+    a, b = torch.empty(1024, 1024, device="cuda"), torch.empty(1024, 1024, device="cuda")
+    dA, dB = dev(A), dev(B)
+    ops.mat_mul(dA, dB, a, 1024, 2048, 1024, 1, 0.0, 0)
+    _f(ref, "ref_mat_mul_relu", P, P, P, I, I, I)(dA.data_ptr(), dB.data_ptr(), b.data_ptr(), 1024, 2048, 1024)
+    close(host(a), host(b))
+    # decode attention at 2300 keys
+    k = rng.standard_normal((8, 2304, 64)).astype(np.float32)
+    v = rng.standard_normal((8, 2304, 64)).astype(np.float32)
+    q = rng.standard_normal((32, 64)).astype(np.float32)
+    a, b = torch.empty(32, 64, device="cuda"), torch.empty(32, 64, device="cuda")
+    dq, dk, dv = dev(q), dev(k), dev(v)
+    ops.attention_decode(dq, dk, dv, a, 32, 4, 64, 2300, 2304, 0)
+    _f(ref, "ref_attention_decode", P, P, P, P, I, I, I, I, I)(dq.data_ptr(), dk.data_ptr(), dv.data_ptr(),
+                                                             b.data_ptr(), 32, 4, 64, 2300, 2304)
+    model_close(host(a), host(b))
+    _f(ref, "ref_sync")()
