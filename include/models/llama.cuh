@@ -1,0 +1,747 @@
+#pragma once
+
+// Llama-3.2 decoder on sm_100a kernels: LlamaModelT<WT> + LlamaSession keep
+// the API of OpWorks include/models/llama.cuh:47-291 (load, create_session,
+// prefill, decode_step, is_eos, last_logits, copy_last_logits, hidden_state,
+// debug_prefill; LlamaModel = fp32 pack, LlamaModelBF16 = bf16 pack), and
+// LlamaEngineT runs B sequences per forward over a paged KV cache.
+//
+// One forward step (rows = prefill tokens of one sequence, or one decode
+// token for each of B sequences):
+//   embed_rmsnorm                      hidden = E[ids], x = rms(hidden) w_in0
+//   per layer:
+//     QKV GEMM (split-K)  -> qkv_finalize: RoPE, K/V into paged cache, q
+//     attention: decode = split-KV flash decoding (+ combine),
+//                prefill = causal GQA flash attention from the cache
+//     O GEMM -> add_rmsnorm (residual + post-attention norm, fused)
+//     gate/up GEMM (interleaved rows) -> silu_mul
+//     down GEMM -> add_rmsnorm (residual + next layer's input norm)
+//   LM head (tied embedding) -> sample (greedy argmax or exact top-p)
+// 9 launches per layer instead of the reference's 17, and the decode step is
+// captured once per batch size as a CUDA graph (input H2D, forward, sampler,
+// token D2H), so a step costs one graph launch and one stream sync.
+//
+// Precision: kFast = bf16 weights and GEMM operands, fp32 residual stream,
+// fp32 KV cache, fp32 attention and softmax; kAccurate = fp32 end to end
+// (shared-weight fp32 GEMV for <= 4 rows, split-precision TF32 tensor-core
+// GEMM otherwise) — the fp32 model's default, for parity with the reference.
+
+#include <cuda_bf16.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <functional>
+#include <map>
+#include <memory>
+#include <stdexcept>
+#include <vector>
+
+#include "../core/cuda_utils.cuh"
+#include "../ops/attention_kernels.cuh"
+#include "../ops/gemm_sm100.cuh"
+#include "../ops/linear.cuh"
+#include "../ops/llama_kernels.cuh"
+#include "../runtime/kv_cache.cuh"
+#include "../runtime/model_config.cuh"
+#include "../runtime/pack_reader.cuh"
+#include "../runtime/weights.cuh"
+
+namespace opworks {
+
+enum class Precision : int { kAccurate = 0, kFast = 1 };
+
+// Sampling controls of one sequence for one step. temperature <= 0: greedy.
+struct SampleArgs {
+    float temperature = 0.f;
+    float top_p = 1.f;
+    double uniform = -1.0; // >= 0: use this uniform (parity tests); < 0: counter RNG (seed, step)
+    uint64_t seed = 0;
+    int step = 0;
+};
+
+namespace detail {
+
+// Inputs of one step, host-staged (pinned) and device-mirrored, one copy.
+struct StepLayout {
+    int64_t ids, seq, pos, lens, step, temp, top_p, uniform, seed, bytes;
+    static int64_t align8(int64_t x) { return (x + 7) & ~int64_t(7); }
+    static StepLayout make(int rows, int batch) {
+        StepLayout L;
+        int64_t o = 0;
+        L.ids = o;
+        o = align8(o + 4 * int64_t(rows));
+        L.seq = o;
+        o = align8(o + 4 * int64_t(rows));
+        L.pos = o;
+        o = align8(o + 4 * int64_t(rows));
+        L.lens = o;
+        o = align8(o + 4 * int64_t(batch));
+        L.step = o;
+        o = align8(o + 4 * int64_t(batch));
+        L.temp = o;
+        o = align8(o + 4 * int64_t(batch));
+        L.top_p = o;
+        o = align8(o + 4 * int64_t(batch));
+        L.uniform = o;
+        o = align8(o + 8 * int64_t(batch));
+        L.seed = o;
+        o = align8(o + 8 * int64_t(batch));
+        L.bytes = o;
+        return L;
+    }
+};
+
+} // namespace detail
+
+template <typename WT> class LlamaEngineT {
+  public:
+    // max_batch sequences of up to max_seq_len tokens; prefill runs in chunks
+    // of at most prefill_rows tokens (0: max_seq_len).
+    LlamaEngineT(const ModelConfig &cfg, const ModelWeights<WT> &w, int max_batch, int max_seq_len, Precision prec,
+                 int prefill_rows = 0)
+        : cfg_(cfg), w_(w), prec_(prec), max_batch_(max_batch), max_seq_len_(max_seq_len) {
+        detail::require(max_batch > 0, "batch capacity must be positive");
+        detail::require(max_seq_len > 0, "max_seq_len must be positive");
+        detail::require(max_seq_len <= w.rope_max_pos, "max_seq_len exceeds the model's RoPE table");
+        detail::require(cfg.head_dim == detail::kAttnD, "this runtime supports head_dim 64");
+        detail::require(cfg.hidden_size % detail::kRowThreads == 0 && cfg.hidden_size / detail::kRowThreads <= 16,
+                        "hidden size must be a multiple of 256 (<= 4096)");
+        const int rep = cfg.kv_rep();
+        detail::require(rep == 1 || rep == 2 || rep == 4 || rep == 8, "GQA ratio must be 1, 2, 4 or 8");
+        if (prec == Precision::kFast)
+            detail::require(w.sets & kWeightsBF16, "bf16 weights were not loaded");
+        else
+            detail::require((w.sets & kWeightsF32) && (w.sets & kWeightsSplit),
+                            "fp32 weights (accurate path) were not loaded");
+        prefill_rows_ = prefill_rows > 0 ? std::min(prefill_rows, max_seq_len) : max_seq_len;
+        rows_max_ = std::max(prefill_rows_, max_batch);
+        blocks_per_seq_ = (max_seq_len + kKvBlockTokens - 1) / kKvBlockTokens;
+        OPWORKS_CUDA_CHECK(cudaGetDevice(&device_));
+        OPWORKS_CUDA_CHECK(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
+        sm_count_ = detail::device_facts().sm_count;
+        err_word_ = sm100::device_error_word();
+
+        kv_ = KvCache(cfg, max_seq_len, max_batch * blocks_per_seq_);
+        alloc_ = BlockAllocator(kv_.num_blocks);
+        slots_.resize(max_batch);
+        table_host_.assign(static_cast<size_t>(max_batch) * blocks_per_seq_, 0);
+        table_dev_ = TypedDeviceBuffer<int32_t>(static_cast<int64_t>(max_batch) * blocks_per_seq_);
+
+        const int64_t H = cfg.hidden_size, I = cfg.intermediate_size, QW = cfg.q_width();
+        const bool fast = prec == Precision::kFast;
+        hidden_ = TypedDeviceBuffer<float>(rows_max_ * H);
+        q_ = TypedDeviceBuffer<float>(rows_max_ * QW);
+        if (fast) {
+            normed_bf_ = TypedDeviceBuffer<__nv_bfloat16>(rows_max_ * H);
+            attn_bf_ = TypedDeviceBuffer<__nv_bfloat16>(rows_max_ * QW);
+            act_bf_ = TypedDeviceBuffer<__nv_bfloat16>(rows_max_ * I);
+        } else {
+            normed_f_ = TypedDeviceBuffer<float>(rows_max_ * H);
+            normed_lo_ = TypedDeviceBuffer<float>(rows_max_ * H);
+            attn_f_ = TypedDeviceBuffer<float>(rows_max_ * QW);
+            attn_lo_ = TypedDeviceBuffer<float>(rows_max_ * QW);
+            act_f_ = TypedDeviceBuffer<float>(rows_max_ * I);
+            act_lo_ = TypedDeviceBuffer<float>(rows_max_ * I);
+        }
+        // split-K partial buffer: the largest plan over every row count
+        int64_t part = 0;
+        const Projection *projs[4] = {&w.layers[0].qkv, &w.layers[0].o, &w.layers[0].gu, &w.layers[0].down};
+        for (int r = 1; r <= rows_max_; r = (r < 64 ? r + 1 : r + 64)) {
+            for (const Projection *p : projs)
+                part = std::max(part, static_cast<int64_t>(plan_splits(*p, r)) * r * p->out);
+        }
+        for (const Projection *p : projs)
+            part = std::max(part, static_cast<int64_t>(plan_splits(*p, rows_max_)) * rows_max_ * p->out);
+        part_ = TypedDeviceBuffer<float>(part);
+        // split-KV partials of decode attention, for every batch size
+        int64_t attn_rows = 0;
+        for (int n = 1; n <= max_batch; ++n) {
+            const int tps = detail::decode_tokens_per_split(n * cfg.num_kv_heads, max_seq_len, sm_count_);
+            attn_rows = std::max(attn_rows, static_cast<int64_t>(n) * ((max_seq_len + tps - 1) / tps));
+        }
+        attn_po_ = TypedDeviceBuffer<float>(attn_rows * cfg.num_q_heads * detail::kAttnD);
+        attn_pml_ = TypedDeviceBuffer<float>(attn_rows * cfg.num_q_heads * 2);
+        logits_ = TypedDeviceBuffer<float>(static_cast<int64_t>(max_batch) * cfg.vocab_size);
+        tokens_ = TypedDeviceBuffer<int32_t>(max_batch);
+
+        layout_ = detail::StepLayout::make(rows_max_, max_batch);
+        in_dev_ = TypedDeviceBuffer<uint8_t>(layout_.bytes);
+        OPWORKS_CUDA_CHECK(cudaMallocHost(&in_host_, layout_.bytes));
+        std::memset(in_host_, 0, layout_.bytes);
+        OPWORKS_CUDA_CHECK(cudaMallocHost(reinterpret_cast<void **>(&out_host_), sizeof(int32_t) * (max_batch + 1)));
+    }
+
+    ~LlamaEngineT() {
+        cudaSetDevice(device_);
+        for (auto &g : graphs_)
+            cudaGraphExecDestroy(g.second);
+        if (stream_)
+            cudaStreamSynchronize(stream_);
+        if (in_host_)
+            cudaFreeHost(in_host_);
+        if (out_host_)
+            cudaFreeHost(out_host_);
+        if (stream_)
+            cudaStreamDestroy(stream_);
+    }
+    LlamaEngineT(const LlamaEngineT &) = delete;
+    LlamaEngineT &operator=(const LlamaEngineT &) = delete;
+
+    int max_batch() const { return max_batch_; }
+    int max_seq_len() const { return max_seq_len_; }
+    int length(int slot) const { return slots_.at(slot).length; }
+    Precision precision() const { return prec_; }
+    cudaStream_t stream() const { return stream_; }
+    KvCache &cache() { return kv_; }
+
+    void reset(int slot) {
+        check_slot(slot);
+        Slot &s = slots_[slot];
+        for (int b : s.blocks)
+            alloc_.release(b);
+        s.blocks.clear();
+        s.length = 0;
+    }
+
+    // Runs `n` tokens of `slot` (appended after its current length) and
+    // returns the next token sampled from the last position. hook(-1) after
+    // the embedding and hook(l) after each layer (debugging; ids stay put).
+    int32_t prefill(int slot, const int32_t *ids, int n, const SampleArgs &sa,
+                    const std::function<void(int)> &hook = nullptr) {
+        check_slot(slot);
+        detail::require(n > 0, "prefill requires at least one token");
+        detail::require(ids != nullptr, "null token buffer");
+        validate_ids(ids, n);
+        Slot &s = slots_[slot];
+        detail::require(s.length + n <= max_seq_len_, "prompt exceeds the session capacity");
+        OPWORKS_CUDA_CHECK(cudaSetDevice(device_));
+        ensure_blocks(slot, s.length + n);
+        flush_table();
+        int done = 0;
+        while (done < n) {
+            const int rows = std::min(prefill_rows_, n - done);
+            int32_t *h_ids = host_i32(layout_.ids), *h_seq = host_i32(layout_.seq), *h_pos = host_i32(layout_.pos);
+            for (int r = 0; r < rows; ++r) {
+                h_ids[r] = ids[done + r];
+                h_seq[r] = slot;
+                h_pos[r] = s.length + done + r;
+            }
+            const bool last = done + rows == n;
+            if (last)
+                stage_sampling(0, sa);
+            OPWORKS_CUDA_CHECK(
+                cudaMemcpyAsync(in_dev_.data(), in_host_, layout_.bytes, cudaMemcpyHostToDevice, stream_));
+            forward(rows, /*decode=*/false, slot, s.length + done, hook);
+            if (last) {
+                sample(1);
+                fetch_tokens(1);
+            } else {
+                OPWORKS_CUDA_CHECK(cudaStreamSynchronize(stream_)); // staging is reused
+            }
+            done += rows;
+        }
+        s.length += n;
+        check_device_error();
+        return out_host_[0];
+    }
+
+    // One decode token for each of n slots (n <= max_batch); prev[i] is the
+    // token appended to slots[i]; out[i] receives the next token.
+    void decode(int n, const int32_t *slots, const int32_t *prev, const SampleArgs *sa, int32_t *out) {
+        detail::require(n > 0 && n <= max_batch_, "decode batch size outside the engine capacity");
+        OPWORKS_CUDA_CHECK(cudaSetDevice(device_));
+        validate_ids(prev, n);
+        int32_t *h_ids = host_i32(layout_.ids), *h_seq = host_i32(layout_.seq), *h_pos = host_i32(layout_.pos);
+        int32_t *h_lens = host_i32(layout_.lens);
+        for (int i = 0; i < n; ++i) {
+            check_slot(slots[i]);
+            for (int j = 0; j < i; ++j)
+                detail::require(slots[j] != slots[i], "a slot appears twice in one decode step");
+            const Slot &s = slots_[slots[i]];
+            detail::require(s.length < max_seq_len_, "session capacity exhausted");
+        }
+        for (int i = 0; i < n; ++i) {
+            Slot &s = slots_[slots[i]];
+            ensure_blocks(slots[i], s.length + 1);
+            h_ids[i] = prev[i];
+            h_seq[i] = slots[i];
+            h_pos[i] = s.length;
+            h_lens[i] = s.length + 1;
+            stage_sampling(i, sa ? sa[i] : SampleArgs{});
+        }
+        flush_table();
+        auto it = graphs_.find(n);
+        if (it == graphs_.end()) {
+            // first step at this batch size runs eagerly (loads modules, sets
+            // kernel attributes), then the step is captured for reuse
+            decode_body(n);
+            OPWORKS_CUDA_CHECK(cudaStreamSynchronize(stream_));
+            cudaGraph_t graph = nullptr;
+            OPWORKS_CUDA_CHECK(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
+            decode_body(n);
+            OPWORKS_CUDA_CHECK(cudaStreamEndCapture(stream_, &graph));
+            cudaGraphExec_t exec = nullptr;
+            OPWORKS_CUDA_CHECK(cudaGraphInstantiate(&exec, graph, 0));
+            OPWORKS_CUDA_CHECK(cudaGraphDestroy(graph));
+            graphs_[n] = exec;
+        } else {
+            OPWORKS_CUDA_CHECK(cudaGraphLaunch(it->second, stream_));
+        }
+        OPWORKS_CUDA_CHECK(cudaStreamSynchronize(stream_));
+        check_device_error();
+        for (int i = 0; i < n; ++i) {
+            slots_[slots[i]].length += 1;
+            out[i] = out_host_[i];
+        }
+    }
+
+    // Logits of row `row` of the last step (prefill: row 0 = last position).
+    void copy_logits(int row, float *out, int n) {
+        detail::require(n == cfg_.vocab_size, "logits buffer must hold vocab_size floats");
+        detail::require(row >= 0 && row < max_batch_, "logits row outside the batch");
+        OPWORKS_CUDA_CHECK(cudaSetDevice(device_));
+        OPWORKS_CUDA_CHECK(cudaMemcpyAsync(out, logits_.data() + static_cast<int64_t>(row) * cfg_.vocab_size,
+                                           sizeof(float) * static_cast<size_t>(n), cudaMemcpyDeviceToHost, stream_));
+        OPWORKS_CUDA_CHECK(cudaStreamSynchronize(stream_));
+    }
+
+    // Residual stream of the last forward, `rows` x hidden.
+    void copy_hidden(float *out, int rows) {
+        OPWORKS_CUDA_CHECK(cudaSetDevice(device_));
+        OPWORKS_CUDA_CHECK(cudaMemcpyAsync(out, hidden_.data(), sizeof(float) * static_cast<size_t>(rows) *
+                                                                    cfg_.hidden_size,
+                                           cudaMemcpyDeviceToHost, stream_));
+        OPWORKS_CUDA_CHECK(cudaStreamSynchronize(stream_));
+    }
+
+  private:
+    struct Slot {
+        int length = 0;
+        std::vector<int> blocks;
+    };
+    struct Act {
+        const __nv_bfloat16 *bf16;
+        const float *f32;
+        const float *lo;
+    };
+
+    void check_slot(int slot) const {
+        detail::require(slot >= 0 && slot < max_batch_, "slot outside the engine capacity");
+    }
+    void validate_ids(const int32_t *ids, int n) const {
+        for (int i = 0; i < n; ++i)
+            if (ids[i] < 0 || ids[i] >= cfg_.vocab_size)
+                throw std::invalid_argument("token id outside the vocabulary");
+    }
+    int32_t *host_i32(int64_t off) { return reinterpret_cast<int32_t *>(static_cast<char *>(in_host_) + off); }
+    template <typename T> T *dev_at(int64_t off) { return reinterpret_cast<T *>(in_dev_.data() + off); }
+
+    void stage_sampling(int row, const SampleArgs &sa) {
+        char *h = static_cast<char *>(in_host_);
+        reinterpret_cast<float *>(h + layout_.temp)[row] = sa.temperature;
+        reinterpret_cast<float *>(h + layout_.top_p)[row] = sa.top_p;
+        reinterpret_cast<double *>(h + layout_.uniform)[row] = sa.uniform;
+        reinterpret_cast<uint64_t *>(h + layout_.seed)[row] = sa.seed;
+        reinterpret_cast<int32_t *>(h + layout_.step)[row] = sa.step;
+    }
+
+    void ensure_blocks(int slot, int tokens) {
+        Slot &s = slots_[slot];
+        const int need = (tokens + kKvBlockTokens - 1) / kKvBlockTokens;
+        while (static_cast<int>(s.blocks.size()) < need) {
+            const int b = alloc_.alloc();
+            table_host_[static_cast<size_t>(slot) * blocks_per_seq_ + s.blocks.size()] = b;
+            s.blocks.push_back(b);
+            table_dirty_ = true;
+        }
+    }
+    void flush_table() {
+        if (!table_dirty_)
+            return;
+        OPWORKS_CUDA_CHECK(cudaMemcpyAsync(table_dev_.data(), table_host_.data(),
+                                           sizeof(int32_t) * table_host_.size(), cudaMemcpyHostToDevice, stream_));
+        OPWORKS_CUDA_CHECK(cudaStreamSynchronize(stream_)); // host table may change next step
+        table_dirty_ = false;
+    }
+
+    void decode_body(int n) {
+        OPWORKS_CUDA_CHECK(cudaMemcpyAsync(in_dev_.data(), in_host_, layout_.bytes, cudaMemcpyHostToDevice, stream_));
+        forward(n, /*decode=*/true, 0, 0, nullptr);
+        sample(n);
+        OPWORKS_CUDA_CHECK(cudaMemcpyAsync(out_host_, tokens_.data(), sizeof(int32_t) * n, cudaMemcpyDeviceToHost,
+                                           stream_));
+        OPWORKS_CUDA_CHECK(cudaMemcpyAsync(out_host_ + max_batch_, err_word_, sizeof(int32_t),
+                                           cudaMemcpyDeviceToHost, stream_));
+        OPWORKS_CUDA_CHECK(cudaMemsetAsync(err_word_, 0, sizeof(int32_t), stream_));
+    }
+
+    void fetch_tokens(int n) {
+        OPWORKS_CUDA_CHECK(cudaMemcpyAsync(out_host_, tokens_.data(), sizeof(int32_t) * n, cudaMemcpyDeviceToHost,
+                                           stream_));
+        OPWORKS_CUDA_CHECK(cudaMemcpyAsync(out_host_ + max_batch_, err_word_, sizeof(int32_t),
+                                           cudaMemcpyDeviceToHost, stream_));
+        OPWORKS_CUDA_CHECK(cudaMemsetAsync(err_word_, 0, sizeof(int32_t), stream_));
+        OPWORKS_CUDA_CHECK(cudaStreamSynchronize(stream_));
+    }
+
+    void check_device_error() {
+        if (out_host_[max_batch_] != 0) {
+            const int code = out_host_[max_batch_];
+            out_host_[max_batch_] = 0;
+            throw std::runtime_error("a device-side wait timed out in the forward pass (code " +
+                                     std::to_string(code) + ")");
+        }
+    }
+
+    // ------------------------------------------------------------ forward
+
+    bool fast() const { return prec_ == Precision::kFast; }
+
+    int plan_bn(int rows) const { return sm100::gemm_pick_bn(sm100::GemmKind::kBF16, rows); }
+
+    int plan_splits(const Projection &p, int rows) const {
+        if (!fast() && rows <= 4)
+            return 1;
+        const int bn = fast() ? plan_bn(rows) : sm100::gemm_pick_bn(sm100::GemmKind::kTF32x3, rows);
+        const int tiles = ((p.out + kUmmaM - 1) / kUmmaM) * ((rows + bn - 1) / bn);
+        const int kb = fast() ? (p.in + 63) / 64 : (p.in + 31) / 32;
+        return sm100::gemm_pick_splits(tiles, kb, sm_count_, fast() ? 4 : 8);
+    }
+
+    // part[s][rows][p.out] = x[rows][p.in] . W^T (partial over split s)
+    int linear(const Projection &p, const Act &x, int rows) {
+        const int splits = plan_splits(p, rows);
+        if (fast()) {
+            sm100::gemm_tn<sm100::GemmKind::kBF16>({p.bf16.data(), nullptr, p.out, p.in}, {x.bf16, nullptr, rows, p.in},
+                                                   p.in, part_.data(), p.out, splits,
+                                                   static_cast<int64_t>(rows) * p.out, stream_, sm100::Identity{},
+                                                   plan_bn(rows));
+        } else if (rows <= 4) {
+            detail::gemv_rows_launch<float>(x.f32, p.in, p.f32.data(), part_.data(), p.out, rows, p.in, p.out,
+                                            stream_);
+        } else {
+            sm100::gemm_tn<sm100::GemmKind::kTF32x3>(
+                {p.hi.data(), p.lo.data(), p.out, p.in}, {x.f32, x.lo, rows, p.in}, p.in, part_.data(), p.out, splits,
+                static_cast<int64_t>(rows) * p.out, stream_, sm100::Identity{},
+                sm100::gemm_pick_bn(sm100::GemmKind::kTF32x3, rows));
+        }
+        return splits;
+    }
+
+    detail::ActOut act_out(__nv_bfloat16 *bf, float *f, float *lo, int64_t ld, int rows) const {
+        detail::ActOut o;
+        o.ld = ld;
+        if (fast())
+            o.bf16 = bf;
+        else {
+            o.f32 = f;
+            o.lo = rows > 4 ? lo : nullptr;
+        }
+        return o;
+    }
+
+    template <int kPer>
+    void launch_add_rmsnorm(int rows, int splits, const float *w, const detail::ActOut &o) {
+        detail::add_rmsnorm_kernel<kPer><<<rows, detail::kRowThreads, 0, stream_>>>(
+            hidden_.data(), part_.data(), splits, static_cast<int64_t>(rows) * cfg_.hidden_size, w, cfg_.rms_norm_eps,
+            o, cfg_.hidden_size);
+    }
+    void add_rmsnorm(int rows, int splits, const float *w, const detail::ActOut &o) {
+        switch (cfg_.hidden_size / detail::kRowThreads) {
+        case 1: launch_add_rmsnorm<1>(rows, splits, w, o); break;
+        case 2: launch_add_rmsnorm<2>(rows, splits, w, o); break;
+        case 4: launch_add_rmsnorm<4>(rows, splits, w, o); break;
+        case 8: launch_add_rmsnorm<8>(rows, splits, w, o); break;
+        case 16: launch_add_rmsnorm<16>(rows, splits, w, o); break;
+        default: throw std::invalid_argument("unsupported hidden size");
+        }
+        OPWORKS_CUDA_CHECK(cudaGetLastError());
+    }
+    template <int kPer, typename T> void launch_embed(int rows, const T *table, const detail::ActOut &o) {
+        detail::embed_rmsnorm_kernel<kPer, T><<<rows, detail::kRowThreads, 0, stream_>>>(
+            table, dev_at<int32_t>(layout_.ids), hidden_.data(), w_.layers[0].input_norm.data(), cfg_.rms_norm_eps, o,
+            cfg_.hidden_size);
+    }
+    template <typename T> void embed(int rows, const T *table, const detail::ActOut &o) {
+        switch (cfg_.hidden_size / detail::kRowThreads) {
+        case 1: launch_embed<1>(rows, table, o); break;
+        case 2: launch_embed<2>(rows, table, o); break;
+        case 4: launch_embed<4>(rows, table, o); break;
+        case 8: launch_embed<8>(rows, table, o); break;
+        case 16: launch_embed<16>(rows, table, o); break;
+        default: throw std::invalid_argument("unsupported hidden size");
+        }
+        OPWORKS_CUDA_CHECK(cudaGetLastError());
+    }
+
+    template <int kRep>
+    void attention(int rows, bool decode, int slot, int pos0, const detail::PagedKV &kv) {
+        const float scale = 1.f / std::sqrt(static_cast<float>(cfg_.head_dim));
+        const int kvh = cfg_.num_kv_heads, qw = cfg_.q_width();
+        if (decode) {
+            const int tps = detail::decode_tokens_per_split(rows * kvh, max_seq_len_, sm_count_);
+            const int splits = (max_seq_len_ + tps - 1) / tps;
+            if (fast())
+                detail::attn_decode_launch<detail::PagedKV, kRep, __nv_bfloat16>(
+                    q_.data(), qw, kv, dev_at<int32_t>(layout_.lens), rows, kvh, tps, splits, scale, attn_po_.data(),
+                    attn_pml_.data(), attn_bf_.data(), qw, stream_);
+            else
+                detail::attn_decode_launch<detail::PagedKV, kRep, float>(
+                    q_.data(), qw, kv, dev_at<int32_t>(layout_.lens), rows, kvh, tps, splits, scale, attn_po_.data(),
+                    attn_pml_.data(), attn_f_.data(), qw, stream_);
+        } else {
+            if (fast())
+                detail::attn_prefill_launch<detail::PagedKV, kRep, __nv_bfloat16>(
+                    q_.data(), qw, detail::kAttnD, attn_bf_.data(), qw, detail::kAttnD, kv, slot, rows, pos0, kvh,
+                    scale, stream_);
+            else
+                detail::attn_prefill_launch<detail::PagedKV, kRep, float>(
+                    q_.data(), qw, detail::kAttnD, attn_f_.data(), qw, detail::kAttnD, kv, slot, rows, pos0, kvh,
+                    scale, stream_);
+        }
+    }
+
+    void forward(int rows, bool decode, int slot, int pos0, const std::function<void(int)> &hook) {
+        const int H = cfg_.hidden_size, I = cfg_.intermediate_size, QW = cfg_.q_width();
+        const int qh = cfg_.num_q_heads, kvh = cfg_.num_kv_heads;
+        const detail::ActOut normed_o = act_out(normed_bf_.data(), normed_f_.data(), normed_lo_.data(), H, rows);
+        const detail::ActOut attn_o = act_out(attn_bf_.data(), attn_f_.data(), attn_lo_.data(), QW, rows);
+        const detail::ActOut act_o = act_out(act_bf_.data(), act_f_.data(), act_lo_.data(), I, rows);
+        const Act normed{normed_o.bf16, normed_o.f32, normed_o.lo};
+        const Act attn{attn_o.bf16, attn_o.f32, attn_o.lo};
+        const Act act{act_o.bf16, act_o.f32, act_o.lo};
+
+        if (w_.embed_f32.size() > 0)
+            embed(rows, w_.embed_f32.data(), normed_o);
+        else
+            embed(rows, w_.embed_bf16.data(), normed_o);
+        if (hook) {
+            OPWORKS_CUDA_CHECK(cudaStreamSynchronize(stream_));
+            hook(-1);
+        }
+        const detail::TokenMap tm{dev_at<int32_t>(layout_.seq), dev_at<int32_t>(layout_.pos)};
+        for (int l = 0; l < cfg_.num_layers; ++l) {
+            const LayerWeights<WT> &L = w_.layers[l];
+            const detail::PagedKV kv{kv_.k(l), kv_.v(l), table_dev_.data(), blocks_per_seq_, kvh};
+            int s = linear(L.qkv, normed, rows);
+            detail::qkv_finalize_kernel<<<rows, 256, 0, stream_>>>(
+                part_.data(), s, static_cast<int64_t>(rows) * L.qkv.out, qh, kvh,
+                reinterpret_cast<const float2 *>(w_.rope_table.data()), tm, kv, kv_.k(l), kv_.v(l), q_.data());
+            OPWORKS_CUDA_CHECK(cudaGetLastError());
+            switch (cfg_.kv_rep()) {
+            case 1: attention<1>(rows, decode, slot, pos0, kv); break;
+            case 2: attention<2>(rows, decode, slot, pos0, kv); break;
+            case 4: attention<4>(rows, decode, slot, pos0, kv); break;
+            default: attention<8>(rows, decode, slot, pos0, kv); break;
+            }
+            if (attn.lo) {
+                launch_async(stream_, detail::split_rows_kernel, detail::grid_for(static_cast<int64_t>(rows) * QW),
+                             kThreads, attn_f_.data(), rows, QW, static_cast<int64_t>(QW), attn_f_.data(),
+                             attn_lo_.data(), static_cast<int64_t>(QW));
+            }
+            s = linear(L.o, attn, rows);
+            add_rmsnorm(rows, s, L.post_norm.data(), normed_o);
+            s = linear(L.gu, normed, rows);
+            launch_async(stream_, detail::silu_mul_kernel, detail::grid_for(static_cast<int64_t>(rows) * I), kThreads,
+                         part_.data(), s, static_cast<int64_t>(rows) * L.gu.out, rows, I, act_o);
+            s = linear(L.down, act, rows);
+            if (l + 1 < cfg_.num_layers) {
+                add_rmsnorm(rows, s, w_.layers[l + 1].input_norm.data(), normed_o);
+            } else {
+                // the final norm feeds only the LM head, which reads full fp32
+                // on the accurate path (never the tf32 hi/lo split)
+                detail::ActOut final_o = normed_o;
+                final_o.lo = nullptr;
+                add_rmsnorm(rows, s, w_.final_norm.data(), final_o);
+            }
+            if (hook) {
+                OPWORKS_CUDA_CHECK(cudaStreamSynchronize(stream_));
+                hook(l);
+            }
+        }
+        // LM head: every row of a decode step, the last row of a prefill
+        const int lrows = decode ? rows : 1;
+        const int64_t first = decode ? 0 : rows - 1;
+        const int V = cfg_.vocab_size;
+        if (fast()) {
+            sm100::gemm_tn<sm100::GemmKind::kBF16>({w_.embed_bf16.data(), nullptr, V, H},
+                                                   {normed_bf_.data() + first * H, nullptr, lrows, H}, H,
+                                                   logits_.data(), V, 1, 0, stream_, sm100::Identity{},
+                                                   plan_bn(lrows));
+        } else {
+            for (int r0 = 0; r0 < lrows; r0 += 4) {
+                const int r = std::min(4, lrows - r0);
+                detail::gemv_rows_launch<float>(normed_f_.data() + (first + r0) * H, H, w_.embed_f32.data(),
+                                                logits_.data() + static_cast<int64_t>(r0) * V, V, r, H, V, stream_);
+            }
+        }
+    }
+
+    void sample(int rows) {
+        detail::SampleParams sp;
+        sp.temperature = dev_at<float>(layout_.temp);
+        sp.top_p = dev_at<float>(layout_.top_p);
+        sp.uniform = dev_at<double>(layout_.uniform);
+        sp.seed = dev_at<uint64_t>(layout_.seed);
+        sp.step = dev_at<int32_t>(layout_.step);
+        detail::sample_kernel<<<rows, detail::kSampleThreads, 0, stream_>>>(logits_.data(), cfg_.vocab_size,
+                                                                            cfg_.vocab_size, sp, tokens_.data());
+        OPWORKS_CUDA_CHECK(cudaGetLastError());
+    }
+
+    ModelConfig cfg_;
+    const ModelWeights<WT> &w_;
+    Precision prec_;
+    int max_batch_, max_seq_len_, prefill_rows_ = 0, rows_max_ = 0, blocks_per_seq_ = 0;
+    int device_ = 0, sm_count_ = 0;
+    cudaStream_t stream_ = nullptr;
+    int *err_word_ = nullptr;
+    KvCache kv_;
+    BlockAllocator alloc_;
+    std::vector<Slot> slots_;
+    std::vector<int32_t> table_host_;
+    TypedDeviceBuffer<int32_t> table_dev_;
+    bool table_dirty_ = true;
+    TypedDeviceBuffer<float> hidden_, q_, part_, attn_po_, attn_pml_, logits_;
+    TypedDeviceBuffer<__nv_bfloat16> normed_bf_, attn_bf_, act_bf_;
+    TypedDeviceBuffer<float> normed_f_, normed_lo_, attn_f_, attn_lo_, act_f_, act_lo_;
+    TypedDeviceBuffer<int32_t> tokens_;
+    detail::StepLayout layout_{};
+    TypedDeviceBuffer<uint8_t> in_dev_;
+    void *in_host_ = nullptr;
+    int32_t *out_host_ = nullptr;
+    std::map<int, cudaGraphExec_t> graphs_;
+};
+
+template <typename WT> class LlamaModelT {
+  public:
+    using Engine = LlamaEngineT<WT>;
+
+    // Session: KV cache + workspace + stream of one sequence. `cache.length`
+    // and `cache.reset()` keep the reference's contract.
+    struct Session {
+        std::unique_ptr<Engine> engine;
+        struct CacheView {
+            Engine *e = nullptr;
+            int max_seq_len = 0;
+            int length_value() const { return e->length(0); }
+            void reset() { e->reset(0); }
+        } cache;
+        cudaStream_t stream() const { return engine->stream(); }
+    };
+
+    // sets: which weight precisions to keep on the device (0 = default: all
+    // for fp32 packs, bf16 for bf16 packs).
+    static LlamaModelT load(const std::string &pack_path, unsigned sets = 0, int max_positions = 8192) {
+        PackReader pack(pack_path);
+        LlamaModelT m;
+        m.cfg_ = ModelConfig::from_manifest(pack.manifest());
+        if (sets == 0)
+            sets = std::is_same_v<WT, float> ? (kWeightsBF16 | kWeightsF32 | kWeightsSplit) : kWeightsBF16;
+        OPWORKS_CUDA_CHECK(cudaGetDevice(&m.device_));
+        m.weights_ = std::make_unique<ModelWeights<WT>>(ModelWeights<WT>::load(pack, m.cfg_, sets, max_positions));
+        m.default_precision_ = std::is_same_v<WT, float> ? Precision::kAccurate : Precision::kFast;
+        if (m.default_precision_ == Precision::kAccurate && !(sets & kWeightsSplit))
+            m.default_precision_ = Precision::kFast;
+        return m;
+    }
+
+    const ModelConfig &config() const { return cfg_; }
+    const ModelWeights<WT> &weights() const { return *weights_; }
+    int device() const { return device_; }
+    Precision default_precision() const { return default_precision_; }
+
+    Session create_session(int max_seq_len) const {
+        if (max_seq_len <= 0 || max_seq_len > weights_->rope_max_pos)
+            throw std::invalid_argument("max_seq_len must be in (0, 8192]");
+        OPWORKS_CUDA_CHECK(cudaSetDevice(device_));
+        Session s;
+        s.engine = std::make_unique<Engine>(cfg_, *weights_, 1, max_seq_len, default_precision_);
+        s.cache.e = s.engine.get();
+        s.cache.max_seq_len = max_seq_len;
+        return s;
+    }
+
+    std::unique_ptr<Engine> create_engine(int max_batch, int max_seq_len, Precision prec, int prefill_rows) const {
+        OPWORKS_CUDA_CHECK(cudaSetDevice(device_));
+        return std::make_unique<Engine>(cfg_, *weights_, max_batch, max_seq_len, prec, prefill_rows);
+    }
+
+    int32_t prefill(Session &s, const std::vector<int32_t> &ids) {
+        if (s.engine->length(0) != 0)
+            throw std::invalid_argument("prefill requires a fresh session (reset first)");
+        for (int32_t id : ids)
+            if (id < 0 || id >= cfg_.vocab_size)
+                throw std::invalid_argument("token id outside the vocabulary");
+        if (ids.empty())
+            throw std::invalid_argument("prefill requires at least one token");
+        if (static_cast<int>(ids.size()) > s.cache.max_seq_len)
+            throw std::invalid_argument("prompt exceeds the session capacity");
+        return s.engine->prefill(0, ids.data(), static_cast<int>(ids.size()), SampleArgs{});
+    }
+
+    int32_t decode_step(Session &s, int32_t token) {
+        if (token < 0 || token >= cfg_.vocab_size)
+            throw std::invalid_argument("token id outside the vocabulary");
+        if (s.engine->length(0) >= s.cache.max_seq_len)
+            throw std::invalid_argument("session capacity exhausted");
+        const int32_t slot = 0;
+        int32_t out = 0;
+        SampleArgs sa;
+        s.engine->decode(1, &slot, &token, &sa, &out);
+        return out;
+    }
+
+    bool is_eos(int32_t token) const {
+        return std::find(cfg_.eos_token_ids.begin(), cfg_.eos_token_ids.end(), token) != cfg_.eos_token_ids.end();
+    }
+
+    std::vector<float> last_logits(Session &s) const {
+        std::vector<float> out(cfg_.vocab_size);
+        s.engine->copy_logits(0, out.data(), cfg_.vocab_size);
+        return out;
+    }
+
+    void copy_last_logits(Session &s, float *out, int n) const {
+        if (n != cfg_.vocab_size)
+            throw std::invalid_argument("logits buffer must hold vocab_size floats");
+        s.engine->copy_logits(0, out, n);
+    }
+
+    std::vector<float> hidden_state(Session &s, int rows) const {
+        std::vector<float> out(static_cast<size_t>(rows) * cfg_.hidden_size);
+        s.engine->copy_hidden(out.data(), rows);
+        return out;
+    }
+
+    // Prefill that also returns the residual stream after the embedding and
+    // after each layer (test/debug hook of the reference).
+    std::vector<std::vector<float>> debug_prefill(Session &s, const std::vector<int32_t> &ids) {
+        if (s.engine->length(0) != 0)
+            throw std::invalid_argument("prefill requires a fresh session (reset first)");
+        if (ids.empty())
+            throw std::invalid_argument("prefill requires at least one token");
+        if (static_cast<int>(ids.size()) > s.cache.max_seq_len)
+            throw std::invalid_argument("prompt exceeds the session capacity");
+        const int n = static_cast<int>(ids.size());
+        std::vector<std::vector<float>> captures;
+        s.engine->prefill(0, ids.data(), n, SampleArgs{}, [&](int) {
+            std::vector<float> h(static_cast<size_t>(n) * cfg_.hidden_size);
+            s.engine->copy_hidden(h.data(), n);
+            captures.push_back(std::move(h));
+        });
+        return captures;
+    }
+
+  private:
+    ModelConfig cfg_;
+    std::unique_ptr<ModelWeights<WT>> weights_;
+    int device_ = 0;
+    Precision default_precision_ = Precision::kFast;
+};
+
+using LlamaModel = LlamaModelT<float>;
+using LlamaModelBF16 = LlamaModelT<__nv_bfloat16>;
+
+} // namespace opworks

@@ -20,6 +20,9 @@
 // online softmax; fully masked tiles beyond the causal diagonal are skipped.
 // This fp32 SIMT kernel is the accurate path.
 
+#include <type_traits>
+#include <cuda_bf16.h>
+
 #include "../core/block_reduce.cuh"
 #include "../core/cuda_utils.cuh"
 #include "detail/sm100.cuh"
@@ -334,9 +337,9 @@ struct PrefillSmem {
 // q[t * q_tok + head * q_head + d], out[t * o_tok + head * o_head + d] for
 // query t in [0, T) at absolute position q_offset + t; keys [0, q_offset + T)
 // of sequence `b` in `kv`. grid = (ceil(T / (64 / kRep)), kvh).
-template <class KV, int kRep>
+template <class KV, int kRep, typename OutT>
 __global__ void __launch_bounds__(256)
-    attn_prefill_kernel(const float *__restrict__ q, int64_t q_tok, int64_t q_head, float *__restrict__ out,
+    attn_prefill_kernel(const float *__restrict__ q, int64_t q_tok, int64_t q_head, OutT *__restrict__ out,
                         int64_t o_tok, int64_t o_head, KV kv, int b, int T, int q_offset, float scale, int *err) {
     constexpr int kPos = kAttnTile / kRep; // query positions per CTA
     using SM = PrefillSmem;
@@ -512,9 +515,15 @@ __global__ void __launch_bounds__(256)
         const int r = r0 + jr;
         const int hd = r / kPos, pi = r % kPos;
         const float inv = l_run[jr] > 0.f ? 1.f / l_run[jr] : 0.f;
-        float *dst = out + static_cast<int64_t>(p0 + pi) * o_tok + static_cast<int64_t>(h * kRep + hd) * o_head + c0;
-        *reinterpret_cast<float4 *>(dst) =
-            make_float4(o[jr][0] * inv, o[jr][1] * inv, o[jr][2] * inv, o[jr][3] * inv);
+        OutT *dst = out + static_cast<int64_t>(p0 + pi) * o_tok + static_cast<int64_t>(h * kRep + hd) * o_head + c0;
+        if constexpr (std::is_same_v<OutT, float>) {
+            *reinterpret_cast<float4 *>(dst) =
+                make_float4(o[jr][0] * inv, o[jr][1] * inv, o[jr][2] * inv, o[jr][3] * inv);
+        } else {
+            __nv_bfloat162 *d2 = reinterpret_cast<__nv_bfloat162 *>(dst);
+            d2[0] = __floats2bfloat162_rn(o[jr][0] * inv, o[jr][1] * inv);
+            d2[1] = __floats2bfloat162_rn(o[jr][2] * inv, o[jr][3] * inv);
+        }
     }
 }
 
@@ -532,12 +541,12 @@ template <class KV, int kRep> inline void prepare_decode_kernel() {
     }
 }
 
-template <class KV, int kRep> inline void prepare_prefill_kernel() {
+template <class KV, int kRep, typename OutT> inline void prepare_prefill_kernel() {
     static thread_local int done = -1;
     int dev = 0;
     OPWORKS_CUDA_CHECK(cudaGetDevice(&dev));
     if (done != dev) {
-        OPWORKS_CUDA_CHECK(cudaFuncSetAttribute(attn_prefill_kernel<KV, kRep>,
+        OPWORKS_CUDA_CHECK(cudaFuncSetAttribute(attn_prefill_kernel<KV, kRep, OutT>,
                                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                 static_cast<int>(PrefillSmem::kBytes)));
         done = dev;
@@ -572,14 +581,14 @@ inline void attn_decode_launch(const float *q, int64_t q_stride, const KV &kv, c
     OPWORKS_CUDA_CHECK(cudaGetLastError());
 }
 
-template <class KV, int kRep>
-inline void attn_prefill_launch(const float *q, int64_t q_tok, int64_t q_head, float *out, int64_t o_tok,
+template <class KV, int kRep, typename OutT = float>
+inline void attn_prefill_launch(const float *q, int64_t q_tok, int64_t q_head, OutT *out, int64_t o_tok,
                                 int64_t o_head, const KV &kv, int b, int T, int q_offset, int kvh, float scale,
                                 cudaStream_t stream) {
-    prepare_prefill_kernel<KV, kRep>();
+    prepare_prefill_kernel<KV, kRep, OutT>();
     constexpr int kPos = kAttnTile / kRep;
     const dim3 grid((T + kPos - 1) / kPos, kvh);
-    attn_prefill_kernel<KV, kRep><<<grid, 256, PrefillSmem::kBytes, stream>>>(
+    attn_prefill_kernel<KV, kRep, OutT><<<grid, 256, PrefillSmem::kBytes, stream>>>(
         q, q_tok, q_head, out, o_tok, o_head, kv, b, T, q_offset, scale, sm100::device_error_word());
     OPWORKS_CUDA_CHECK(cudaGetLastError());
 }

@@ -44,14 +44,19 @@ template <> struct GemvVec<__nv_bfloat16> {
     }
 };
 
-// Requires in % kPer == 0 and 16-byte aligned W and x.
-template <typename WT>
+// y[r][o] = sum_i x[r][i] W[o][i] for R <= 4 rows sharing every weight read.
+// x rows are staged once per block in shared memory; one warp per output
+// row, 16-byte weight loads four deep per lane, warp-shuffle reduction.
+// Requires in % kPer == 0 and 16-byte aligned W and x rows.
+template <typename WT, int R>
 __global__ void __launch_bounds__(kThreads)
-    gemv_kernel(const float *__restrict__ x, const WT *__restrict__ W, float *__restrict__ y, int in, int out) {
+    gemv_rows_kernel(const float *__restrict__ x, int64_t ldx, const WT *__restrict__ W, float *__restrict__ y,
+                     int64_t ldy, int in, int out) {
     extern __shared__ float4 xs4[];
     float *xs = reinterpret_cast<float *>(xs4);
-    for (int j = threadIdx.x; j < in / 4; j += blockDim.x)
-        xs4[j] = reinterpret_cast<const float4 *>(x)[j];
+    for (int r = 0; r < R; ++r)
+        for (int j = threadIdx.x; j < in / 4; j += blockDim.x)
+            xs4[r * (in / 4) + j] = reinterpret_cast<const float4 *>(x + r * ldx)[j];
     __syncthreads();
     constexpr int kPer = GemvVec<WT>::kPer;
     const int nvec = in / kPer;
@@ -59,21 +64,69 @@ __global__ void __launch_bounds__(kThreads)
     const int warps_total = gridDim.x * (blockDim.x / kWarpSize);
     for (int row = blockIdx.x * (blockDim.x / kWarpSize) + threadIdx.x / kWarpSize; row < out; row += warps_total) {
         const uint4 *w = reinterpret_cast<const uint4 *>(W + static_cast<int64_t>(row) * in);
-        float acc0 = 0.f, acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
+        float acc[R][2];
+#pragma unroll
+        for (int r = 0; r < R; ++r)
+            acc[r][0] = acc[r][1] = 0.f;
         int v = lane;
-        for (; v + 3 * kWarpSize < nvec; v += 4 * kWarpSize) {
+        for (; v + kWarpSize < nvec; v += 2 * kWarpSize) {
             const uint4 a = __ldg(w + v), b = __ldg(w + v + kWarpSize);
-            const uint4 c = __ldg(w + v + 2 * kWarpSize), d = __ldg(w + v + 3 * kWarpSize);
-            acc0 += GemvVec<WT>::dot(a, xs + v * kPer);
-            acc1 += GemvVec<WT>::dot(b, xs + (v + kWarpSize) * kPer);
-            acc2 += GemvVec<WT>::dot(c, xs + (v + 2 * kWarpSize) * kPer);
-            acc3 += GemvVec<WT>::dot(d, xs + (v + 3 * kWarpSize) * kPer);
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                acc[r][0] += GemvVec<WT>::dot(a, xs + r * in + v * kPer);
+                acc[r][1] += GemvVec<WT>::dot(b, xs + r * in + (v + kWarpSize) * kPer);
+            }
         }
-        for (; v < nvec; v += kWarpSize)
-            acc0 += GemvVec<WT>::dot(__ldg(w + v), xs + v * kPer);
-        const float acc = warp_reduce<ReduceSum>((acc0 + acc1) + (acc2 + acc3));
-        if (lane == 0)
-            y[row] = acc;
+        if (v < nvec) {
+            const uint4 a = __ldg(w + v);
+#pragma unroll
+            for (int r = 0; r < R; ++r)
+                acc[r][0] += GemvVec<WT>::dot(a, xs + r * in + v * kPer);
+        }
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            const float t = warp_reduce<ReduceSum>(acc[r][0] + acc[r][1]);
+            if (lane == 0)
+                y[r * ldy + row] = t;
+        }
+    }
+}
+
+template <typename WT, int R>
+inline void gemv_rows_launch_r(const float *x, int64_t ldx, const WT *W, float *y, int64_t ldy, int in, int out,
+                               cudaStream_t stream) {
+    const int rows_per_block = kThreads / kWarpSize;
+    const int need = (out + rows_per_block - 1) / rows_per_block;
+    const int cap = device_facts().sm_count * 8;
+    const int grid = need < cap ? need : cap;
+    const size_t smem = sizeof(float) * static_cast<size_t>(in) * R;
+    static thread_local int attr_dev = -1;
+    static thread_local size_t attr_bytes = 0;
+    int dev = 0;
+    OPWORKS_CUDA_CHECK(cudaGetDevice(&dev));
+    if (smem > 48 * 1024 && (attr_dev != dev || attr_bytes < smem)) {
+        OPWORKS_CUDA_CHECK(cudaFuncSetAttribute(gemv_rows_kernel<WT, R>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                static_cast<int>(smem)));
+        attr_dev = dev;
+        attr_bytes = smem;
+    }
+    gemv_rows_kernel<WT, R><<<grid, kThreads, smem, stream>>>(x, ldx, W, y, ldy, in, out);
+    OPWORKS_CUDA_CHECK(cudaGetLastError());
+}
+
+inline bool gemv_rows_supported(int in, int rows, size_t kper) {
+    return in % static_cast<int>(kper) == 0 && sizeof(float) * static_cast<size_t>(in) * rows <= 200 * 1024;
+}
+
+// rows in [1, 4]; vector path requirements as gemv_rows_kernel.
+template <typename WT>
+inline void gemv_rows_launch(const float *x, int64_t ldx, const WT *W, float *y, int64_t ldy, int rows, int in,
+                             int out, cudaStream_t stream) {
+    switch (rows) {
+    case 1: gemv_rows_launch_r<WT, 1>(x, ldx, W, y, ldy, in, out, stream); break;
+    case 2: gemv_rows_launch_r<WT, 2>(x, ldx, W, y, ldy, in, out, stream); break;
+    case 3: gemv_rows_launch_r<WT, 3>(x, ldx, W, y, ldy, in, out, stream); break;
+    default: gemv_rows_launch_r<WT, 4>(x, ldx, W, y, ldy, in, out, stream); break;
     }
 }
 
@@ -97,22 +150,16 @@ __global__ void __launch_bounds__(kThreads)
 template <typename WT>
 inline void gemv_launch(const float *x, const WT *W, float *y, int in, int out, cudaStream_t stream) {
     constexpr int kPer = GemvVec<WT>::kPer;
-    const int rows_per_block = kThreads / kWarpSize;
-    const int need = (out + rows_per_block - 1) / rows_per_block;
-    const int cap = device_facts().sm_count * 16;
-    const int grid = need < cap ? need : cap;
-    const size_t smem = sizeof(float) * static_cast<size_t>(in);
-    const bool vec = in % kPer == 0 && reinterpret_cast<uintptr_t>(W) % 16 == 0 &&
-                     reinterpret_cast<uintptr_t>(x) % 16 == 0 && smem <= 200 * 1024;
+    const bool vec = reinterpret_cast<uintptr_t>(W) % 16 == 0 && reinterpret_cast<uintptr_t>(x) % 16 == 0 &&
+                     gemv_rows_supported(in, 1, kPer);
     if (!vec) {
-        launch_async(stream, gemv_scalar_kernel<WT>, grid, kThreads, x, W, y, in, out);
+        const int rows_per_block = kThreads / kWarpSize;
+        const int need = (out + rows_per_block - 1) / rows_per_block;
+        const int cap = device_facts().sm_count * 16;
+        launch_async(stream, gemv_scalar_kernel<WT>, need < cap ? need : cap, kThreads, x, W, y, in, out);
         return;
     }
-    if (smem > 48 * 1024)
-        OPWORKS_CUDA_CHECK(
-            cudaFuncSetAttribute(gemv_kernel<WT>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
-    gemv_kernel<WT><<<grid, kThreads, smem, stream>>>(x, W, y, in, out);
-    OPWORKS_CUDA_CHECK(cudaGetLastError());
+    gemv_rows_launch<WT>(x, in, W, y, out, 1, in, out, stream);
 }
 
 static __global__ void copy_bf16_rows_kernel(const __nv_bfloat16 *__restrict__ src, int rows, int cols,

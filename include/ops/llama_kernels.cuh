@@ -108,7 +108,7 @@ struct TokenMap {
 // part: [splits][rows][qkv] with qkv = (qh + 2 kvh) * 64 columns (q | k | v).
 // q_out: [rows][qh][64] fp32. rope: [max_pos][32][2] (cos, sin) fp32.
 // One CTA (256 threads) per token row.
-__global__ void __launch_bounds__(256)
+static __global__ void __launch_bounds__(256)
     qkv_finalize_kernel(const float *__restrict__ part, int splits, int64_t split_stride, int qh, int kvh,
                         const float2 *__restrict__ rope, TokenMap tm, PagedKV kv, float *__restrict__ kpool,
                         float *__restrict__ vpool, float *__restrict__ q_out) {
@@ -155,7 +155,7 @@ __global__ void __launch_bounds__(256)
 
 // part: [splits][rows][2 * inter] with interleaved columns (2j = gate_j,
 // 2j + 1 = up_j); act[row][j] = silu(g) * u = g / (1 + exp(-g)) * u.
-__global__ void silu_mul_kernel(const float *__restrict__ part, int splits, int64_t split_stride, int rows, int inter,
+static __global__ void silu_mul_kernel(const float *__restrict__ part, int splits, int64_t split_stride, int rows, int inter,
                                 ActOut out) {
     OPWORKS_GRID_LOOP(i, static_cast<int64_t>(rows) * inter) {
         const int64_t row = i / inter;
@@ -174,7 +174,7 @@ __global__ void silu_mul_kernel(const float *__restrict__ part, int splits, int6
 
 // cos/sin table of RoPE: table[pos][i] = (cosf(a), sinf(a)), a = fp32(pos) *
 // inv_freq[i], the same fp32 expression as ops::rope.
-__global__ void rope_table_kernel(const float *__restrict__ inv_freq, int max_pos, int half, float2 *__restrict__ out) {
+static __global__ void rope_table_kernel(const float *__restrict__ inv_freq, int max_pos, int half, float2 *__restrict__ out) {
     OPWORKS_GRID_LOOP(i, static_cast<int64_t>(max_pos) * half) {
         const int pos = static_cast<int>(i / half), j = static_cast<int>(i % half);
         const float a = static_cast<float>(pos) * inv_freq[j];
@@ -184,7 +184,7 @@ __global__ void rope_table_kernel(const float *__restrict__ inv_freq, int max_po
 
 // fp32 weight -> bf16 copy with optional row interleave of two sources:
 // dst row 2j = a[j], 2j + 1 = b[j] (b == nullptr: plain copy of a).
-__global__ void weights_to_bf16_kernel(const float *__restrict__ a, const float *__restrict__ b, int rows, int cols,
+static __global__ void weights_to_bf16_kernel(const float *__restrict__ a, const float *__restrict__ b, int rows, int cols,
                                        __nv_bfloat16 *__restrict__ dst) {
     const int64_t total = static_cast<int64_t>(b ? 2 * rows : rows) * cols;
     OPWORKS_GRID_LOOP(i, total) {
@@ -196,7 +196,7 @@ __global__ void weights_to_bf16_kernel(const float *__restrict__ a, const float 
 }
 
 // Same into a tf32 hi/lo pair.
-__global__ void weights_to_split_kernel(const float *__restrict__ a, const float *__restrict__ b, int rows, int cols,
+static __global__ void weights_to_split_kernel(const float *__restrict__ a, const float *__restrict__ b, int rows, int cols,
                                         float *__restrict__ hi, float *__restrict__ lo) {
     const int64_t total = static_cast<int64_t>(b ? 2 * rows : rows) * cols;
     OPWORKS_GRID_LOOP(i, total) {
@@ -211,7 +211,7 @@ __global__ void weights_to_split_kernel(const float *__restrict__ a, const float
 }
 
 // Same into fp32 (interleave only).
-__global__ void weights_interleave_kernel(const float *__restrict__ a, const float *__restrict__ b, int rows, int cols,
+static __global__ void weights_interleave_kernel(const float *__restrict__ a, const float *__restrict__ b, int rows, int cols,
                                           float *__restrict__ dst) {
     const int64_t total = static_cast<int64_t>(2 * rows) * cols;
     OPWORKS_GRID_LOOP(i, total) {
@@ -221,7 +221,7 @@ __global__ void weights_interleave_kernel(const float *__restrict__ a, const flo
 }
 
 // bf16 weight rows interleave (bf16 packs): dst 2j = a[j], 2j+1 = b[j].
-__global__ void bf16_interleave_kernel(const __nv_bfloat16 *__restrict__ a, const __nv_bfloat16 *__restrict__ b,
+static __global__ void bf16_interleave_kernel(const __nv_bfloat16 *__restrict__ a, const __nv_bfloat16 *__restrict__ b,
                                        int rows, int cols, __nv_bfloat16 *__restrict__ dst) {
     const int64_t total = static_cast<int64_t>(2 * rows) * cols;
     OPWORKS_GRID_LOOP(i, total) {
@@ -236,7 +236,7 @@ __global__ void bf16_interleave_kernel(const __nv_bfloat16 *__restrict__ a, cons
 struct SampleParams {
     const float *temperature; // [rows]; <= 0 selects greedy argmax
     const float *top_p;       // [rows]
-    const double *uniform;    // [rows] host-supplied uniforms, or nullptr
+    const double *uniform;    // [rows] host-supplied uniforms (< 0: use seed/step), or nullptr
     const uint64_t *seed;     // [rows] counter-based uniforms when uniform == nullptr
     const int *step;          // [rows]
 };
@@ -323,7 +323,7 @@ __device__ __forceinline__ void block_exclusive_scan(double v, int c, double *ds
 // return the first index whose cumulative kept mass exceeds u (numpy's
 // Generator.choice rule). The sorted order is found by a 3-level radix
 // select on the float bits of the logits, so no sort is materialised.
-__global__ void __launch_bounds__(kSampleThreads)
+static __global__ void __launch_bounds__(kSampleThreads)
     sample_kernel(const float *__restrict__ logits, int64_t ld, int vocab, SampleParams sp, int *__restrict__ out) {
     __shared__ double hist[kRadixBuckets];
     __shared__ int cnt[kRadixBuckets];
@@ -379,7 +379,10 @@ __global__ void __launch_bounds__(kSampleThreads)
     const double t = fmax(static_cast<double>(temp), 1e-6);
     const double zmax = static_cast<double>(bv) / t;
     const double top_p = sp.top_p ? static_cast<double>(sp.top_p[row]) : 1.0;
-    const double u = sp.uniform ? sp.uniform[row] : counter_uniform(sp.seed[row], sp.step[row]);
+    // host-supplied uniform when >= 0, else the counter-based stream
+    const double u = (sp.uniform && sp.uniform[row] >= 0.0)
+                         ? sp.uniform[row]
+                         : counter_uniform(sp.seed ? sp.seed[row] : 0ull, sp.step ? sp.step[row] : 0);
 
     // mass of every token: e_i = exp(l_i / T - zmax)
     double z = 0.0;

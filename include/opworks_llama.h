@@ -1,0 +1,89 @@
+/* C ABI of the OpWorks-B200 Llama runtime (libopworks_llama.so).
+ *
+ * The first eleven entry points are the ones OpWorks' src/llama_c_api.cu
+ * exports (same names, signatures, return values and error convention:
+ * guarded calls return -1 / NULL, copy at most err_len - 1 bytes of the
+ * message plus a NUL into `err`, and set a thread-local message readable with
+ * opw_llama_last_error()). Sessions must be destroyed before their model.
+ * prefill / decode_step block until the next token is on the host.
+ *
+ * The opw_llama_batch_* / *_ex / set_device entry points are new API: a
+ * batched engine (many sequences per forward over a paged KV cache, CUDA
+ * graph per batch size, device-side greedy or top-p sampling).
+ */
+#ifndef OPWORKS_LLAMA_H
+#define OPWORKS_LLAMA_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* --- OpWorks interface (src/llama_c_api.cu:54-159) --- */
+
+/* replaces opw_llama_load (src/llama_c_api.cu:57-73): float32 or bfloat16 pack */
+void *opw_llama_load(const char *pack_path, char *err, int err_len);
+/* replaces opw_llama_free (src/llama_c_api.cu:75) */
+void opw_llama_free(void *model);
+/* replaces opw_llama_create_session (src/llama_c_api.cu:77-91); max_seq_len in (0, 8192] */
+void *opw_llama_create_session(void *model, int max_seq_len, char *err, int err_len);
+/* replaces opw_llama_destroy_session (src/llama_c_api.cu:93) */
+void opw_llama_destroy_session(void *session);
+/* replaces opw_llama_reset_session (src/llama_c_api.cu:95-102) */
+int opw_llama_reset_session(void *session, char *err, int err_len);
+/* replaces opw_llama_prefill (src/llama_c_api.cu:105-116): first greedy token or -1 */
+int opw_llama_prefill(void *session, const int32_t *tokens, int n, char *err, int err_len);
+/* replaces opw_llama_decode_step (src/llama_c_api.cu:119-126): next greedy token or -1 */
+int opw_llama_decode_step(void *session, int32_t prev_token, char *err, int err_len);
+/* replaces opw_llama_is_eos (src/llama_c_api.cu:129-136): 1, 0 or -1 */
+int opw_llama_is_eos(void *session, int32_t token, char *err, int err_len);
+/* replaces opw_llama_last_logits (src/llama_c_api.cu:139-149): n must be vocab_size */
+int opw_llama_last_logits(void *session, float *out, int n, char *err, int err_len);
+/* replaces opw_llama_vocab_size (src/llama_c_api.cu:151-154); not guarded, as in OpWorks */
+int opw_llama_vocab_size(void *session);
+/* replaces opw_llama_last_error (src/llama_c_api.cu:156) */
+const char *opw_llama_last_error(void);
+
+/* --- extensions (no counterpart in OpWorks) --- */
+
+/* Select the CUDA device used by subsequent loads on this thread. */
+int opw_llama_set_device(int device);
+/* Load keeping only some weight precisions: bit 1 = bf16 (fast path),
+ * 2 = fp32 (accurate GEMV), 4 = tf32 hi/lo (accurate GEMM); 0 = default.
+ * max_positions sizes the RoPE table (>= the longest session). */
+void *opw_llama_load_ex(const char *pack_path, unsigned weight_sets, int max_positions, char *err, int err_len);
+/* Model hyper-parameters: out[0..7] = layers, hidden, intermediate, q heads,
+ * kv heads, head dim, vocab, device. */
+int opw_llama_model_info(void *model, int32_t *out8, char *err, int err_len);
+
+/* Batched engine: max_batch sequences (slots) of up to max_seq_len tokens
+ * each over one paged KV cache. precision: 0 = accurate (fp32), 1 = fast
+ * (bf16 weights and GEMM operands, fp32 residual / KV / softmax).
+ * prefill_rows: prefill chunk size (0 = max_seq_len). */
+void *opw_llama_create_batch(void *model, int max_batch, int max_seq_len, int precision, int prefill_rows, char *err,
+                             int err_len);
+void opw_llama_destroy_batch(void *batch);
+/* Frees the slot's KV blocks; the slot starts empty. */
+int opw_llama_batch_reset(void *batch, int slot, char *err, int err_len);
+/* Current token count of a slot, or -1. */
+int opw_llama_batch_length(void *batch, int slot);
+/* Appends n prompt tokens to `slot` and returns the next token sampled from
+ * the last position: temperature <= 0 -> greedy argmax; otherwise top-p with
+ * the uniform `uniform` when >= 0, else a counter-based draw from (seed, 0). */
+int opw_llama_batch_prefill(void *batch, int slot, const int32_t *tokens, int n, float temperature, float top_p,
+                            double uniform, uint64_t seed, char *err, int err_len);
+/* One decode step for n slots: prev_tokens[i] is appended to slots[i] and
+ * out_tokens[i] receives the next token. temperature / top_p / uniforms /
+ * seeds / steps may be NULL (greedy; counter RNG at step 0). Returns 0 / -1. */
+int opw_llama_batch_decode(void *batch, int n, const int32_t *slots, const int32_t *prev_tokens,
+                           const float *temperature, const float *top_p, const double *uniforms,
+                           const uint64_t *seeds, const int32_t *steps, int32_t *out_tokens, char *err, int err_len);
+/* Logits (vocab_size floats) of row `row` of the last step. */
+int opw_llama_batch_logits(void *batch, int row, float *out, int n, char *err, int err_len);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* OPWORKS_LLAMA_H */

@@ -87,6 +87,13 @@ int opw_attention_prefill_chunked(const float *q_heads, const float *kcache, con
                                   int S, int q_offset, int num_q_heads, int kv_rep, int head_dim, int cap,
                                   void *stream);
 
+/* Fused greedy / top-p sampler of the Llama runtime (ops/llama_kernels.cuh),
+ * the device form of OpWorks' host sampler examples/llama/generate.py:83-109:
+ * one token per row of logits [rows, vocab]; temperature[r] <= 0 selects the
+ * first argmax, otherwise top-p with uniform[r] (device arrays). */
+int opw_sample(const float *logits, int rows, int vocab, const float *temperature, const float *top_p,
+               const double *uniform, int32_t *out, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

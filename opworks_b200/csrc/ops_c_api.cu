@@ -16,6 +16,7 @@
 #include "ops/embedding.cuh"
 #include "ops/linear.cuh"
 #include "ops/linear_mma.cuh"
+#include "ops/llama_kernels.cuh"
 #include "ops/rms_norm.cuh"
 #include "ops/rope.cuh"
 #include "ops/split_heads.cuh"
@@ -251,6 +252,20 @@ int opw_attention_prefill_chunked(const float *q_heads, const float *kcache, con
     return guarded([&] {
         opworks::ops::attention_prefill_chunked(q_heads, kcache, vcache, out, T, S, q_offset, num_q_heads, kv_rep,
                                                 head_dim, cap, as_stream(stream));
+    });
+}
+
+int opw_sample(const float *logits, int rows, int vocab, const float *temperature, const float *top_p,
+               const double *uniform, int32_t *out, void *stream) {
+    return guarded([&] {
+        opworks::detail::require(rows >= 0 && vocab > 0, "sample requires rows >= 0 and vocab > 0");
+        opworks::detail::require(logits && temperature && top_p && uniform && out, "sample requires non-null pointers");
+        if (rows == 0)
+            return;
+        opworks::detail::SampleParams sp{temperature, top_p, uniform, nullptr, nullptr};
+        opworks::detail::sample_kernel<<<rows, opworks::detail::kSampleThreads, 0, as_stream(stream)>>>(
+            logits, vocab, vocab, sp, out);
+        OPWORKS_CUDA_CHECK(cudaGetLastError());
     });
 }
 

@@ -42,6 +42,7 @@ SIGNATURES = {
     "opw_argmax": [P, I, P, P],
     "opw_attention_decode": [P, P, P, P, I, I, I, I, I, P],
     "opw_attention_prefill_chunked": [P, P, P, P, I, I, I, I, I, I, I, P],
+    "opw_sample": [P, I, I, P, P, P, P, P],
 }
 
 
