@@ -35,6 +35,8 @@
 #include <map>
 #include <memory>
 #include <stdexcept>
+#include <string>
+#include <utility>
 #include <vector>
 
 #include "../core/cuda_utils.cuh"
@@ -165,10 +167,13 @@ template <typename WT> class LlamaEngineT {
         logits_ = TypedDeviceBuffer<float>(static_cast<int64_t>(max_batch) * cfg.vocab_size);
         tokens_ = TypedDeviceBuffer<int32_t>(max_batch);
 
-        layout_ = detail::StepLayout::make(rows_max_, max_batch);
-        in_dev_ = TypedDeviceBuffer<uint8_t>(layout_.bytes);
-        OPWORKS_CUDA_CHECK(cudaMallocHost(&in_host_, layout_.bytes));
-        std::memset(in_host_, 0, layout_.bytes);
+        // decode and prefill stage their inputs in separate regions so a decode
+        // step copies only decode-sized arrays
+        dec_ = detail::StepLayout::make(max_batch, max_batch);
+        pre_ = detail::StepLayout::make(prefill_rows_, 1);
+        in_dev_ = TypedDeviceBuffer<uint8_t>(dec_.bytes + pre_.bytes);
+        OPWORKS_CUDA_CHECK(cudaMallocHost(&in_host_, dec_.bytes + pre_.bytes));
+        std::memset(in_host_, 0, dec_.bytes + pre_.bytes);
         OPWORKS_CUDA_CHECK(cudaMallocHost(reinterpret_cast<void **>(&out_host_), sizeof(int32_t) * (max_batch + 1)));
     }
 
@@ -219,6 +224,7 @@ template <typename WT> class LlamaEngineT {
         ensure_blocks(slot, s.length + n);
         flush_table();
         int done = 0;
+        use_layout(pre_, dec_.bytes);
         while (done < n) {
             const int rows = std::min(prefill_rows_, n - done);
             int32_t *h_ids = host_i32(layout_.ids), *h_seq = host_i32(layout_.seq), *h_pos = host_i32(layout_.pos);
@@ -230,8 +236,8 @@ template <typename WT> class LlamaEngineT {
             const bool last = done + rows == n;
             if (last)
                 stage_sampling(0, sa);
-            OPWORKS_CUDA_CHECK(
-                cudaMemcpyAsync(in_dev_.data(), in_host_, layout_.bytes, cudaMemcpyHostToDevice, stream_));
+            OPWORKS_CUDA_CHECK(cudaMemcpyAsync(in_dev_.data() + base_, static_cast<char *>(in_host_) + base_,
+                                               layout_.bytes, cudaMemcpyHostToDevice, stream_));
             forward(rows, /*decode=*/false, slot, s.length + done, hook);
             if (last) {
                 sample(1);
@@ -252,6 +258,7 @@ template <typename WT> class LlamaEngineT {
         detail::require(n > 0 && n <= max_batch_, "decode batch size outside the engine capacity");
         OPWORKS_CUDA_CHECK(cudaSetDevice(device_));
         validate_ids(prev, n);
+        use_layout(dec_, 0);
         int32_t *h_ids = host_i32(layout_.ids), *h_seq = host_i32(layout_.seq), *h_pos = host_i32(layout_.pos);
         int32_t *h_lens = host_i32(layout_.lens);
         for (int i = 0; i < n; ++i) {
@@ -306,6 +313,55 @@ template <typename WT> class LlamaEngineT {
         OPWORKS_CUDA_CHECK(cudaStreamSynchronize(stream_));
     }
 
+    // Bytes the host copies in / out around one decode step of n rows.
+    int64_t decode_h2d_bytes() const { return dec_.bytes; }
+    int64_t decode_d2h_bytes(int n) const { return static_cast<int64_t>(sizeof(int32_t)) * (n + 1); }
+
+    // Device time of every kernel group of one decode step, measured with CUDA
+    // events on the engine stream while re-running the last decode step of n
+    // rows eagerly `iters` times (same inputs; rewrites the same KV entries;
+    // lengths are not advanced). Returns (label, ms per step, launches per
+    // step) in launch order of first appearance.
+    struct KernelTime {
+        std::string label;
+        double ms_per_step = 0.0;
+        int launches_per_step = 0;
+    };
+    std::vector<KernelTime> profile_decode(int n, int iters) {
+        detail::require(graphs_.count(n) != 0, "profile a batch size after one decode step at that size");
+        detail::require(iters > 0, "iters must be positive");
+        OPWORKS_CUDA_CHECK(cudaSetDevice(device_));
+        use_layout(dec_, 0);
+        std::vector<KernelTime> out;
+        for (int it = 0; it < iters; ++it) {
+            marks_.clear();
+            marks_enabled_ = true;
+            mark("");
+            forward(n, /*decode=*/true, 0, 0, nullptr);
+            sample(n);
+            mark("sample");
+            marks_enabled_ = false;
+            OPWORKS_CUDA_CHECK(cudaStreamSynchronize(stream_));
+            for (size_t i = 1; i < marks_.size(); ++i) {
+                float ms = 0.f;
+                OPWORKS_CUDA_CHECK(cudaEventElapsedTime(&ms, marks_[i - 1].second, marks_[i].second));
+                auto f = std::find_if(out.begin(), out.end(),
+                                      [&](const KernelTime &k) { return k.label == marks_[i].first; });
+                if (f == out.end()) {
+                    out.push_back({marks_[i].first, 0.0, 0});
+                    f = out.end() - 1;
+                }
+                f->ms_per_step += ms / iters;
+                if (it == 0)
+                    f->launches_per_step += 1;
+            }
+            for (auto &m : marks_)
+                cudaEventDestroy(m.second);
+            marks_.clear();
+        }
+        return out;
+    }
+
     // Residual stream of the last forward, `rows` x hidden.
     void copy_hidden(float *out, int rows) {
         OPWORKS_CUDA_CHECK(cudaSetDevice(device_));
@@ -326,6 +382,15 @@ template <typename WT> class LlamaEngineT {
         const float *lo;
     };
 
+    void mark(const char *label) {
+        if (!marks_enabled_)
+            return;
+        cudaEvent_t e;
+        OPWORKS_CUDA_CHECK(cudaEventCreate(&e));
+        OPWORKS_CUDA_CHECK(cudaEventRecord(e, stream_));
+        marks_.emplace_back(label, e);
+    }
+
     void check_slot(int slot) const {
         detail::require(slot >= 0 && slot < max_batch_, "slot outside the engine capacity");
     }
@@ -334,11 +399,17 @@ template <typename WT> class LlamaEngineT {
             if (ids[i] < 0 || ids[i] >= cfg_.vocab_size)
                 throw std::invalid_argument("token id outside the vocabulary");
     }
-    int32_t *host_i32(int64_t off) { return reinterpret_cast<int32_t *>(static_cast<char *>(in_host_) + off); }
-    template <typename T> T *dev_at(int64_t off) { return reinterpret_cast<T *>(in_dev_.data() + off); }
+    void use_layout(const detail::StepLayout &L, int64_t base) {
+        layout_ = L;
+        base_ = base;
+    }
+    int32_t *host_i32(int64_t off) {
+        return reinterpret_cast<int32_t *>(static_cast<char *>(in_host_) + base_ + off);
+    }
+    template <typename T> T *dev_at(int64_t off) { return reinterpret_cast<T *>(in_dev_.data() + base_ + off); }
 
     void stage_sampling(int row, const SampleArgs &sa) {
-        char *h = static_cast<char *>(in_host_);
+        char *h = static_cast<char *>(in_host_) + base_;
         reinterpret_cast<float *>(h + layout_.temp)[row] = sa.temperature;
         reinterpret_cast<float *>(h + layout_.top_p)[row] = sa.top_p;
         reinterpret_cast<double *>(h + layout_.uniform)[row] = sa.uniform;
@@ -366,7 +437,7 @@ template <typename WT> class LlamaEngineT {
     }
 
     void decode_body(int n) {
-        OPWORKS_CUDA_CHECK(cudaMemcpyAsync(in_dev_.data(), in_host_, layout_.bytes, cudaMemcpyHostToDevice, stream_));
+        OPWORKS_CUDA_CHECK(cudaMemcpyAsync(in_dev_.data(), in_host_, dec_.bytes, cudaMemcpyHostToDevice, stream_));
         forward(n, /*decode=*/true, 0, 0, nullptr);
         sample(n);
         OPWORKS_CUDA_CHECK(cudaMemcpyAsync(out_host_, tokens_.data(), sizeof(int32_t) * n, cudaMemcpyDeviceToHost,
@@ -516,6 +587,7 @@ template <typename WT> class LlamaEngineT {
             embed(rows, w_.embed_f32.data(), normed_o);
         else
             embed(rows, w_.embed_bf16.data(), normed_o);
+        mark("embed_rmsnorm");
         if (hook) {
             OPWORKS_CUDA_CHECK(cudaStreamSynchronize(stream_));
             hook(-1);
@@ -525,27 +597,35 @@ template <typename WT> class LlamaEngineT {
             const LayerWeights<WT> &L = w_.layers[l];
             const detail::PagedKV kv{kv_.k(l), kv_.v(l), table_dev_.data(), blocks_per_seq_, kvh};
             int s = linear(L.qkv, normed, rows);
+            mark("gemm_qkv");
             detail::qkv_finalize_kernel<<<rows, 256, 0, stream_>>>(
                 part_.data(), s, static_cast<int64_t>(rows) * L.qkv.out, qh, kvh,
                 reinterpret_cast<const float2 *>(w_.rope_table.data()), tm, kv, kv_.k(l), kv_.v(l), q_.data());
             OPWORKS_CUDA_CHECK(cudaGetLastError());
+            mark("qkv_rope_kv_write");
             switch (cfg_.kv_rep()) {
             case 1: attention<1>(rows, decode, slot, pos0, kv); break;
             case 2: attention<2>(rows, decode, slot, pos0, kv); break;
             case 4: attention<4>(rows, decode, slot, pos0, kv); break;
             default: attention<8>(rows, decode, slot, pos0, kv); break;
             }
+            mark("attention");
             if (attn.lo) {
                 launch_async(stream_, detail::split_rows_kernel, detail::grid_for(static_cast<int64_t>(rows) * QW),
                              kThreads, attn_f_.data(), rows, QW, static_cast<int64_t>(QW), attn_f_.data(),
                              attn_lo_.data(), static_cast<int64_t>(QW));
             }
             s = linear(L.o, attn, rows);
+            mark("gemm_o");
             add_rmsnorm(rows, s, L.post_norm.data(), normed_o);
+            mark("residual_rmsnorm");
             s = linear(L.gu, normed, rows);
+            mark("gemm_gate_up");
             launch_async(stream_, detail::silu_mul_kernel, detail::grid_for(static_cast<int64_t>(rows) * I), kThreads,
                          part_.data(), s, static_cast<int64_t>(rows) * L.gu.out, rows, I, act_o);
+            mark("silu_mul");
             s = linear(L.down, act, rows);
+            mark("gemm_down");
             if (l + 1 < cfg_.num_layers) {
                 add_rmsnorm(rows, s, w_.layers[l + 1].input_norm.data(), normed_o);
             } else {
@@ -555,6 +635,7 @@ template <typename WT> class LlamaEngineT {
                 final_o.lo = nullptr;
                 add_rmsnorm(rows, s, w_.final_norm.data(), final_o);
             }
+            mark("residual_rmsnorm");
             if (hook) {
                 OPWORKS_CUDA_CHECK(cudaStreamSynchronize(stream_));
                 hook(l);
@@ -576,6 +657,7 @@ template <typename WT> class LlamaEngineT {
                                                 logits_.data() + static_cast<int64_t>(r0) * V, V, r, H, V, stream_);
             }
         }
+        mark("lm_head");
     }
 
     void sample(int rows) {
@@ -607,11 +689,14 @@ template <typename WT> class LlamaEngineT {
     TypedDeviceBuffer<__nv_bfloat16> normed_bf_, attn_bf_, act_bf_;
     TypedDeviceBuffer<float> normed_f_, normed_lo_, attn_f_, attn_lo_, act_f_, act_lo_;
     TypedDeviceBuffer<int32_t> tokens_;
-    detail::StepLayout layout_{};
+    detail::StepLayout layout_{}, dec_{}, pre_{};
+    int64_t base_ = 0;
     TypedDeviceBuffer<uint8_t> in_dev_;
     void *in_host_ = nullptr;
     int32_t *out_host_ = nullptr;
     std::map<int, cudaGraphExec_t> graphs_;
+    bool marks_enabled_ = false;
+    std::vector<std::pair<std::string, cudaEvent_t>> marks_;
 };
 
 template <typename WT> class LlamaModelT {

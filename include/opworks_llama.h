@@ -82,6 +82,19 @@ int opw_llama_batch_decode(void *batch, int n, const int32_t *slots, const int32
 /* Logits (vocab_size floats) of row `row` of the last step. */
 int opw_llama_batch_logits(void *batch, int row, float *out, int n, char *err, int err_len);
 
+/* The engine's CUDA stream (cudaStream_t), e.g. to record timing events. */
+void *opw_llama_batch_stream(void *batch);
+/* Bytes copied host->device and device->host around one decode step of n
+ * rows: out2[0] = h2d, out2[1] = d2h. */
+int opw_llama_batch_io_bytes(void *batch, int n, int64_t *out2);
+/* Per-kernel device time of the last decode step of n rows (re-run eagerly
+ * `iters` times with CUDA events between launch groups; lengths are not
+ * advanced). Writes up to max_kernels entries: ms_per_step[i],
+ * launches_per_step[i] and a NUL-terminated label of at most 31 characters
+ * at labels + 32 * i. Returns the number of entries, or -1. */
+int opw_llama_batch_profile(void *batch, int n, int iters, float *ms_per_step, int32_t *launches_per_step,
+                            char *labels, int max_kernels, char *err, int err_len);
+
 #ifdef __cplusplus
 }
 #endif

@@ -399,4 +399,46 @@ int opw_llama_batch_logits(void *batch, int row, float *out, int n, char *err, i
         err, err_len);
 }
 
+void *opw_llama_batch_stream(void *batch) {
+    if (!batch)
+        return nullptr;
+    auto *b = static_cast<BatchHolder *>(batch);
+    return with_engine(b, [](auto &e) { return static_cast<void *>(e.stream()); });
+}
+
+int opw_llama_batch_io_bytes(void *batch, int n, int64_t *out2) {
+    if (!batch || !out2)
+        return -1;
+    auto *b = static_cast<BatchHolder *>(batch);
+    with_engine(b, [&](auto &e) {
+        out2[0] = e.decode_h2d_bytes();
+        out2[1] = e.decode_d2h_bytes(n);
+        return 0;
+    });
+    return 0;
+}
+
+int opw_llama_batch_profile(void *batch, int n, int iters, float *ms_per_step, int32_t *launches_per_step,
+                            char *labels, int max_kernels, char *err, int err_len) {
+    return guard(
+        [&] {
+            if (!batch || !ms_per_step || !launches_per_step || !labels)
+                throw std::invalid_argument("null argument");
+            auto *b = static_cast<BatchHolder *>(batch);
+            set_device(b->owner);
+            return with_engine(b, [&](auto &e) {
+                const auto times = e.profile_decode(n, iters);
+                const int count = std::min<int>(max_kernels, static_cast<int>(times.size()));
+                for (int i = 0; i < count; ++i) {
+                    ms_per_step[i] = static_cast<float>(times[i].ms_per_step);
+                    launches_per_step[i] = times[i].launches_per_step;
+                    std::strncpy(labels + 32 * i, times[i].label.c_str(), 31);
+                    labels[32 * i + 31] = '\0';
+                }
+                return count;
+            });
+        },
+        err, err_len);
+}
+
 } // extern "C"

@@ -61,6 +61,9 @@ def bind(lib):
         "opw_llama_batch_prefill": (I, [P, I, I32P, I, F, F, D, U64, S, I]),
         "opw_llama_batch_decode": (I, [P, I, I32P, I32P, FP, FP, DP, U64P, I32P, I32P, S, I]),
         "opw_llama_batch_logits": (I, [P, I, FP, I, S, I]),
+        "opw_llama_batch_stream": (P, [P]),
+        "opw_llama_batch_io_bytes": (I, [P, I, ctypes.POINTER(ctypes.c_int64)]),
+        "opw_llama_batch_profile": (I, [P, I, I, FP, I32P, S, I, S, I]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -161,6 +164,28 @@ class LlamaBatch:
             opt(uniforms, np.float64, DP), opt(seeds, np.uint64, U64P), opt(steps, np.int32, I32P),
             out.ctypes.data_as(I32P), self.err, _ERR_LEN), "decode")
         return out.copy()
+
+    def stream(self):
+        """The engine's cudaStream_t as an integer."""
+        return self.lib.opw_llama_batch_stream(self.handle) or 0
+
+    def io_bytes(self, n):
+        out = np.zeros(2, np.int64)
+        self.lib.opw_llama_batch_io_bytes(self.handle, n, out.ctypes.data_as(ctypes.POINTER(ctypes.c_int64)))
+        return int(out[0]), int(out[1])
+
+    def profile(self, n, iters=3):
+        """[(label, ms per step, launches per step)] of the last decode step of n rows."""
+        k = 32
+        ms = np.zeros(k, np.float32)
+        launches = np.zeros(k, np.int32)
+        labels = ctypes.create_string_buffer(32 * k)
+        cnt = self._check(self.lib.opw_llama_batch_profile(self.handle, n, iters, ms.ctypes.data_as(FP),
+                                                           launches.ctypes.data_as(I32P), labels, k, self.err,
+                                                           _ERR_LEN), "profile")
+        raw = labels.raw
+        return [(raw[32 * i:32 * i + 32].split(b"\0")[0].decode(), float(ms[i]), int(launches[i]))
+                for i in range(cnt)]
 
     def logits(self, row):
         out = np.empty(self.model.vocab, np.float32)

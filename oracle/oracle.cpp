@@ -127,18 +127,29 @@ void orc_rms_norm(const float *x, const float *w, float *out, int rows, int cols
     }
 }
 
+// Double-accumulated dot product with eight independent partial sums (fixed
+// order, so results are deterministic; the independent chains let the CPU
+// pipeline the FMAs instead of waiting on one accumulator).
+static inline double dot_f64(const float *x, const float *w, int n) {
+    double a[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    int i = 0;
+    for (; i + 8 <= n; i += 8)
+        for (int j = 0; j < 8; ++j)
+            a[j] += static_cast<double>(x[i + j]) * w[i + j];
+    for (; i < n; ++i)
+        a[0] += static_cast<double>(x[i]) * w[i];
+    return ((a[0] + a[1]) + (a[2] + a[3])) + ((a[4] + a[5]) + (a[6] + a[7]));
+}
+
 // Y[rows, out] = X[rows, in] @ W[out, in]^T (include/ops/linear.cuh:18-121).
+// Each weight row is streamed once for all rows of X.
 void orc_linear(const float *X, const float *W, float *Y, int rows, int in, int out) {
-#pragma omp parallel for schedule(static) collapse(2)
-    for (int r = 0; r < rows; ++r)
-        for (int o = 0; o < out; ++o) {
-            const float *x = X + static_cast<int64_t>(r) * in;
-            const float *w = W + static_cast<int64_t>(o) * in;
-            double acc = 0.0;
-            for (int i = 0; i < in; ++i)
-                acc += static_cast<double>(x[i]) * w[i];
-            Y[static_cast<int64_t>(r) * out + o] = static_cast<float>(acc);
-        }
+#pragma omp parallel for schedule(static)
+    for (int o = 0; o < out; ++o) {
+        const float *w = W + static_cast<int64_t>(o) * in;
+        for (int r = 0; r < rows; ++r)
+            Y[static_cast<int64_t>(r) * out + o] = static_cast<float>(dot_f64(X + static_cast<int64_t>(r) * in, w, in));
+    }
 }
 
 // Same with bf16 weights (raw uint16 bits).
