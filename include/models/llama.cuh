@@ -332,15 +332,25 @@ template <typename WT> class LlamaEngineT {
         detail::require(iters > 0, "iters must be positive");
         OPWORKS_CUDA_CHECK(cudaSetDevice(device_));
         use_layout(dec_, 0);
+        // the step is captured with event-record nodes between kernel groups,
+        // so the measured intervals contain no host launch latency
+        marks_.clear();
+        marks_enabled_ = true;
+        cudaGraph_t graph = nullptr;
+        OPWORKS_CUDA_CHECK(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
+        mark("");
+        forward(n, /*decode=*/true, 0, 0, nullptr);
+        sample(n);
+        mark("sample");
+        OPWORKS_CUDA_CHECK(cudaStreamEndCapture(stream_, &graph));
+        marks_enabled_ = false;
+        cudaGraphExec_t exec = nullptr;
+        OPWORKS_CUDA_CHECK(cudaGraphInstantiate(&exec, graph, 0));
+        OPWORKS_CUDA_CHECK(cudaGraphDestroy(graph));
         std::vector<KernelTime> out;
+        OPWORKS_CUDA_CHECK(cudaGraphLaunch(exec, stream_)); // warm
         for (int it = 0; it < iters; ++it) {
-            marks_.clear();
-            marks_enabled_ = true;
-            mark("");
-            forward(n, /*decode=*/true, 0, 0, nullptr);
-            sample(n);
-            mark("sample");
-            marks_enabled_ = false;
+            OPWORKS_CUDA_CHECK(cudaGraphLaunch(exec, stream_));
             OPWORKS_CUDA_CHECK(cudaStreamSynchronize(stream_));
             for (size_t i = 1; i < marks_.size(); ++i) {
                 float ms = 0.f;
@@ -355,10 +365,11 @@ template <typename WT> class LlamaEngineT {
                 if (it == 0)
                     f->launches_per_step += 1;
             }
-            for (auto &m : marks_)
-                cudaEventDestroy(m.second);
-            marks_.clear();
         }
+        OPWORKS_CUDA_CHECK(cudaGraphExecDestroy(exec));
+        for (auto &m : marks_)
+            cudaEventDestroy(m.second);
+        marks_.clear();
         return out;
     }
 
@@ -387,7 +398,7 @@ template <typename WT> class LlamaEngineT {
             return;
         cudaEvent_t e;
         OPWORKS_CUDA_CHECK(cudaEventCreate(&e));
-        OPWORKS_CUDA_CHECK(cudaEventRecord(e, stream_));
+        OPWORKS_CUDA_CHECK(cudaEventRecordWithFlags(e, stream_, cudaEventRecordExternal));
         marks_.emplace_back(label, e);
     }
 
