@@ -138,6 +138,9 @@ template <typename WT> class LlamaEngineT {
             normed_bf_ = TypedDeviceBuffer<__nv_bfloat16>(rows_max_ * H);
             attn_bf_ = TypedDeviceBuffer<__nv_bfloat16>(rows_max_ * QW);
             act_bf_ = TypedDeviceBuffer<__nv_bfloat16>(rows_max_ * I);
+            normed_bflo_ = TypedDeviceBuffer<__nv_bfloat16>(rows_max_ * H);
+            attn_bflo_ = TypedDeviceBuffer<__nv_bfloat16>(rows_max_ * QW);
+            act_bflo_ = TypedDeviceBuffer<__nv_bfloat16>(rows_max_ * I);
         } else {
             normed_f_ = TypedDeviceBuffer<float>(rows_max_ * H);
             normed_lo_ = TypedDeviceBuffer<float>(rows_max_ * H);
@@ -389,6 +392,7 @@ template <typename WT> class LlamaEngineT {
     };
     struct Act {
         const __nv_bfloat16 *bf16;
+        const __nv_bfloat16 *bf16_lo;
         const float *f32;
         const float *lo;
     };
@@ -480,7 +484,7 @@ template <typename WT> class LlamaEngineT {
 
     bool fast() const { return prec_ == Precision::kFast; }
 
-    int plan_bn(int rows) const { return sm100::gemm_pick_bn(sm100::GemmKind::kBF16, rows); }
+    int plan_bn(int rows) const { return sm100::gemm_pick_bn(sm100::GemmKind::kBF16x2, rows); }
 
     int plan_splits(const Projection &p, int rows) const {
         if (!fast() && rows <= 4)
@@ -495,10 +499,10 @@ template <typename WT> class LlamaEngineT {
     int linear(const Projection &p, const Act &x, int rows) {
         const int splits = plan_splits(p, rows);
         if (fast()) {
-            sm100::gemm_tn<sm100::GemmKind::kBF16>({p.bf16.data(), nullptr, p.out, p.in}, {x.bf16, nullptr, rows, p.in},
-                                                   p.in, part_.data(), p.out, splits,
-                                                   static_cast<int64_t>(rows) * p.out, stream_, sm100::Identity{},
-                                                   plan_bn(rows));
+            sm100::gemm_tn<sm100::GemmKind::kBF16x2>({p.bf16.data(), nullptr, p.out, p.in},
+                                                     {x.bf16, x.bf16_lo, rows, p.in}, p.in, part_.data(), p.out,
+                                                     splits, static_cast<int64_t>(rows) * p.out, stream_,
+                                                     sm100::Identity{}, plan_bn(rows));
         } else if (rows <= 4) {
             detail::gemv_rows_launch<float>(x.f32, p.in, p.f32.data(), part_.data(), p.out, rows, p.in, p.out,
                                             stream_);
@@ -511,12 +515,14 @@ template <typename WT> class LlamaEngineT {
         return splits;
     }
 
-    detail::ActOut act_out(__nv_bfloat16 *bf, float *f, float *lo, int64_t ld, int rows) const {
+    detail::ActOut act_out(__nv_bfloat16 *bf, __nv_bfloat16 *bflo, float *f, float *lo, int64_t ld,
+                           int rows) const {
         detail::ActOut o;
         o.ld = ld;
-        if (fast())
+        if (fast()) {
             o.bf16 = bf;
-        else {
+            o.bf16_lo = bflo;
+        } else {
             o.f32 = f;
             o.lo = rows > 4 ? lo : nullptr;
         }
@@ -558,41 +564,32 @@ template <typename WT> class LlamaEngineT {
     }
 
     template <int kRep>
-    void attention(int rows, bool decode, int slot, int pos0, const detail::PagedKV &kv) {
+    void attention(int rows, bool decode, int slot, int pos0, const detail::PagedKV &kv, const detail::ActOut &out) {
         const float scale = 1.f / std::sqrt(static_cast<float>(cfg_.head_dim));
         const int kvh = cfg_.num_kv_heads, qw = cfg_.q_width();
         if (decode) {
             const int tps = detail::decode_tokens_per_split(rows * kvh, max_seq_len_, sm_count_);
             const int splits = (max_seq_len_ + tps - 1) / tps;
-            if (fast())
-                detail::attn_decode_launch<detail::PagedKV, kRep, __nv_bfloat16>(
-                    q_.data(), qw, kv, dev_at<int32_t>(layout_.lens), rows, kvh, tps, splits, scale, attn_po_.data(),
-                    attn_pml_.data(), attn_bf_.data(), qw, stream_);
-            else
-                detail::attn_decode_launch<detail::PagedKV, kRep, float>(
-                    q_.data(), qw, kv, dev_at<int32_t>(layout_.lens), rows, kvh, tps, splits, scale, attn_po_.data(),
-                    attn_pml_.data(), attn_f_.data(), qw, stream_);
+            detail::attn_decode_launch<detail::PagedKV, kRep, detail::ActOut>(
+                q_.data(), qw, kv, dev_at<int32_t>(layout_.lens), rows, kvh, tps, splits, scale, attn_po_.data(),
+                attn_pml_.data(), out, stream_);
         } else {
-            if (fast())
-                detail::attn_prefill_launch<detail::PagedKV, kRep, __nv_bfloat16>(
-                    q_.data(), qw, detail::kAttnD, attn_bf_.data(), qw, detail::kAttnD, kv, slot, rows, pos0, kvh,
-                    scale, stream_);
-            else
-                detail::attn_prefill_launch<detail::PagedKV, kRep, float>(
-                    q_.data(), qw, detail::kAttnD, attn_f_.data(), qw, detail::kAttnD, kv, slot, rows, pos0, kvh,
-                    scale, stream_);
+            detail::attn_prefill_launch<detail::PagedKV, kRep, detail::ActOut>(q_.data(), qw, detail::kAttnD, out, kv,
+                                                                               slot, rows, pos0, kvh, scale, stream_);
         }
     }
 
     void forward(int rows, bool decode, int slot, int pos0, const std::function<void(int)> &hook) {
         const int H = cfg_.hidden_size, I = cfg_.intermediate_size, QW = cfg_.q_width();
         const int qh = cfg_.num_q_heads, kvh = cfg_.num_kv_heads;
-        const detail::ActOut normed_o = act_out(normed_bf_.data(), normed_f_.data(), normed_lo_.data(), H, rows);
-        const detail::ActOut attn_o = act_out(attn_bf_.data(), attn_f_.data(), attn_lo_.data(), QW, rows);
-        const detail::ActOut act_o = act_out(act_bf_.data(), act_f_.data(), act_lo_.data(), I, rows);
-        const Act normed{normed_o.bf16, normed_o.f32, normed_o.lo};
-        const Act attn{attn_o.bf16, attn_o.f32, attn_o.lo};
-        const Act act{act_o.bf16, act_o.f32, act_o.lo};
+        const detail::ActOut normed_o =
+            act_out(normed_bf_.data(), normed_bflo_.data(), normed_f_.data(), normed_lo_.data(), H, rows);
+        const detail::ActOut attn_o =
+            act_out(attn_bf_.data(), attn_bflo_.data(), attn_f_.data(), attn_lo_.data(), QW, rows);
+        const detail::ActOut act_o = act_out(act_bf_.data(), act_bflo_.data(), act_f_.data(), act_lo_.data(), I, rows);
+        const Act normed{normed_o.bf16, normed_o.bf16_lo, normed_o.f32, normed_o.lo};
+        const Act attn{attn_o.bf16, attn_o.bf16_lo, attn_o.f32, attn_o.lo};
+        const Act act{act_o.bf16, act_o.bf16_lo, act_o.f32, act_o.lo};
 
         if (w_.embed_f32.size() > 0)
             embed(rows, w_.embed_f32.data(), normed_o);
@@ -615,17 +612,12 @@ template <typename WT> class LlamaEngineT {
             OPWORKS_CUDA_CHECK(cudaGetLastError());
             mark("qkv_rope_kv_write");
             switch (cfg_.kv_rep()) {
-            case 1: attention<1>(rows, decode, slot, pos0, kv); break;
-            case 2: attention<2>(rows, decode, slot, pos0, kv); break;
-            case 4: attention<4>(rows, decode, slot, pos0, kv); break;
-            default: attention<8>(rows, decode, slot, pos0, kv); break;
+            case 1: attention<1>(rows, decode, slot, pos0, kv, attn_o); break;
+            case 2: attention<2>(rows, decode, slot, pos0, kv, attn_o); break;
+            case 4: attention<4>(rows, decode, slot, pos0, kv, attn_o); break;
+            default: attention<8>(rows, decode, slot, pos0, kv, attn_o); break;
             }
             mark("attention");
-            if (attn.lo) {
-                launch_async(stream_, detail::split_rows_kernel, detail::grid_for(static_cast<int64_t>(rows) * QW),
-                             kThreads, attn_f_.data(), rows, QW, static_cast<int64_t>(QW), attn_f_.data(),
-                             attn_lo_.data(), static_cast<int64_t>(QW));
-            }
             s = linear(L.o, attn, rows);
             mark("gemm_o");
             add_rmsnorm(rows, s, L.post_norm.data(), normed_o);
@@ -657,10 +649,10 @@ template <typename WT> class LlamaEngineT {
         const int64_t first = decode ? 0 : rows - 1;
         const int V = cfg_.vocab_size;
         if (fast()) {
-            sm100::gemm_tn<sm100::GemmKind::kBF16>({w_.embed_bf16.data(), nullptr, V, H},
-                                                   {normed_bf_.data() + first * H, nullptr, lrows, H}, H,
-                                                   logits_.data(), V, 1, 0, stream_, sm100::Identity{},
-                                                   plan_bn(lrows));
+            sm100::gemm_tn<sm100::GemmKind::kBF16x2>(
+                {w_.embed_bf16.data(), nullptr, V, H},
+                {normed_bf_.data() + first * H, normed_bflo_.data() + first * H, lrows, H}, H, logits_.data(), V, 1,
+                0, stream_, sm100::Identity{}, plan_bn(lrows));
         } else {
             for (int r0 = 0; r0 < lrows; r0 += 4) {
                 const int r = std::min(4, lrows - r0);
@@ -678,9 +670,7 @@ template <typename WT> class LlamaEngineT {
         sp.uniform = dev_at<double>(layout_.uniform);
         sp.seed = dev_at<uint64_t>(layout_.seed);
         sp.step = dev_at<int32_t>(layout_.step);
-        detail::sample_kernel<<<rows, detail::kSampleThreads, 0, stream_>>>(logits_.data(), cfg_.vocab_size,
-                                                                            cfg_.vocab_size, sp, tokens_.data());
-        OPWORKS_CUDA_CHECK(cudaGetLastError());
+        detail::sample_launch(logits_.data(), cfg_.vocab_size, rows, cfg_.vocab_size, sp, tokens_.data(), stream_);
     }
 
     ModelConfig cfg_;
@@ -697,7 +687,7 @@ template <typename WT> class LlamaEngineT {
     TypedDeviceBuffer<int32_t> table_dev_;
     bool table_dirty_ = true;
     TypedDeviceBuffer<float> hidden_, q_, part_, attn_po_, attn_pml_, logits_;
-    TypedDeviceBuffer<__nv_bfloat16> normed_bf_, attn_bf_, act_bf_;
+    TypedDeviceBuffer<__nv_bfloat16> normed_bf_, attn_bf_, act_bf_, normed_bflo_, attn_bflo_, act_bflo_;
     TypedDeviceBuffer<float> normed_f_, normed_lo_, attn_f_, attn_lo_, act_f_, act_lo_;
     TypedDeviceBuffer<int32_t> tokens_;
     detail::StepLayout layout_{}, dec_{}, pre_{};

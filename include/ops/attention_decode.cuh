@@ -30,11 +30,12 @@ inline void attention_decode(const float *q, const float *kcache, const float *v
     int *lens = scratch.as<int>(po + pml);
     OPWORKS_CUDA_CHECK(cudaMemcpyAsync(lens, &len, sizeof(int), cudaMemcpyHostToDevice, stream));
     const detail::ContigKV kv{kcache, vcache, max_seq};
+    const detail::StridedOut<float> o{out, 0, detail::kAttnD};
     switch (kv_rep) {
-    case 1: detail::attn_decode_launch<detail::ContigKV, 1>(q, 0, kv, lens, 1, kvh, tps, splits, scale, part_o, part_ml, out, 0, stream); break;
-    case 2: detail::attn_decode_launch<detail::ContigKV, 2>(q, 0, kv, lens, 1, kvh, tps, splits, scale, part_o, part_ml, out, 0, stream); break;
-    case 4: detail::attn_decode_launch<detail::ContigKV, 4>(q, 0, kv, lens, 1, kvh, tps, splits, scale, part_o, part_ml, out, 0, stream); break;
-    case 8: detail::attn_decode_launch<detail::ContigKV, 8>(q, 0, kv, lens, 1, kvh, tps, splits, scale, part_o, part_ml, out, 0, stream); break;
+    case 1: detail::attn_decode_launch<detail::ContigKV, 1>(q, 0, kv, lens, 1, kvh, tps, splits, scale, part_o, part_ml, o, stream); break;
+    case 2: detail::attn_decode_launch<detail::ContigKV, 2>(q, 0, kv, lens, 1, kvh, tps, splits, scale, part_o, part_ml, o, stream); break;
+    case 4: detail::attn_decode_launch<detail::ContigKV, 4>(q, 0, kv, lens, 1, kvh, tps, splits, scale, part_o, part_ml, o, stream); break;
+    case 8: detail::attn_decode_launch<detail::ContigKV, 8>(q, 0, kv, lens, 1, kvh, tps, splits, scale, part_o, part_ml, o, stream); break;
     default: detail::require(false, "attention_decode supports kv_rep in {1, 2, 4, 8}");
     }
     // the host value `len` must outlive the async copy

@@ -30,6 +30,68 @@
 namespace opworks::detail {
 
 constexpr int kAttnD = 64;      // head dim supported by these kernels
+
+// Attention output writers: out(t, head, d) = v for query token t.
+template <typename T> struct StridedOut {
+    T *p;
+    int64_t tok, head; // element strides
+    __device__ __forceinline__ void put(int64_t t, int h, int d, float v) const {
+        if constexpr (std::is_same_v<T, float>)
+            p[t * tok + h * head + d] = v;
+        else
+            p[t * tok + h * head + d] = __float2bfloat16_rn(v);
+    }
+    __device__ __forceinline__ void put4(int64_t t, int h, int d0, float a, float b, float c, float e) const {
+        T *dst = p + t * tok + h * head + d0;
+        if constexpr (std::is_same_v<T, float>) {
+            *reinterpret_cast<float4 *>(dst) = make_float4(a, b, c, e);
+        } else {
+            __nv_bfloat162 *d2 = reinterpret_cast<__nv_bfloat162 *>(dst);
+            d2[0] = __floats2bfloat162_rn(a, b);
+            d2[1] = __floats2bfloat162_rn(c, e);
+        }
+    }
+};
+
+// Row-major activation [tokens][qh * 64] for the next GEMM: bf16 (optionally
+// with the bf16 remainder term), or fp32 (optionally split into tf32 hi/lo).
+struct ActOut {
+    __nv_bfloat16 *bf16 = nullptr;    // hi part when bf16_lo != nullptr
+    __nv_bfloat16 *bf16_lo = nullptr; // bf16(x - hi)
+    float *f32 = nullptr;             // tf32 hi part when lo != nullptr
+    float *lo = nullptr;              // x - tf32(x)
+    int64_t ld = 0;                   // row stride (elements)
+    __device__ __forceinline__ static float tf32_rn(float x) {
+        uint32_t u = __float_as_uint(x);
+        if ((u & 0x7f800000u) == 0x7f800000u)
+            return x;
+        u += 0xfffu + ((u >> 13) & 1u);
+        return __uint_as_float(u & 0xffffe000u);
+    }
+    __device__ __forceinline__ void put(int64_t row, int col, float v) const {
+        const int64_t i = row * ld + col;
+        if (bf16) {
+            const __nv_bfloat16 h = __float2bfloat16_rn(v);
+            bf16[i] = h;
+            if (bf16_lo)
+                bf16_lo[i] = __float2bfloat16_rn(v - __bfloat162float(h));
+        } else if (lo) {
+            const float h = tf32_rn(v);
+            f32[i] = h;
+            lo[i] = v - h;
+        } else {
+            f32[i] = v;
+        }
+    }
+    // attention-writer form (head-major columns)
+    __device__ __forceinline__ void put(int64_t t, int h, int d, float v) const { put(t, h * 64 + d, v); }
+    __device__ __forceinline__ void put4(int64_t t, int h, int d0, float a, float b, float c, float e) const {
+        put(t, h * 64 + d0, a);
+        put(t, h * 64 + d0 + 1, b);
+        put(t, h * 64 + d0 + 2, c);
+        put(t, h * 64 + d0 + 3, e);
+    }
+};
 constexpr int kKvChunk = 16;    // tokens per chunk / paged block
 constexpr int kAttnTile = 64;   // keys per staged tile (4 chunks)
 
@@ -93,40 +155,68 @@ __device__ __forceinline__ void stage_kv_tile(const KV &kv, int b, int h, int t0
 
 // ------------------------------------------------------------------ decode
 
-constexpr int kDecodeStages = 3;
+// Decode: one producer warp streams 32-token K/V tiles (2 chunks) through a
+// kDecodeStages-deep ring of bulk copies; 8 consumer warps each own HPW query
+// heads x TPW tokens of every tile and keep their own online-softmax state,
+// so tiles flow without block-wide barriers (a warp releases a stage with one
+// mbarrier arrive). The warps' states are merged once at the end.
+constexpr int kDecodeStages = 4;
+constexpr int kDecodeTile = 32;
+constexpr int kDecodeWarps = 8;
 
-template <int kRep> struct DecodeSmem {
-    static constexpr int kTileFloats = kAttnTile * kAttnD;
-    static constexpr size_t kBytes =
-        sizeof(float) * (2 * kDecodeStages * kTileFloats // K, V stages
-                         + kRep * kAttnD                 // q
-                         + 2 * kRep * kAttnTile          // score halves
-                         + kRep * kAttnTile              // probabilities
-                         + 4 * kRep * kAttnD             // cross-warp reduction
-                         + 4 * kRep)                     // alpha, m, l
-        + 8 * kDecodeStages + 64;
+template <int kRep> struct DecodeGeo {
+    static constexpr int kHPW = kRep < 2 ? kRep : 2;      // heads per warp
+    static constexpr int kG = kRep / kHPW;                // head groups
+    static constexpr int kTG = kDecodeWarps / kG;         // token groups
+    static constexpr int kTPW = kDecodeTile / kTG;        // tokens per warp per tile
+    static constexpr int kDG = 32 / kTPW;                 // lanes per token (dim groups)
+    static constexpr int kDims = kAttnD / kDG;            // dims per lane in QK
+    static constexpr int kVec = kDims / 4;                // float4 per lane per K row
+    static constexpr int kTileFloats = kDecodeTile * kAttnD;
+    static constexpr size_t kBytes = sizeof(float) * (2 * kDecodeStages * kTileFloats + kRep * kAttnD +
+                                                      kTG * kRep * (kAttnD + 2)) +
+                                     16 * kDecodeStages + 64;
+    static_assert(kG * kTG == kDecodeWarps && kTPW * kTG == kDecodeTile && kDG * kTPW == 32, "decode geometry");
 };
 
+template <class KV>
+__device__ __forceinline__ void stage_kv_chunks(const KV &kv, int b, int h, int t0, int t_end, int chunks, float *ks,
+                                                float *vs, uint64_t *bar) {
+    uint32_t bytes = 0;
+    for (int c = 0; c < chunks; ++c) {
+        const int chunk = t0 / kKvChunk + c;
+        if (chunk * kKvChunk < t_end)
+            bytes += 2u * static_cast<uint32_t>(kv.chunk_tokens(chunk)) * kAttnD * 4u;
+    }
+    sm100::mbar_arrive_expect_tx(bar, bytes);
+    for (int c = 0; c < chunks; ++c) {
+        const int chunk = t0 / kKvChunk + c;
+        if (chunk * kKvChunk < t_end) {
+            const uint32_t n = static_cast<uint32_t>(kv.chunk_tokens(chunk)) * kAttnD * 4u;
+            const int64_t off = kv.chunk_offset(b, h, chunk);
+            sm100::bulk_load(ks + c * kKvChunk * kAttnD, kv.k + off, n, bar);
+            sm100::bulk_load(vs + c * kKvChunk * kAttnD, kv.v + off, n, bar);
+        }
+    }
+}
+
 // q: [B][q_stride] with heads at h*64; part_o [B][qh][splits][64]; part_ml
-// [B][qh][splits][2] (running max, running sum).
+// [B][qh][splits][2] (running max, running sum). grid = (splits, kvh, B).
 template <class KV, int kRep>
-__global__ void __launch_bounds__(128)
+__global__ void __launch_bounds__((kDecodeWarps + 1) * 32)
     attn_decode_partial_kernel(const float *__restrict__ q, int64_t q_stride, KV kv, const int *__restrict__ lens,
                                int tokens_per_split, float scale, float *__restrict__ part_o,
                                float *__restrict__ part_ml, int *err) {
-    using SM = DecodeSmem<kRep>;
-    constexpr int kHPW = (kRep + 3) / 4; // heads per softmax warp
+    using G = DecodeGeo<kRep>;
     extern __shared__ __align__(128) uint8_t smem_raw[];
     float *ks = reinterpret_cast<float *>(smem_raw);
-    float *vs = ks + kDecodeStages * SM::kTileFloats;
-    float *qs = vs + kDecodeStages * SM::kTileFloats;
-    float *sc = qs + kRep * kAttnD;
-    float *ps = sc + 2 * kRep * kAttnTile;
-    float *red = ps + kRep * kAttnTile;
-    float *al = red + 4 * kRep * kAttnD;
-    float *mls = al + kRep;
+    float *vs = ks + kDecodeStages * G::kTileFloats;
+    float *qs = vs + kDecodeStages * G::kTileFloats;
+    float *red = qs + kRep * kAttnD;              // [kTG][kRep][64]
+    float *mls = red + G::kTG * kRep * kAttnD;    // [kTG][kRep][2]
     uint64_t *full = reinterpret_cast<uint64_t *>(
-        (reinterpret_cast<uintptr_t>(mls + 3 * kRep) + 7) & ~static_cast<uintptr_t>(7));
+        (reinterpret_cast<uintptr_t>(mls + G::kTG * kRep * 2) + 15) & ~static_cast<uintptr_t>(15));
+    uint64_t *empty = full + kDecodeStages;
 
     const int b = blockIdx.z, h = blockIdx.y, split = blockIdx.x, splits = gridDim.x;
     const int qh_total = gridDim.y * kRep;
@@ -134,174 +224,186 @@ __global__ void __launch_bounds__(128)
     const int len = lens[b];
     const int t_begin = split * tokens_per_split;
     const int t_end = min(len, t_begin + tokens_per_split);
-    const int n_tiles = t_end > t_begin ? (t_end - t_begin + kAttnTile - 1) / kAttnTile : 0;
+    const int n_tiles = t_end > t_begin ? (t_end - t_begin + kDecodeTile - 1) / kDecodeTile : 0;
 
     for (int i = tid; i < kRep * kAttnD; i += blockDim.x)
         qs[i] = q[static_cast<int64_t>(b) * q_stride + static_cast<int64_t>(h) * kRep * kAttnD + i];
     if (tid == 0) {
-        for (int s = 0; s < kDecodeStages; ++s)
+        for (int s = 0; s < kDecodeStages; ++s) {
             sm100::mbar_init(&full[s], 1);
+            sm100::mbar_init(&empty[s], kDecodeWarps);
+        }
         sm100::fence_mbarrier_init();
     }
     __syncthreads();
-    int issued = 0;
-    if (tid == 0) {
-        for (; issued < kDecodeStages && issued < n_tiles; ++issued)
-            stage_kv_tile(kv, b, h, t_begin + issued * kAttnTile, t_end, ks + issued * SM::kTileFloats,
-                          vs + issued * SM::kTileFloats, &full[issued]);
-    }
-
-    float m_run[kHPW], l_run[kHPW];
-#pragma unroll
-    for (int j = 0; j < kHPW; ++j) {
-        m_run[j] = kNegInf;
-        l_run[j] = 0.f;
-    }
-    float acc[kRep][2];
-#pragma unroll
-    for (int hd = 0; hd < kRep; ++hd)
-        acc[hd][0] = acc[hd][1] = 0.f;
 
     bool ok = true;
-    int consumed = 0;
-    for (int tile = 0; tile < n_tiles; ++tile) {
-        const int s = tile % kDecodeStages;
-        const bool landed = sm100::mbar_wait(&full[s], static_cast<uint32_t>(tile / kDecodeStages) & 1u);
-        if (!__syncthreads_and(landed)) {
-            ok = false;
-            break;
-        }
-        consumed = tile + 1;
-        const int t0 = t_begin + tile * kAttnTile;
-        const int valid = min(kAttnTile, t_end - t0);
-        const float *K = ks + s * SM::kTileFloats;
-        const float *V = vs + s * SM::kTileFloats;
-
-        { // partial scores: thread = (token, half of the head dim)
-            const int t = tid & 63, half = tid >> 6;
-            float d[kRep];
-#pragma unroll
-            for (int hd = 0; hd < kRep; ++hd)
-                d[hd] = 0.f;
-            if (t < valid) {
-                const float4 *kr = reinterpret_cast<const float4 *>(K + t * kAttnD + half * 32);
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const int c = (j + t) & 7; // staggered to spread smem banks
-                    const float4 kv4 = kr[c];
-#pragma unroll
-                    for (int hd = 0; hd < kRep; ++hd) {
-                        const float4 qv = reinterpret_cast<const float4 *>(qs + hd * kAttnD + half * 32)[c];
-                        d[hd] += kv4.x * qv.x + kv4.y * qv.y + kv4.z * qv.z + kv4.w * qv.w;
-                    }
+    if (warp == kDecodeWarps) {
+        // producer warp: one elected lane streams the tiles
+        if (lane == 0) {
+            int issued = 0;
+            for (; issued < n_tiles; ++issued) {
+                const int s = issued % kDecodeStages;
+                if (issued >= kDecodeStages &&
+                    !sm100::mbar_wait(&empty[s], static_cast<uint32_t>((issued / kDecodeStages) - 1) & 1u)) {
+                    ok = false;
+                    break;
                 }
+                stage_kv_chunks(kv, b, h, t_begin + issued * kDecodeTile, t_end, kDecodeTile / kKvChunk,
+                                ks + s * G::kTileFloats, vs + s * G::kTileFloats, &full[s]);
             }
-#pragma unroll
-            for (int hd = 0; hd < kRep; ++hd)
-                sc[(half * kRep + hd) * kAttnTile + t] = d[hd];
-        }
-        __syncthreads();
-#pragma unroll
-        for (int j = 0; j < kHPW; ++j) { // online softmax, one warp per head
-            const int hd = warp + 4 * j;
-            if (hd < kRep) {
-                const float s0 = lane < valid
-                                     ? (sc[hd * kAttnTile + lane] + sc[(kRep + hd) * kAttnTile + lane]) * scale
-                                     : kNegInf;
-                const float s1 = lane + 32 < valid ? (sc[hd * kAttnTile + lane + 32] +
-                                                      sc[(kRep + hd) * kAttnTile + lane + 32]) *
-                                                         scale
-                                                   : kNegInf;
-                const float mt = warp_reduce<ReduceMax>(fmaxf(s0, s1));
-                const float m_new = fmaxf(m_run[j], mt);
-                const float alpha = m_run[j] == kNegInf ? 0.f : expf(m_run[j] - m_new);
-                const float p0 = lane < valid ? expf(s0 - m_new) : 0.f;
-                const float p1 = lane + 32 < valid ? expf(s1 - m_new) : 0.f;
-                l_run[j] = l_run[j] * alpha + warp_reduce<ReduceSum>(p0 + p1);
-                m_run[j] = m_new;
-                ps[hd * kAttnTile + lane] = p0;
-                ps[hd * kAttnTile + lane + 32] = p1;
-                if (lane == 0)
-                    al[hd] = alpha;
-            }
-        }
-        __syncthreads();
-        { // P V: warp w takes tokens [16w, 16w+16), lane owns dims 2*lane, 2*lane+1
-#pragma unroll
-            for (int hd = 0; hd < kRep; ++hd) {
-                const float a = al[hd];
-                acc[hd][0] *= a;
-                acc[hd][1] *= a;
-            }
-#pragma unroll 4
-            for (int tt = 0; tt < 16; ++tt) {
-                const int t = warp * 16 + tt;
-                if (t < valid) {
-                    const float2 v2 = *reinterpret_cast<const float2 *>(V + t * kAttnD + 2 * lane);
-#pragma unroll
-                    for (int hd = 0; hd < kRep; ++hd) {
-                        const float p = ps[hd * kAttnTile + t];
-                        acc[hd][0] += p * v2.x;
-                        acc[hd][1] += p * v2.y;
-                    }
-                }
-            }
-        }
-        __syncthreads(); // stage s, scores and probabilities are free again
-        if (tid == 0 && issued < n_tiles) {
-            const int ns = issued % kDecodeStages;
-            stage_kv_tile(kv, b, h, t_begin + issued * kAttnTile, t_end, ks + ns * SM::kTileFloats,
-                          vs + ns * SM::kTileFloats, &full[ns]);
-            ++issued;
+            // every issued copy must land before the CTA may exit
+            for (int j = (issued > kDecodeStages ? issued - kDecodeStages : 0); j < issued; ++j)
+                if (!sm100::mbar_wait(&full[j % kDecodeStages], static_cast<uint32_t>(j / kDecodeStages) & 1u))
+                    ok = false;
         }
     }
 
-    if (!ok) {
-        // drain copies still in flight before the CTA exits
-        if (tid == 0) {
-            for (int j = consumed; j < issued; ++j)
-                sm100::mbar_wait(&full[j % kDecodeStages], static_cast<uint32_t>(j / kDecodeStages) & 1u);
-            atomicExch(err, 2);
+    // consumer geometry
+    const int hg = warp % G::kG;           // head group: heads hg*HPW ...
+    const int tg = warp / G::kG;           // token group within every tile
+    const int tl = lane / G::kDG;          // token of this lane within the warp's tokens
+    const int dq = lane % G::kDG;          // dim group of this lane (QK)
+    float m_run[G::kHPW], l_run[G::kHPW], acc[G::kHPW][2];
+#pragma unroll
+    for (int j = 0; j < G::kHPW; ++j) {
+        m_run[j] = kNegInf;
+        l_run[j] = 0.f;
+        acc[j][0] = acc[j][1] = 0.f;
+    }
+    if (warp < kDecodeWarps) {
+        for (int tile = 0; tile < n_tiles; ++tile) {
+            const int s = tile % kDecodeStages;
+            if (!sm100::mbar_wait(&full[s], static_cast<uint32_t>(tile / kDecodeStages) & 1u)) {
+                ok = false;
+                break;
+            }
+            const float *K = ks + s * G::kTileFloats;
+            const float *V = vs + s * G::kTileFloats;
+            const int t0 = t_begin + tile * kDecodeTile;
+            const int tok = tg * G::kTPW + tl; // token within the tile
+            const bool valid = t0 + tok < t_end;
+            // QK: this lane's kDims dims of one token for the warp's heads
+            float d[G::kHPW];
+#pragma unroll
+            for (int j = 0; j < G::kHPW; ++j)
+                d[j] = 0.f;
+            if (valid) {
+                const float4 *kr = reinterpret_cast<const float4 *>(K + tok * kAttnD + dq * G::kDims);
+#pragma unroll
+                for (int c = 0; c < G::kVec; ++c) {
+                    const int cc = (c + tok) % G::kVec; // staggered: spreads smem banks
+                    const float4 k4 = kr[cc];
+#pragma unroll
+                    for (int j = 0; j < G::kHPW; ++j) {
+                        const float4 q4 =
+                            reinterpret_cast<const float4 *>(qs + (hg * G::kHPW + j) * kAttnD + dq * G::kDims)[cc];
+                        d[j] += k4.x * q4.x + k4.y * q4.y + k4.z * q4.z + k4.w * q4.w;
+                    }
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < G::kHPW; ++j) {
+#pragma unroll
+                for (int off = 1; off < G::kDG; off <<= 1)
+                    d[j] += __shfl_xor_sync(kFullWarpMask, d[j], off);
+                d[j] = valid ? d[j] * scale : kNegInf;
+            }
+            // online softmax over the warp's tokens, per head
+            float p[G::kHPW], alpha[G::kHPW];
+#pragma unroll
+            for (int j = 0; j < G::kHPW; ++j) {
+                float mt = d[j];
+#pragma unroll
+                for (int off = G::kDG; off < 32; off <<= 1)
+                    mt = fmaxf(mt, __shfl_xor_sync(kFullWarpMask, mt, off));
+                const float m_new = fmaxf(m_run[j], mt);
+                alpha[j] = m_run[j] == kNegInf ? (m_new == kNegInf ? 1.f : 0.f) : expf(m_run[j] - m_new);
+                p[j] = valid ? expf(d[j] - m_new) : 0.f;
+                float ps = dq == 0 ? p[j] : 0.f;
+#pragma unroll
+                for (int off = 1; off < 32; off <<= 1)
+                    ps += __shfl_xor_sync(kFullWarpMask, ps, off);
+                l_run[j] = l_run[j] * alpha[j] + ps;
+                m_run[j] = m_new;
+                acc[j][0] *= alpha[j];
+                acc[j][1] *= alpha[j];
+            }
+            // PV: lane owns dims 2*lane, 2*lane + 1
+#pragma unroll
+            for (int t = 0; t < G::kTPW; ++t) {
+                const int tt = tg * G::kTPW + t;
+                const bool tv = t0 + tt < t_end;
+                float pt[G::kHPW];
+#pragma unroll
+                for (int j = 0; j < G::kHPW; ++j)
+                    pt[j] = __shfl_sync(kFullWarpMask, p[j], t * G::kDG);
+                if (tv) {
+                    const float2 v2 = *reinterpret_cast<const float2 *>(V + tt * kAttnD + 2 * lane);
+#pragma unroll
+                    for (int j = 0; j < G::kHPW; ++j) {
+                        acc[j][0] += pt[j] * v2.x;
+                        acc[j][1] += pt[j] * v2.y;
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0)
+                sm100::mbar_arrive(&empty[s]);
         }
+    }
+    ok = __syncthreads_and(ok);
+    if (!ok) {
+        if (tid == 0)
+            atomicExch(err, 2);
         return;
     }
+    // merge the token groups: every warp publishes its (m, l, acc)
+    if (warp < kDecodeWarps) {
 #pragma unroll
-    for (int hd = 0; hd < kRep; ++hd) {
-        red[(warp * kRep + hd) * kAttnD + 2 * lane] = acc[hd][0];
-        red[(warp * kRep + hd) * kAttnD + 2 * lane + 1] = acc[hd][1];
-    }
-#pragma unroll
-    for (int j = 0; j < kHPW; ++j) {
-        const int hd = warp + 4 * j;
-        if (hd < kRep && lane == 0) {
-            mls[2 * hd] = m_run[j];
-            mls[2 * hd + 1] = l_run[j];
+        for (int j = 0; j < G::kHPW; ++j) {
+            const int head = hg * G::kHPW + j;
+            float *o = red + (tg * kRep + head) * kAttnD;
+            o[2 * lane] = acc[j][0];
+            o[2 * lane + 1] = acc[j][1];
+            if (lane == 0) {
+                mls[(tg * kRep + head) * 2] = m_run[j];
+                mls[(tg * kRep + head) * 2 + 1] = l_run[j];
+            }
         }
     }
     __syncthreads();
     for (int i = tid; i < kRep * kAttnD; i += blockDim.x) {
-        const int hd = i / kAttnD, d = i % kAttnD;
-        const float o = red[(0 * kRep + hd) * kAttnD + d] + red[(1 * kRep + hd) * kAttnD + d] +
-                        red[(2 * kRep + hd) * kAttnD + d] + red[(3 * kRep + hd) * kAttnD + d];
-        const int64_t row = (static_cast<int64_t>(b) * qh_total + h * kRep + hd) * splits + split;
-        part_o[row * kAttnD + d] = o;
-    }
-    if (tid < kRep) {
-        const int64_t row = (static_cast<int64_t>(b) * qh_total + h * kRep + tid) * splits + split;
-        part_ml[2 * row] = mls[2 * tid];
-        part_ml[2 * row + 1] = mls[2 * tid + 1];
+        const int head = i / kAttnD, dd = i % kAttnD;
+        float M = kNegInf;
+        for (int g = 0; g < G::kTG; ++g)
+            M = fmaxf(M, mls[(g * kRep + head) * 2]);
+        float L = 0.f, O = 0.f;
+        if (M != kNegInf) {
+            for (int g = 0; g < G::kTG; ++g) {
+                const float mg = mls[(g * kRep + head) * 2];
+                if (mg == kNegInf)
+                    continue;
+                const float w = expf(mg - M);
+                L += w * mls[(g * kRep + head) * 2 + 1];
+                O += w * red[(g * kRep + head) * kAttnD + dd];
+            }
+        }
+        const int64_t row = (static_cast<int64_t>(b) * qh_total + h * kRep + head) * splits + split;
+        part_o[row * kAttnD + dd] = O;
+        if (dd == 0) {
+            part_ml[2 * row] = M;
+            part_ml[2 * row + 1] = L;
+        }
     }
 }
 
-__device__ __forceinline__ void store_out(float *p, float v) { *p = v; }
-__device__ __forceinline__ void store_out(__nv_bfloat16 *p, float v) { *p = __float2bfloat16_rn(v); }
-
 // Merge the split partials of every (sequence, q head): block = 64 threads
-// (one per dim), grid = (qh, B). out[b * out_stride + hq * 64 + d].
-template <typename OutT>
+// (one per dim), grid = (qh, B); out(b, hq, d).
+template <typename Out>
 __global__ void __launch_bounds__(64)
     attn_decode_combine_kernel(const float *__restrict__ part_o, const float *__restrict__ part_ml, int splits,
-                               OutT *__restrict__ out, int64_t out_stride) {
+                               Out out) {
     const int hq = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
     const int64_t base = (static_cast<int64_t>(b) * gridDim.x + hq) * splits;
     float M = kNegInf;
@@ -318,8 +420,7 @@ __global__ void __launch_bounds__(64)
             o += w * part_o[(base + s) * kAttnD + d];
         }
     }
-    store_out(out + static_cast<int64_t>(b) * out_stride + static_cast<int64_t>(hq) * kAttnD + d,
-              L > 0.f ? o / L : 0.f);
+    out.put(b, hq, d, L > 0.f ? o / L : 0.f);
 }
 
 // ----------------------------------------------------------------- prefill
@@ -337,10 +438,10 @@ struct PrefillSmem {
 // q[t * q_tok + head * q_head + d], out[t * o_tok + head * o_head + d] for
 // query t in [0, T) at absolute position q_offset + t; keys [0, q_offset + T)
 // of sequence `b` in `kv`. grid = (ceil(T / (64 / kRep)), kvh).
-template <class KV, int kRep, typename OutT>
+template <class KV, int kRep, typename Out>
 __global__ void __launch_bounds__(256)
-    attn_prefill_kernel(const float *__restrict__ q, int64_t q_tok, int64_t q_head, OutT *__restrict__ out,
-                        int64_t o_tok, int64_t o_head, KV kv, int b, int T, int q_offset, float scale, int *err) {
+    attn_prefill_kernel(const float *__restrict__ q, int64_t q_tok, int64_t q_head, Out out, KV kv, int b, int T,
+                        int q_offset, float scale, int *err) {
     constexpr int kPos = kAttnTile / kRep; // query positions per CTA
     using SM = PrefillSmem;
     extern __shared__ __align__(128) uint8_t smem_raw[];
@@ -515,15 +616,7 @@ __global__ void __launch_bounds__(256)
         const int r = r0 + jr;
         const int hd = r / kPos, pi = r % kPos;
         const float inv = l_run[jr] > 0.f ? 1.f / l_run[jr] : 0.f;
-        OutT *dst = out + static_cast<int64_t>(p0 + pi) * o_tok + static_cast<int64_t>(h * kRep + hd) * o_head + c0;
-        if constexpr (std::is_same_v<OutT, float>) {
-            *reinterpret_cast<float4 *>(dst) =
-                make_float4(o[jr][0] * inv, o[jr][1] * inv, o[jr][2] * inv, o[jr][3] * inv);
-        } else {
-            __nv_bfloat162 *d2 = reinterpret_cast<__nv_bfloat162 *>(dst);
-            d2[0] = __floats2bfloat162_rn(o[jr][0] * inv, o[jr][1] * inv);
-            d2[1] = __floats2bfloat162_rn(o[jr][2] * inv, o[jr][3] * inv);
-        }
+        out.put4(p0 + pi, h * kRep + hd, c0, o[jr][0] * inv, o[jr][1] * inv, o[jr][2] * inv, o[jr][3] * inv);
     }
 }
 
@@ -536,17 +629,17 @@ template <class KV, int kRep> inline void prepare_decode_kernel() {
     if (done != dev) {
         OPWORKS_CUDA_CHECK(cudaFuncSetAttribute(attn_decode_partial_kernel<KV, kRep>,
                                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                static_cast<int>(DecodeSmem<kRep>::kBytes)));
+                                                static_cast<int>(DecodeGeo<kRep>::kBytes)));
         done = dev;
     }
 }
 
-template <class KV, int kRep, typename OutT> inline void prepare_prefill_kernel() {
+template <class KV, int kRep, typename Out> inline void prepare_prefill_kernel() {
     static thread_local int done = -1;
     int dev = 0;
     OPWORKS_CUDA_CHECK(cudaGetDevice(&dev));
     if (done != dev) {
-        OPWORKS_CUDA_CHECK(cudaFuncSetAttribute(attn_prefill_kernel<KV, kRep, OutT>,
+        OPWORKS_CUDA_CHECK(cudaFuncSetAttribute(attn_prefill_kernel<KV, kRep, Out>,
                                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                 static_cast<int>(PrefillSmem::kBytes)));
         done = dev;
@@ -567,29 +660,27 @@ inline int decode_tokens_per_split(int pairs, int max_len, int sm_count) {
     return (tiles_per_split > 0 ? tiles_per_split : 1) * kAttnTile;
 }
 
-template <class KV, int kRep, typename OutT>
+template <class KV, int kRep, typename Out>
 inline void attn_decode_launch(const float *q, int64_t q_stride, const KV &kv, const int *lens, int batch, int kvh,
                                int tokens_per_split, int splits, float scale, float *part_o, float *part_ml,
-                               OutT *out, int64_t out_stride, cudaStream_t stream) {
+                               const Out &out, cudaStream_t stream) {
     prepare_decode_kernel<KV, kRep>();
     const dim3 grid(splits, kvh, batch);
-    attn_decode_partial_kernel<KV, kRep><<<grid, 128, DecodeSmem<kRep>::kBytes, stream>>>(
+    attn_decode_partial_kernel<KV, kRep><<<grid, (kDecodeWarps + 1) * 32, DecodeGeo<kRep>::kBytes, stream>>>(
         q, q_stride, kv, lens, tokens_per_split, scale, part_o, part_ml, sm100::device_error_word());
     OPWORKS_CUDA_CHECK(cudaGetLastError());
-    attn_decode_combine_kernel<OutT><<<dim3(kvh * kRep, batch), 64, 0, stream>>>(part_o, part_ml, splits, out,
-                                                                                 out_stride);
+    attn_decode_combine_kernel<Out><<<dim3(kvh * kRep, batch), 64, 0, stream>>>(part_o, part_ml, splits, out);
     OPWORKS_CUDA_CHECK(cudaGetLastError());
 }
 
-template <class KV, int kRep, typename OutT = float>
-inline void attn_prefill_launch(const float *q, int64_t q_tok, int64_t q_head, OutT *out, int64_t o_tok,
-                                int64_t o_head, const KV &kv, int b, int T, int q_offset, int kvh, float scale,
-                                cudaStream_t stream) {
-    prepare_prefill_kernel<KV, kRep, OutT>();
+template <class KV, int kRep, typename Out>
+inline void attn_prefill_launch(const float *q, int64_t q_tok, int64_t q_head, const Out &out, const KV &kv, int b,
+                                int T, int q_offset, int kvh, float scale, cudaStream_t stream) {
+    prepare_prefill_kernel<KV, kRep, Out>();
     constexpr int kPos = kAttnTile / kRep;
     const dim3 grid((T + kPos - 1) / kPos, kvh);
-    attn_prefill_kernel<KV, kRep, OutT><<<grid, 256, PrefillSmem::kBytes, stream>>>(
-        q, q_tok, q_head, out, o_tok, o_head, kv, b, T, q_offset, scale, sm100::device_error_word());
+    attn_prefill_kernel<KV, kRep, Out><<<grid, 256, PrefillSmem::kBytes, stream>>>(
+        q, q_tok, q_head, out, kv, b, T, q_offset, scale, sm100::device_error_word());
     OPWORKS_CUDA_CHECK(cudaGetLastError());
 }
 

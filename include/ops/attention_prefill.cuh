@@ -24,11 +24,12 @@ inline void attention_prefill_chunked(const float *q_heads, const float *kcache,
     const float scale = 1.f / sqrtf(static_cast<float>(head_dim));
     const detail::ContigKV kv{kcache, vcache, cap};
     const int64_t tok = detail::kAttnD, head = static_cast<int64_t>(T) * detail::kAttnD;
+    const detail::StridedOut<float> o{out, tok, head};
     switch (kv_rep) {
-    case 1: detail::attn_prefill_launch<detail::ContigKV, 1>(q_heads, tok, head, out, tok, head, kv, 0, T, q_offset, kvh, scale, stream); break;
-    case 2: detail::attn_prefill_launch<detail::ContigKV, 2>(q_heads, tok, head, out, tok, head, kv, 0, T, q_offset, kvh, scale, stream); break;
-    case 4: detail::attn_prefill_launch<detail::ContigKV, 4>(q_heads, tok, head, out, tok, head, kv, 0, T, q_offset, kvh, scale, stream); break;
-    case 8: detail::attn_prefill_launch<detail::ContigKV, 8>(q_heads, tok, head, out, tok, head, kv, 0, T, q_offset, kvh, scale, stream); break;
+    case 1: detail::attn_prefill_launch<detail::ContigKV, 1>(q_heads, tok, head, o, kv, 0, T, q_offset, kvh, scale, stream); break;
+    case 2: detail::attn_prefill_launch<detail::ContigKV, 2>(q_heads, tok, head, o, kv, 0, T, q_offset, kvh, scale, stream); break;
+    case 4: detail::attn_prefill_launch<detail::ContigKV, 4>(q_heads, tok, head, o, kv, 0, T, q_offset, kvh, scale, stream); break;
+    case 8: detail::attn_prefill_launch<detail::ContigKV, 8>(q_heads, tok, head, o, kv, 0, T, q_offset, kvh, scale, stream); break;
     default: detail::require(false, "attention_prefill_chunked supports kv_rep in {1, 2, 4, 8}");
     }
 }

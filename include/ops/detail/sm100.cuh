@@ -196,16 +196,16 @@ constexpr uint32_t kFmtTF32 = 2;
 
 // ------------------------------------------------------------------ host ---
 
+inline PFN_cuTensorMapEncodeTiled_v12000 load_tensor_map_encoder() {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    OPWORKS_CUDA_CHECK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q));
+    detail::require(q == cudaDriverEntryPointSuccess && p != nullptr, "cuTensorMapEncodeTiled is unavailable");
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+}
+
 inline PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void *p = nullptr;
-        cudaDriverEntryPointQueryResult q{};
-        OPWORKS_CUDA_CHECK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q));
-        detail::require(q == cudaDriverEntryPointSuccess && p != nullptr, "cuTensorMapEncodeTiled is unavailable");
-        fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-    });
+    static const PFN_cuTensorMapEncodeTiled_v12000 fn = load_tensor_map_encoder(); // thread-safe static init
     return fn;
 }
 

@@ -21,6 +21,9 @@
 //
 // Precision kinds:
 //   kBF16   one kind::f16 MMA per 16-wide K step (bf16 x bf16 -> fp32)
+//   kBF16x2 bf16 weights times a two-term bf16 activation (x = hi + lo, lo =
+//           bf16(x - hi)): two kind::f16 MMAs per K step, so activations keep
+//           ~16 mantissa bits while the weight stream stays 2 bytes/element
 //   kTF32x3 split-precision fp32: operands pre-split into tf32 hi/lo parts,
 //           three kind::tf32 MMAs per K step (hi*hi + hi*lo + lo*hi) give
 //           ~fp32 accuracy on the tensor cores.
@@ -32,7 +35,7 @@
 
 namespace opworks::sm100 {
 
-enum class GemmKind { kBF16, kTF32x3 };
+enum class GemmKind { kBF16, kTF32x3, kBF16x2 };
 
 struct GemmParams {
     float *out;           // [splits][m_tok][ldo]
@@ -62,9 +65,11 @@ __device__ __forceinline__ float apply_epilogue(const Epi &epi, float v, int tok
 
 template <GemmKind kKind, int BN> struct GemmShape {
     static constexpr bool kSplit3 = kKind == GemmKind::kTF32x3;
+    static constexpr bool kSplitB = kKind == GemmKind::kBF16x2; // B_lo tile, A shared
     static constexpr uint32_t kABytes = kUmmaM * kUmmaKBytes;
     static constexpr uint32_t kBBytes = BN * kUmmaKBytes;
-    static constexpr uint32_t kStageBytes = (kABytes + kBBytes) * (kSplit3 ? 2u : 1u);
+    static constexpr uint32_t kStageBytes =
+        kSplit3 ? 2u * (kABytes + kBBytes) : (kSplitB ? kABytes + 2u * kBBytes : kABytes + kBBytes);
     static constexpr int kBudget = 192 * 1024;
     static constexpr int kStagesRaw = kBudget / static_cast<int>(kStageBytes);
     static constexpr int kStages = kStagesRaw > 8 ? 8 : kStagesRaw;
@@ -120,6 +125,8 @@ __global__ void __launch_bounds__(192, 1)
             prefetch_tmap(&tmA_lo);
             prefetch_tmap(&tmB_lo);
         }
+        if constexpr (S::kSplitB)
+            prefetch_tmap(&tmB_lo);
     }
     if (warp == 1) {
         tmem_alloc(tmem_slot, S::kTmemCols);
@@ -150,6 +157,8 @@ __global__ void __launch_bounds__(192, 1)
                     tma_load_2d(st + S::kABytes + S::kBBytes, &tmA_lo, &full[s], kc, f0);
                     tma_load_2d(st + 2 * S::kABytes + S::kBBytes, &tmB_lo, &full[s], kc, t0);
                 }
+                if constexpr (S::kSplitB)
+                    tma_load_2d(st + S::kABytes + S::kBBytes, &tmB_lo, &full[s], kc, t0);
             }
             // never leave the CTA with copies in flight: the last issued
             // phase of every slot must have landed (returns at once when the
@@ -161,6 +170,7 @@ __global__ void __launch_bounds__(192, 1)
     } else if (warp == 1) {
         if (lane == 0) {
             constexpr uint32_t idesc = idesc_make(S::kSplit3 ? kFmtTF32 : kFmtBF16, kUmmaM, BN);
+            (void)idesc;
             int it = 0;
             for (int kb = kb_begin; kb < kb_end; ++kb, ++it) {
                 const int s = it % kStages;
@@ -194,6 +204,11 @@ __global__ void __launch_bounds__(192, 1)
                         umma_tf32(dst, ad, bd_lo, idesc, acc);
                         umma_tf32(dst, ad_lo, bd, idesc, 1u);
                         umma_tf32(dst, ad, bd, idesc, 1u);
+                    } else if constexpr (S::kSplitB) {
+                        const uint32_t acc = (kb > kb_begin || k > 0) ? 1u : 0u;
+                        const uint64_t bd_lo = sdesc_k128(b + S::kBBytes + 32 * k);
+                        umma_bf16(dst, ad, bd_lo, idesc, acc);
+                        umma_bf16(dst, ad, bd, idesc, 1u);
                     } else {
                         const uint32_t acc = (kb > kb_begin || k > 0) ? 1u : 0u;
                         umma_bf16(dst, ad, bd, idesc, acc);
@@ -311,7 +326,7 @@ inline int gemm_pick_bn(GemmKind kind, int m_tok) {
         return 32;
     if (m_tok <= 64)
         return 64;
-    if (m_tok <= 128 || kind == GemmKind::kTF32x3)
+    if (m_tok <= 128 || kind != GemmKind::kBF16)
         return 128;
     return 256;
 }
@@ -341,7 +356,7 @@ inline int gemm_pick_splits(int tiles, int num_kb, int sm_count, int min_kb = 4)
 template <GemmKind kKind, typename Epi = Identity>
 inline void gemm_tn(const GemmOperand &A, const GemmOperand &B, int k, float *out, int64_t ldo, int splits,
                     int64_t split_stride, cudaStream_t stream, const Epi &epi = {}, int force_bn = 0) {
-    constexpr bool kBf16 = kKind == GemmKind::kBF16;
+    constexpr bool kBf16 = kKind != GemmKind::kTF32x3;
     constexpr int kKElems = kBf16 ? 64 : 32;
     detail::require(k > 0, "gemm_tn: K must be positive");
     detail::require(A.rows > 0 && B.rows > 0, "gemm_tn: empty operand");
@@ -369,15 +384,17 @@ inline void gemm_tn(const GemmOperand &A, const GemmOperand &B, int k, float *ou
         ta_lo = make_tmap_2d(A.lo, false, static_cast<uint64_t>(k), A.rows, A.ld, kKElems, kUmmaM);
         tb_lo = make_tmap_2d(B.lo, false, static_cast<uint64_t>(k), B.rows, B.ld, kKElems, bn);
     }
+    if constexpr (kKind == GemmKind::kBF16x2)
+        tb_lo = make_tmap_2d(B.lo, true, static_cast<uint64_t>(k), B.rows, B.ld, kKElems, bn);
     switch (bn) {
     case 32: gemm_launch<kKind, 32, Epi>(ta, tb, ta_lo, tb_lo, p, epi, stream); break;
     case 64: gemm_launch<kKind, 64, Epi>(ta, tb, ta_lo, tb_lo, p, epi, stream); break;
     case 128: gemm_launch<kKind, 128, Epi>(ta, tb, ta_lo, tb_lo, p, epi, stream); break;
     default:
-        if constexpr (kBf16)
-            gemm_launch<kKind, 256, Epi>(ta, tb, ta_lo, tb_lo, p, epi, stream);
-        else
+        if constexpr (kKind == GemmKind::kTF32x3)
             gemm_launch<kKind, 128, Epi>(ta, tb, ta_lo, tb_lo, p, epi, stream);
+        else
+            gemm_launch<kKind, 256, Epi>(ta, tb, ta_lo, tb_lo, p, epi, stream);
         break;
     }
 }

@@ -14,6 +14,7 @@
 // directly) or fp32, optionally with the tf32 hi/lo split of the accurate
 // (split-precision) GEMM path.
 
+#include <cooperative_groups.h>
 #include <cuda_bf16.h>
 
 #include "../core/block_reduce.cuh"
@@ -22,26 +23,6 @@
 #include "detail/operand_prep.cuh"
 
 namespace opworks::detail {
-
-// Where a row-wise producer writes the operand of the next GEMM.
-struct ActOut {
-    __nv_bfloat16 *bf16 = nullptr; // fast path
-    float *f32 = nullptr;          // accurate path (tf32 hi part when lo != nullptr)
-    float *lo = nullptr;           // tf32 lo part (split-precision GEMM)
-    int64_t ld = 0;                // row stride (elements)
-    __device__ __forceinline__ void put(int64_t row, int col, float v) const {
-        const int64_t i = row * ld + col;
-        if (bf16) {
-            bf16[i] = __float2bfloat16_rn(v);
-        } else if (lo) {
-            const float h = tf32_round(v);
-            f32[i] = h;
-            lo[i] = v - h;
-        } else {
-            f32[i] = v;
-        }
-    }
-};
 
 constexpr int kRowThreads = 256;
 
@@ -254,34 +235,41 @@ __device__ __forceinline__ double counter_uniform(uint64_t seed, int step) {
     return static_cast<double>(h >> 11) * (1.0 / 9007199254740992.0);
 }
 
-// Order-preserving key of a float (larger float -> larger key; NaN excluded).
+// Order-preserving key of a float (larger float -> larger key).
 __device__ __forceinline__ uint32_t float_key(float f) {
     const uint32_t u = __float_as_uint(f);
     return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
-
-constexpr int kSampleThreads = 1024;
-constexpr int kRadixBits = 11;
-constexpr int kRadixBuckets = 1 << kRadixBits;
-
-__device__ __forceinline__ double block_sum_d(double v, double *scratch) {
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1)
-        v += __shfl_xor_sync(kFullWarpMask, v, off);
-    __syncthreads();
-    if ((threadIdx.x & 31) == 0)
-        scratch[threadIdx.x >> 5] = v;
-    __syncthreads();
-    double t = 0.0;
-    for (int w = 0; w < kSampleThreads / 32; ++w)
-        t += scratch[w];
-    return t;
+__device__ __forceinline__ float key_float(uint32_t k) {
+    return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
 }
 
-// Exclusive prefix (over threads in index order) of a per-thread double and int.
-__device__ __forceinline__ void block_exclusive_scan(double v, int c, double *dscr, int *iscr, double &v_before,
-                                                     int &c_before, double &v_total, int &c_total) {
+constexpr int kSampleCluster = 8;    // CTAs per row (portable cluster size)
+constexpr int kSampleThreads = 512;  // threads per CTA
+constexpr int kSampleChunkMax = 16384; // logits per CTA held in shared memory
+constexpr int kRadixBuckets = 2048;
+
+struct SampleShared {
+    float x[kSampleChunkMax];      // this CTA's slice of the row
+    double hist[kRadixBuckets];    // mass per radix bucket
+    int cnt[kRadixBuckets];        // tokens per radix bucket
+    double dscr[32];
+    int iscr[32];
+    float best_v;
+    int best_i;
+    double part_mass;              // final pass: kept mass of this CTA
+    int part_ties;                 // final pass: boundary ties of this CTA
+    // results of the leader (rank 0), read by every CTA through DSMEM
+    uint32_t prefix;
+    double above, z;
+    int above_cnt;
+};
+
+// Block-wide exclusive prefix (threads in index order) of a double and an int.
+__device__ __forceinline__ void block_scan_excl(double v, int c, double *dscr, int *iscr, double &v_before,
+                                                int &c_before, double &v_total, int &c_total) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int nw = blockDim.x >> 5;
     double vi = v;
     int ci = c;
 #pragma unroll
@@ -301,7 +289,7 @@ __device__ __forceinline__ void block_exclusive_scan(double v, int c, double *ds
     __syncthreads();
     double wv = 0.0, tv = 0.0;
     int wc = 0, tc = 0;
-    for (int w = 0; w < kSampleThreads / 32; ++w) {
+    for (int w = 0; w < nw; ++w) {
         if (w < warp) {
             wv += dscr[w];
             wc += iscr[w];
@@ -315,38 +303,42 @@ __device__ __forceinline__ void block_exclusive_scan(double v, int c, double *ds
     c_total = tc;
 }
 
-// One CTA per row of `logits` ([rows][vocab] fp32). Greedy: first index of the
-// maximum. Top-p: the host sampler of OpWorks examples/llama/generate.py:83-109
-// in float64 — p = softmax(logits / max(T, 1e-6)); keep the descending-sorted
-// prefix up to and including the first token whose cumulative mass reaches
-// top_p (ties at that boundary kept in ascending index order); renormalise;
-// return the first index whose cumulative kept mass exceeds u (numpy's
-// Generator.choice rule). The sorted order is found by a 3-level radix
-// select on the float bits of the logits, so no sort is materialised.
-static __global__ void __launch_bounds__(kSampleThreads)
+// One 8-CTA cluster per row of logits [rows][ld]. Greedy (temperature <= 0):
+// first index of the maximum. Otherwise the host sampler of OpWorks
+// examples/llama/generate.py:83-109: p = softmax(logits / max(T, 1e-6));
+// keep the descending-sorted prefix up to and including the first token whose
+// cumulative mass reaches top_p (tokens tied at that boundary are kept in
+// ascending index order); renormalise; return the first index whose
+// cumulative kept mass (index order) exceeds u * total, numpy's
+// Generator.choice rule. The sorted order is found by a 3-level radix select
+// over the float bits of the logits (11 + 11 + 10 bits) with per-bucket mass
+// histograms; masses are expf in fp32 accumulated in fp64. Each CTA keeps its
+// slice of the row in shared memory; partial results meet in the leader CTA
+// through distributed shared memory.
+static __global__ void __cluster_dims__(kSampleCluster, 1, 1) __launch_bounds__(kSampleThreads)
     sample_kernel(const float *__restrict__ logits, int64_t ld, int vocab, SampleParams sp, int *__restrict__ out) {
-    __shared__ double hist[kRadixBuckets];
-    __shared__ int cnt[kRadixBuckets];
-    __shared__ double dscr[32];
-    __shared__ int iscr[32];
-    __shared__ float best_v[32];
-    __shared__ int best_i[32];
-    __shared__ uint32_t s_prefix;
-    __shared__ double s_above;
-    __shared__ int s_above_cnt;
-
-    const int row = blockIdx.x;
-    const float *x = logits + static_cast<int64_t>(row) * ld;
+    namespace cg = cooperative_groups;
+    cg::cluster_group cluster = cg::this_cluster();
+    extern __shared__ __align__(16) uint8_t smem_raw[];
+    SampleShared &sh = *reinterpret_cast<SampleShared *>(smem_raw);
+    const int rank = static_cast<int>(cluster.block_rank());
+    const int row = blockIdx.x / kSampleCluster;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int chunk = (vocab + kSampleCluster - 1) / kSampleCluster;
+    const int lo = rank * chunk;
+    const int n = max(0, min(vocab, lo + chunk) - lo);
+    const float *src = logits + static_cast<int64_t>(row) * ld + lo;
+    SampleShared *leader = cluster.map_shared_rank(&sh, 0);
 
-    // pass 1: max (first index)
+    // pass 0: stage the slice, local (max, first index)
     float bv = kNegInf;
     int bi = 0x7fffffff;
-    for (int i = tid; i < vocab; i += blockDim.x) {
-        const float v = x[i];
-        if (v > bv || (v == bv && i < bi)) {
+    for (int i = tid; i < n; i += blockDim.x) {
+        const float v = src[i];
+        sh.x[i] = v;
+        if (v > bv) {
             bv = v;
-            bi = i;
+            bi = lo + i;
         }
     }
 #pragma unroll
@@ -359,170 +351,247 @@ static __global__ void __launch_bounds__(kSampleThreads)
         }
     }
     if (lane == 0) {
-        best_v[warp] = bv;
-        best_i[warp] = bi;
+        sh.dscr[warp] = bv;
+        sh.iscr[warp] = bi;
     }
     __syncthreads();
-    bv = best_v[0];
-    bi = best_i[0];
-    for (int w = 1; w < 32; ++w)
-        if (best_v[w] > bv || (best_v[w] == bv && best_i[w] < bi)) {
-            bv = best_v[w];
-            bi = best_i[w];
+    if (tid == 0) {
+        float v = kNegInf;
+        int i0 = 0x7fffffff;
+        for (int w = 0; w < kSampleThreads / 32; ++w) {
+            const float ov = static_cast<float>(sh.dscr[w]);
+            if (ov > v || (ov == v && sh.iscr[w] < i0)) {
+                v = ov;
+                i0 = sh.iscr[w];
+            }
         }
+        sh.best_v = v;
+        sh.best_i = i0;
+    }
+    cluster.sync();
+    float gmax = kNegInf;
+    int garg = 0x7fffffff;
+    for (int r = 0; r < kSampleCluster; ++r) {
+        const SampleShared *peer = cluster.map_shared_rank(&sh, r);
+        const float v = peer->best_v;
+        const int i0 = peer->best_i;
+        if (v > gmax || (v == gmax && i0 < garg)) {
+            gmax = v;
+            garg = i0;
+        }
+    }
     const float temp = sp.temperature ? sp.temperature[row] : 0.f;
     if (!(temp > 0.f)) {
-        if (tid == 0)
-            out[row] = bi;
+        if (rank == 0 && tid == 0)
+            out[row] = garg;
+        cluster.sync(); // peers finished reading this CTA's shared memory
         return;
     }
-    const double t = fmax(static_cast<double>(temp), 1e-6);
-    const double zmax = static_cast<double>(bv) / t;
+    const float inv_t = 1.f / fmaxf(temp, 1e-6f);
     const double top_p = sp.top_p ? static_cast<double>(sp.top_p[row]) : 1.0;
-    // host-supplied uniform when >= 0, else the counter-based stream
     const double u = (sp.uniform && sp.uniform[row] >= 0.0)
                          ? sp.uniform[row]
                          : counter_uniform(sp.seed ? sp.seed[row] : 0ull, sp.step ? sp.step[row] : 0);
+    auto mass = [&](float v) { return expf((v - gmax) * inv_t); };
 
-    // mass of every token: e_i = exp(l_i / T - zmax)
-    double z = 0.0;
-    for (int i = tid; i < vocab; i += blockDim.x)
-        z += exp(static_cast<double>(x[i]) / t - zmax);
-    z = block_sum_d(z, dscr);
-
-    // radix select of the crossing key: largest k with mass(key >= k) >= p z
+    const bool filtered = top_p < 1.0;
     uint32_t prefix = 0;
-    double above = 0.0; // mass with key above the current prefix range
-    int above_cnt = 0;
-    uint32_t key_star = 0;
-    double e_star = 0.0;
+    double above = 0.0, z = 0.0;
+    for (int level = 0; level < (filtered ? 3 : 1); ++level) {
+        const int shift = level == 0 ? 21 : (level == 1 ? 10 : 0);
+        const int nb = level == 2 ? 1024 : kRadixBuckets;
+        const uint32_t mask_hi = level == 0 ? 0u : (0xffffffffu << (level == 1 ? 21 : 10));
+        for (int b = tid; b < nb; b += blockDim.x) {
+            sh.hist[b] = 0.0;
+            sh.cnt[b] = 0;
+        }
+        __syncthreads();
+        for (int i = tid; i < n; i += blockDim.x) {
+            const float v = sh.x[i];
+            const uint32_t k = float_key(v);
+            if ((k & mask_hi) == prefix) {
+                const int b = static_cast<int>((k >> shift) & static_cast<uint32_t>(nb - 1));
+                atomicAdd(&sh.hist[b], static_cast<double>(mass(v)));
+                atomicAdd(&sh.cnt[b], 1);
+            }
+        }
+        cluster.sync();
+        if (rank == 0) {
+            // leader: sum the cluster's histograms; buckets scanned from the top
+            const int per = nb / kSampleThreads; // 4 or 2 buckets per thread
+            double my = 0.0;
+            int myc = 0;
+            double bm[4];
+            int bc[4];
+            for (int j = 0; j < per; ++j) {
+                const int b = nb - 1 - (tid * per + j);
+                double m = 0.0;
+                int c = 0;
+                for (int r = 0; r < kSampleCluster; ++r) {
+                    const SampleShared *peer = cluster.map_shared_rank(&sh, r);
+                    m += peer->hist[b];
+                    c += peer->cnt[b];
+                }
+                bm[j] = m;
+                bc[j] = c;
+                my += m;
+                myc += c;
+            }
+            double before, total;
+            int cbefore, ctotal;
+            block_scan_excl(my, myc, sh.dscr, sh.iscr, before, cbefore, total, ctotal);
+            if (level == 0)
+                z = total;
+            else
+                z = leader->z;
+            const double target = top_p * z;
+            if (!filtered) {
+                if (tid == 0) {
+                    sh.z = total;
+                    sh.prefix = 0;
+                    sh.above = 0.0;
+                    sh.above_cnt = 0;
+                }
+            } else {
+                // the crossing bucket: first (from the top) where above + cum >= target
+                double acc = above + before;
+                int accc = cbefore;
+                for (int j = 0; j < per; ++j) {
+                    const int b = nb - 1 - (tid * per + j);
+                    const bool last_bucket = b == 0;
+                    if ((acc + bm[j] >= target || last_bucket) && acc < target) {
+                        sh.prefix = prefix | (static_cast<uint32_t>(b) << shift);
+                        sh.above = acc;
+                        sh.above_cnt = accc;
+                    }
+                    acc += bm[j];
+                    accc += bc[j];
+                }
+                // target beyond everything (rounding): keep the lowest bucket
+                if (tid == kSampleThreads - 1 && !(above + total >= target) && level == 0) {
+                    sh.prefix = 0;
+                    sh.above = above;
+                    sh.above_cnt = 0;
+                }
+                if (tid == 0 && level == 0)
+                    sh.z = total;
+            }
+        }
+        cluster.sync();
+        prefix = leader->prefix;
+        above = leader->above;
+        z = leader->z;
+    }
+    const uint32_t key_star = prefix;
+    const double e_star = filtered ? static_cast<double>(mass(key_float(key_star))) : 0.0;
     int n_keep_ties = 0x7fffffff;
-    bool filtered = top_p < 1.0;
     if (filtered) {
-        const double target = top_p * z;
-        for (int level = 0; level < 3; ++level) {
-            const int shift = level == 0 ? 21 : (level == 1 ? 10 : 0);
-            const int nb = level == 2 ? (1 << 10) : kRadixBuckets;
-            const uint32_t mask_hi = level == 0 ? 0u : (0xffffffffu << (level == 1 ? 21 : 10));
-            for (int b = tid; b < nb; b += blockDim.x) {
-                hist[b] = 0.0;
-                cnt[b] = 0;
-            }
-            __syncthreads();
-            for (int i = tid; i < vocab; i += blockDim.x) {
-                const float v = x[i];
-                const uint32_t k = float_key(v);
-                if ((k & mask_hi) == prefix) {
-                    const int b = static_cast<int>((k >> shift) & static_cast<uint32_t>(nb - 1));
-                    atomicAdd(&hist[b], exp(static_cast<double>(v) / t - zmax));
-                    atomicAdd(&cnt[b], 1);
-                }
-            }
-            __syncthreads();
-            if (tid == 0) {
-                double acc = above;
-                int acc_cnt = above_cnt;
-                int b = nb - 1;
-                for (; b > 0; --b) {
-                    if (acc + hist[b] >= target)
-                        break;
-                    acc += hist[b];
-                    acc_cnt += cnt[b];
-                }
-                s_prefix = prefix | (static_cast<uint32_t>(b) << shift);
-                s_above = acc;
-                s_above_cnt = acc_cnt;
-            }
-            __syncthreads();
-            prefix = s_prefix;
-            above = s_above;
-            above_cnt = s_above_cnt;
-            __syncthreads();
-        }
-        key_star = prefix;
-        // all tokens with key == key_star share one mass value
-        float fstar;
-        {
-            const uint32_t u32 = (key_star & 0x80000000u) ? (key_star & 0x7fffffffu) : ~key_star;
-            fstar = __uint_as_float(u32);
-        }
-        e_star = exp(static_cast<double>(fstar) / t - zmax);
-        const double need = (target - above) / e_star;
+        const double need = (top_p * z - above) / e_star;
         n_keep_ties = need <= 1.0 ? 1 : static_cast<int>(ceil(need - 1e-12));
-        if (n_keep_ties < 1)
-            n_keep_ties = 1;
     }
 
-    // inverse-CDF over the kept tokens in index order: contiguous chunk/thread
-    const int chunk = (vocab + blockDim.x - 1) / blockDim.x;
-    const int lo = tid * chunk, hi = min(vocab, lo + chunk);
+    // final pass: kept mass in index order; each thread owns a contiguous run
+    const int per_t = (n + kSampleThreads - 1) / kSampleThreads;
+    const int t_lo = min(n, tid * per_t), t_hi = min(n, t_lo + per_t);
     double my = 0.0;
     int my_ties = 0;
-    for (int i = lo; i < hi; ++i) {
-        const float v = x[i];
+    for (int i = t_lo; i < t_hi; ++i) {
+        const float v = sh.x[i];
         if (!filtered) {
-            my += exp(static_cast<double>(v) / t - zmax);
+            my += mass(v);
         } else {
             const uint32_t k = float_key(v);
             if (k > key_star)
-                my += exp(static_cast<double>(v) / t - zmax);
+                my += mass(v);
             else if (k == key_star)
                 ++my_ties;
         }
     }
-    // ties at the boundary: the first n_keep_ties (index order) are kept
     double before, total;
     int ties_before, ties_total;
-    block_exclusive_scan(my, my_ties, dscr, iscr, before, ties_before, total, ties_total);
-    if (filtered) {
-        const int keep_total = min(n_keep_ties, ties_total);
-        const int mine = max(0, min(my_ties, keep_total - ties_before));
-        // recompute the running mass including this thread's kept ties
-        const double tie_mass_before = e_star * static_cast<double>(min(ties_before, keep_total));
-        before += tie_mass_before;
-        my += e_star * mine;
-        total += e_star * static_cast<double>(keep_total);
+    block_scan_excl(my, my_ties, sh.dscr, sh.iscr, before, ties_before, total, ties_total);
+    if (tid == 0) {
+        sh.part_mass = total;
+        sh.part_ties = ties_total;
     }
-    const double goal = u * total;
-    if (before <= goal && goal < before + my) {
-        double run = before;
-        int ties_seen = ties_before;
-        int pick = hi - 1;
-        for (int i = lo; i < hi; ++i) {
-            const float v = x[i];
+    cluster.sync();
+    // cluster prefix over ranks (every CTA computes it from the peers)
+    double rank_before = 0.0, grand = 0.0;
+    int ties_rank_before = 0, ties_grand = 0;
+    for (int r = 0; r < kSampleCluster; ++r) {
+        const SampleShared *peer = cluster.map_shared_rank(&sh, r);
+        if (r < rank) {
+            rank_before += peer->part_mass;
+            ties_rank_before += peer->part_ties;
+        }
+        grand += peer->part_mass;
+        ties_grand += peer->part_ties;
+    }
+    const int keep_total = filtered ? min(n_keep_ties, ties_grand) : 0;
+    const int tb = ties_rank_before + ties_before; // boundary ties before this thread
+    const int mine = filtered ? max(0, min(my_ties, keep_total - tb)) : 0;
+    const double t_before = rank_before + before + e_star * static_cast<double>(min(tb, keep_total));
+    const double t_mine = my + e_star * static_cast<double>(mine);
+    const double all = grand + e_star * static_cast<double>(keep_total);
+    const double goal = u * all;
+    if (t_before <= goal && goal < t_before + t_mine) {
+        double run = t_before;
+        int ties_seen = tb;
+        int pick = lo + t_hi - 1;
+        for (int i = t_lo; i < t_hi; ++i) {
+            const float v = sh.x[i];
             double e = 0.0;
             if (!filtered) {
-                e = exp(static_cast<double>(v) / t - zmax);
+                e = mass(v);
             } else {
                 const uint32_t k = float_key(v);
                 if (k > key_star)
-                    e = exp(static_cast<double>(v) / t - zmax);
-                else if (k == key_star && ties_seen++ < n_keep_ties)
+                    e = mass(v);
+                else if (k == key_star && ties_seen++ < keep_total)
                     e = e_star;
             }
             if (e > 0.0) {
                 run += e;
                 if (run > goal) {
-                    pick = i;
+                    pick = lo + i;
                     break;
                 }
             }
         }
         out[row] = pick;
     }
-    // numerical edge: goal at the very top (u -> 1) lands in no interval;
-    // the last kept token is the answer (numpy's searchsorted clamps likewise)
-    if (tid == blockDim.x - 1 && !(goal < total)) {
+    // u -> 1 rounding: the goal lands past the last kept token
+    if (rank == kSampleCluster - 1 && tid == 0 && !(goal < all)) {
         int last = vocab - 1;
-        for (int i = vocab - 1; i >= 0; --i) {
-            const uint32_t k = float_key(x[i]);
-            if (!filtered || k >= key_star) {
-                last = i;
-                break;
-            }
+        for (int r = kSampleCluster - 1; r >= 0 && last == vocab - 1; --r) {
+            const SampleShared *peer = cluster.map_shared_rank(&sh, r);
+            const int plo = r * chunk, pn = max(0, min(vocab, plo + chunk) - plo);
+            for (int i = pn - 1; i >= 0; --i)
+                if (!filtered || float_key(peer->x[i]) >= key_star) {
+                    last = plo + i;
+                    break;
+                }
         }
         out[row] = last;
     }
+    cluster.sync(); // keep shared memory alive until every peer is done with it
+}
+
+inline size_t sample_smem_bytes() { return sizeof(SampleShared); }
+
+inline void sample_launch(const float *logits, int64_t ld, int rows, int vocab, const SampleParams &sp, int *out,
+                          cudaStream_t stream) {
+    require((vocab + kSampleCluster - 1) / kSampleCluster <= kSampleChunkMax, "vocabulary too large for the sampler");
+    static thread_local int done = -1;
+    int dev = 0;
+    OPWORKS_CUDA_CHECK(cudaGetDevice(&dev));
+    if (done != dev) {
+        OPWORKS_CUDA_CHECK(cudaFuncSetAttribute(sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                static_cast<int>(sample_smem_bytes())));
+        done = dev;
+    }
+    sample_kernel<<<rows * kSampleCluster, kSampleThreads, sample_smem_bytes(), stream>>>(logits, ld, vocab, sp, out);
+    OPWORKS_CUDA_CHECK(cudaGetLastError());
 }
 
 } // namespace opworks::detail

@@ -16,6 +16,12 @@
 
 #include <stdint.h>
 
+/* Only the C ABI is exported; the libraries are built with hidden default
+ * visibility so two of them (or the reference's library) can share a process. */
+#ifndef OPW_API
+#define OPW_API __attribute__((visibility("default")))
+#endif
+
 #ifdef __cplusplus
 extern "C" {
 #endif
@@ -23,76 +29,76 @@ extern "C" {
 /* --- OpWorks interface (src/llama_c_api.cu:54-159) --- */
 
 /* replaces opw_llama_load (src/llama_c_api.cu:57-73): float32 or bfloat16 pack */
-void *opw_llama_load(const char *pack_path, char *err, int err_len);
+OPW_API void *opw_llama_load(const char *pack_path, char *err, int err_len);
 /* replaces opw_llama_free (src/llama_c_api.cu:75) */
-void opw_llama_free(void *model);
+OPW_API void opw_llama_free(void *model);
 /* replaces opw_llama_create_session (src/llama_c_api.cu:77-91); max_seq_len in (0, 8192] */
-void *opw_llama_create_session(void *model, int max_seq_len, char *err, int err_len);
+OPW_API void *opw_llama_create_session(void *model, int max_seq_len, char *err, int err_len);
 /* replaces opw_llama_destroy_session (src/llama_c_api.cu:93) */
-void opw_llama_destroy_session(void *session);
+OPW_API void opw_llama_destroy_session(void *session);
 /* replaces opw_llama_reset_session (src/llama_c_api.cu:95-102) */
-int opw_llama_reset_session(void *session, char *err, int err_len);
+OPW_API int opw_llama_reset_session(void *session, char *err, int err_len);
 /* replaces opw_llama_prefill (src/llama_c_api.cu:105-116): first greedy token or -1 */
-int opw_llama_prefill(void *session, const int32_t *tokens, int n, char *err, int err_len);
+OPW_API int opw_llama_prefill(void *session, const int32_t *tokens, int n, char *err, int err_len);
 /* replaces opw_llama_decode_step (src/llama_c_api.cu:119-126): next greedy token or -1 */
-int opw_llama_decode_step(void *session, int32_t prev_token, char *err, int err_len);
+OPW_API int opw_llama_decode_step(void *session, int32_t prev_token, char *err, int err_len);
 /* replaces opw_llama_is_eos (src/llama_c_api.cu:129-136): 1, 0 or -1 */
-int opw_llama_is_eos(void *session, int32_t token, char *err, int err_len);
+OPW_API int opw_llama_is_eos(void *session, int32_t token, char *err, int err_len);
 /* replaces opw_llama_last_logits (src/llama_c_api.cu:139-149): n must be vocab_size */
-int opw_llama_last_logits(void *session, float *out, int n, char *err, int err_len);
+OPW_API int opw_llama_last_logits(void *session, float *out, int n, char *err, int err_len);
 /* replaces opw_llama_vocab_size (src/llama_c_api.cu:151-154); not guarded, as in OpWorks */
-int opw_llama_vocab_size(void *session);
+OPW_API int opw_llama_vocab_size(void *session);
 /* replaces opw_llama_last_error (src/llama_c_api.cu:156) */
-const char *opw_llama_last_error(void);
+OPW_API const char *opw_llama_last_error(void);
 
 /* --- extensions (no counterpart in OpWorks) --- */
 
 /* Select the CUDA device used by subsequent loads on this thread. */
-int opw_llama_set_device(int device);
+OPW_API int opw_llama_set_device(int device);
 /* Load keeping only some weight precisions: bit 1 = bf16 (fast path),
  * 2 = fp32 (accurate GEMV), 4 = tf32 hi/lo (accurate GEMM); 0 = default.
  * max_positions sizes the RoPE table (>= the longest session). */
-void *opw_llama_load_ex(const char *pack_path, unsigned weight_sets, int max_positions, char *err, int err_len);
+OPW_API void *opw_llama_load_ex(const char *pack_path, unsigned weight_sets, int max_positions, char *err, int err_len);
 /* Model hyper-parameters: out[0..7] = layers, hidden, intermediate, q heads,
  * kv heads, head dim, vocab, device. */
-int opw_llama_model_info(void *model, int32_t *out8, char *err, int err_len);
+OPW_API int opw_llama_model_info(void *model, int32_t *out8, char *err, int err_len);
 
 /* Batched engine: max_batch sequences (slots) of up to max_seq_len tokens
  * each over one paged KV cache. precision: 0 = accurate (fp32), 1 = fast
  * (bf16 weights and GEMM operands, fp32 residual / KV / softmax).
  * prefill_rows: prefill chunk size (0 = max_seq_len). */
-void *opw_llama_create_batch(void *model, int max_batch, int max_seq_len, int precision, int prefill_rows, char *err,
+OPW_API void *opw_llama_create_batch(void *model, int max_batch, int max_seq_len, int precision, int prefill_rows, char *err,
                              int err_len);
-void opw_llama_destroy_batch(void *batch);
+OPW_API void opw_llama_destroy_batch(void *batch);
 /* Frees the slot's KV blocks; the slot starts empty. */
-int opw_llama_batch_reset(void *batch, int slot, char *err, int err_len);
+OPW_API int opw_llama_batch_reset(void *batch, int slot, char *err, int err_len);
 /* Current token count of a slot, or -1. */
-int opw_llama_batch_length(void *batch, int slot);
+OPW_API int opw_llama_batch_length(void *batch, int slot);
 /* Appends n prompt tokens to `slot` and returns the next token sampled from
  * the last position: temperature <= 0 -> greedy argmax; otherwise top-p with
  * the uniform `uniform` when >= 0, else a counter-based draw from (seed, 0). */
-int opw_llama_batch_prefill(void *batch, int slot, const int32_t *tokens, int n, float temperature, float top_p,
+OPW_API int opw_llama_batch_prefill(void *batch, int slot, const int32_t *tokens, int n, float temperature, float top_p,
                             double uniform, uint64_t seed, char *err, int err_len);
 /* One decode step for n slots: prev_tokens[i] is appended to slots[i] and
  * out_tokens[i] receives the next token. temperature / top_p / uniforms /
  * seeds / steps may be NULL (greedy; counter RNG at step 0). Returns 0 / -1. */
-int opw_llama_batch_decode(void *batch, int n, const int32_t *slots, const int32_t *prev_tokens,
+OPW_API int opw_llama_batch_decode(void *batch, int n, const int32_t *slots, const int32_t *prev_tokens,
                            const float *temperature, const float *top_p, const double *uniforms,
                            const uint64_t *seeds, const int32_t *steps, int32_t *out_tokens, char *err, int err_len);
 /* Logits (vocab_size floats) of row `row` of the last step. */
-int opw_llama_batch_logits(void *batch, int row, float *out, int n, char *err, int err_len);
+OPW_API int opw_llama_batch_logits(void *batch, int row, float *out, int n, char *err, int err_len);
 
 /* The engine's CUDA stream (cudaStream_t), e.g. to record timing events. */
-void *opw_llama_batch_stream(void *batch);
+OPW_API void *opw_llama_batch_stream(void *batch);
 /* Bytes copied host->device and device->host around one decode step of n
  * rows: out2[0] = h2d, out2[1] = d2h. */
-int opw_llama_batch_io_bytes(void *batch, int n, int64_t *out2);
+OPW_API int opw_llama_batch_io_bytes(void *batch, int n, int64_t *out2);
 /* Per-kernel device time of the last decode step of n rows (re-run eagerly
  * `iters` times with CUDA events between launch groups; lengths are not
  * advanced). Writes up to max_kernels entries: ms_per_step[i],
  * launches_per_step[i] and a NUL-terminated label of at most 31 characters
  * at labels + 32 * i. Returns the number of entries, or -1. */
-int opw_llama_batch_profile(void *batch, int n, int iters, float *ms_per_step, int32_t *launches_per_step,
+OPW_API int opw_llama_batch_profile(void *batch, int n, int iters, float *ms_per_step, int32_t *launches_per_step,
                             char *labels, int max_kernels, char *err, int err_len);
 
 #ifdef __cplusplus

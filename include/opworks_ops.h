@@ -20,70 +20,76 @@
 #include <stddef.h>
 #include <stdint.h>
 
+/* Only the C ABI is exported; the libraries are built with hidden default
+ * visibility so two of them (or the reference's library) can share a process. */
+#ifndef OPW_API
+#define OPW_API __attribute__((visibility("default")))
+#endif
+
 #ifdef __cplusplus
 extern "C" {
 #endif
 
 /* Thread-local message of the last failed call. */
-const char *opw_ops_last_error(void);
+OPW_API const char *opw_ops_last_error(void);
 /* Waits for `stream`; returns 0, or -1 if the device error word is set (a
  * bounded device-side wait ran out), clearing it. */
-int opw_ops_sync(void *stream);
+OPW_API int opw_ops_sync(void *stream);
 
 /* ops::map with fixed functors (include/ops/elementwise.cuh:63-77;
  * tests/integration/vector_add.cu, relu.cu). */
-int opw_map_add(const float *a, const float *b, float *out, int n, void *stream);
-int opw_map_relu(const float *in, float *out, int n, void *stream);
-int opw_map_scale(const float *in, float *out, int n, float factor, void *stream);
+OPW_API int opw_map_add(const float *a, const float *b, float *out, int n, void *stream);
+OPW_API int opw_map_relu(const float *in, float *out, int n, void *stream);
+OPW_API int opw_map_scale(const float *in, float *out, int n, float factor, void *stream);
 
 /* ops::reduce<Sum|Max> (include/ops/reduction.cuh:34-67;
  * tests/integration/reduction.cu). kind: 0 = sum, 1 = max, 2 = product.
  * workspace may be NULL with workspace_size 0 to use stream-ordered scratch. */
-int opw_reduction_workspace_size(int n);
-int opw_reduce(int kind, const float *in, float *out, int n, float *workspace, int workspace_size, void *stream);
+OPW_API int opw_reduction_workspace_size(int n);
+OPW_API int opw_reduce(int kind, const float *in, float *out, int n, float *workspace, int workspace_size, void *stream);
 
 /* ops::softmax / ops::layer_norm (softmax.cuh:36-43, layer_norm.cuh:38-47). */
-int opw_softmax(const float *in, float *out, int rows, int cols, void *stream);
-int opw_layer_norm(const float *in, float *out, const float *gamma, const float *beta, int rows, int cols, float eps,
+OPW_API int opw_softmax(const float *in, float *out, int rows, int cols, void *stream);
+OPW_API int opw_layer_norm(const float *in, float *out, const float *gamma, const float *beta, int rows, int cols, float eps,
                    void *stream);
 
 /* ops::mat_mul (matmul.cuh:78-91): C(MxK) = epi(A(MxN) @ B(NxK)).
  * epilogue: 0 = pass-through, 1 = relu, 2 = scale by `param`. */
-int opw_mat_mul(const float *A, const float *B, float *C, int M, int N, int K, int epilogue, float param,
+OPW_API int opw_mat_mul(const float *A, const float *B, float *C, int M, int N, int K, int epilogue, float param,
                 void *stream);
 
 /* MatmulBuilder + ops::matmul_launcher (builders/matmul.cuh:9-57): bias may
  * be NULL; activation 0 none, 1 relu, 2 gelu. */
-int opw_matmul_builder(const float *A, const float *B, float *C, int M, int N, int K, int transpose_a,
+OPW_API int opw_matmul_builder(const float *A, const float *B, float *C, int M, int N, int K, int transpose_a,
                        int transpose_b, const float *bias, int activation, void *stream);
 
 /* RowwiseBuilder + ops::rowwise_launcher (builders/rowwise.cuh:11-63):
  * op 0 softmax, 1 layer_norm (param, beta), 2 rms_norm (param). */
-int opw_rowwise_builder(int op, const float *in, float *out, const float *param, const float *beta, int rows,
+OPW_API int opw_rowwise_builder(int op, const float *in, float *out, const float *param, const float *beta, int rows,
                         int cols, float eps, void *stream);
 
 /* Model operators (include/ops/*.cuh of OpWorks, same argument order). */
-int opw_rms_norm(const float *x, const float *weight, float *out, int rows, int cols, float eps, void *stream);
-int opw_linear_f32(const float *X, const float *W, float *Y, int rows, int in_features, int out_features,
+OPW_API int opw_rms_norm(const float *x, const float *weight, float *out, int rows, int cols, float eps, void *stream);
+OPW_API int opw_linear_f32(const float *X, const float *W, float *Y, int rows, int in_features, int out_features,
                    void *stream);
-int opw_linear_bf16(const float *X, const uint16_t *W_bf16, float *Y, int rows, int in_features, int out_features,
+OPW_API int opw_linear_bf16(const float *X, const uint16_t *W_bf16, float *Y, int rows, int in_features, int out_features,
                     void *stream);
-int opw_linear_mma_bf16(const float *X, const uint16_t *W_bf16, float *Y, int rows, int in_features,
+OPW_API int opw_linear_mma_bf16(const float *X, const uint16_t *W_bf16, float *Y, int rows, int in_features,
                         int out_features, void *stream);
-int opw_embedding_f32(const float *table, const int32_t *ids, float *out, int n, int hidden, void *stream);
-int opw_embedding_bf16(const uint16_t *table, const int32_t *ids, float *out, int n, int hidden, void *stream);
-int opw_rope(float *x, const float *inv_freq, int rows, int heads, int head_dim, int pos_start, void *stream);
-int opw_split_heads(const float *in, float *out, int rows, int heads, int head_dim, int out_row_stride,
+OPW_API int opw_embedding_f32(const float *table, const int32_t *ids, float *out, int n, int hidden, void *stream);
+OPW_API int opw_embedding_bf16(const uint16_t *table, const int32_t *ids, float *out, int n, int hidden, void *stream);
+OPW_API int opw_rope(float *x, const float *inv_freq, int rows, int heads, int head_dim, int pos_start, void *stream);
+OPW_API int opw_split_heads(const float *in, float *out, int rows, int heads, int head_dim, int out_row_stride,
                     int out_row_offset, void *stream);
-int opw_merge_heads(const float *in, float *out, int rows, int heads, int head_dim, int in_row_stride,
+OPW_API int opw_merge_heads(const float *in, float *out, int rows, int heads, int head_dim, int in_row_stride,
                     int in_row_offset, void *stream);
-int opw_causal_scale(float *scores, int rows, int cols, float scale, void *stream);
-int opw_swiglu(const float *gate, const float *up, float *out, int64_t n, void *stream);
-int opw_add(const float *a, const float *b, float *out, int64_t n, void *stream);
-int opw_argmax(const float *x, int n, int32_t *out, void *stream);
-int opw_attention_decode(const float *q, const float *kcache, const float *vcache, float *out, int num_q_heads,
+OPW_API int opw_causal_scale(float *scores, int rows, int cols, float scale, void *stream);
+OPW_API int opw_swiglu(const float *gate, const float *up, float *out, int64_t n, void *stream);
+OPW_API int opw_add(const float *a, const float *b, float *out, int64_t n, void *stream);
+OPW_API int opw_argmax(const float *x, int n, int32_t *out, void *stream);
+OPW_API int opw_attention_decode(const float *q, const float *kcache, const float *vcache, float *out, int num_q_heads,
                          int kv_rep, int head_dim, int len, int max_seq, void *stream);
-int opw_attention_prefill_chunked(const float *q_heads, const float *kcache, const float *vcache, float *out, int T,
+OPW_API int opw_attention_prefill_chunked(const float *q_heads, const float *kcache, const float *vcache, float *out, int T,
                                   int S, int q_offset, int num_q_heads, int kv_rep, int head_dim, int cap,
                                   void *stream);
 
@@ -91,7 +97,7 @@ int opw_attention_prefill_chunked(const float *q_heads, const float *kcache, con
  * the device form of OpWorks' host sampler examples/llama/generate.py:83-109:
  * one token per row of logits [rows, vocab]; temperature[r] <= 0 selects the
  * first argmax, otherwise top-p with uniform[r] (device arrays). */
-int opw_sample(const float *logits, int rows, int vocab, const float *temperature, const float *top_p,
+OPW_API int opw_sample(const float *logits, int rows, int vocab, const float *temperature, const float *top_p,
                const double *uniform, int32_t *out, void *stream);
 
 #ifdef __cplusplus

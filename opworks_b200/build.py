@@ -25,7 +25,8 @@ CSRC = os.path.join(ROOT, "opworks_b200", "csrc")
 LIBDIR = os.path.join(ROOT, "opworks_b200", "lib")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-NVCC_FLAGS = ["-std=c++17", "-O3", "-lineinfo", "-Xcompiler", "-fPIC", "-shared", "--expt-relaxed-constexpr",
+NVCC_FLAGS = ["-std=c++17", "-O3", "-lineinfo", "-Xcompiler", "-fPIC,-fvisibility=hidden", "-shared",
+              "--expt-relaxed-constexpr",
               "-Xcudafe", "--diag_suppress=177"] + ARCH
 
 

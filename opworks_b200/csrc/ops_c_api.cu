@@ -263,9 +263,7 @@ int opw_sample(const float *logits, int rows, int vocab, const float *temperatur
         if (rows == 0)
             return;
         opworks::detail::SampleParams sp{temperature, top_p, uniform, nullptr, nullptr};
-        opworks::detail::sample_kernel<<<rows, opworks::detail::kSampleThreads, 0, as_stream(stream)>>>(
-            logits, vocab, vocab, sp, out);
-        OPWORKS_CUDA_CHECK(cudaGetLastError());
+        opworks::detail::sample_launch(logits, vocab, rows, vocab, sp, out, as_stream(stream));
     });
 }
 

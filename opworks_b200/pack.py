@@ -110,10 +110,19 @@ def write_pack(path, specs, produce, extra=None, aliases=None, dtype="float32"):
     return path
 
 
-def random_llama_pack(path, cfg=None, seed=1234, std=0.02, norm_value=1.0, eos=None):
+def round_to_bf16_grid(a):
+    """fp32 values rounded (nearest-even) to the bf16 grid, kept as fp32."""
+    u = np.ascontiguousarray(a, dtype=np.float32).view(np.uint32)
+    r = (u + np.uint32(0x7FFF) + ((u >> np.uint32(16)) & np.uint32(1))) & np.uint32(0xFFFF0000)
+    return r.view(np.float32)
+
+
+def random_llama_pack(path, cfg=None, seed=1234, std=0.02, norm_value=1.0, eos=None, bf16_grid=True):
     """Random-init Llama pack: projections/embedding ~ N(0, std) drawn from
     numpy default_rng(seed) in HF order, RMSNorm gains = norm_value (the HF
-    init), lm_head.weight aliased to the embedding (tied)."""
+    init), lm_head.weight aliased to the embedding (tied). With bf16_grid the
+    fp32 values are rounded to the bf16 grid, so the bf16 copy the fast path
+    makes at load is exact and the fp32 and bf16 paths run the same model."""
     cfg = dict(cfg or LLAMA_3_2_1B)
     rng = np.random.default_rng(seed)
     specs = llama_tensor_specs(cfg)
@@ -123,10 +132,11 @@ def random_llama_pack(path, cfg=None, seed=1234, std=0.02, norm_value=1.0, eos=N
             return np.full(shape, norm_value, np.float32)
         a = rng.standard_normal(shape, dtype=np.float32)
         a *= np.float32(std)
-        return a
+        return round_to_bf16_grid(a) if bf16_grid else a
 
     extra = {"config": cfg, "eos_token_ids": list(eos if eos is not None else LLAMA_EOS),
-             "meta": {"init": "random", "seed": seed, "std": std, "norm_value": norm_value}}
+             "meta": {"init": "random", "seed": seed, "std": std, "norm_value": norm_value,
+                      "bf16_grid": bool(bf16_grid)}}
     return write_pack(path, [(n, s) for n, s, _ in specs], produce, extra=extra,
                       aliases={"lm_head.weight": "model.embed_tokens.weight"})
 
@@ -161,7 +171,7 @@ def ensure_random_llama_pack(cfg=None, seed=1234, name=None):
     cfg = cfg or LLAMA_3_2_1B
     d = default_pack_dir()
     os.makedirs(d, exist_ok=True)
-    tag = name or f"llama_L{cfg['num_hidden_layers']}_H{cfg['hidden_size']}_V{cfg['vocab_size']}_s{seed}"
+    tag = name or f"llama_L{cfg['num_hidden_layers']}_H{cfg['hidden_size']}_V{cfg['vocab_size']}_s{seed}_bf16grid"
     path = os.path.join(d, tag + ".pack")
     if not os.path.exists(path):
         random_llama_pack(path, cfg, seed)

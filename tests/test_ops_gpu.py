@@ -167,7 +167,7 @@ def test_linear_fixture_paths(ops):
 def test_gemv_shapes(ops, in_f, out_f):
     rng = np.random.default_rng(in_f + out_f)
     x = rng.standard_normal((1, in_f)).astype(np.float32)
-    w = rng.standard_normal((out_f, in_f)).astype(np.float32)
+    w = (rng.standard_normal((out_f, in_f)) / math.sqrt(in_f)).astype(np.float32)
     y = torch.empty(1, out_f, device="cuda")
     ops.linear_f32(dev(x), dev(w), y, 1, in_f, out_f, 0)
     model_close(host(y), oracle.linear(x, w))
