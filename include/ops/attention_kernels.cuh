@@ -156,66 +156,77 @@ __device__ __forceinline__ void stage_kv_tile(const KV &kv, int b, int h, int t0
 // ------------------------------------------------------------------ decode
 
 // Decode: one producer warp streams 32-token K/V tiles (2 chunks) through a
-// kDecodeStages-deep ring of bulk copies; 8 consumer warps each own HPW query
-// heads x TPW tokens of every tile and keep their own online-softmax state,
-// so tiles flow without block-wide barriers (a warp releases a stage with one
-// mbarrier arrive). The warps' states are merged once at the end.
-constexpr int kDecodeStages = 4;
+// kDecodeStages-deep ring of bulk copies; 8 consumer warps take 4 tokens of
+// every tile each. A token's 64 dims are spread over kDG lanes (8, or 16 for
+// 8 query heads per KV head) and every lane keeps the query heads' dims and
+// its own online-softmax state (m, l, o) for all kRep heads of the KV head in
+// registers. So every staged K/V element is read from shared memory exactly
+// once, the softmax needs no per-tile cross-lane reduction beyond the QK dot
+// product, and a warp releases a stage with one mbarrier arrive. Lane states
+// are merged once, at the end of the split.
+#ifndef OPWORKS_DECODE_STAGES
+#define OPWORKS_DECODE_STAGES 6
+#endif
+constexpr int kDecodeStages = OPWORKS_DECODE_STAGES;
 constexpr int kDecodeTile = 32;
 constexpr int kDecodeWarps = 8;
+constexpr int kDecodeThreads = (kDecodeWarps + 1) * 32;
+constexpr int kDecodeCtasPerSm = kDecodeStages <= 4 ? 3 : 2; // shared-memory bound residency
 
 template <int kRep> struct DecodeGeo {
-    static constexpr int kHPW = kRep < 2 ? kRep : 2;      // heads per warp
-    static constexpr int kG = kRep / kHPW;                // head groups
-    static constexpr int kTG = kDecodeWarps / kG;         // token groups
-    static constexpr int kTPW = kDecodeTile / kTG;        // tokens per warp per tile
-    static constexpr int kDG = 32 / kTPW;                 // lanes per token (dim groups)
-    static constexpr int kDims = kAttnD / kDG;            // dims per lane in QK
-    static constexpr int kVec = kDims / 4;                // float4 per lane per K row
+    static constexpr int kDG = kRep == 8 ? 16 : 8;          // lanes per token
+    static constexpr int kTL = 32 / kDG;                    // tokens a warp holds at once
+    static constexpr int kVec = kAttnD / (4 * kDG);         // float4 per lane per K/V row
+    static constexpr int kDims = 4 * kVec;                  // dims per lane
+    static constexpr int kTPW = kDecodeTile / kDecodeWarps; // tokens per warp per tile
+    static constexpr int kSteps = kTPW / kTL;
     static constexpr int kTileFloats = kDecodeTile * kAttnD;
-    static constexpr size_t kBytes = sizeof(float) * (2 * kDecodeStages * kTileFloats + kRep * kAttnD +
-                                                      kTG * kRep * (kAttnD + 2)) +
-                                     16 * kDecodeStages + 64;
-    static_assert(kG * kTG == kDecodeWarps && kTPW * kTG == kDecodeTile && kDG * kTPW == 32, "decode geometry");
+    static constexpr int kPipeFloats = 2 * kDecodeStages * kTileFloats;
+    static constexpr int kRedFloats = kDecodeWarps * kRep * (kAttnD + 2);
+    static constexpr size_t kBytes =
+        sizeof(float) * (kPipeFloats > kRedFloats ? kPipeFloats : kRedFloats) + 8 * kDecodeStages * 2 + 64;
+    static_assert(kTL * kDG == 32 && kSteps * kTL == kTPW && kVec >= 1, "decode geometry");
 };
 
+// Issue the bulk copies of one tile (chunks of `kDecodeTile / kKvChunk`),
+// given the per-chunk source offsets and token counts (0 = past t_end).
 template <class KV>
-__device__ __forceinline__ void stage_kv_chunks(const KV &kv, int b, int h, int t0, int t_end, int chunks, float *ks,
-                                                float *vs, uint64_t *bar) {
+__device__ __forceinline__ void stage_kv_tile_offsets(const KV &kv, const int64_t *off, const int *ntok, float *ks,
+                                                      float *vs, uint64_t *bar) {
+    constexpr int kChunks = kDecodeTile / kKvChunk;
     uint32_t bytes = 0;
-    for (int c = 0; c < chunks; ++c) {
-        const int chunk = t0 / kKvChunk + c;
-        if (chunk * kKvChunk < t_end)
-            bytes += 2u * static_cast<uint32_t>(kv.chunk_tokens(chunk)) * kAttnD * 4u;
-    }
+#pragma unroll
+    for (int c = 0; c < kChunks; ++c)
+        bytes += 2u * static_cast<uint32_t>(ntok[c]) * kAttnD * 4u;
     sm100::mbar_arrive_expect_tx(bar, bytes);
-    for (int c = 0; c < chunks; ++c) {
-        const int chunk = t0 / kKvChunk + c;
-        if (chunk * kKvChunk < t_end) {
-            const uint32_t n = static_cast<uint32_t>(kv.chunk_tokens(chunk)) * kAttnD * 4u;
-            const int64_t off = kv.chunk_offset(b, h, chunk);
-            sm100::bulk_load(ks + c * kKvChunk * kAttnD, kv.k + off, n, bar);
-            sm100::bulk_load(vs + c * kKvChunk * kAttnD, kv.v + off, n, bar);
+#pragma unroll
+    for (int c = 0; c < kChunks; ++c) {
+        if (ntok[c] > 0) {
+            const uint32_t n = static_cast<uint32_t>(ntok[c]) * kAttnD * 4u;
+            sm100::bulk_load(ks + c * kKvChunk * kAttnD, kv.k + off[c], n, bar);
+            sm100::bulk_load(vs + c * kKvChunk * kAttnD, kv.v + off[c], n, bar);
         }
     }
 }
 
-// q: [B][q_stride] with heads at h*64; part_o [B][qh][splits][64]; part_ml
-// [B][qh][splits][2] (running max, running sum). grid = (splits, kvh, B).
-template <class KV, int kRep>
-__global__ void __launch_bounds__((kDecodeWarps + 1) * 32)
+// q: [B][q_stride] with heads at h*64. grid = (splits, kvh, B). With one
+// split the normalised result goes straight to `out`; otherwise part_o
+// [B][qh][splits][64] and part_ml [B][qh][splits][2] (running max, running
+// sum) hold the split partials for attn_decode_combine_kernel.
+template <class KV, int kRep, typename Out>
+__global__ void __launch_bounds__(kDecodeThreads, kDecodeCtasPerSm)
     attn_decode_partial_kernel(const float *__restrict__ q, int64_t q_stride, KV kv, const int *__restrict__ lens,
                                int tokens_per_split, float scale, float *__restrict__ part_o,
-                               float *__restrict__ part_ml, int *err) {
+                               float *__restrict__ part_ml, Out out, int *err) {
     using G = DecodeGeo<kRep>;
+    constexpr int kChunks = kDecodeTile / kKvChunk;
     extern __shared__ __align__(128) uint8_t smem_raw[];
     float *ks = reinterpret_cast<float *>(smem_raw);
     float *vs = ks + kDecodeStages * G::kTileFloats;
-    float *qs = vs + kDecodeStages * G::kTileFloats;
-    float *red = qs + kRep * kAttnD;              // [kTG][kRep][64]
-    float *mls = red + G::kTG * kRep * kAttnD;    // [kTG][kRep][2]
-    uint64_t *full = reinterpret_cast<uint64_t *>(
-        (reinterpret_cast<uintptr_t>(mls + G::kTG * kRep * 2) + 15) & ~static_cast<uintptr_t>(15));
+    float *red = ks;                                // [warps][kRep][64], reuses the ring after the loop
+    float *mls = red + kDecodeWarps * kRep * kAttnD; // [warps][kRep][2]
+    const int pipe_floats = G::kPipeFloats > G::kRedFloats ? G::kPipeFloats : G::kRedFloats;
+    uint64_t *full = reinterpret_cast<uint64_t *>(ks + pipe_floats);
     uint64_t *empty = full + kDecodeStages;
 
     const int b = blockIdx.z, h = blockIdx.y, split = blockIdx.x, splits = gridDim.x;
@@ -226,8 +237,6 @@ __global__ void __launch_bounds__((kDecodeWarps + 1) * 32)
     const int t_end = min(len, t_begin + tokens_per_split);
     const int n_tiles = t_end > t_begin ? (t_end - t_begin + kDecodeTile - 1) / kDecodeTile : 0;
 
-    for (int i = tid; i < kRep * kAttnD; i += blockDim.x)
-        qs[i] = q[static_cast<int64_t>(b) * q_stride + static_cast<int64_t>(h) * kRep * kAttnD + i];
     if (tid == 0) {
         for (int s = 0; s < kDecodeStages; ++s) {
             sm100::mbar_init(&full[s], 1);
@@ -238,118 +247,157 @@ __global__ void __launch_bounds__((kDecodeWarps + 1) * 32)
     __syncthreads();
 
     bool ok = true;
+    const int tl = lane / G::kDG, dq = lane % G::kDG;
+    float m_run[kRep], l_run[kRep], acc[kRep][G::kDims];
     if (warp == kDecodeWarps) {
-        // producer warp: one elected lane streams the tiles
-        if (lane == 0) {
-            int issued = 0;
-            for (; issued < n_tiles; ++issued) {
-                const int s = issued % kDecodeStages;
-                if (issued >= kDecodeStages &&
-                    !sm100::mbar_wait(&empty[s], static_cast<uint32_t>((issued / kDecodeStages) - 1) & 1u)) {
+        // producer warp: the lanes look up 32 chunks' block offsets at a time,
+        // lane 0 issues the copies
+        int issued = 0;
+        const int chunk0 = t_begin / kKvChunk;
+        for (int base = 0; base < n_tiles && ok; base += 32 / kChunks) {
+            const int my_chunk = chunk0 + base * kChunks + lane;
+            int64_t my_off = 0;
+            int my_tok = 0;
+            if (my_chunk * kKvChunk < t_end) {
+                my_off = kv.chunk_offset(b, h, my_chunk);
+                my_tok = kv.chunk_tokens(my_chunk);
+            }
+            const int stop = min(n_tiles, base + 32 / kChunks);
+            for (int tile = base; tile < stop; ++tile) {
+                int64_t off[kChunks];
+                int ntok[kChunks];
+#pragma unroll
+                for (int c = 0; c < kChunks; ++c) {
+                    off[c] = __shfl_sync(kFullWarpMask, my_off, (tile - base) * kChunks + c);
+                    ntok[c] = __shfl_sync(kFullWarpMask, my_tok, (tile - base) * kChunks + c);
+                }
+                const int s = tile % kDecodeStages;
+                bool go = true;
+                if (lane == 0) {
+                    if (tile >= kDecodeStages)
+                        go = sm100::mbar_wait(&empty[s], static_cast<uint32_t>((tile / kDecodeStages) - 1) & 1u);
+                    if (go)
+                        stage_kv_tile_offsets(kv, off, ntok, ks + s * G::kTileFloats, vs + s * G::kTileFloats,
+                                              &full[s]);
+                }
+                go = __shfl_sync(kFullWarpMask, go, 0);
+                if (!go) {
                     ok = false;
                     break;
                 }
-                stage_kv_chunks(kv, b, h, t_begin + issued * kDecodeTile, t_end, kDecodeTile / kKvChunk,
-                                ks + s * G::kTileFloats, vs + s * G::kTileFloats, &full[s]);
+                ++issued;
             }
-            // every issued copy must land before the CTA may exit
+        }
+        // every issued copy must land before the CTA may exit or reuse the ring
+        if (lane == 0)
             for (int j = (issued > kDecodeStages ? issued - kDecodeStages : 0); j < issued; ++j)
                 if (!sm100::mbar_wait(&full[j % kDecodeStages], static_cast<uint32_t>(j / kDecodeStages) & 1u))
                     ok = false;
-        }
-    }
-
-    // consumer geometry
-    const int hg = warp % G::kG;           // head group: heads hg*HPW ...
-    const int tg = warp / G::kG;           // token group within every tile
-    const int tl = lane / G::kDG;          // token of this lane within the warp's tokens
-    const int dq = lane % G::kDG;          // dim group of this lane (QK)
-    float m_run[G::kHPW], l_run[G::kHPW], acc[G::kHPW][2];
+    } else {
+        // this lane's slice of the query heads, in registers
+        float qr[kRep][G::kDims];
+        const float *qb = q + static_cast<int64_t>(b) * q_stride + static_cast<int64_t>(h) * kRep * kAttnD;
 #pragma unroll
-    for (int j = 0; j < G::kHPW; ++j) {
-        m_run[j] = kNegInf;
-        l_run[j] = 0.f;
-        acc[j][0] = acc[j][1] = 0.f;
-    }
-    if (warp < kDecodeWarps) {
+        for (int j = 0; j < kRep; ++j) {
+            m_run[j] = kNegInf;
+            l_run[j] = 0.f;
+#pragma unroll
+            for (int c = 0; c < G::kVec; ++c)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    qr[j][4 * c + e] = qb[j * kAttnD + c * 4 * G::kDG + dq * 4 + e] * scale;
+                    acc[j][4 * c + e] = 0.f;
+                }
+        }
         for (int tile = 0; tile < n_tiles; ++tile) {
             const int s = tile % kDecodeStages;
             if (!sm100::mbar_wait(&full[s], static_cast<uint32_t>(tile / kDecodeStages) & 1u)) {
                 ok = false;
                 break;
             }
-            const float *K = ks + s * G::kTileFloats;
-            const float *V = vs + s * G::kTileFloats;
+            const float4 *K = reinterpret_cast<const float4 *>(ks + s * G::kTileFloats);
+            const float4 *V = reinterpret_cast<const float4 *>(vs + s * G::kTileFloats);
             const int t0 = t_begin + tile * kDecodeTile;
-            const int tok = tg * G::kTPW + tl; // token within the tile
-            const bool valid = t0 + tok < t_end;
-            // QK: this lane's kDims dims of one token for the warp's heads
-            float d[G::kHPW];
 #pragma unroll
-            for (int j = 0; j < G::kHPW; ++j)
-                d[j] = 0.f;
-            if (valid) {
-                const float4 *kr = reinterpret_cast<const float4 *>(K + tok * kAttnD + dq * G::kDims);
+            for (int st = 0; st < G::kSteps; ++st) {
+                const int tok = warp * G::kTPW + st * G::kTL + tl;
+                const bool valid = t0 + tok < t_end;
+                float4 kk[G::kVec], vv[G::kVec];
 #pragma unroll
                 for (int c = 0; c < G::kVec; ++c) {
-                    const int cc = (c + tok) % G::kVec; // staggered: spreads smem banks
-                    const float4 k4 = kr[cc];
-#pragma unroll
-                    for (int j = 0; j < G::kHPW; ++j) {
-                        const float4 q4 =
-                            reinterpret_cast<const float4 *>(qs + (hg * G::kHPW + j) * kAttnD + dq * G::kDims)[cc];
-                        d[j] += k4.x * q4.x + k4.y * q4.y + k4.z * q4.z + k4.w * q4.w;
-                    }
+                    kk[c] = K[tok * (kAttnD / 4) + c * G::kDG + dq];
+                    vv[c] = V[tok * (kAttnD / 4) + c * G::kDG + dq];
                 }
-            }
+                float d[kRep];
 #pragma unroll
-            for (int j = 0; j < G::kHPW; ++j) {
+                for (int j = 0; j < kRep; ++j) {
+                    float x = 0.f;
 #pragma unroll
-                for (int off = 1; off < G::kDG; off <<= 1)
-                    d[j] += __shfl_xor_sync(kFullWarpMask, d[j], off);
-                d[j] = valid ? d[j] * scale : kNegInf;
-            }
-            // online softmax over the warp's tokens, per head
-            float p[G::kHPW], alpha[G::kHPW];
+                    for (int c = 0; c < G::kVec; ++c) {
+                        x = fmaf(qr[j][4 * c + 0], kk[c].x, x);
+                        x = fmaf(qr[j][4 * c + 1], kk[c].y, x);
+                        x = fmaf(qr[j][4 * c + 2], kk[c].z, x);
+                        x = fmaf(qr[j][4 * c + 3], kk[c].w, x);
+                    }
+                    d[j] = x;
+                }
 #pragma unroll
-            for (int j = 0; j < G::kHPW; ++j) {
-                float mt = d[j];
+                for (int j = 0; j < kRep; ++j)
 #pragma unroll
-                for (int off = G::kDG; off < 32; off <<= 1)
-                    mt = fmaxf(mt, __shfl_xor_sync(kFullWarpMask, mt, off));
-                const float m_new = fmaxf(m_run[j], mt);
-                alpha[j] = m_run[j] == kNegInf ? (m_new == kNegInf ? 1.f : 0.f) : expf(m_run[j] - m_new);
-                p[j] = valid ? expf(d[j] - m_new) : 0.f;
-                float ps = dq == 0 ? p[j] : 0.f;
+                    for (int off = 1; off < G::kDG; off <<= 1)
+                        d[j] += __shfl_xor_sync(kFullWarpMask, d[j], off);
+                if (valid) {
 #pragma unroll
-                for (int off = 1; off < 32; off <<= 1)
-                    ps += __shfl_xor_sync(kFullWarpMask, ps, off);
-                l_run[j] = l_run[j] * alpha[j] + ps;
-                m_run[j] = m_new;
-                acc[j][0] *= alpha[j];
-                acc[j][1] *= alpha[j];
-            }
-            // PV: lane owns dims 2*lane, 2*lane + 1
+                    for (int j = 0; j < kRep; ++j) {
+                        float p;
+                        if (d[j] > m_run[j]) {
+                            const float a = expf(m_run[j] - d[j]);
+                            m_run[j] = d[j];
+                            l_run[j] *= a;
 #pragma unroll
-            for (int t = 0; t < G::kTPW; ++t) {
-                const int tt = tg * G::kTPW + t;
-                const bool tv = t0 + tt < t_end;
-                float pt[G::kHPW];
+                            for (int e = 0; e < G::kDims; ++e)
+                                acc[j][e] *= a;
+                            p = 1.f;
+                        } else {
+                            p = expf(d[j] - m_run[j]);
+                        }
+                        l_run[j] += p;
 #pragma unroll
-                for (int j = 0; j < G::kHPW; ++j)
-                    pt[j] = __shfl_sync(kFullWarpMask, p[j], t * G::kDG);
-                if (tv) {
-                    const float2 v2 = *reinterpret_cast<const float2 *>(V + tt * kAttnD + 2 * lane);
-#pragma unroll
-                    for (int j = 0; j < G::kHPW; ++j) {
-                        acc[j][0] += pt[j] * v2.x;
-                        acc[j][1] += pt[j] * v2.y;
+                        for (int c = 0; c < G::kVec; ++c) {
+                            acc[j][4 * c + 0] = fmaf(p, vv[c].x, acc[j][4 * c + 0]);
+                            acc[j][4 * c + 1] = fmaf(p, vv[c].y, acc[j][4 * c + 1]);
+                            acc[j][4 * c + 2] = fmaf(p, vv[c].z, acc[j][4 * c + 2]);
+                            acc[j][4 * c + 3] = fmaf(p, vv[c].w, acc[j][4 * c + 3]);
+                        }
                     }
                 }
             }
             __syncwarp();
             if (lane == 0)
                 sm100::mbar_arrive(&empty[s]);
+        }
+        // merge the token lanes of the warp (lanes with the same dq)
+#pragma unroll
+        for (int j = 0; j < kRep; ++j) {
+            float M = m_run[j];
+#pragma unroll
+            for (int off = G::kDG; off < 32; off <<= 1)
+                M = fmaxf(M, __shfl_xor_sync(kFullWarpMask, M, off));
+            const float a = m_run[j] == kNegInf ? 0.f : expf(m_run[j] - M);
+            float L = l_run[j] * a;
+#pragma unroll
+            for (int off = G::kDG; off < 32; off <<= 1)
+                L += __shfl_xor_sync(kFullWarpMask, L, off);
+#pragma unroll
+            for (int e = 0; e < G::kDims; ++e) {
+                float o = acc[j][e] * a;
+#pragma unroll
+                for (int off = G::kDG; off < 32; off <<= 1)
+                    o += __shfl_xor_sync(kFullWarpMask, o, off);
+                acc[j][e] = o;
+            }
+            m_run[j] = M;
+            l_run[j] = L;
         }
     }
     ok = __syncthreads_and(ok);
@@ -358,17 +406,18 @@ __global__ void __launch_bounds__((kDecodeWarps + 1) * 32)
             atomicExch(err, 2);
         return;
     }
-    // merge the token groups: every warp publishes its (m, l, acc)
-    if (warp < kDecodeWarps) {
+    // the ring is idle: every warp publishes its (m, l, o) there
+    if (warp < kDecodeWarps && tl == 0) {
 #pragma unroll
-        for (int j = 0; j < G::kHPW; ++j) {
-            const int head = hg * G::kHPW + j;
-            float *o = red + (tg * kRep + head) * kAttnD;
-            o[2 * lane] = acc[j][0];
-            o[2 * lane + 1] = acc[j][1];
-            if (lane == 0) {
-                mls[(tg * kRep + head) * 2] = m_run[j];
-                mls[(tg * kRep + head) * 2 + 1] = l_run[j];
+        for (int j = 0; j < kRep; ++j) {
+            float *o = red + (warp * kRep + j) * kAttnD;
+#pragma unroll
+            for (int c = 0; c < G::kVec; ++c)
+                *reinterpret_cast<float4 *>(o + c * 4 * G::kDG + dq * 4) =
+                    make_float4(acc[j][4 * c], acc[j][4 * c + 1], acc[j][4 * c + 2], acc[j][4 * c + 3]);
+            if (dq == 0) {
+                mls[(warp * kRep + j) * 2] = m_run[j];
+                mls[(warp * kRep + j) * 2 + 1] = l_run[j];
             }
         }
     }
@@ -376,11 +425,11 @@ __global__ void __launch_bounds__((kDecodeWarps + 1) * 32)
     for (int i = tid; i < kRep * kAttnD; i += blockDim.x) {
         const int head = i / kAttnD, dd = i % kAttnD;
         float M = kNegInf;
-        for (int g = 0; g < G::kTG; ++g)
+        for (int g = 0; g < kDecodeWarps; ++g)
             M = fmaxf(M, mls[(g * kRep + head) * 2]);
         float L = 0.f, O = 0.f;
         if (M != kNegInf) {
-            for (int g = 0; g < G::kTG; ++g) {
+            for (int g = 0; g < kDecodeWarps; ++g) {
                 const float mg = mls[(g * kRep + head) * 2];
                 if (mg == kNegInf)
                     continue;
@@ -389,11 +438,15 @@ __global__ void __launch_bounds__((kDecodeWarps + 1) * 32)
                 O += w * red[(g * kRep + head) * kAttnD + dd];
             }
         }
-        const int64_t row = (static_cast<int64_t>(b) * qh_total + h * kRep + head) * splits + split;
-        part_o[row * kAttnD + dd] = O;
-        if (dd == 0) {
-            part_ml[2 * row] = M;
-            part_ml[2 * row + 1] = L;
+        if (splits == 1) {
+            out.put(b, h * kRep + head, dd, L > 0.f ? O / L : 0.f);
+        } else {
+            const int64_t row = (static_cast<int64_t>(b) * qh_total + h * kRep + head) * splits + split;
+            part_o[row * kAttnD + dd] = O;
+            if (dd == 0) {
+                part_ml[2 * row] = M;
+                part_ml[2 * row + 1] = L;
+            }
         }
     }
 }
@@ -622,12 +675,12 @@ __global__ void __launch_bounds__(256)
 
 // ----------------------------------------------------------- host helpers
 
-template <class KV, int kRep> inline void prepare_decode_kernel() {
+template <class KV, int kRep, typename Out> inline void prepare_decode_kernel() {
     static thread_local int done = -1;
     int dev = 0;
     OPWORKS_CUDA_CHECK(cudaGetDevice(&dev));
     if (done != dev) {
-        OPWORKS_CUDA_CHECK(cudaFuncSetAttribute(attn_decode_partial_kernel<KV, kRep>,
+        OPWORKS_CUDA_CHECK(cudaFuncSetAttribute(attn_decode_partial_kernel<KV, kRep, Out>,
                                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                 static_cast<int>(DecodeGeo<kRep>::kBytes)));
         done = dev;
@@ -647,30 +700,34 @@ template <class KV, int kRep, typename Out> inline void prepare_prefill_kernel()
 }
 
 // Split-KV geometry for `pairs` (sequence, kv head) pairs whose longest
-// visible length is max_len: tokens per split is a multiple of the tile.
+// visible length is max_len: as many splits as keep every CTA resident in one
+// wave (kDecodeCtasPerSm per SM), so the KV stream is one pass over HBM with
+// no tail wave; tokens per split is a multiple of the tile.
 inline int decode_tokens_per_split(int pairs, int max_len, int sm_count) {
-    const int tiles = (max_len + kAttnTile - 1) / kAttnTile;
-    const int target = 4 * sm_count; // ~2 waves at 2 CTAs per SM
-    int splits = (target + pairs - 1) / pairs;
+    const int tiles = (max_len + kDecodeTile - 1) / kDecodeTile;
+    const int slots = kDecodeCtasPerSm * sm_count;
+    int splits = slots / (pairs > 0 ? pairs : 1);
     if (splits > tiles)
         splits = tiles;
     if (splits < 1)
         splits = 1;
     const int tiles_per_split = (tiles + splits - 1) / splits;
-    return (tiles_per_split > 0 ? tiles_per_split : 1) * kAttnTile;
+    return (tiles_per_split > 0 ? tiles_per_split : 1) * kDecodeTile;
 }
 
 template <class KV, int kRep, typename Out>
 inline void attn_decode_launch(const float *q, int64_t q_stride, const KV &kv, const int *lens, int batch, int kvh,
                                int tokens_per_split, int splits, float scale, float *part_o, float *part_ml,
                                const Out &out, cudaStream_t stream) {
-    prepare_decode_kernel<KV, kRep>();
+    prepare_decode_kernel<KV, kRep, Out>();
     const dim3 grid(splits, kvh, batch);
-    attn_decode_partial_kernel<KV, kRep><<<grid, (kDecodeWarps + 1) * 32, DecodeGeo<kRep>::kBytes, stream>>>(
-        q, q_stride, kv, lens, tokens_per_split, scale, part_o, part_ml, sm100::device_error_word());
+    attn_decode_partial_kernel<KV, kRep, Out><<<grid, kDecodeThreads, DecodeGeo<kRep>::kBytes, stream>>>(
+        q, q_stride, kv, lens, tokens_per_split, scale, part_o, part_ml, out, sm100::device_error_word());
     OPWORKS_CUDA_CHECK(cudaGetLastError());
-    attn_decode_combine_kernel<Out><<<dim3(kvh * kRep, batch), 64, 0, stream>>>(part_o, part_ml, splits, out);
-    OPWORKS_CUDA_CHECK(cudaGetLastError());
+    if (splits > 1) {
+        attn_decode_combine_kernel<Out><<<dim3(kvh * kRep, batch), 64, 0, stream>>>(part_o, part_ml, splits, out);
+        OPWORKS_CUDA_CHECK(cudaGetLastError());
+    }
 }
 
 template <class KV, int kRep, typename Out>

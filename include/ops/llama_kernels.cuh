@@ -406,13 +406,32 @@ static __global__ void __cluster_dims__(kSampleCluster, 1, 1) __launch_bounds__(
             sh.cnt[b] = 0;
         }
         __syncthreads();
-        for (int i = tid; i < n; i += blockDim.x) {
-            const float v = sh.x[i];
-            const uint32_t k = float_key(v);
-            if ((k & mask_hi) == prefix) {
-                const int b = static_cast<int>((k >> shift) & static_cast<uint32_t>(nb - 1));
-                atomicAdd(&sh.hist[b], static_cast<double>(mass(v)));
-                atomicAdd(&sh.cnt[b], 1);
+        // warp-aggregated histogram: lanes hitting the same bucket are summed
+        // in registers and one lane issues the shared-memory atomics (the
+        // top-level buckets of a logit row are few and heavily shared)
+        const int n_pad = (n + kWarpSize - 1) / kWarpSize * kWarpSize;
+        for (int i = tid; i < n_pad; i += blockDim.x) {
+            int b = -1;
+            float e = 0.f;
+            if (i < n) {
+                const float v = sh.x[i];
+                const uint32_t k = float_key(v);
+                if ((k & mask_hi) == prefix) {
+                    b = static_cast<int>((k >> shift) & static_cast<uint32_t>(nb - 1));
+                    e = mass(v);
+                }
+            }
+            const unsigned peers = __match_any_sync(kFullWarpMask, b);
+            double sum = 0.0;
+#pragma unroll 4
+            for (int j = 0; j < kWarpSize; ++j) {
+                const float ej = __shfl_sync(kFullWarpMask, e, j);
+                if ((peers >> j) & 1u)
+                    sum += static_cast<double>(ej);
+            }
+            if (b >= 0 && lane == __ffs(peers) - 1) {
+                atomicAdd(&sh.hist[b], sum);
+                atomicAdd(&sh.cnt[b], __popc(peers));
             }
         }
         cluster.sync();

@@ -100,6 +100,19 @@ OPW_API int opw_attention_prefill_chunked(const float *q_heads, const float *kca
 OPW_API int opw_sample(const float *logits, int rows, int vocab, const float *temperature, const float *top_p,
                const double *uniform, int32_t *out, void *stream);
 
+/* Batched decode attention over a paged fp32 KV cache (the Llama runtime's
+ * kernel): q [B][qh*64], pools [blocks][kvh][16][64], block_table
+ * [B][table_stride], lens[B] (device int32); out [B][qh*64] fp32. Scratch for
+ * the split-KV partials comes from stream-ordered allocation. */
+OPW_API int opw_paged_attention_decode(const float *q, const float *kpool, const float *vpool,
+                                       const int32_t *block_table, int table_stride, const int32_t *lens, int B,
+                                       int max_len, int num_q_heads, int num_kv_heads, float *out, void *stream);
+/* out[split][M][N] (fp32 partials) = W[N][K] (bf16) . (Xhi + Xlo)[M][K]^T with
+ * the runtime's two-term bf16 activation GEMM; splits = 0 picks the runtime's
+ * split-K plan. Returns the split count used, or -1. */
+OPW_API int opw_gemm_bf16x2(const uint16_t *W, const uint16_t *x_hi, const uint16_t *x_lo, float *out, int N, int K,
+                            int M, int splits, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

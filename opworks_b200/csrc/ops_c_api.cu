@@ -255,6 +255,53 @@ int opw_attention_prefill_chunked(const float *q_heads, const float *kcache, con
     });
 }
 
+int opw_paged_attention_decode(const float *q, const float *kpool, const float *vpool, const int32_t *block_table,
+                               int table_stride, const int32_t *lens, int B, int max_len, int num_q_heads,
+                               int num_kv_heads, float *out, void *stream) {
+    return guarded([&] {
+        using namespace opworks::detail;
+        require(B > 0 && max_len > 0 && num_kv_heads > 0 && num_q_heads % num_kv_heads == 0,
+                "paged attention: bad shape");
+        require(q && kpool && vpool && block_table && lens && out, "paged attention: null pointer");
+        const int rep = num_q_heads / num_kv_heads;
+        const int tps = decode_tokens_per_split(B * num_kv_heads, max_len, device_facts().sm_count);
+        const int splits = (max_len + tps - 1) / tps;
+        const size_t po = sizeof(float) * static_cast<size_t>(B) * num_q_heads * splits * kAttnD;
+        const size_t pml = sizeof(float) * static_cast<size_t>(B) * num_q_heads * splits * 2;
+        StreamScratch scratch(po + pml, as_stream(stream));
+        const PagedKV kv{kpool, vpool, block_table, table_stride, num_kv_heads};
+        const StridedOut<float> o{out, static_cast<int64_t>(num_q_heads) * kAttnD, kAttnD};
+        float *part_o = scratch.as<float>(0), *part_ml = scratch.as<float>(po);
+        const float scale = 0.125f;
+        switch (rep) {
+        case 1: attn_decode_launch<PagedKV, 1>(q, num_q_heads * kAttnD, kv, lens, B, num_kv_heads, tps, splits, scale, part_o, part_ml, o, as_stream(stream)); break;
+        case 2: attn_decode_launch<PagedKV, 2>(q, num_q_heads * kAttnD, kv, lens, B, num_kv_heads, tps, splits, scale, part_o, part_ml, o, as_stream(stream)); break;
+        case 4: attn_decode_launch<PagedKV, 4>(q, num_q_heads * kAttnD, kv, lens, B, num_kv_heads, tps, splits, scale, part_o, part_ml, o, as_stream(stream)); break;
+        case 8: attn_decode_launch<PagedKV, 8>(q, num_q_heads * kAttnD, kv, lens, B, num_kv_heads, tps, splits, scale, part_o, part_ml, o, as_stream(stream)); break;
+        default: throw std::invalid_argument("paged attention: GQA ratio must be 1, 2, 4 or 8");
+        }
+    });
+}
+
+int opw_gemm_bf16x2(const uint16_t *W, const uint16_t *x_hi, const uint16_t *x_lo, float *out, int N, int K, int M,
+                    int splits, void *stream) {
+    int used = -1;
+    const int rc = guarded([&] {
+        using namespace opworks;
+        detail::require(W && x_hi && x_lo && out && N > 0 && K > 0 && M > 0, "gemm_bf16x2: bad arguments");
+        const int bn = sm100::gemm_pick_bn(sm100::GemmKind::kBF16x2, M);
+        if (splits <= 0) {
+            const int tiles = ((N + kUmmaM - 1) / kUmmaM) * ((M + bn - 1) / bn);
+            splits = sm100::gemm_pick_splits(tiles, (K + 63) / 64, detail::device_facts().sm_count, 4);
+        }
+        sm100::gemm_tn<sm100::GemmKind::kBF16x2>({as_bf16(W), nullptr, N, K}, {as_bf16(x_hi), as_bf16(x_lo), M, K},
+                                                 K, out, N, splits, static_cast<int64_t>(M) * N, as_stream(stream),
+                                                 sm100::Identity{}, bn);
+        used = splits;
+    });
+    return rc == 0 ? used : -1;
+}
+
 int opw_sample(const float *logits, int rows, int vocab, const float *temperature, const float *top_p,
                const double *uniform, int32_t *out, void *stream) {
     return guarded([&] {

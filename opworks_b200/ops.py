@@ -43,6 +43,8 @@ SIGNATURES = {
     "opw_attention_decode": [P, P, P, P, I, I, I, I, I, P],
     "opw_attention_prefill_chunked": [P, P, P, P, I, I, I, I, I, I, I, P],
     "opw_sample": [P, I, I, P, P, P, P, P],
+    "opw_paged_attention_decode": [P, P, P, P, I, P, I, I, I, I, P, P],
+    "opw_gemm_bf16x2": [P, P, P, P, I, I, I, I, P],
 }
 
 
