@@ -244,37 +244,78 @@ __device__ __forceinline__ float key_float(uint32_t k) {
     return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
 }
 
-constexpr int kSampleCluster = 8;    // CTAs per row (portable cluster size)
-constexpr int kSampleThreads = 512;  // threads per CTA
+constexpr int kSampleCluster = 8;      // CTAs per row (portable cluster size)
+constexpr int kSampleThreads = 512;    // threads per CTA
 constexpr int kSampleChunkMax = 16384; // logits per CTA held in shared memory
-constexpr int kRadixBuckets = 2048;
+constexpr int kSampleBuckets = 256;    // buckets per select level
+constexpr int kSampleCandMax = 2048;   // compacted boundary-band tokens per CTA
+constexpr float kSampleDistScale = 8.f;           // level-0 buckets per nat of (max - logit) / T
+constexpr float kSampleTailDist = 23.f * 8.f;     // beyond 23 nats a token's fixed-point mass is 0
+constexpr float kSampleMassScale = 2147483648.f;  // 2^31: masses in fixed point
+
+// Scaled distance of logit v from the row max, (max - v) / T * 8, and its
+// level-0 band (monotone in v: a larger logit never lands in a later band).
+__device__ __forceinline__ float sample_dist(float v, float gmax, float dscale) { return (gmax - v) * dscale; }
+constexpr int kSampleBandCap = 251; // last distance band; byte codes above it mark boundary-band tokens
+constexpr uint8_t kBandKept = 252, kBandTie = 253, kBandDrop = 254;
+__device__ __forceinline__ int sample_bucket(float t) {
+    return t < static_cast<float>(kSampleBandCap) ? static_cast<int>(t) : kSampleBandCap;
+}
+
+// Token mass exp((v - max) / T) in fixed point: round(e * 2^31) with e the
+// fp32 exp (so the top token weighs exactly 2^31), 0 beyond 23 nats (where it
+// rounds to 0 anyway). A row's total stays below 2^17 * 2^31, and integer sums
+// are exact and independent of summation order, so the kept set and the draw
+// are deterministic.
+__device__ __forceinline__ uint32_t sample_qmass(float v, float t, float gmax, float inv_t) {
+    return t < kSampleTailDist ? __float2uint_rn(expf((v - gmax) * inv_t) * kSampleMassScale) : 0u;
+}
+
+// Shared-memory positions of slice element i in the 32-bit array (one pad
+// word per 32) and in the byte array (one pad word per 128): a thread walking
+// a contiguous run and a warp walking consecutive elements are both free of
+// bank conflicts.
+__device__ __forceinline__ int sample_pos(int i) { return i + (i >> 5); }
+__device__ __forceinline__ int sample_bpos(int i) { return i + ((i >> 7) << 2); }
 
 struct SampleShared {
-    float x[kSampleChunkMax];      // this CTA's slice of the row
-    double hist[kRadixBuckets];    // mass per radix bucket
-    int cnt[kRadixBuckets];        // tokens per radix bucket
-    double dscr[32];
-    int iscr[32];
+    // this CTA's slice of the row: the logits, replaced by their fixed-point
+    // masses once the row max is known
+    union {
+        float x[kSampleChunkMax + kSampleChunkMax / 32];
+        uint32_t q[kSampleChunkMax + kSampleChunkMax / 32];
+    };
+    uint8_t band[kSampleChunkMax + kSampleChunkMax / 32]; // level-0 bucket of every token
+    // histograms: per bucket the sums of mass bits [0,16) and [16,32) in
+    // 32-bit counters (no overflow for 16384 tokens); level 0, then levels
+    // 1-4 alternating between two buffers
+    uint32_t h0[2][kSampleBuckets];
+    uint32_t hk[2][2][kSampleBuckets];
+    int warp_cnt[kSampleThreads / 32];
+    uint32_t cand_key[kSampleCandMax];                     // boundary-band tokens: float key,
+    uint32_t cand_q[kSampleCandMax];                       //   mass
+    uint16_t cand_pos[kSampleCandMax];                     //   and slice position
+    unsigned long long uscr[kSampleThreads / 32];
+    int iscr[kSampleThreads / 32];
     float best_v;
     int best_i;
-    double part_mass;              // final pass: kept mass of this CTA
-    int part_ties;                 // final pass: boundary ties of this CTA
-    // results of the leader (rank 0), read by every CTA through DSMEM
-    uint32_t prefix;
-    double above, z;
-    int above_cnt;
+    unsigned long long part_mass; // final pass: kept mass of this CTA
+    int part_ties;                // final pass: boundary ties of this CTA
+    int res_bucket;               // crossing bucket of the current level
+    unsigned long long res_above; // mass above it
 };
 
-// Block-wide exclusive prefix (threads in index order) of a double and an int.
-__device__ __forceinline__ void block_scan_excl(double v, int c, double *dscr, int *iscr, double &v_before,
-                                                int &c_before, double &v_total, int &c_total) {
+// Block-wide exclusive prefix (threads in index order) of a u64 and an int.
+__device__ __forceinline__ void block_scan_excl(unsigned long long v, int c, unsigned long long *uscr, int *iscr,
+                                                unsigned long long &v_before, int &c_before,
+                                                unsigned long long &v_total, int &c_total) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int nw = blockDim.x >> 5;
-    double vi = v;
+    unsigned long long vi = v;
     int ci = c;
 #pragma unroll
     for (int off = 1; off < 32; off <<= 1) {
-        const double vo = __shfl_up_sync(kFullWarpMask, vi, off);
+        const unsigned long long vo = __shfl_up_sync(kFullWarpMask, vi, off);
         const int co = __shfl_up_sync(kFullWarpMask, ci, off);
         if (lane >= off) {
             vi += vo;
@@ -283,24 +324,42 @@ __device__ __forceinline__ void block_scan_excl(double v, int c, double *dscr, i
     }
     __syncthreads();
     if (lane == 31) {
-        dscr[warp] = vi;
+        uscr[warp] = vi;
         iscr[warp] = ci;
     }
     __syncthreads();
-    double wv = 0.0, tv = 0.0;
+    unsigned long long wv = 0, tv = 0;
     int wc = 0, tc = 0;
     for (int w = 0; w < nw; ++w) {
         if (w < warp) {
-            wv += dscr[w];
+            wv += uscr[w];
             wc += iscr[w];
         }
-        tv += dscr[w];
+        tv += uscr[w];
         tc += iscr[w];
     }
     v_before = wv + vi - v;
     c_before = wc + ci - c;
     v_total = tv;
     c_total = tc;
+}
+
+// Histogram add of a 31-bit mass as two 16-bit halves in 32-bit counters
+// (native shared-memory atomics); a warp whose lanes all hit one bucket
+// (flat rows) adds once. Whole warps must call it.
+__device__ __forceinline__ void sample_hist_add(uint32_t (*h)[kSampleBuckets], int bkt, uint32_t q, int lane) {
+    const int b0 = __shfl_sync(kFullWarpMask, bkt, 0);
+    if (__all_sync(kFullWarpMask, bkt == b0)) {
+        const uint32_t lo = __reduce_add_sync(kFullWarpMask, q & 0xffffu);
+        const uint32_t hi = __reduce_add_sync(kFullWarpMask, q >> 16);
+        if (lane == 0 && b0 >= 0 && (lo | hi)) {
+            atomicAdd(&h[0][b0], lo);
+            atomicAdd(&h[1][b0], hi);
+        }
+    } else if (bkt >= 0 && q) {
+        atomicAdd(&h[0][bkt], q & 0xffffu);
+        atomicAdd(&h[1][bkt], q >> 16);
+    }
 }
 
 // One 8-CTA cluster per row of logits [rows][ld]. Greedy (temperature <= 0):
@@ -310,12 +369,19 @@ __device__ __forceinline__ void block_scan_excl(double v, int c, double *dscr, i
 // cumulative mass reaches top_p (tokens tied at that boundary are kept in
 // ascending index order); renormalise; return the first index whose
 // cumulative kept mass (index order) exceeds u * total, numpy's
-// Generator.choice rule. The sorted order is found by a 3-level radix select
-// over the float bits of the logits (11 + 11 + 10 bits) with per-bucket mass
-// histograms; masses are expf in fp32 accumulated in fp64. Each CTA keeps its
-// slice of the row in shared memory; partial results meet in the leader CTA
-// through distributed shared memory.
-static __global__ void __cluster_dims__(kSampleCluster, 1, 1) __launch_bounds__(kSampleThreads)
+// Generator.choice rule.
+//
+// The boundary token is found by a 5-level select over 256-bucket
+// histograms. Level 0 buckets every token by its distance from the max in
+// 1/8 nat, floor((max - v) / T * 8) (capped at 255), and replaces the
+// logits in shared memory by their masses and bands; the tokens of the
+// crossing band are compacted into a short list (float key, mass) and levels
+// 1-4 refine it by the float bits of the logit, 8 bits at a time. Each CTA keeps its slice of
+// the row in shared memory and builds a histogram of its slice; after a
+// cluster barrier every CTA sums the 8 histograms through distributed shared
+// memory (256 x 8 loads) and finds the crossing bucket itself (identical
+// integer arithmetic everywhere), so one barrier per level suffices.
+static __global__ void __cluster_dims__(kSampleCluster, 1, 1) __launch_bounds__(kSampleThreads, 2)
     sample_kernel(const float *__restrict__ logits, int64_t ld, int vocab, SampleParams sp, int *__restrict__ out) {
     namespace cg = cooperative_groups;
     cg::cluster_group cluster = cg::this_cluster();
@@ -327,20 +393,33 @@ static __global__ void __cluster_dims__(kSampleCluster, 1, 1) __launch_bounds__(
     const int chunk = (vocab + kSampleCluster - 1) / kSampleCluster;
     const int lo = rank * chunk;
     const int n = max(0, min(vocab, lo + chunk) - lo);
+    const int n_pad = (n + kWarpSize - 1) / kWarpSize * kWarpSize;
     const float *src = logits + static_cast<int64_t>(row) * ld + lo;
-    SampleShared *leader = cluster.map_shared_rank(&sh, 0);
 
     // pass 0: stage the slice, local (max, first index)
     float bv = kNegInf;
     int bi = 0x7fffffff;
-    for (int i = tid; i < n; i += blockDim.x) {
-        const float v = src[i];
-        sh.x[i] = v;
+    auto take = [&](int i, float v) {
+        sh.x[sample_pos(i)] = v;
         if (v > bv) {
             bv = v;
             bi = lo + i;
         }
+    };
+    int head = 0;
+    if ((reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+        const float4 *s4 = reinterpret_cast<const float4 *>(src);
+        for (int i4 = tid; i4 < n / 4; i4 += blockDim.x) {
+            const float4 f = __ldg(s4 + i4);
+            take(4 * i4, f.x);
+            take(4 * i4 + 1, f.y);
+            take(4 * i4 + 2, f.z);
+            take(4 * i4 + 3, f.w);
+        }
+        head = (n / 4) * 4;
     }
+    for (int i = head + tid; i < n; i += blockDim.x)
+        take(i, __ldg(src + i));
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) {
         const float ov = __shfl_xor_sync(kFullWarpMask, bv, off);
@@ -351,15 +430,17 @@ static __global__ void __cluster_dims__(kSampleCluster, 1, 1) __launch_bounds__(
         }
     }
     if (lane == 0) {
-        sh.dscr[warp] = bv;
+        sh.uscr[warp] = __float_as_uint(bv);
         sh.iscr[warp] = bi;
     }
+    for (int b = tid; b < kSampleBuckets; b += blockDim.x)
+        sh.h0[0][b] = sh.h0[1][b] = 0u;
     __syncthreads();
     if (tid == 0) {
         float v = kNegInf;
         int i0 = 0x7fffffff;
         for (int w = 0; w < kSampleThreads / 32; ++w) {
-            const float ov = static_cast<float>(sh.dscr[w]);
+            const float ov = __uint_as_float(static_cast<uint32_t>(sh.uscr[w]));
             if (ov > v || (ov == v && sh.iscr[w] < i0)) {
                 v = ov;
                 i0 = sh.iscr[w];
@@ -371,6 +452,7 @@ static __global__ void __cluster_dims__(kSampleCluster, 1, 1) __launch_bounds__(
     cluster.sync();
     float gmax = kNegInf;
     int garg = 0x7fffffff;
+#pragma unroll
     for (int r = 0; r < kSampleCluster; ++r) {
         const SampleShared *peer = cluster.map_shared_rank(&sh, r);
         const float v = peer->best_v;
@@ -388,190 +470,271 @@ static __global__ void __cluster_dims__(kSampleCluster, 1, 1) __launch_bounds__(
         return;
     }
     const float inv_t = 1.f / fmaxf(temp, 1e-6f);
+    const float dscale = inv_t * kSampleDistScale;
     const double top_p = sp.top_p ? static_cast<double>(sp.top_p[row]) : 1.0;
     const double u = (sp.uniform && sp.uniform[row] >= 0.0)
                          ? sp.uniform[row]
                          : counter_uniform(sp.seed ? sp.seed[row] : 0ull, sp.step ? sp.step[row] : 0);
-    auto mass = [&](float v) { return expf((v - gmax) * inv_t); };
 
     const bool filtered = top_p < 1.0;
-    uint32_t prefix = 0;
-    double above = 0.0, z = 0.0;
-    for (int level = 0; level < (filtered ? 3 : 1); ++level) {
-        const int shift = level == 0 ? 21 : (level == 1 ? 10 : 0);
-        const int nb = level == 2 ? 1024 : kRadixBuckets;
-        const uint32_t mask_hi = level == 0 ? 0u : (0xffffffffu << (level == 1 ? 21 : 10));
-        for (int b = tid; b < nb; b += blockDim.x) {
-            sh.hist[b] = 0.0;
-            sh.cnt[b] = 0;
+    // level 0: the mass and band of every token (masses replace the logits
+    // in shared memory); the band histogram when filtering. Two tokens per
+    // thread per iteration; whole warps iterate together.
+    for (int i = tid; i < n_pad; i += 2 * kSampleThreads) {
+        const int i2 = i + kSampleThreads;
+        const float v0 = i < n ? sh.x[sample_pos(i)] : kNegInf;
+        const float v1 = i2 < n ? sh.x[sample_pos(i2)] : kNegInf;
+        const float t0 = sample_dist(v0, gmax, dscale), t1 = sample_dist(v1, gmax, dscale);
+        const uint32_t q0 = i < n ? sample_qmass(v0, t0, gmax, inv_t) : 0u;
+        const uint32_t q1 = i2 < n ? sample_qmass(v1, t1, gmax, inv_t) : 0u;
+        const int b0 = sample_bucket(t0), b1 = sample_bucket(t1);
+        if (i < n) {
+            sh.q[sample_pos(i)] = q0;
+            sh.band[sample_bpos(i)] = static_cast<uint8_t>(b0);
         }
-        __syncthreads();
-        // warp-aggregated histogram: lanes hitting the same bucket are summed
-        // in registers and one lane issues the shared-memory atomics (the
-        // top-level buckets of a logit row are few and heavily shared)
-        const int n_pad = (n + kWarpSize - 1) / kWarpSize * kWarpSize;
-        for (int i = tid; i < n_pad; i += blockDim.x) {
-            int b = -1;
-            float e = 0.f;
-            if (i < n) {
-                const float v = sh.x[i];
-                const uint32_t k = float_key(v);
-                if ((k & mask_hi) == prefix) {
-                    b = static_cast<int>((k >> shift) & static_cast<uint32_t>(nb - 1));
-                    e = mass(v);
+        if (i2 < n) {
+            sh.q[sample_pos(i2)] = q1;
+            sh.band[sample_bpos(i2)] = static_cast<uint8_t>(b1);
+        }
+        if (filtered) {
+            sample_hist_add(sh.h0, i < n ? b0 : -1, q0, lane);
+            sample_hist_add(sh.h0, i2 < n ? b1 : -1, q1, lane);
+        }
+    }
+    uint32_t key_star = 0;
+    int bstar = kSampleBuckets;
+    unsigned long long above = 0, z = 0;
+    if (filtered) {
+        uint32_t prefix = 0;
+        bool listed = true; // band compacted (else levels 1-4 rescan the slice)
+        int n_cand = 0;
+        for (int level = 0; level < 5; ++level) {
+            uint32_t(*hk)[kSampleBuckets] = sh.hk[level & 1];
+            const int shift = level == 0 ? 0 : 32 - 8 * level;
+            const uint32_t mask_hi = level <= 1 ? 0u : (0xffffffffu << (shift + 8));
+            if (level > 0) {
+                for (int b = tid; b < kSampleBuckets; b += blockDim.x)
+                    hk[0][b] = hk[1][b] = 0u;
+                __syncthreads();
+                if (listed) {
+                    const int nc_pad = (n_cand + kWarpSize - 1) / kWarpSize * kWarpSize;
+                    for (int c = tid; c < nc_pad; c += kSampleThreads) {
+                        int bkt = -1;
+                        uint32_t q = 0;
+                        if (c < n_cand) {
+                            const uint32_t k = sh.cand_key[c];
+                            if ((k & mask_hi) == prefix) {
+                                bkt = static_cast<int>((k >> shift) & 0xffu);
+                                q = sh.cand_q[c];
+                            }
+                        }
+                        sample_hist_add(hk, bkt, q, lane);
+                    }
+                } else {
+                    // band too large to list (flat rows): scan the slice,
+                    // keys from global memory, 8 loads in flight per thread
+                    for (int base = tid; base < n_pad; base += 8 * kSampleThreads) {
+                        uint32_t key[8];
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) {
+                            const int i = base + j * kSampleThreads;
+                            key[j] = i < n && sh.band[sample_bpos(i)] == bstar ? float_key(__ldg(src + i)) : 0u;
+                        }
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) {
+                            const int i = base + j * kSampleThreads;
+                            int bkt = -1;
+                            uint32_t q = 0;
+                            if (i < n && sh.band[sample_bpos(i)] == bstar && (key[j] & mask_hi) == prefix) {
+                                bkt = static_cast<int>((key[j] >> shift) & 0xffu);
+                                q = sh.q[sample_pos(i)];
+                            }
+                            sample_hist_add(hk, bkt, q, lane);
+                        }
+                    }
                 }
             }
-            const unsigned peers = __match_any_sync(kFullWarpMask, b);
-            double sum = 0.0;
-#pragma unroll 4
-            for (int j = 0; j < kWarpSize; ++j) {
-                const float ej = __shfl_sync(kFullWarpMask, e, j);
-                if ((peers >> j) & 1u)
-                    sum += static_cast<double>(ej);
-            }
-            if (b >= 0 && lane == __ffs(peers) - 1) {
-                atomicAdd(&sh.hist[b], sum);
-                atomicAdd(&sh.cnt[b], __popc(peers));
-            }
-        }
-        cluster.sync();
-        if (rank == 0) {
-            // leader: sum the cluster's histograms; buckets scanned from the top
-            const int per = nb / kSampleThreads; // 4 or 2 buckets per thread
-            double my = 0.0;
-            int myc = 0;
-            double bm[4];
-            int bc[4];
-            for (int j = 0; j < per; ++j) {
-                const int b = nb - 1 - (tid * per + j);
-                double m = 0.0;
-                int c = 0;
+            cluster.sync();
+            // every CTA: the cluster's histogram (thread t < 256 sums bucket
+            // t of the 8 slices), scanned from the heaviest bucket: distance 0
+            // first, then the largest float bits first
+            unsigned long long bm = 0;
+            if (tid < kSampleBuckets) {
+                const int b = level == 0 ? tid : kSampleBuckets - 1 - tid;
+#pragma unroll
                 for (int r = 0; r < kSampleCluster; ++r) {
                     const SampleShared *peer = cluster.map_shared_rank(&sh, r);
-                    m += peer->hist[b];
-                    c += peer->cnt[b];
+                    const uint32_t(*h)[kSampleBuckets] = level == 0 ? peer->h0 : peer->hk[level & 1];
+                    bm += (static_cast<unsigned long long>(h[1][b]) << 16) + h[0][b];
                 }
-                bm[j] = m;
-                bc[j] = c;
-                my += m;
-                myc += c;
             }
-            double before, total;
-            int cbefore, ctotal;
-            block_scan_excl(my, myc, sh.dscr, sh.iscr, before, cbefore, total, ctotal);
+            unsigned long long before, total;
+            int ib, it;
+            block_scan_excl(bm, 0, sh.uscr, sh.iscr, before, ib, total, it);
             if (level == 0)
                 z = total;
+            const double target = top_p * static_cast<double>(z);
+            if (tid < kSampleBuckets) {
+                const unsigned long long acc = above + before;
+                const bool last = tid == kSampleBuckets - 1;
+                if ((static_cast<double>(acc + bm) >= target || last) && static_cast<double>(acc) < target) {
+                    sh.res_bucket = level == 0 ? tid : kSampleBuckets - 1 - tid;
+                    sh.res_above = acc;
+                }
+            }
+            __syncthreads();
+            if (level == 0)
+                bstar = sh.res_bucket;
             else
-                z = leader->z;
-            const double target = top_p * z;
-            if (!filtered) {
-                if (tid == 0) {
-                    sh.z = total;
-                    sh.prefix = 0;
-                    sh.above = 0.0;
-                    sh.above_cnt = 0;
+                prefix |= static_cast<uint32_t>(sh.res_bucket) << shift;
+            above = sh.res_above;
+            if (level == 0) {
+                // compact the crossing band's positions: count per warp,
+                // offsets by a scan of the warp counts, then place; then
+                // fetch their keys, all loads in flight
+                int cnt = 0;
+                for (int i = tid; i < n_pad; i += kSampleThreads)
+                    cnt += __popc(__ballot_sync(kFullWarpMask, i < n && sh.band[sample_bpos(i)] == bstar));
+                if (lane == 0)
+                    sh.warp_cnt[warp] = cnt;
+                __syncthreads();
+                int slot = 0;
+                n_cand = 0;
+                for (int w = 0; w < kSampleThreads / 32; ++w) {
+                    slot += w < warp ? sh.warp_cnt[w] : 0;
+                    n_cand += sh.warp_cnt[w];
                 }
-            } else {
-                // the crossing bucket: first (from the top) where above + cum >= target
-                double acc = above + before;
-                int accc = cbefore;
-                for (int j = 0; j < per; ++j) {
-                    const int b = nb - 1 - (tid * per + j);
-                    const bool last_bucket = b == 0;
-                    if ((acc + bm[j] >= target || last_bucket) && acc < target) {
-                        sh.prefix = prefix | (static_cast<uint32_t>(b) << shift);
-                        sh.above = acc;
-                        sh.above_cnt = accc;
+                for (int i = tid; i < n_pad; i += kSampleThreads) {
+                    const bool in = i < n && sh.band[sample_bpos(i)] == bstar;
+                    const unsigned m = __ballot_sync(kFullWarpMask, in);
+                    const int s = slot + __popc(m & ((1u << lane) - 1u));
+                    if (in && s < kSampleCandMax)
+                        sh.cand_pos[s] = static_cast<uint16_t>(i);
+                    slot += __popc(m);
+                }
+                __syncthreads();
+                listed = n_cand <= kSampleCandMax;
+                if (listed)
+                    for (int c = tid; c < n_cand; c += kSampleThreads) {
+                        const int i = sh.cand_pos[c];
+                        sh.cand_key[c] = float_key(__ldg(src + i));
+                        sh.cand_q[c] = sh.q[sample_pos(i)];
                     }
-                    acc += bm[j];
-                    accc += bc[j];
+            }
+            __syncthreads(); // res_* is rewritten by the next level
+        }
+        key_star = prefix;
+        // mark the boundary band's tokens kept / tied / dropped, so the
+        // final pass reads only shared memory
+        if (listed) {
+            for (int c = tid; c < n_cand; c += kSampleThreads) {
+                const uint32_t k = sh.cand_key[c];
+                sh.band[sample_bpos(sh.cand_pos[c])] = k > key_star ? kBandKept : (k == key_star ? kBandTie : kBandDrop);
+            }
+        } else {
+            for (int base = tid; base < n; base += 8 * kSampleThreads) {
+                uint32_t key[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const int i = base + j * kSampleThreads;
+                    key[j] = i < n && sh.band[sample_bpos(i)] == bstar ? float_key(__ldg(src + i)) : 0u;
                 }
-                // target beyond everything (rounding): keep the lowest bucket
-                if (tid == kSampleThreads - 1 && !(above + total >= target) && level == 0) {
-                    sh.prefix = 0;
-                    sh.above = above;
-                    sh.above_cnt = 0;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const int i = base + j * kSampleThreads;
+                    if (i < n && sh.band[sample_bpos(i)] == bstar)
+                        sh.band[sample_bpos(i)] =
+                            key[j] > key_star ? kBandKept : (key[j] == key_star ? kBandTie : kBandDrop);
                 }
-                if (tid == 0 && level == 0)
-                    sh.z = total;
             }
         }
-        cluster.sync();
-        prefix = leader->prefix;
-        above = leader->above;
-        z = leader->z;
+        __syncthreads();
     }
-    const uint32_t key_star = prefix;
-    const double e_star = filtered ? static_cast<double>(mass(key_float(key_star))) : 0.0;
+    const float v_star = key_float(key_star);
+    const unsigned long long q_star =
+        filtered ? sample_qmass(v_star, sample_dist(v_star, gmax, dscale), gmax, inv_t) : 0ull;
     int n_keep_ties = 0x7fffffff;
-    if (filtered) {
-        const double need = (top_p * z - above) / e_star;
-        n_keep_ties = need <= 1.0 ? 1 : static_cast<int>(ceil(need - 1e-12));
+    if (filtered && q_star > 0) {
+        const double need =
+            (top_p * static_cast<double>(z) - static_cast<double>(above)) / static_cast<double>(q_star);
+        n_keep_ties = need <= 1.0 ? 1 : (need >= 2e9 ? 0x7fffffff : static_cast<int>(ceil(need - 1e-12)));
     }
 
-    // final pass: kept mass in index order; each thread owns a contiguous run
+    // final pass: kept mass in index order; each thread owns a contiguous
+    // run. A token is kept when its logit's key is above key_star: bands
+    // before the boundary band are kept whole, later ones dropped, and the
+    // boundary band's tokens carry their mark. `tie` flags a boundary tie.
+    auto kept_mass = [&](int i, bool &tie) -> uint32_t {
+        const uint32_t q = sh.q[sample_pos(i)];
+        if (!filtered) {
+            tie = false;
+            return q;
+        }
+        const int b = sh.band[sample_bpos(i)];
+        tie = b == kBandTie;
+        return (b < bstar || b == kBandKept) ? q : 0u;
+    };
     const int per_t = (n + kSampleThreads - 1) / kSampleThreads;
     const int t_lo = min(n, tid * per_t), t_hi = min(n, t_lo + per_t);
-    double my = 0.0;
+    unsigned long long my = 0, my1 = 0;
     int my_ties = 0;
-    for (int i = t_lo; i < t_hi; ++i) {
-        const float v = sh.x[i];
-        if (!filtered) {
-            my += mass(v);
-        } else {
-            const uint32_t k = float_key(v);
-            if (k > key_star)
-                my += mass(v);
-            else if (k == key_star)
-                ++my_ties;
+    {
+        bool tie0, tie1;
+        int i = t_lo;
+        for (; i + 1 < t_hi; i += 2) {
+            my += kept_mass(i, tie0);
+            my1 += kept_mass(i + 1, tie1);
+            my_ties += tie0 + tie1;
         }
+        if (i < t_hi) {
+            my += kept_mass(i, tie0);
+            my_ties += tie0;
+        }
+        my += my1;
     }
-    double before, total;
+    unsigned long long before, total;
     int ties_before, ties_total;
-    block_scan_excl(my, my_ties, sh.dscr, sh.iscr, before, ties_before, total, ties_total);
+    block_scan_excl(my, my_ties, sh.uscr, sh.iscr, before, ties_before, total, ties_total);
     if (tid == 0) {
         sh.part_mass = total;
         sh.part_ties = ties_total;
     }
     cluster.sync();
     // cluster prefix over ranks (every CTA computes it from the peers)
-    double rank_before = 0.0, grand = 0.0;
+    unsigned long long rank_before = 0, grand = 0;
     int ties_rank_before = 0, ties_grand = 0;
+#pragma unroll
     for (int r = 0; r < kSampleCluster; ++r) {
         const SampleShared *peer = cluster.map_shared_rank(&sh, r);
+        const unsigned long long pm = peer->part_mass;
+        const int pt = peer->part_ties;
         if (r < rank) {
-            rank_before += peer->part_mass;
-            ties_rank_before += peer->part_ties;
+            rank_before += pm;
+            ties_rank_before += pt;
         }
-        grand += peer->part_mass;
-        ties_grand += peer->part_ties;
+        grand += pm;
+        ties_grand += pt;
     }
     const int keep_total = filtered ? min(n_keep_ties, ties_grand) : 0;
     const int tb = ties_rank_before + ties_before; // boundary ties before this thread
     const int mine = filtered ? max(0, min(my_ties, keep_total - tb)) : 0;
-    const double t_before = rank_before + before + e_star * static_cast<double>(min(tb, keep_total));
-    const double t_mine = my + e_star * static_cast<double>(mine);
-    const double all = grand + e_star * static_cast<double>(keep_total);
-    const double goal = u * all;
-    if (t_before <= goal && goal < t_before + t_mine) {
-        double run = t_before;
+    const unsigned long long t_before =
+        rank_before + before + q_star * static_cast<unsigned long long>(min(tb, keep_total));
+    const unsigned long long t_mine = my + q_star * static_cast<unsigned long long>(mine);
+    const unsigned long long all = grand + q_star * static_cast<unsigned long long>(keep_total);
+    const double goal = u * static_cast<double>(all);
+    if (static_cast<double>(t_before) <= goal && goal < static_cast<double>(t_before + t_mine)) {
+        unsigned long long run = t_before;
         int ties_seen = tb;
         int pick = lo + t_hi - 1;
         for (int i = t_lo; i < t_hi; ++i) {
-            const float v = sh.x[i];
-            double e = 0.0;
-            if (!filtered) {
-                e = mass(v);
-            } else {
-                const uint32_t k = float_key(v);
-                if (k > key_star)
-                    e = mass(v);
-                else if (k == key_star && ties_seen++ < keep_total)
-                    e = e_star;
-            }
-            if (e > 0.0) {
+            bool tie;
+            unsigned long long e = kept_mass(i, tie);
+            if (tie && ties_seen++ < keep_total)
+                e = q_star;
+            if (e > 0) {
                 run += e;
-                if (run > goal) {
+                if (static_cast<double>(run) > goal) {
                     pick = lo + i;
                     break;
                 }
@@ -580,17 +743,14 @@ static __global__ void __cluster_dims__(kSampleCluster, 1, 1) __launch_bounds__(
         out[row] = pick;
     }
     // u -> 1 rounding: the goal lands past the last kept token
-    if (rank == kSampleCluster - 1 && tid == 0 && !(goal < all)) {
+    if (rank == kSampleCluster - 1 && tid == 0 && !(goal < static_cast<double>(all))) {
+        const float *rowp = logits + static_cast<int64_t>(row) * ld;
         int last = vocab - 1;
-        for (int r = kSampleCluster - 1; r >= 0 && last == vocab - 1; --r) {
-            const SampleShared *peer = cluster.map_shared_rank(&sh, r);
-            const int plo = r * chunk, pn = max(0, min(vocab, plo + chunk) - plo);
-            for (int i = pn - 1; i >= 0; --i)
-                if (!filtered || float_key(peer->x[i]) >= key_star) {
-                    last = plo + i;
-                    break;
-                }
-        }
+        for (int i = vocab - 1; i >= 0; --i)
+            if (!filtered || float_key(rowp[i]) >= key_star) {
+                last = i;
+                break;
+            }
         out[row] = last;
     }
     cluster.sync(); // keep shared memory alive until every peer is done with it
