@@ -135,6 +135,12 @@ def algorithmic_bytes(label, cfg, batch, ctx_mean):
         "gemm_o": L * (H * qw * 2 + act(qw) * 2 + act(H) * 4),
         "gemm_gate_up": L * (2 * I * H * 2 + act(H) * 2 + act(2 * I) * 4),
         "gemm_down": L * (H * I * 2 + act(I) * 2 + act(H) * 4),
+        # fused fast path: bf16 weights, two-term bf16 activations in (4 bytes
+        # per element), fused epilogue traffic out
+        "gemm_qkv_rope_kv_write": L * ((qw + 2 * kvw) * H * 2 + act(H) * 4 + act(qw + 2 * kvw) * 4),
+        "gemm_o_residual": L * (H * qw * 2 + act(qw) * 4 + act(H) * 8),
+        "gemm_gate_up_silu": L * (2 * I * H * 2 + act(H) * 4 + act(I) * 4),
+        "gemm_down_residual": L * (H * I * 2 + act(I) * 4 + act(H) * 8),
         "attention": L * (batch * ctx_mean * kvw * 4 * 2 + act(qw) * 4 + act(qw) * 2),
         "lm_head": V * H * 2 + act(H) * 2 + act(V) * 4,
     }
@@ -143,7 +149,8 @@ def algorithmic_bytes(label, cfg, batch, ctx_mean):
 
 def step_bytes(cfg, batch, ctx_mean):
     tot = 0
-    for lab in ("gemm_qkv", "gemm_o", "gemm_gate_up", "gemm_down", "attention", "lm_head"):
+    for lab in ("gemm_qkv_rope_kv_write", "gemm_o_residual", "gemm_gate_up_silu", "gemm_down_residual", "attention",
+                "lm_head"):
         tot += algorithmic_bytes(lab, cfg, batch, ctx_mean)
     return tot
 
@@ -260,8 +267,11 @@ def run_ours(args):
         b = algorithmic_bytes(label, cfg, BATCH, ctx_now)
         rows.append({"kernel": label, "ms_per_step": round(ms, 4), "launches_per_step": launches,
                      "gbs": round(b / (ms / 1e3) / 1e9, 1) if b and ms > 0 else None})
-    # launch groups: attention = split-KV partial + combine kernels
-    gpu_launches_per_step = sum(k[2] * (2 if k[0] == "attention" else 1) for k in kernels)
+    # launch groups: attention = split-KV partial (+ combine kernel when the
+    # KV range is split: fewer (sequence, kv head) pairs than 2 CTAs per SM)
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    attn_kernels = 1 if (2 * sms) // (BATCH * cfg["kv_heads"]) <= 1 else 2
+    gpu_launches_per_step = sum(k[2] * (attn_kernels if k[0] == "attention" else 1) for k in kernels)
     dom = max((r for r in rows if r["gbs"] is not None), key=lambda r: r["ms_per_step"])
     dom_bytes = algorithmic_bytes(dom["kernel"], cfg, BATCH, ctx_now) / dom["launches_per_step"]
     dom_ms = dom["ms_per_step"] / dom["launches_per_step"]

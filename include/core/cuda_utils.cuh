@@ -117,6 +117,92 @@ inline void launch_async(cudaStream_t stream, void (*kernel)(Params...), dim3 gr
 
 inline void synchronize(cudaStream_t stream = nullptr) { OPWORKS_CUDA_CHECK(cudaStreamSynchronize(stream)); }
 
+// ------------------------------------------------ programmatic dependent launch
+//
+// Launches made on a host thread while a PdlScope is active carry the
+// programmatic-stream-serialization attribute: the next kernel in the stream
+// may be scheduled as soon as every CTA of the current one has called
+// pdl_trigger(), so its prologue (barrier setup, TMEM allocation, weight
+// prefetch) overlaps the current kernel's tail. Every kernel launched that
+// way calls pdl_wait() before it touches memory that an earlier kernel of the
+// stream writes or reads; pdl_wait() returns once those kernels completed and
+// their writes are visible. Both are no-ops for an ordinary launch.
+namespace detail {
+inline bool &pdl_flag() {
+    static thread_local bool on = false;
+    return on;
+}
+} // namespace detail
+
+class PdlScope {
+  public:
+    explicit PdlScope(bool on) : prev_(detail::pdl_flag()) { detail::pdl_flag() = on; }
+    ~PdlScope() { detail::pdl_flag() = prev_; }
+    PdlScope(const PdlScope &) = delete;
+    PdlScope &operator=(const PdlScope &) = delete;
+
+  private:
+    bool prev_;
+};
+
+__device__ __forceinline__ void pdl_wait() {
+#if defined(__CUDA_ARCH__) && __CUDA_ARCH__ >= 900
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+#endif
+}
+__device__ __forceinline__ void pdl_trigger() {
+#if defined(__CUDA_ARCH__) && __CUDA_ARCH__ >= 900
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+#endif
+}
+
+// cudaLaunchKernelEx with the calling thread's PDL policy.
+template <typename... Params, typename... Args>
+inline void launch_ex(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                      Args &&...args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    if (detail::pdl_flag()) {
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+    }
+    OPWORKS_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kernel, static_cast<Args &&>(args)...));
+}
+
+// Same with a runtime thread-block cluster shape (1 x 1 x 1 = no cluster).
+template <typename... Params, typename... Args>
+inline void launch_ex_cluster(void (*kernel)(Params...), dim3 grid, dim3 cluster, dim3 block, size_t smem,
+                              cudaStream_t stream, Args &&...args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    int n = 0;
+    if (cluster.x * cluster.y * cluster.z > 1) {
+        attr[n].id = cudaLaunchAttributeClusterDimension;
+        attr[n].val.clusterDim.x = cluster.x;
+        attr[n].val.clusterDim.y = cluster.y;
+        attr[n].val.clusterDim.z = cluster.z;
+        ++n;
+    }
+    if (detail::pdl_flag()) {
+        attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[n].val.programmaticStreamSerializationAllowed = 1;
+        ++n;
+    }
+    cfg.attrs = n ? attr : nullptr;
+    cfg.numAttrs = static_cast<unsigned>(n);
+    OPWORKS_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kernel, static_cast<Args &&>(args)...));
+}
+
 template <typename... Params, typename... Args>
 inline void launch(void (*kernel)(Params...), dim3 grid, dim3 block, Args... args) {
     launch_async(nullptr, kernel, grid, block, args...);

@@ -30,6 +30,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <functional>
 #include <map>
@@ -486,13 +487,24 @@ template <typename WT> class LlamaEngineT {
 
     int plan_bn(int rows) const { return sm100::gemm_pick_bn(sm100::GemmKind::kBF16x2, rows); }
 
-    int plan_splits(const Projection &p, int rows) const {
+    int plan_splits(const Projection &p, int rows, int max_splits = 64) const {
         if (!fast() && rows <= 4)
             return 1;
         const int bn = fast() ? plan_bn(rows) : sm100::gemm_pick_bn(sm100::GemmKind::kTF32x3, rows);
         const int tiles = ((p.out + kUmmaM - 1) / kUmmaM) * ((rows + bn - 1) / bn);
         const int kb = fast() ? (p.in + 63) / 64 : (p.in + 31) / 32;
-        return sm100::gemm_pick_splits(tiles, kb, sm_count_, fast() ? 4 : 8);
+        return sm100::gemm_pick_splits(tiles, kb, sm_count_ * sm100::gemm_ctas_per_sm(bn), fast() ? 2 : 8,
+                                       max_splits);
+    }
+
+    // fast path: x . W^T with the split-K reduction and `epi` fused into the
+    // GEMM (K splits of a tile form one cluster)
+    template <typename Epi> void linear_tile(const Projection &p, const Act &x, int rows, const Epi &epi) {
+        const int splits = plan_splits(p, rows, sm100::kMaxClusterSplits);
+        sm100::gemm_tn<sm100::GemmKind::kBF16x2, Epi>({p.bf16.data(), nullptr, p.out, p.in},
+                                                      {x.bf16, x.bf16_lo, rows, p.in}, p.in, part_.data(), p.out,
+                                                      splits, static_cast<int64_t>(rows) * p.out, stream_, epi,
+                                                      plan_bn(rows));
     }
 
     // part[s][rows][p.out] = x[rows][p.in] . W^T (partial over split s)
@@ -531,9 +543,9 @@ template <typename WT> class LlamaEngineT {
 
     template <int kPer>
     void launch_add_rmsnorm(int rows, int splits, const float *w, const detail::ActOut &o) {
-        detail::add_rmsnorm_kernel<kPer><<<rows, detail::kRowThreads, 0, stream_>>>(
-            hidden_.data(), part_.data(), splits, static_cast<int64_t>(rows) * cfg_.hidden_size, w, cfg_.rms_norm_eps,
-            o, cfg_.hidden_size);
+        launch_ex(detail::add_rmsnorm_kernel<kPer>, dim3(rows), dim3(detail::kRowThreads), 0, stream_, hidden_.data(),
+                  static_cast<const float *>(part_.data()), splits, static_cast<int64_t>(rows) * cfg_.hidden_size, w,
+                  cfg_.rms_norm_eps, o, cfg_.hidden_size);
     }
     void add_rmsnorm(int rows, int splits, const float *w, const detail::ActOut &o) {
         switch (cfg_.hidden_size / detail::kRowThreads) {
@@ -580,6 +592,7 @@ template <typename WT> class LlamaEngineT {
     }
 
     void forward(int rows, bool decode, int slot, int pos0, const std::function<void(int)> &hook) {
+        const PdlScope pdl(pdl_);
         const int H = cfg_.hidden_size, I = cfg_.intermediate_size, QW = cfg_.q_width();
         const int qh = cfg_.num_q_heads, kvh = cfg_.num_kv_heads;
         const detail::ActOut normed_o =
@@ -604,13 +617,20 @@ template <typename WT> class LlamaEngineT {
         for (int l = 0; l < cfg_.num_layers; ++l) {
             const LayerWeights<WT> &L = w_.layers[l];
             const detail::PagedKV kv{kv_.k(l), kv_.v(l), table_dev_.data(), blocks_per_seq_, kvh};
-            int s = linear(L.qkv, normed, rows);
-            mark("gemm_qkv");
-            detail::qkv_finalize_kernel<<<rows, 256, 0, stream_>>>(
-                part_.data(), s, static_cast<int64_t>(rows) * L.qkv.out, qh, kvh,
-                reinterpret_cast<const float2 *>(w_.rope_table.data()), tm, kv, kv_.k(l), kv_.v(l), q_.data());
-            OPWORKS_CUDA_CHECK(cudaGetLastError());
-            mark("qkv_rope_kv_write");
+            const float2 *rope = reinterpret_cast<const float2 *>(w_.rope_table.data());
+            int s = 0;
+            if (fast()) {
+                linear_tile(L.qkv, normed, rows,
+                            detail::QkvTileEpi{q_.data(), qh, kvh, rope, tm, kv, kv_.k(l), kv_.v(l)});
+                mark("gemm_qkv_rope_kv_write");
+            } else {
+                s = linear(L.qkv, normed, rows);
+                mark("gemm_qkv");
+                launch_ex(detail::qkv_finalize_kernel, dim3(rows), dim3(256), 0, stream_,
+                          static_cast<const float *>(part_.data()), s, static_cast<int64_t>(rows) * L.qkv.out, qh,
+                          kvh, rope, tm, kv, kv_.k(l), kv_.v(l), q_.data());
+                mark("qkv_rope_kv_write");
+            }
             switch (cfg_.kv_rep()) {
             case 1: attention<1>(rows, decode, slot, pos0, kv, attn_o); break;
             case 2: attention<2>(rows, decode, slot, pos0, kv, attn_o); break;
@@ -618,17 +638,30 @@ template <typename WT> class LlamaEngineT {
             default: attention<8>(rows, decode, slot, pos0, kv, attn_o); break;
             }
             mark("attention");
-            s = linear(L.o, attn, rows);
-            mark("gemm_o");
-            add_rmsnorm(rows, s, L.post_norm.data(), normed_o);
-            mark("residual_rmsnorm");
-            s = linear(L.gu, normed, rows);
-            mark("gemm_gate_up");
-            launch_async(stream_, detail::silu_mul_kernel, detail::grid_for(static_cast<int64_t>(rows) * I), kThreads,
-                         part_.data(), s, static_cast<int64_t>(rows) * L.gu.out, rows, I, act_o);
-            mark("silu_mul");
-            s = linear(L.down, act, rows);
-            mark("gemm_down");
+            if (fast()) {
+                linear_tile(L.o, attn, rows, detail::ResidualTileEpi{hidden_.data(), H});
+                mark("gemm_o_residual");
+                add_rmsnorm(rows, 0, L.post_norm.data(), normed_o);
+                mark("rmsnorm");
+                linear_tile(L.gu, normed, rows, detail::SiluMulTileEpi{act_o});
+                mark("gemm_gate_up_silu");
+                linear_tile(L.down, act, rows, detail::ResidualTileEpi{hidden_.data(), H});
+                mark("gemm_down_residual");
+                s = 0; // residual already added: the norm below reads hidden only
+            } else {
+                s = linear(L.o, attn, rows);
+                mark("gemm_o");
+                add_rmsnorm(rows, s, L.post_norm.data(), normed_o);
+                mark("residual_rmsnorm");
+                s = linear(L.gu, normed, rows);
+                mark("gemm_gate_up");
+                launch_ex(detail::silu_mul_kernel, dim3(detail::grid_for(static_cast<int64_t>(rows) * I)),
+                          dim3(kThreads), 0, stream_, static_cast<const float *>(part_.data()), s,
+                          static_cast<int64_t>(rows) * L.gu.out, rows, I, act_o);
+                mark("silu_mul");
+                s = linear(L.down, act, rows);
+                mark("gemm_down");
+            }
             if (l + 1 < cfg_.num_layers) {
                 add_rmsnorm(rows, s, w_.layers[l + 1].input_norm.data(), normed_o);
             } else {
@@ -638,7 +671,7 @@ template <typename WT> class LlamaEngineT {
                 final_o.lo = nullptr;
                 add_rmsnorm(rows, s, w_.final_norm.data(), final_o);
             }
-            mark("residual_rmsnorm");
+            mark(fast() ? "rmsnorm" : "residual_rmsnorm");
             if (hook) {
                 OPWORKS_CUDA_CHECK(cudaStreamSynchronize(stream_));
                 hook(l);
@@ -664,6 +697,7 @@ template <typename WT> class LlamaEngineT {
     }
 
     void sample(int rows) {
+        const PdlScope pdl(pdl_);
         detail::SampleParams sp;
         sp.temperature = dev_at<float>(layout_.temp);
         sp.top_p = dev_at<float>(layout_.top_p);
@@ -697,6 +731,12 @@ template <typename WT> class LlamaEngineT {
     int32_t *out_host_ = nullptr;
     std::map<int, cudaGraphExec_t> graphs_;
     bool marks_enabled_ = false;
+    // programmatic dependent launch between the kernels of a step
+    // (OPWORKS_PDL=0 turns it off)
+    bool pdl_ = [] {
+        const char *e = std::getenv("OPWORKS_PDL");
+        return !(e && e[0] == '0');
+    }();
     std::vector<std::pair<std::string, cudaEvent_t>> marks_;
 };
 

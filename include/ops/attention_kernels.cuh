@@ -232,6 +232,8 @@ __global__ void __launch_bounds__(kDecodeThreads, kDecodeCtasPerSm)
     const int b = blockIdx.z, h = blockIdx.y, split = blockIdx.x, splits = gridDim.x;
     const int qh_total = gridDim.y * kRep;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    pdl_trigger();
+    pdl_wait();
     const int len = lens[b];
     const int t_begin = split * tokens_per_split;
     const int t_end = min(len, t_begin + tokens_per_split);
@@ -458,6 +460,8 @@ __global__ void __launch_bounds__(64)
     attn_decode_combine_kernel(const float *__restrict__ part_o, const float *__restrict__ part_ml, int splits,
                                Out out) {
     const int hq = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
+    pdl_trigger();
+    pdl_wait();
     const int64_t base = (static_cast<int64_t>(b) * gridDim.x + hq) * splits;
     float M = kNegInf;
     for (int s = 0; s < splits; ++s)
@@ -504,6 +508,8 @@ __global__ void __launch_bounds__(256)
     float *kt = qt + kAttnD * kPad;                    // [64 d][kPad]
     float *pm = kt + kAttnD * kPad;                    // [64 rows][kPad]
     uint64_t *full = reinterpret_cast<uint64_t *>(pm + kAttnD * kPad);
+    pdl_trigger();
+    pdl_wait();
 
     const int h = blockIdx.y;
     const int tid = threadIdx.x;
@@ -721,13 +727,11 @@ inline void attn_decode_launch(const float *q, int64_t q_stride, const KV &kv, c
                                const Out &out, cudaStream_t stream) {
     prepare_decode_kernel<KV, kRep, Out>();
     const dim3 grid(splits, kvh, batch);
-    attn_decode_partial_kernel<KV, kRep, Out><<<grid, kDecodeThreads, DecodeGeo<kRep>::kBytes, stream>>>(
-        q, q_stride, kv, lens, tokens_per_split, scale, part_o, part_ml, out, sm100::device_error_word());
-    OPWORKS_CUDA_CHECK(cudaGetLastError());
-    if (splits > 1) {
-        attn_decode_combine_kernel<Out><<<dim3(kvh * kRep, batch), 64, 0, stream>>>(part_o, part_ml, splits, out);
-        OPWORKS_CUDA_CHECK(cudaGetLastError());
-    }
+    launch_ex(attn_decode_partial_kernel<KV, kRep, Out>, grid, dim3(kDecodeThreads), DecodeGeo<kRep>::kBytes, stream, q,
+              q_stride, kv, lens, tokens_per_split, scale, part_o, part_ml, out, sm100::device_error_word());
+    if (splits > 1)
+        launch_ex(attn_decode_combine_kernel<Out>, dim3(kvh * kRep, batch), dim3(64), 0, stream,
+                  static_cast<const float *>(part_o), static_cast<const float *>(part_ml), splits, out);
 }
 
 template <class KV, int kRep, typename Out>
@@ -736,9 +740,8 @@ inline void attn_prefill_launch(const float *q, int64_t q_tok, int64_t q_head, c
     prepare_prefill_kernel<KV, kRep, Out>();
     constexpr int kPos = kAttnTile / kRep;
     const dim3 grid((T + kPos - 1) / kPos, kvh);
-    attn_prefill_kernel<KV, kRep, Out><<<grid, 256, PrefillSmem::kBytes, stream>>>(
-        q, q_tok, q_head, out, kv, b, T, q_offset, scale, sm100::device_error_word());
-    OPWORKS_CUDA_CHECK(cudaGetLastError());
+    launch_ex(attn_prefill_kernel<KV, kRep, Out>, grid, dim3(256), PrefillSmem::kBytes, stream, q, q_tok, q_head, out,
+              kv, b, T, q_offset, scale, sm100::device_error_word());
 }
 
 } // namespace opworks::detail

@@ -29,6 +29,7 @@
 //           ~fp32 accuracy on the tensor cores.
 
 #include <type_traits>
+#include <cooperative_groups.h>
 #include <cuda_bf16.h>
 
 #include "detail/sm100.cuh"
@@ -52,9 +53,21 @@ struct Identity {
     __device__ __forceinline__ float operator()(float x) const { return x; }
 };
 
-// Epilogues are unary `float(float)` functors (the ops::mat_mul contract) or
-// position-aware `float(float, int tok, int feat)` functors (bias, fused
-// model epilogues).
+// Epilogues are unary `float(float)` functors (the ops::mat_mul contract),
+// position-aware `float(float, int tok, int feat)` functors (bias), or tile
+// epilogues (a `kTile` member), which see finished fp32 tiles in shared
+// memory: the K splits of a tile then run as one thread-block cluster, each
+// CTA keeps its partial tile in shared memory, and after a cluster barrier
+// CTA r sums rows [r*ceil(BN/S), ...) of all S partials through distributed
+// shared memory in rank order (a fixed order: deterministic) and hands them
+// to the epilogue,
+//   epi(tile [ntok][128], tok0, ntok, f0, nfeat, tid in [0, 128)),
+// so split-K needs no global workspace and no separate reduction kernel.
+template <typename Epi, typename = void> struct is_tile_epilogue : std::false_type {};
+template <typename Epi> struct is_tile_epilogue<Epi, std::void_t<decltype(Epi::kTile)>> : std::true_type {};
+constexpr int kMaxClusterSplits = 8; // portable cluster size
+
+__device__ __forceinline__ void epilogue_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 template <typename Epi>
 __device__ __forceinline__ float apply_epilogue(const Epi &epi, float v, int tok, int feat) {
     if constexpr (std::is_invocable_v<const Epi &, float, int, int>)
@@ -70,7 +83,10 @@ template <GemmKind kKind, int BN> struct GemmShape {
     static constexpr uint32_t kBBytes = BN * kUmmaKBytes;
     static constexpr uint32_t kStageBytes =
         kSplit3 ? 2u * (kABytes + kBBytes) : (kSplitB ? kABytes + 2u * kBBytes : kABytes + kBBytes);
-    static constexpr int kBudget = 192 * 1024;
+    // narrow token tiles (decode) run two CTAs per SM so that a split-K grid
+    // of up to 2 x SMs CTAs is resident in one wave
+    static constexpr int kCtasPerSm = BN <= 64 ? 2 : 1;
+    static constexpr int kBudget = kCtasPerSm == 2 ? 98 * 1024 : 192 * 1024;
     static constexpr int kStagesRaw = kBudget / static_cast<int>(kStageBytes);
     static constexpr int kStages = kStagesRaw > 8 ? 8 : kStagesRaw;
     static constexpr int kKElems = kSplit3 ? 32 : 64; // elements per 128-byte K block
@@ -85,12 +101,15 @@ template <GemmKind kKind, int BN> struct GemmShape {
 };
 
 template <GemmKind kKind, int BN, typename Epi>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(192, GemmShape<kKind, BN>::kCtasPerSm)
     umma_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmA_lo, const __grid_constant__ CUtensorMap tmB_lo,
                      GemmParams p, Epi epi) {
     using S = GemmShape<kKind, BN>;
     constexpr int kStages = S::kStages;
+    constexpr bool kTileEpi = is_tile_epilogue<Epi>::value;
+    static_assert(!kTileEpi || 2u * BN * kUmmaM * 4u <= kStages * S::kStageBytes,
+                  "tile epilogue: partial and reduced tiles must fit in the pipeline stages");
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + kStages * S::kStageBytes);
@@ -132,6 +151,7 @@ __global__ void __launch_bounds__(192, 1)
         tmem_alloc(tmem_slot, S::kTmemCols);
         tmem_relinquish();
     }
+    pdl_trigger();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -140,25 +160,44 @@ __global__ void __launch_bounds__(192, 1)
 
     if (warp == 0) {
         if (lane == 0) {
-            int it = 0;
-            for (int kb = kb_begin; kb < kb_end; ++kb, ++it) {
+            // A (weights) of the first stages does not depend on earlier
+            // kernels: it streams in while the previous kernel drains; B
+            // (activations) follows the programmatic-launch wait
+            auto load_a = [&](int kb, int s) {
+                uint8_t *st = smem + s * S::kStageBytes;
+                const int kc = kb * S::kKElems;
+                tma_load_2d(st, &tmA, &full[s], kc, f0);
+                if constexpr (S::kSplit3)
+                    tma_load_2d(st + S::kABytes + S::kBBytes, &tmA_lo, &full[s], kc, f0);
+            };
+            auto load_b = [&](int kb, int s) {
+                uint8_t *st = smem + s * S::kStageBytes;
+                const int kc = kb * S::kKElems;
+                tma_load_2d(st + S::kABytes, &tmB, &full[s], kc, t0);
+                if constexpr (S::kSplit3)
+                    tma_load_2d(st + 2 * S::kABytes + S::kBBytes, &tmB_lo, &full[s], kc, t0);
+                if constexpr (S::kSplitB)
+                    tma_load_2d(st + S::kABytes + S::kBBytes, &tmB_lo, &full[s], kc, t0);
+            };
+            const int pre = min(kStages, kb_end - kb_begin);
+            for (int j = 0; j < pre; ++j) {
+                mbar_arrive_expect_tx(&full[j], S::kStageBytes);
+                load_a(kb_begin + j, j);
+            }
+            pdl_wait();
+            for (int j = 0; j < pre; ++j)
+                load_b(kb_begin + j, j);
+            int it = pre;
+            for (int kb = kb_begin + pre; kb < kb_end; ++kb, ++it) {
                 const int s = it % kStages;
                 const uint32_t ph = static_cast<uint32_t>(it / kStages) & 1u;
                 if (!mbar_wait(&empty[s], ph ^ 1u)) {
                     ok = false;
                     break;
                 }
-                uint8_t *st = smem + s * S::kStageBytes;
                 mbar_arrive_expect_tx(&full[s], S::kStageBytes);
-                const int kc = kb * S::kKElems;
-                tma_load_2d(st, &tmA, &full[s], kc, f0);
-                tma_load_2d(st + S::kABytes, &tmB, &full[s], kc, t0);
-                if constexpr (S::kSplit3) {
-                    tma_load_2d(st + S::kABytes + S::kBBytes, &tmA_lo, &full[s], kc, f0);
-                    tma_load_2d(st + 2 * S::kABytes + S::kBBytes, &tmB_lo, &full[s], kc, t0);
-                }
-                if constexpr (S::kSplitB)
-                    tma_load_2d(st + S::kABytes + S::kBBytes, &tmB_lo, &full[s], kc, t0);
+                load_a(kb, s);
+                load_b(kb, s);
             }
             // never leave the CTA with copies in flight: the last issued
             // phase of every slot must have landed (returns at once when the
@@ -222,11 +261,16 @@ __global__ void __launch_bounds__(192, 1)
                 umma_commit(accum);
         }
     } else {
+        pdl_wait(); // the output may still be read by an earlier kernel
         const int q = warp & 3; // TMEM lane quarter this warp may access
         const int feat = f0 + q * 32 + lane;
         float *out = p.out + static_cast<int64_t>(split) * p.split_stride;
         const bool feat_ok = feat < p.n_feat;
         const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
+        // tile epilogues: the partial tile goes to shared memory [BN][128]
+        // (the pipeline stages are idle once the accumulator is final)
+        float *ptile = reinterpret_cast<float *>(smem);
+        const int col = q * 32 + lane;
         if constexpr (S::kSplit3) {
             // promote each group's TMEM partial into fp32 registers: the
             // tensor core's accumulator only ever holds kPromoteKb blocks
@@ -256,7 +300,9 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
             for (int i = 0; i < BN; ++i) {
                 const int tok = t0 + i;
-                if (feat_ok && tok < p.m_tok)
+                if constexpr (kTileEpi)
+                    ptile[i * kUmmaM + col] = acc[i];
+                else if (feat_ok && tok < p.m_tok)
                     out[static_cast<int64_t>(tok) * p.ldo + feat] = apply_epilogue(epi, acc[i], tok, feat);
             }
         } else {
@@ -272,12 +318,55 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
                 const int tok = t0 + c + i;
-                if (feat_ok && tok < p.m_tok)
+                if constexpr (kTileEpi)
+                    ptile[(c + i) * kUmmaM + col] = __uint_as_float(r[i]);
+                else if (feat_ok && tok < p.m_tok)
                     out[static_cast<int64_t>(tok) * p.ldo + feat] =
                         apply_epilogue(epi, __uint_as_float(r[i]), tok, feat);
             }
         }
         }
+    }
+    if constexpr (kTileEpi) {
+        // every thread of every CTA of the cluster takes both barriers, on
+        // the error path too
+        namespace cg = cooperative_groups;
+        const int nsplit = p.splits;
+        float *ptile = reinterpret_cast<float *>(smem);
+        float *rtile = ptile + BN * kUmmaM;
+        const int per = (BN + nsplit - 1) / nsplit;
+        const int tl0 = min(BN, split * per), tl1 = min(BN, tl0 + per);
+        if (nsplit > 1)
+            cg::this_cluster().sync();
+        else
+            __syncthreads();
+        if (warp >= 2) {
+            const int et = threadIdx.x - 64;
+            const float *src = ptile;
+            if (nsplit > 1) {
+                cg::cluster_group cluster = cg::this_cluster();
+                for (int idx = et; idx < (tl1 - tl0) * (kUmmaM / 4); idx += 128) {
+                    const int t = tl0 + idx / (kUmmaM / 4), c4 = idx % (kUmmaM / 4);
+                    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+                    for (int r = 0; r < nsplit; ++r) {
+                        const float4 v =
+                            reinterpret_cast<const float4 *>(cluster.map_shared_rank(ptile, r))[t * (kUmmaM / 4) + c4];
+                        acc.x += v.x;
+                        acc.y += v.y;
+                        acc.z += v.z;
+                        acc.w += v.w;
+                    }
+                    reinterpret_cast<float4 *>(rtile)[(t - tl0) * (kUmmaM / 4) + c4] = acc;
+                }
+                src = rtile;
+                epilogue_bar();
+            }
+            const int tb = nsplit > 1 ? tl0 : 0;
+            const int ntok = max(0, min(nsplit > 1 ? tl1 - tl0 : BN, p.m_tok - (t0 + tb)));
+            epi(src, t0 + tb, ntok, f0, min(kUmmaM, p.n_feat - f0), et);
+        }
+        if (nsplit > 1)
+            cg::this_cluster().sync(); // peers are done reading this CTA's tile
     }
     if (!ok)
         atomicExch(p.err, 1);
@@ -309,8 +398,13 @@ inline void gemm_launch(const CUtensorMap &a, const CUtensorMap &b, const CUtens
     gemm_prepare_kernel<kKind, BN, Epi>();
     const dim3 grid((p.n_feat + kUmmaM - 1) / kUmmaM, (p.m_tok + BN - 1) / BN, p.splits);
     detail::require(grid.y <= 65535 && grid.z <= 65535, "GEMM grid exceeds the CUDA limits");
-    umma_gemm_kernel<kKind, BN, Epi><<<grid, 192, S::kSmemBytes, stream>>>(a, b, a_lo, b_lo, p, epi);
-    OPWORKS_CUDA_CHECK(cudaGetLastError());
+    if constexpr (is_tile_epilogue<Epi>::value) {
+        detail::require(p.splits >= 1 && p.splits <= kMaxClusterSplits, "tile epilogue: at most 8 K splits");
+        launch_ex_cluster(umma_gemm_kernel<kKind, BN, Epi>, grid, dim3(1, 1, p.splits), dim3(192), S::kSmemBytes,
+                          stream, a, b, a_lo, b_lo, p, epi);
+    } else {
+        launch_ex(umma_gemm_kernel<kKind, BN, Epi>, grid, dim3(192), S::kSmemBytes, stream, a, b, a_lo, b_lo, p, epi);
+    }
 }
 
 // Operand description for the host launcher.
@@ -331,23 +425,22 @@ inline int gemm_pick_bn(GemmKind kind, int m_tok) {
     return 256;
 }
 
-// Number of K splits that brings the CTA count near a multiple of the SM
-// count without making a split shorter than `min_kb` blocks.
-inline int gemm_pick_splits(int tiles, int num_kb, int sm_count, int min_kb = 4) {
-    if (tiles >= sm_count)
+// CTAs of one tile shape resident per SM.
+inline int gemm_ctas_per_sm(int bn) { return bn <= 64 ? 2 : 1; }
+
+// Number of K splits: the most that keep tiles x splits CTAs resident in one
+// wave (`slots` = SMs x CTAs per SM) without making a split shorter than
+// `min_kb` blocks. A grid of at least one wave of tiles is not split.
+inline int gemm_pick_splits(int tiles, int num_kb, int slots, int min_kb = 2, int max_splits = 64) {
+    if (tiles >= slots / 2)
         return 1;
-    int best = 1;
-    double best_eff = 0.0;
-    for (int s = 1; s <= 32 && s * min_kb <= num_kb; ++s) {
-        const int ctas = tiles * s;
-        const int waves = (ctas + sm_count - 1) / sm_count;
-        const double eff = static_cast<double>(ctas) / (static_cast<double>(waves) * sm_count);
-        if (eff > best_eff + 0.02) {
-            best_eff = eff;
-            best = s;
-        }
-    }
-    return best;
+    int s = slots / tiles;
+    if (s > max_splits)
+        s = max_splits;
+    const int cap = num_kb / (min_kb > 0 ? min_kb : 1);
+    if (s > cap)
+        s = cap;
+    return s > 1 ? s : 1;
 }
 
 // out[split][tok][feat] = epi(sum_k A[feat][k] B[tok][k]); `k` is the logical
@@ -391,7 +484,8 @@ inline void gemm_tn(const GemmOperand &A, const GemmOperand &B, int k, float *ou
     case 64: gemm_launch<kKind, 64, Epi>(ta, tb, ta_lo, tb_lo, p, epi, stream); break;
     case 128: gemm_launch<kKind, 128, Epi>(ta, tb, ta_lo, tb_lo, p, epi, stream); break;
     default:
-        if constexpr (kKind == GemmKind::kTF32x3)
+        // BN = 256 only for plain bf16 and elementwise epilogues
+        if constexpr (kKind == GemmKind::kTF32x3 || is_tile_epilogue<Epi>::value)
             gemm_launch<kKind, 128, Epi>(ta, tb, ta_lo, tb_lo, p, epi, stream);
         else
             gemm_launch<kKind, 256, Epi>(ta, tb, ta_lo, tb_lo, p, epi, stream);

@@ -52,6 +52,8 @@ template <typename WT, int R>
 __global__ void __launch_bounds__(kThreads)
     gemv_rows_kernel(const float *__restrict__ x, int64_t ldx, const WT *__restrict__ W, float *__restrict__ y,
                      int64_t ldy, int in, int out) {
+    pdl_trigger();
+    pdl_wait();
     extern __shared__ float4 xs4[];
     float *xs = reinterpret_cast<float *>(xs4);
     for (int r = 0; r < R; ++r)
@@ -110,8 +112,7 @@ inline void gemv_rows_launch_r(const float *x, int64_t ldx, const WT *W, float *
         attr_dev = dev;
         attr_bytes = smem;
     }
-    gemv_rows_kernel<WT, R><<<grid, kThreads, smem, stream>>>(x, ldx, W, y, ldy, in, out);
-    OPWORKS_CUDA_CHECK(cudaGetLastError());
+    launch_ex(gemv_rows_kernel<WT, R>, dim3(grid), dim3(kThreads), smem, stream, x, ldx, W, y, ldy, in, out);
 }
 
 inline bool gemv_rows_supported(int in, int rows, size_t kper) {

@@ -34,6 +34,8 @@ template <int kPer, typename WT>
 __global__ void __launch_bounds__(kRowThreads)
     embed_rmsnorm_kernel(const WT *__restrict__ table, const int *__restrict__ ids, float *__restrict__ hidden,
                          const float *__restrict__ w, float eps, ActOut out, int cols) {
+    pdl_trigger();
+    pdl_wait();
     const int64_t row = blockIdx.x;
     const WT *src = table + static_cast<int64_t>(ids[row]) * cols;
     float v[kPer];
@@ -58,6 +60,8 @@ template <int kPer>
 __global__ void __launch_bounds__(kRowThreads)
     add_rmsnorm_kernel(float *__restrict__ hidden, const float *__restrict__ part, int splits, int64_t split_stride,
                        const float *__restrict__ w, float eps, ActOut out, int cols) {
+    pdl_trigger();
+    pdl_wait();
     const int64_t row = blockIdx.x;
     float v[kPer];
     float ss = 0.f;
@@ -93,6 +97,8 @@ static __global__ void __launch_bounds__(256)
     qkv_finalize_kernel(const float *__restrict__ part, int splits, int64_t split_stride, int qh, int kvh,
                         const float2 *__restrict__ rope, TokenMap tm, PagedKV kv, float *__restrict__ kpool,
                         float *__restrict__ vpool, float *__restrict__ q_out) {
+    pdl_trigger();
+    pdl_wait();
     const int64_t row = blockIdx.x;
     const int width = (qh + 2 * kvh) * kAttnD;
     const float *src = part + row * width;
@@ -138,6 +144,8 @@ static __global__ void __launch_bounds__(256)
 // 2j + 1 = up_j); act[row][j] = silu(g) * u = g / (1 + exp(-g)) * u.
 static __global__ void silu_mul_kernel(const float *__restrict__ part, int splits, int64_t split_stride, int rows, int inter,
                                 ActOut out) {
+    pdl_trigger();
+    pdl_wait();
     OPWORKS_GRID_LOOP(i, static_cast<int64_t>(rows) * inter) {
         const int64_t row = i / inter;
         const int j = static_cast<int>(i % inter);
@@ -152,6 +160,91 @@ static __global__ void silu_mul_kernel(const float *__restrict__ part, int split
         out.put(row, j, gu.x / (1.f + expf(-gu.x)) * gu.y);
     }
 }
+
+// ------------------------------------------------- fused GEMM tile epilogues
+//
+// Tile epilogues of the tcgen05 GEMM (sm100::umma_gemm_kernel): they receive
+// finished fp32 values of tokens [tok0, tok0 + ntok) x features
+// [f0, f0 + nfeat) as a shared-memory tile [ntok][128], on the 128 epilogue
+// threads (tid), after the split-K reduction.
+
+// hidden[tok][f] += value: the o and down projections' residual add.
+struct ResidualTileEpi {
+    static constexpr bool kTile = true;
+    float *hidden;
+    int64_t ld;
+    __device__ __forceinline__ void operator()(const float *tile, int tok0, int ntok, int f0, int nfeat,
+                                               int tid) const {
+        for (int idx = tid; idx < ntok * 128; idx += 128) {
+            const int t = idx >> 7, c = idx & 127;
+            if (c < nfeat)
+                hidden[static_cast<int64_t>(tok0 + t) * ld + f0 + c] += tile[idx];
+        }
+    }
+};
+
+// Interleaved gate/up columns (2j = gate_j, 2j + 1 = up_j) -> act[tok][j] =
+// silu(g) * u = g / (1 + exp(-g)) * u, the expression of silu_mul_kernel.
+struct SiluMulTileEpi {
+    static constexpr bool kTile = true;
+    ActOut act;
+    __device__ __forceinline__ void operator()(const float *tile, int tok0, int ntok, int f0, int nfeat,
+                                               int tid) const {
+        for (int idx = tid; idx < ntok * 64; idx += 128) {
+            const int t = idx >> 6, j = idx & 63;
+            if (2 * j + 1 < nfeat) {
+                const float g = tile[t * 128 + 2 * j], u = tile[t * 128 + 2 * j + 1];
+                act.put(tok0 + t, f0 / 2 + j, g / (1.f + expf(-g)) * u);
+            }
+        }
+    }
+};
+
+// q | k | v columns of the fused QKV projection (two 64-wide heads per tile):
+// RoPE on q and k heads (the pairs (i, i + 32) and the cos/sin table of
+// qkv_finalize_kernel), q to q_out [rows][qh][64], k and v into the paged
+// cache at the token's position.
+struct QkvTileEpi {
+    static constexpr bool kTile = true;
+    float *q_out;
+    int qh, kvh;
+    const float2 *rope;
+    TokenMap tm;
+    PagedKV kv;
+    float *kpool, *vpool;
+    __device__ __forceinline__ void operator()(const float *tile, int tok0, int ntok, int f0, int nfeat,
+                                               int tid) const {
+        for (int idx = tid; idx < ntok * 64; idx += 128) {
+            const int t = idx >> 6, hh = (idx >> 5) & 1, i = idx & 31;
+            if (hh * 64 + 64 > nfeat)
+                continue;
+            const int head = f0 / kAttnD + hh;
+            const int64_t row = tok0 + t;
+            const float a = tile[t * 128 + hh * 64 + i], b = tile[t * 128 + hh * 64 + i + 32];
+            const int pos = tm.pos[row];
+            if (head < qh) {
+                const float2 r = rope[static_cast<int64_t>(pos) * (kAttnD / 2) + i];
+                float *q = q_out + row * qh * kAttnD + head * kAttnD;
+                q[i] = a * r.x - b * r.y;
+                q[i + kAttnD / 2] = b * r.x + a * r.y;
+                continue;
+            }
+            const int seq = tm.seq[row];
+            const int blk = kv.table[static_cast<int64_t>(seq) * kv.table_stride + pos / kKvChunk];
+            const int slot = pos % kKvChunk;
+            if (head < qh + kvh) {
+                const float2 r = rope[static_cast<int64_t>(pos) * (kAttnD / 2) + i];
+                float *k = kpool + ((static_cast<int64_t>(blk) * kvh + (head - qh)) * kKvChunk + slot) * kAttnD;
+                k[i] = a * r.x - b * r.y;
+                k[i + kAttnD / 2] = b * r.x + a * r.y;
+            } else {
+                float *v = vpool + ((static_cast<int64_t>(blk) * kvh + (head - qh - kvh)) * kKvChunk + slot) * kAttnD;
+                v[i] = a;
+                v[i + kAttnD / 2] = b;
+            }
+        }
+    }
+};
 
 // cos/sin table of RoPE: table[pos][i] = (cosf(a), sinf(a)), a = fp32(pos) *
 // inv_freq[i], the same fp32 expression as ops::rope.
@@ -395,6 +488,8 @@ static __global__ void __cluster_dims__(kSampleCluster, 1, 1) __launch_bounds__(
     const int n = max(0, min(vocab, lo + chunk) - lo);
     const int n_pad = (n + kWarpSize - 1) / kWarpSize * kWarpSize;
     const float *src = logits + static_cast<int64_t>(row) * ld + lo;
+    pdl_trigger();
+    pdl_wait();
 
     // pass 0: stage the slice, local (max, first index)
     float bv = kNegInf;
@@ -769,8 +864,8 @@ inline void sample_launch(const float *logits, int64_t ld, int rows, int vocab, 
                                                 static_cast<int>(sample_smem_bytes())));
         done = dev;
     }
-    sample_kernel<<<rows * kSampleCluster, kSampleThreads, sample_smem_bytes(), stream>>>(logits, ld, vocab, sp, out);
-    OPWORKS_CUDA_CHECK(cudaGetLastError());
+    launch_ex(sample_kernel, dim3(rows * kSampleCluster), dim3(kSampleThreads), sample_smem_bytes(), stream, logits, ld,
+              vocab, sp, out);
 }
 
 } // namespace opworks::detail

@@ -292,7 +292,8 @@ int opw_gemm_bf16x2(const uint16_t *W, const uint16_t *x_hi, const uint16_t *x_l
         const int bn = sm100::gemm_pick_bn(sm100::GemmKind::kBF16x2, M);
         if (splits <= 0) {
             const int tiles = ((N + kUmmaM - 1) / kUmmaM) * ((M + bn - 1) / bn);
-            splits = sm100::gemm_pick_splits(tiles, (K + 63) / 64, detail::device_facts().sm_count, 4);
+            splits = sm100::gemm_pick_splits(tiles, (K + 63) / 64,
+                                             detail::device_facts().sm_count * sm100::gemm_ctas_per_sm(bn));
         }
         sm100::gemm_tn<sm100::GemmKind::kBF16x2>({as_bf16(W), nullptr, N, K}, {as_bf16(x_hi), as_bf16(x_lo), M, K},
                                                  K, out, N, splits, static_cast<int64_t>(M) * N, as_stream(stream),
