@@ -48,6 +48,19 @@ OPW_API int opw_map_scale(const float *in, float *out, int n, float factor, void
 OPW_API int opw_reduction_workspace_size(int n);
 OPW_API int opw_reduce(int kind, const float *in, float *out, int n, float *workspace, int workspace_size, void *stream);
 
+/* Allocation-free reduction: no reference counterpart (an extension of this
+ * library). Same kinds and result as opw_reduce, with the workspace taken
+ * from a static device buffer of 1025 floats (4100 bytes, the largest
+ * workspace any n needs) instead of a caller buffer or a stream-ordered
+ * allocation; a request that would need more is rejected with an error.
+ * Each call clears the buffer's arrival counter before its kernel.
+ * - The buffer is shared by every call on a device: calls that may overlap
+ *   (different streams, host threads or graph branches without an ordering
+ *   between them) race on it and must be serialised by the caller.
+ * - The first call on each device looks the buffer's address up and must not
+ *   run inside a stream capture; later calls may be captured. */
+OPW_API int opw_reduce_static(int kind, const float *in, float *out, int n, void *stream);
+
 /* ops::softmax / ops::layer_norm (softmax.cuh:36-43, layer_norm.cuh:38-47). */
 OPW_API int opw_softmax(const float *in, float *out, int rows, int cols, void *stream);
 OPW_API int opw_layer_norm(const float *in, float *out, const float *gamma, const float *beta, int rows, int cols, float eps,

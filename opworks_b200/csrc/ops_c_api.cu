@@ -5,6 +5,7 @@
 #include <opworks>
 
 #include <cstring>
+#include <mutex>
 #include <string>
 
 #include "opworks_ops.h"
@@ -73,6 +74,38 @@ void reduce_with(const float *in, float *out, int n, float *ws, int ws_size, cud
 
 const __nv_bfloat16 *as_bf16(const uint16_t *p) { return reinterpret_cast<const __nv_bfloat16 *>(p); }
 
+// Scratch of opw_reduce_static: the largest reduction workspace there is
+// (kReduceMaxBlocks partial slots + the arrival counter = 1025 floats,
+// 4100 bytes), one copy per device context.
+constexpr int kStaticReduceFloats = opworks::detail::kReduceMaxBlocks + 1;
+static __device__ __align__(256) float g_reduce_scratch[kStaticReduceFloats];
+
+// Device address of g_reduce_scratch on the current device, looked up once per
+// device (cudaGetSymbolAddress may load the module, which a stream capture
+// does not allow: the first call on a device must not be captured).
+float *static_reduce_scratch() {
+    constexpr int kMaxDevices = 64;
+    static std::mutex mu;
+    static float *addr[kMaxDevices] = {};
+    int dev = 0;
+    OPWORKS_CUDA_CHECK(cudaGetDevice(&dev));
+    opworks::detail::require(dev >= 0 && dev < kMaxDevices, "opw_reduce_static: device index out of range");
+    const std::lock_guard<std::mutex> lock(mu);
+    if (addr[dev] == nullptr)
+        OPWORKS_CUDA_CHECK(cudaGetSymbolAddress(reinterpret_cast<void **>(&addr[dev]), g_reduce_scratch));
+    return addr[dev];
+}
+
+template <typename Op> void reduce_static_with(const float *in, float *out, int n, cudaStream_t s) {
+    const int needed = opworks::ops::reduction_workspace_size(n);
+    opworks::detail::require(needed <= kStaticReduceFloats,
+                             "opw_reduce_static: the reduction needs more scratch than the static buffer holds");
+    float *ws = needed > 0 ? static_reduce_scratch() : nullptr;
+    // the workspace overload clears the arrival counter (a memset node) before
+    // the kernel, so every call starts from a clean state
+    opworks::ops::reduce<Op>(in, out, n, opworks::DeviceSpan<float>(ws, needed), s);
+}
+
 } // namespace
 
 extern "C" {
@@ -114,6 +147,17 @@ int opw_reduce(int kind, const float *in, float *out, int n, float *workspace, i
         case 0: reduce_with<SumF>(in, out, n, workspace, workspace_size, as_stream(stream)); break;
         case 1: reduce_with<MaxF>(in, out, n, workspace, workspace_size, as_stream(stream)); break;
         case 2: reduce_with<ProdF>(in, out, n, workspace, workspace_size, as_stream(stream)); break;
+        default: throw std::invalid_argument("unknown reduction kind");
+        }
+    });
+}
+
+int opw_reduce_static(int kind, const float *in, float *out, int n, void *stream) {
+    return guarded([&] {
+        switch (kind) {
+        case 0: reduce_static_with<SumF>(in, out, n, as_stream(stream)); break;
+        case 1: reduce_static_with<MaxF>(in, out, n, as_stream(stream)); break;
+        case 2: reduce_static_with<ProdF>(in, out, n, as_stream(stream)); break;
         default: throw std::invalid_argument("unknown reduction kind");
         }
     });

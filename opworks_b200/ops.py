@@ -22,6 +22,7 @@ SIGNATURES = {
     "opw_map_scale": [P, P, I, F, P],
     "opw_reduction_workspace_size": [I],
     "opw_reduce": [I, P, P, I, P, I, P],
+    "opw_reduce_static": [I, P, P, I, P],
     "opw_softmax": [P, P, I, I, P],
     "opw_layer_norm": [P, P, P, P, I, I, F, P],
     "opw_mat_mul": [P, P, P, I, I, I, I, F, P],
