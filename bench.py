@@ -60,6 +60,7 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill-8k", action="store_true")
+    ap.add_argument("--no-extras", action="store_true", help="skip the C1 operator and reference-CUDA sections")
     ap.add_argument("--profile-iters", type=int, default=3)
     return ap.parse_args()
 
@@ -310,11 +311,42 @@ def run_ours(args):
                      "frac_of_bf16_peak": round((gemm_flop + attn_flop) / (ms8 / 1e3) / 1e12 / tc_peak, 4)}
         eng8.close()
 
+    # ---- C2: batch 1, 128-token prompt, then greedy decode (fast path, our
+    # batched ABI with one slot; host wall clock per blocking call)
+    c2 = None
+    if world == 1 and not args.no_extras:
+        with LlamaBatch(model, 1, 128 + 128 + 8, "fast", prefill_rows=128) as e2:
+            ids2 = np.random.default_rng(5).integers(0, model.vocab, 128).astype(np.int32)
+            e2.prefill(0, ids2)  # warm: module loads and graph capture happen here
+            e2.decode([0], [0])
+            e2.reset(0)
+            t = time.perf_counter()
+            tok = e2.prefill(0, ids2)
+            ttft = time.perf_counter() - t
+            t = time.perf_counter()
+            for _ in range(128):
+                tok = int(e2.decode([0], [tok])[0])
+            dec = time.perf_counter() - t
+        c2 = {"prompt": 128, "ttft_ms": round(ttft * 1e3, 2), "decode_steps": 128,
+              "decode_tok_s": round(128 / dec, 1), "precision": "fast (bf16 weights)",
+              "timing": "host wall clock per blocking call"}
+
+    # ---- C1 operator configs, ours and the reference's kernels (rank 0, N = 1)
+    c1 = None
+    if world == 1 and not args.no_extras:
+        from opworks_b200 import microbench
+
+        c1 = microbench.c1(iters=10)
+
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    ref_cuda = None
+    if rank == 0 and world == 1:
         eng.close()
         model.close()
-        cpu = cpu_baseline(pack_path, steps=2)
+        if not args.no_extras:
+            ref_cuda = reference_cuda_path(pack_path)
+        if not args.no_cpu_baseline:
+            cpu = cpu_baseline(pack_path, steps=2)
 
     if rank == 0:
         line = {
@@ -343,6 +375,12 @@ def run_ours(args):
         }
         if cpu is not None:
             line["cpu_baseline"] = cpu
+        if c1 is not None:
+            line["c1_ops"] = c1
+        if c2 is not None:
+            line["c2"] = c2
+        if ref_cuda is not None:
+            line["reference_cuda"] = ref_cuda
         print(json.dumps(line), flush=True)
     try:
         eng.close()
@@ -351,6 +389,77 @@ def run_ours(args):
         pass
     if world > 1:
         dist.destroy_process_group()
+
+
+# ------------------------------------- the reference's own CUDA path (same GPU)
+
+REF_LLAMA = os.path.join(ROOT, "oracle", "_ref", "libopworks_llama_ref.so")
+
+
+def reference_cuda_path(pack_path, c3_sessions=2, c3_steps=8, c2_steps=64):
+    """The reference's CUDA library (built from its own sources into
+    oracle/_ref) through its C ABI on the same GPU and pack: C2 (128-token
+    prompt, then greedy decode, batch 1) and C3-style decode at context 2048.
+    The reference has no batched decode: C3 serving is one session step after
+    another (round robin), so its C3 throughput is one token per session
+    step; it is measured on `c3_sessions` sessions and is the same for 32."""
+    if not os.path.exists(REF_LLAMA):
+        return None
+    import ctypes
+
+    lib = ctypes.CDLL(REF_LLAMA)
+    lib.opw_llama_load.restype = ctypes.c_void_p
+    lib.opw_llama_load.argtypes = [ctypes.c_char_p, ctypes.c_char_p, ctypes.c_int]
+    lib.opw_llama_create_session.restype = ctypes.c_void_p
+    lib.opw_llama_create_session.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_char_p, ctypes.c_int]
+    lib.opw_llama_prefill.restype = ctypes.c_int32
+    lib.opw_llama_prefill.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int32), ctypes.c_int, ctypes.c_char_p,
+                                      ctypes.c_int]
+    lib.opw_llama_decode_step.restype = ctypes.c_int32
+    lib.opw_llama_decode_step.argtypes = [ctypes.c_void_p, ctypes.c_int32, ctypes.c_char_p, ctypes.c_int]
+    lib.opw_llama_destroy_session.argtypes = [ctypes.c_void_p]
+    lib.opw_llama_free.argtypes = [ctypes.c_void_p]
+    err = ctypes.create_string_buffer(512)
+    m = lib.opw_llama_load(pack_path.encode(), err, 512)
+    if not m:
+        return {"unavailable": err.value.decode(errors="replace")}
+    out = {"library": "oracle/_ref/libopworks_llama_ref.so (reference sources, unchanged, nvcc sm_100a)",
+           "weights": "fp32 pack as loaded by the reference"}
+    try:
+        rng = np.random.default_rng(5)
+        prompt = rng.integers(0, 128256, 128).astype(np.int32)
+        s = lib.opw_llama_create_session(m, 128 + c2_steps + 8, err, 512)
+        arr = (ctypes.c_int32 * len(prompt))(*prompt.tolist())
+        t = time.perf_counter()
+        tok = lib.opw_llama_prefill(s, arr, len(prompt), err, 512)
+        ttft = time.perf_counter() - t
+        t = time.perf_counter()
+        for _ in range(c2_steps):
+            tok = lib.opw_llama_decode_step(s, tok, err, 512)
+        dec = time.perf_counter() - t
+        lib.opw_llama_destroy_session(s)
+        out["c2"] = {"prompt": 128, "ttft_ms": round(ttft * 1e3, 2), "decode_steps": c2_steps,
+                     "decode_tok_s": round(c2_steps / dec, 1), "timing": "host wall clock per call (blocking ABI)"}
+        sess, toks = [], []
+        for i in range(c3_sessions):
+            ids = np.random.default_rng(60 + i).integers(0, 128256, CTX).astype(np.int32)
+            si = lib.opw_llama_create_session(m, CTX + c3_steps + 8, err, 512)
+            a = (ctypes.c_int32 * CTX)(*ids.tolist())
+            toks.append(lib.opw_llama_prefill(si, a, CTX, err, 512))
+            sess.append(si)
+        t = time.perf_counter()
+        for _ in range(c3_steps):
+            for i, si in enumerate(sess):
+                toks[i] = lib.opw_llama_decode_step(si, toks[i], err, 512)
+        dt = time.perf_counter() - t
+        for si in sess:
+            lib.opw_llama_destroy_session(si)
+        out["c3"] = {"value": round(c3_sessions * c3_steps / dt, 1), "unit": UNIT,
+                     "sample": f"{c3_sessions} sessions prefilled to {CTX}, {c3_steps} round-robin greedy decode "
+                               "steps each (device sampling excluded: the reference samples on the host)"}
+    finally:
+        lib.opw_llama_free(m)
+    return out
 
 
 # ------------------------------------------------- CPU arm (oracle port)
