@@ -61,6 +61,8 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill-8k", action="store_true")
     ap.add_argument("--no-extras", action="store_true", help="skip the C1 operator and reference-CUDA sections")
+    ap.add_argument("--batch", type=int, default=BATCH, help="sequences per GPU (C3: 32; smaller for profiling)")
+    ap.add_argument("--ctx", type=int, default=CTX, help="prefilled context (C3: 2048; smaller for profiling)")
     ap.add_argument("--profile-iters", type=int, default=3)
     return ap.parse_args()
 
@@ -354,8 +356,8 @@ def run_ours(args):
             "ms_per_step": round(dev_ms / K, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic: random-init weights N(0,0.02) (norm gains 1.0), uniform random token ids",
-            "config": {"workload": "C3 batched decode: Llama-3.2-1B random-init, 32 sequences per GPU prefilled "
-                                   "to 2048 random ids, T=0.7 top-p=0.9 device sampling, fp32 paged KV "
+            "config": {"workload": f"C3 batched decode: Llama-3.2-1B random-init, {BATCH} sequences per GPU "
+                                   f"prefilled to {CTX} random ids, T=0.7 top-p=0.9 device sampling, fp32 paged KV "
                                    "(16-token blocks)",
                        "model": "Llama-3.2-1B (16 layers, 2048 hidden, 32/8 heads, 128256 vocab)",
                        "global_batch": BATCH * world, "seq_len": CTX, "ctx_range": [CTX + W, CTX + W + K],
@@ -538,7 +540,9 @@ def run_reference(args):
 
 
 def main():
+    global BATCH, CTX
     args = parse()
+    BATCH, CTX = args.batch, args.ctx
     if args.impl == "reference":
         run_reference(args)
     else:

@@ -500,7 +500,7 @@ template <typename WT> class LlamaEngineT {
     // fast path: x . W^T with the split-K reduction and `epi` fused into the
     // GEMM (K splits of a tile form one cluster)
     template <typename Epi> void linear_tile(const Projection &p, const Act &x, int rows, const Epi &epi) {
-        const int splits = plan_splits(p, rows, sm100::kMaxClusterSplits);
+        const int splits = plan_splits(p, rows, max_cluster_splits_);
         sm100::gemm_tn<sm100::GemmKind::kBF16x2, Epi>({p.bf16.data(), nullptr, p.out, p.in},
                                                       {x.bf16, x.bf16_lo, rows, p.in}, p.in, part_.data(), p.out,
                                                       splits, static_cast<int64_t>(rows) * p.out, stream_, epi,
@@ -731,6 +731,40 @@ template <typename WT> class LlamaEngineT {
     int32_t *out_host_ = nullptr;
     std::map<int, cudaGraphExec_t> graphs_;
     bool marks_enabled_ = false;
+    // K splits per cluster of the fused GEMMs: the portable 8 (measured faster
+    // than 16-CTA clusters for the decode projections); OPWORKS_CLUSTER_SPLITS
+    // may ask for up to 16 where the GPU schedules such clusters
+    int max_cluster_splits_ = [] {
+        const char *e = std::getenv("OPWORKS_CLUSTER_SPLITS");
+        const int want = e ? std::atoi(e) : sm100::kMaxClusterSplits;
+        if (want <= sm100::kMaxClusterSplits)
+            return want > 0 ? want : 1;
+        return std::min(want, cluster_splits_supported());
+    }();
+
+    static int cluster_splits_supported() {
+        using K = sm100::GemmShape<sm100::GemmKind::kBF16x2, 32>;
+        sm100::gemm_prepare_kernel<sm100::GemmKind::kBF16x2, 32, detail::ResidualTileEpi>();
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = dim3(16, 1, sm100::kMaxClusterSplitsNonPortable);
+        cfg.blockDim = dim3(192);
+        cfg.dynamicSmemBytes = K::kSmemBytes;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 1;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = sm100::kMaxClusterSplitsNonPortable;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        int clusters = 0;
+        const cudaError_t e = cudaOccupancyMaxActiveClusters(
+            &clusters, sm100::umma_gemm_kernel<sm100::GemmKind::kBF16x2, 32, detail::ResidualTileEpi>, &cfg);
+        if (e != cudaSuccess) {
+            (void)cudaGetLastError();
+            return sm100::kMaxClusterSplits;
+        }
+        return clusters >= 1 ? sm100::kMaxClusterSplitsNonPortable : sm100::kMaxClusterSplits;
+    }
     // programmatic dependent launch between the kernels of a step
     // (OPWORKS_PDL=0 turns it off)
     bool pdl_ = [] {

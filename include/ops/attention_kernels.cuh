@@ -155,6 +155,15 @@ __device__ __forceinline__ void stage_kv_tile(const KV &kv, int b, int h, int t0
 
 // ------------------------------------------------------------------ decode
 
+constexpr float kLog2e = 1.4426950408889634f; // log2(e): exp(x) = 2^(x log2 e)
+
+// 2^x by the SFU's ex2.approx (relative error ~2^-22; 2^-inf = 0).
+__device__ __forceinline__ float exp2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 // Decode: one producer warp streams 32-token K/V tiles (2 chunks) through a
 // kDecodeStages-deep ring of bulk copies; 8 consumer warps take 4 tokens of
 // every tile each. A token's 64 dims are spread over kDG lanes (8, or 16 for
@@ -211,7 +220,7 @@ __device__ __forceinline__ void stage_kv_tile_offsets(const KV &kv, const int64_
 
 // q: [B][q_stride] with heads at h*64. grid = (splits, kvh, B). With one
 // split the normalised result goes straight to `out`; otherwise part_o
-// [B][qh][splits][64] and part_ml [B][qh][splits][2] (running max, running
+// [B][qh][splits][64] and part_ml [B][qh][splits][2] (running max in log2 units, running
 // sum) hold the split partials for attn_decode_combine_kernel.
 template <class KV, int kRep, typename Out>
 __global__ void __launch_bounds__(kDecodeThreads, kDecodeCtasPerSm)
@@ -296,7 +305,9 @@ __global__ void __launch_bounds__(kDecodeThreads, kDecodeCtasPerSm)
                 if (!sm100::mbar_wait(&full[j % kDecodeStages], static_cast<uint32_t>(j / kDecodeStages) & 1u))
                     ok = false;
     } else {
-        // this lane's slice of the query heads, in registers
+        // this lane's slice of the query heads, in registers, pre-scaled so
+        // that scores come out in log2 units (softmax by exp2)
+        const float qscale = scale * kLog2e;
         float qr[kRep][G::kDims];
         const float *qb = q + static_cast<int64_t>(b) * q_stride + static_cast<int64_t>(h) * kRep * kAttnD;
 #pragma unroll
@@ -307,7 +318,7 @@ __global__ void __launch_bounds__(kDecodeThreads, kDecodeCtasPerSm)
             for (int c = 0; c < G::kVec; ++c)
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
-                    qr[j][4 * c + e] = qb[j * kAttnD + c * 4 * G::kDG + dq * 4 + e] * scale;
+                    qr[j][4 * c + e] = qb[j * kAttnD + c * 4 * G::kDG + dq * 4 + e] * qscale;
                     acc[j][4 * c + e] = 0.f;
                 }
         }
@@ -353,7 +364,7 @@ __global__ void __launch_bounds__(kDecodeThreads, kDecodeCtasPerSm)
                     for (int j = 0; j < kRep; ++j) {
                         float p;
                         if (d[j] > m_run[j]) {
-                            const float a = expf(m_run[j] - d[j]);
+                            const float a = exp2_approx(m_run[j] - d[j]);
                             m_run[j] = d[j];
                             l_run[j] *= a;
 #pragma unroll
@@ -361,7 +372,7 @@ __global__ void __launch_bounds__(kDecodeThreads, kDecodeCtasPerSm)
                                 acc[j][e] *= a;
                             p = 1.f;
                         } else {
-                            p = expf(d[j] - m_run[j]);
+                            p = exp2_approx(d[j] - m_run[j]);
                         }
                         l_run[j] += p;
 #pragma unroll
@@ -385,7 +396,7 @@ __global__ void __launch_bounds__(kDecodeThreads, kDecodeCtasPerSm)
 #pragma unroll
             for (int off = G::kDG; off < 32; off <<= 1)
                 M = fmaxf(M, __shfl_xor_sync(kFullWarpMask, M, off));
-            const float a = m_run[j] == kNegInf ? 0.f : expf(m_run[j] - M);
+            const float a = m_run[j] == kNegInf ? 0.f : exp2_approx(m_run[j] - M);
             float L = l_run[j] * a;
 #pragma unroll
             for (int off = G::kDG; off < 32; off <<= 1)
@@ -435,7 +446,7 @@ __global__ void __launch_bounds__(kDecodeThreads, kDecodeCtasPerSm)
                 const float mg = mls[(g * kRep + head) * 2];
                 if (mg == kNegInf)
                     continue;
-                const float w = expf(mg - M);
+                const float w = exp2_approx(mg - M);
                 L += w * mls[(g * kRep + head) * 2 + 1];
                 O += w * red[(g * kRep + head) * kAttnD + dd];
             }
@@ -472,7 +483,7 @@ __global__ void __launch_bounds__(64)
             const float m = part_ml[2 * (base + s)];
             if (m == kNegInf)
                 continue;
-            const float w = expf(m - M);
+            const float w = exp2_approx(m - M);
             L += w * part_ml[2 * (base + s) + 1];
             o += w * part_o[(base + s) * kAttnD + d];
         }

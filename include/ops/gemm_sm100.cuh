@@ -63,11 +63,26 @@ struct Identity {
 // to the epilogue,
 //   epi(tile [ntok][128], tok0, ntok, f0, nfeat, tid in [0, 128)),
 // so split-K needs no global workspace and no separate reduction kernel.
+//
+// A tile epilogue may also define
+//   prepare(tok0, ntok, f0, nfeat, tid, void *scratch)
+// which runs on the epilogue threads while the main loop streams, before the
+// accumulator is final (metadata loads such as token positions), with 2 KB of
+// shared scratch that stays valid for operator().
 template <typename Epi, typename = void> struct is_tile_epilogue : std::false_type {};
 template <typename Epi> struct is_tile_epilogue<Epi, std::void_t<decltype(Epi::kTile)>> : std::true_type {};
-constexpr int kMaxClusterSplits = 8; // portable cluster size
+template <typename Epi, typename = void> struct has_prepare : std::false_type {};
+template <typename Epi>
+struct has_prepare<Epi, std::void_t<decltype(std::declval<const Epi &>().prepare(0, 0, 0, 0, 0, nullptr))>>
+    : std::true_type {};
+constexpr int kMaxClusterSplits = 8;           // portable cluster size
+constexpr int kMaxClusterSplitsNonPortable = 16; // with the non-portable opt-in
 
 __device__ __forceinline__ void epilogue_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// split cluster barrier: arrive (release this CTA's shared-memory writes) and
+// wait (acquire the peers'); every thread of every CTA takes both
+__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
 template <typename Epi>
 __device__ __forceinline__ float apply_epilogue(const Epi &epi, float v, int tok, int feat) {
     if constexpr (std::is_invocable_v<const Epi &, float, int, int>)
@@ -95,7 +110,8 @@ template <GemmKind kKind, int BN> struct GemmShape {
     // K blocks accumulated in TMEM before the epilogue promotes the partial
     // sum into fp32 registers (split-precision path only)
     static constexpr int kPromoteKb = 2;
-    static constexpr size_t kSmemBytes = 1024 + static_cast<size_t>(kStages) * kStageBytes + 256;
+    static constexpr size_t kEpiScratchBytes = 2048; // tile epilogue metadata (prepare())
+    static constexpr size_t kSmemBytes = 1024 + static_cast<size_t>(kStages) * kStageBytes + 256 + kEpiScratchBytes;
     static_assert(kStages >= 2, "GEMM tile does not fit two pipeline stages");
     static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N must be a multiple of 16 in [16, 256]");
 };
@@ -118,6 +134,7 @@ __global__ void __launch_bounds__(192, GemmShape<kKind, BN>::kCtasPerSm)
     uint64_t *ready = accum + 1;   // [2] promotion buffers filled (split path)
     uint64_t *drained = ready + 2; // [2] promotion buffers read (split path)
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drained + 2);
+    void *epi_scratch = smem + kStages * S::kStageBytes + 256;
 
     const int warp = threadIdx.x / kWarpSize;
     const int lane = threadIdx.x % kWarpSize;
@@ -271,6 +288,13 @@ __global__ void __launch_bounds__(192, GemmShape<kKind, BN>::kCtasPerSm)
         // (the pipeline stages are idle once the accumulator is final)
         float *ptile = reinterpret_cast<float *>(smem);
         const int col = q * 32 + lane;
+        if constexpr (kTileEpi && has_prepare<Epi>::value) {
+            const int per = (BN + p.splits - 1) / p.splits;
+            const int tb = p.splits > 1 ? min(BN, split * per) : 0;
+            const int nt = p.splits > 1 ? min(BN, tb + per) - tb : BN;
+            epi.prepare(t0 + tb, max(0, min(nt, p.m_tok - (t0 + tb))), f0, min(kUmmaM, p.n_feat - f0),
+                        static_cast<int>(threadIdx.x) - 64, epi_scratch);
+        }
         if constexpr (S::kSplit3) {
             // promote each group's TMEM partial into fp32 registers: the
             // tensor core's accumulator only ever holds kPromoteKb blocks
@@ -336,14 +360,16 @@ __global__ void __launch_bounds__(192, GemmShape<kKind, BN>::kCtasPerSm)
         float *rtile = ptile + BN * kUmmaM;
         const int per = (BN + nsplit - 1) / nsplit;
         const int tl0 = min(BN, split * per), tl1 = min(BN, tl0 + per);
-        if (nsplit > 1)
-            cg::this_cluster().sync();
-        else
+        if (nsplit > 1) {
+            cluster_arrive(); // this CTA's partial tile is published
+            cluster_wait();   // and every peer's
+        } else {
             __syncthreads();
-        if (warp >= 2) {
-            const int et = threadIdx.x - 64;
-            const float *src = ptile;
-            if (nsplit > 1) {
+        }
+        const float *src = ptile;
+        if (nsplit > 1) {
+            if (warp >= 2) {
+                const int et = threadIdx.x - 64;
                 cg::cluster_group cluster = cg::this_cluster();
                 for (int idx = et; idx < (tl1 - tl0) * (kUmmaM / 4); idx += 128) {
                     const int t = tl0 + idx / (kUmmaM / 4), c4 = idx % (kUmmaM / 4);
@@ -358,15 +384,18 @@ __global__ void __launch_bounds__(192, GemmShape<kKind, BN>::kCtasPerSm)
                     }
                     reinterpret_cast<float4 *>(rtile)[(t - tl0) * (kUmmaM / 4) + c4] = acc;
                 }
-                src = rtile;
                 epilogue_bar();
             }
+            src = rtile;
+            cluster_arrive(); // done reading the peers' tiles; the epilogue runs under the barrier
+        }
+        if (warp >= 2) {
             const int tb = nsplit > 1 ? tl0 : 0;
             const int ntok = max(0, min(nsplit > 1 ? tl1 - tl0 : BN, p.m_tok - (t0 + tb)));
-            epi(src, t0 + tb, ntok, f0, min(kUmmaM, p.n_feat - f0), et);
+            epi(src, t0 + tb, ntok, f0, min(kUmmaM, p.n_feat - f0), static_cast<int>(threadIdx.x) - 64, epi_scratch);
         }
         if (nsplit > 1)
-            cg::this_cluster().sync(); // peers are done reading this CTA's tile
+            cluster_wait(); // peers are done reading this CTA's tile
     }
     if (!ok)
         atomicExch(p.err, 1);
@@ -387,6 +416,9 @@ template <GemmKind kKind, int BN, typename Epi> inline void gemm_prepare_kernel(
         OPWORKS_CUDA_CHECK(cudaFuncSetAttribute(umma_gemm_kernel<kKind, BN, Epi>,
                                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                 static_cast<int>(S::kSmemBytes)));
+        if constexpr (is_tile_epilogue<Epi>::value)
+            OPWORKS_CUDA_CHECK(cudaFuncSetAttribute(umma_gemm_kernel<kKind, BN, Epi>,
+                                                    cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
         done_device = dev;
     }
 }
@@ -399,7 +431,7 @@ inline void gemm_launch(const CUtensorMap &a, const CUtensorMap &b, const CUtens
     const dim3 grid((p.n_feat + kUmmaM - 1) / kUmmaM, (p.m_tok + BN - 1) / BN, p.splits);
     detail::require(grid.y <= 65535 && grid.z <= 65535, "GEMM grid exceeds the CUDA limits");
     if constexpr (is_tile_epilogue<Epi>::value) {
-        detail::require(p.splits >= 1 && p.splits <= kMaxClusterSplits, "tile epilogue: at most 8 K splits");
+        detail::require(p.splits >= 1 && p.splits <= kMaxClusterSplitsNonPortable, "tile epilogue: at most 16 K splits");
         launch_ex_cluster(umma_gemm_kernel<kKind, BN, Epi>, grid, dim3(1, 1, p.splits), dim3(192), S::kSmemBytes,
                           stream, a, b, a_lo, b_lo, p, epi);
     } else {

@@ -166,15 +166,16 @@ static __global__ void silu_mul_kernel(const float *__restrict__ part, int split
 // Tile epilogues of the tcgen05 GEMM (sm100::umma_gemm_kernel): they receive
 // finished fp32 values of tokens [tok0, tok0 + ntok) x features
 // [f0, f0 + nfeat) as a shared-memory tile [ntok][128], on the 128 epilogue
-// threads (tid), after the split-K reduction.
+// threads (tid), after the split-K reduction, plus 2 KB of shared scratch
+// filled by their optional prepare().
 
 // hidden[tok][f] += value: the o and down projections' residual add.
 struct ResidualTileEpi {
     static constexpr bool kTile = true;
     float *hidden;
     int64_t ld;
-    __device__ __forceinline__ void operator()(const float *tile, int tok0, int ntok, int f0, int nfeat,
-                                               int tid) const {
+    __device__ __forceinline__ void operator()(const float *tile, int tok0, int ntok, int f0, int nfeat, int tid,
+                                               void *) const {
         for (int idx = tid; idx < ntok * 128; idx += 128) {
             const int t = idx >> 7, c = idx & 127;
             if (c < nfeat)
@@ -188,8 +189,8 @@ struct ResidualTileEpi {
 struct SiluMulTileEpi {
     static constexpr bool kTile = true;
     ActOut act;
-    __device__ __forceinline__ void operator()(const float *tile, int tok0, int ntok, int f0, int nfeat,
-                                               int tid) const {
+    __device__ __forceinline__ void operator()(const float *tile, int tok0, int ntok, int f0, int nfeat, int tid,
+                                               void *) const {
         for (int idx = tid; idx < ntok * 64; idx += 128) {
             const int t = idx >> 6, j = idx & 63;
             if (2 * j + 1 < nfeat) {
@@ -212,8 +213,21 @@ struct QkvTileEpi {
     TokenMap tm;
     PagedKV kv;
     float *kpool, *vpool;
-    __device__ __forceinline__ void operator()(const float *tile, int tok0, int ntok, int f0, int nfeat,
-                                               int tid) const {
+    // per token of the slice: position, KV block and slot in it (loaded while
+    // the GEMM main loop streams)
+    __device__ __forceinline__ void prepare(int tok0, int ntok, int, int, int tid, void *scratch) const {
+        int *meta = static_cast<int *>(scratch);
+        for (int t = tid; t < ntok; t += 128) {
+            const int64_t row = tok0 + t;
+            const int pos = tm.pos[row];
+            meta[3 * t] = pos;
+            meta[3 * t + 1] = kv.table[static_cast<int64_t>(tm.seq[row]) * kv.table_stride + pos / kKvChunk];
+            meta[3 * t + 2] = pos % kKvChunk;
+        }
+    }
+    __device__ __forceinline__ void operator()(const float *tile, int tok0, int ntok, int f0, int nfeat, int tid,
+                                               void *scratch) const {
+        const int *meta = static_cast<const int *>(scratch);
         for (int idx = tid; idx < ntok * 64; idx += 128) {
             const int t = idx >> 6, hh = (idx >> 5) & 1, i = idx & 31;
             if (hh * 64 + 64 > nfeat)
@@ -221,7 +235,7 @@ struct QkvTileEpi {
             const int head = f0 / kAttnD + hh;
             const int64_t row = tok0 + t;
             const float a = tile[t * 128 + hh * 64 + i], b = tile[t * 128 + hh * 64 + i + 32];
-            const int pos = tm.pos[row];
+            const int pos = meta[3 * t];
             if (head < qh) {
                 const float2 r = rope[static_cast<int64_t>(pos) * (kAttnD / 2) + i];
                 float *q = q_out + row * qh * kAttnD + head * kAttnD;
@@ -229,9 +243,8 @@ struct QkvTileEpi {
                 q[i + kAttnD / 2] = b * r.x + a * r.y;
                 continue;
             }
-            const int seq = tm.seq[row];
-            const int blk = kv.table[static_cast<int64_t>(seq) * kv.table_stride + pos / kKvChunk];
-            const int slot = pos % kKvChunk;
+            const int blk = meta[3 * t + 1];
+            const int slot = meta[3 * t + 2];
             if (head < qh + kvh) {
                 const float2 r = rope[static_cast<int64_t>(pos) * (kAttnD / 2) + i];
                 float *k = kpool + ((static_cast<int64_t>(blk) * kvh + (head - qh)) * kKvChunk + slot) * kAttnD;
