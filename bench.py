@@ -158,6 +158,18 @@ def step_bytes(cfg, batch, ctx_mean):
     return tot
 
 
+def scaled_traffic(label, tr, batch, ctx):
+    """DRAM bytes per launch from an ncu capture (profiles/traffic.json),
+    scaled to this launch by the units it processes: attention traffic grows
+    with batch x context (KV tokens read), a GEMM's does not change."""
+    if not isinstance(tr, dict) or "dram_bytes_per_launch" not in tr:
+        return None
+    b = float(tr["dram_bytes_per_launch"])
+    if label == "attention":
+        b *= (batch * ctx) / float(tr["batch"] * tr["ctx"])
+    return int(b)
+
+
 def load_traffic():
     p = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(p):
@@ -282,7 +294,7 @@ def run_ours(args):
     tr = traffic.get(dom["kernel"])
     roofline = {"bound": "hbm", "kernel": dom["kernel"], "achieved": round(achieved, 1), "peak": hbm_peak,
                 "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
-                "traffic": tr.get("bytes_per_launch_scaled") if isinstance(tr, dict) else None,
+                "traffic": scaled_traffic(dom["kernel"], tr, BATCH, ctx_now),
                 "algorithmic_bytes_per_launch": int(dom_bytes), "avg_launch_ms": round(dom_ms, 5),
                 "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)"}
     sb = step_bytes(cfg, BATCH, ctx_mean)
