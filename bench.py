@@ -141,11 +141,12 @@ def algorithmic_bytes(label, cfg, batch, ctx_mean):
         # fused fast path: bf16 weights, two-term bf16 activations in (4 bytes
         # per element), fused epilogue traffic out
         "gemm_qkv_rope_kv_write": L * ((qw + 2 * kvw) * H * 2 + act(H) * 4 + act(qw + 2 * kvw) * 4),
-        "gemm_o_residual": L * (H * qw * 2 + act(qw) * 4 + act(H) * 8),
+        # residual epilogues: hidden read + write, next operand h * gain out
+        "gemm_o_residual": L * (H * qw * 2 + act(qw) * 4 + act(H) * 12),
         "gemm_gate_up_silu": L * (2 * I * H * 2 + act(H) * 4 + act(I) * 4),
-        "gemm_down_residual": L * (H * I * 2 + act(I) * 4 + act(H) * 8),
+        "gemm_down_residual": L * (H * I * 2 + act(I) * 4 + act(H) * 12),
         "attention": L * (batch * ctx_mean * kvw * 4 * 2 + act(qw) * 4 + act(qw) * 2),
-        "lm_head": V * H * 2 + act(H) * 2 + act(V) * 4,
+        "lm_head": V * H * 2 + act(H) * 4 + act(V) * 4,
     }
     return table.get(label)
 

@@ -134,6 +134,8 @@ template <typename WT> class LlamaEngineT {
         const int64_t H = cfg.hidden_size, I = cfg.intermediate_size, QW = cfg.q_width();
         const bool fast = prec == Precision::kFast;
         hidden_ = TypedDeviceBuffer<float>(rows_max_ * H);
+        // per-tile partial sums of squares of the residual stream (deferred norm)
+        ss_ = TypedDeviceBuffer<float>(rows_max_ * ((H + kUmmaM - 1) / kUmmaM));
         q_ = TypedDeviceBuffer<float>(rows_max_ * QW);
         if (fast) {
             normed_bf_ = TypedDeviceBuffer<__nv_bfloat16>(rows_max_ * H);
@@ -499,12 +501,17 @@ template <typename WT> class LlamaEngineT {
 
     // fast path: x . W^T with the split-K reduction and `epi` fused into the
     // GEMM (K splits of a tile form one cluster)
-    template <typename Epi> void linear_tile(const Projection &p, const Act &x, int rows, const Epi &epi) {
+    // `next` (optional): the projection that streams after this one; its
+    // weights are pulled into L2 while this GEMM runs (latency-bound decode
+    // GEMMs leave HBM bandwidth idle)
+    template <typename Epi>
+    void linear_tile(const Projection &p, const Act &x, int rows, const Epi &epi, const Projection *next = nullptr) {
         const int splits = plan_splits(p, rows, max_cluster_splits_);
-        sm100::gemm_tn<sm100::GemmKind::kBF16x2, Epi>({p.bf16.data(), nullptr, p.out, p.in},
-                                                      {x.bf16, x.bf16_lo, rows, p.in}, p.in, part_.data(), p.out,
-                                                      splits, static_cast<int64_t>(rows) * p.out, stream_, epi,
-                                                      plan_bn(rows));
+        const bool pf = next != nullptr && l2_prefetch_ && rows <= 64;
+        sm100::gemm_tn<sm100::GemmKind::kBF16x2, Epi>(
+            {p.bf16.data(), nullptr, p.out, p.in}, {x.bf16, x.bf16_lo, rows, p.in}, p.in, part_.data(), p.out, splits,
+            static_cast<int64_t>(rows) * p.out, stream_, epi, plan_bn(rows), pf ? next->bf16.data() : nullptr,
+            pf ? sizeof(__nv_bfloat16) * static_cast<uint64_t>(next->out) * next->in : 0);
     }
 
     // part[s][rows][p.out] = x[rows][p.in] . W^T (partial over split s)
@@ -561,7 +568,17 @@ template <typename WT> class LlamaEngineT {
     template <int kPer, typename T> void launch_embed(int rows, const T *table, const detail::ActOut &o) {
         detail::embed_rmsnorm_kernel<kPer, T><<<rows, detail::kRowThreads, 0, stream_>>>(
             table, dev_at<int32_t>(layout_.ids), hidden_.data(), w_.layers[0].input_norm.data(), cfg_.rms_norm_eps, o,
-            cfg_.hidden_size);
+            cfg_.hidden_size, fast() ? row_sumsq() : detail::RowSumSq{});
+    }
+    // deferred RMSNorm bookkeeping of the fast path (see detail::RowSumSq)
+    detail::RowSumSq row_sumsq() {
+        detail::RowSumSq rs;
+        rs.part = ss_.data();
+        rs.ld = rows_max_;
+        rs.tiles = (cfg_.hidden_size + kUmmaM - 1) / kUmmaM;
+        rs.cols = cfg_.hidden_size;
+        rs.eps = cfg_.rms_norm_eps;
+        return rs;
     }
     template <typename T> void embed(int rows, const T *table, const detail::ActOut &o) {
         switch (cfg_.hidden_size / detail::kRowThreads) {
@@ -619,9 +636,11 @@ template <typename WT> class LlamaEngineT {
             const detail::PagedKV kv{kv_.k(l), kv_.v(l), table_dev_.data(), blocks_per_seq_, kvh};
             const float2 *rope = reinterpret_cast<const float2 *>(w_.rope_table.data());
             int s = 0;
+            const detail::RowSumSq rs = row_sumsq();
             if (fast()) {
                 linear_tile(L.qkv, normed, rows,
-                            detail::QkvTileEpi{q_.data(), qh, kvh, rope, tm, kv, kv_.k(l), kv_.v(l)});
+                            detail::QkvTileEpi{q_.data(), qh, kvh, rope, tm, kv, kv_.k(l), kv_.v(l), rs},
+                            l2_prefetch_qkv_o_ ? &L.o : nullptr);
                 mark("gemm_qkv_rope_kv_write");
             } else {
                 s = linear(L.qkv, normed, rows);
@@ -639,15 +658,19 @@ template <typename WT> class LlamaEngineT {
             }
             mark("attention");
             if (fast()) {
-                linear_tile(L.o, attn, rows, detail::ResidualTileEpi{hidden_.data(), H});
+                // the residual epilogues also emit the next projection's
+                // operand h * gain and the tiles' sums of squares; the
+                // consuming epilogues apply the norm's per-token scale
+                linear_tile(L.o, attn, rows, detail::ResidualTileEpi{hidden_.data(), H, L.post_norm.data(), normed_o, rs},
+                            &L.gu);
                 mark("gemm_o_residual");
-                add_rmsnorm(rows, 0, L.post_norm.data(), normed_o);
-                mark("rmsnorm");
-                linear_tile(L.gu, normed, rows, detail::SiluMulTileEpi{act_o});
+                linear_tile(L.gu, normed, rows, detail::SiluMulTileEpi{act_o, rs}, &L.down);
                 mark("gemm_gate_up_silu");
-                linear_tile(L.down, act, rows, detail::ResidualTileEpi{hidden_.data(), H});
+                const float *next_gain =
+                    l + 1 < cfg_.num_layers ? w_.layers[l + 1].input_norm.data() : w_.final_norm.data();
+                linear_tile(L.down, act, rows, detail::ResidualTileEpi{hidden_.data(), H, next_gain, normed_o, rs},
+                            l + 1 < cfg_.num_layers ? &w_.layers[l + 1].qkv : nullptr);
                 mark("gemm_down_residual");
-                s = 0; // residual already added: the norm below reads hidden only
             } else {
                 s = linear(L.o, attn, rows);
                 mark("gemm_o");
@@ -662,16 +685,18 @@ template <typename WT> class LlamaEngineT {
                 s = linear(L.down, act, rows);
                 mark("gemm_down");
             }
-            if (l + 1 < cfg_.num_layers) {
-                add_rmsnorm(rows, s, w_.layers[l + 1].input_norm.data(), normed_o);
-            } else {
-                // the final norm feeds only the LM head, which reads full fp32
-                // on the accurate path (never the tf32 hi/lo split)
-                detail::ActOut final_o = normed_o;
-                final_o.lo = nullptr;
-                add_rmsnorm(rows, s, w_.final_norm.data(), final_o);
+            if (!fast()) {
+                if (l + 1 < cfg_.num_layers) {
+                    add_rmsnorm(rows, s, w_.layers[l + 1].input_norm.data(), normed_o);
+                } else {
+                    // the final norm feeds only the LM head, which reads full
+                    // fp32 on the accurate path (never the tf32 hi/lo split)
+                    detail::ActOut final_o = normed_o;
+                    final_o.lo = nullptr;
+                    add_rmsnorm(rows, s, w_.final_norm.data(), final_o);
+                }
+                mark("residual_rmsnorm");
             }
-            mark(fast() ? "rmsnorm" : "residual_rmsnorm");
             if (hook) {
                 OPWORKS_CUDA_CHECK(cudaStreamSynchronize(stream_));
                 hook(l);
@@ -682,10 +707,11 @@ template <typename WT> class LlamaEngineT {
         const int64_t first = decode ? 0 : rows - 1;
         const int V = cfg_.vocab_size;
         if (fast()) {
-            sm100::gemm_tn<sm100::GemmKind::kBF16x2>(
+            // deferred final norm: the epilogue scales each row's logits
+            sm100::gemm_tn<sm100::GemmKind::kBF16x2, detail::LogitsTileEpi>(
                 {w_.embed_bf16.data(), nullptr, V, H},
                 {normed_bf_.data() + first * H, normed_bflo_.data() + first * H, lrows, H}, H, logits_.data(), V, 1,
-                0, stream_, sm100::Identity{}, plan_bn(lrows));
+                0, stream_, detail::LogitsTileEpi{logits_.data(), V, row_sumsq(), first}, plan_bn(lrows));
         } else {
             for (int r0 = 0; r0 < lrows; r0 += 4) {
                 const int r = std::min(4, lrows - r0);
@@ -720,7 +746,7 @@ template <typename WT> class LlamaEngineT {
     std::vector<int32_t> table_host_;
     TypedDeviceBuffer<int32_t> table_dev_;
     bool table_dirty_ = true;
-    TypedDeviceBuffer<float> hidden_, q_, part_, attn_po_, attn_pml_, logits_;
+    TypedDeviceBuffer<float> hidden_, ss_, q_, part_, attn_po_, attn_pml_, logits_;
     TypedDeviceBuffer<__nv_bfloat16> normed_bf_, attn_bf_, act_bf_, normed_bflo_, attn_bflo_, act_bflo_;
     TypedDeviceBuffer<float> normed_f_, normed_lo_, attn_f_, attn_lo_, act_f_, act_lo_;
     TypedDeviceBuffer<int32_t> tokens_;
@@ -731,40 +757,23 @@ template <typename WT> class LlamaEngineT {
     int32_t *out_host_ = nullptr;
     std::map<int, cudaGraphExec_t> graphs_;
     bool marks_enabled_ = false;
-    // K splits per cluster of the fused GEMMs: the portable 8 (measured faster
-    // than 16-CTA clusters for the decode projections); OPWORKS_CLUSTER_SPLITS
-    // may ask for up to 16 where the GPU schedules such clusters
+    // upper bound on the K splits (one cluster) of the fused GEMMs: the
+    // portable 8 measured fastest at C3 (4 and 16 were slower);
+    // OPWORKS_CLUSTER_SPLITS overrides it (up to 16, non-portable clusters)
     int max_cluster_splits_ = [] {
         const char *e = std::getenv("OPWORKS_CLUSTER_SPLITS");
         const int want = e ? std::atoi(e) : sm100::kMaxClusterSplits;
-        if (want <= sm100::kMaxClusterSplits)
-            return want > 0 ? want : 1;
-        return std::min(want, cluster_splits_supported());
+        return std::max(1, std::min(want, sm100::kMaxClusterSplitsNonPortable));
     }();
-
-    static int cluster_splits_supported() {
-        using K = sm100::GemmShape<sm100::GemmKind::kBF16x2, 32>;
-        sm100::gemm_prepare_kernel<sm100::GemmKind::kBF16x2, 32, detail::ResidualTileEpi>();
-        cudaLaunchConfig_t cfg{};
-        cfg.gridDim = dim3(16, 1, sm100::kMaxClusterSplitsNonPortable);
-        cfg.blockDim = dim3(192);
-        cfg.dynamicSmemBytes = K::kSmemBytes;
-        cudaLaunchAttribute attr[1];
-        attr[0].id = cudaLaunchAttributeClusterDimension;
-        attr[0].val.clusterDim.x = 1;
-        attr[0].val.clusterDim.y = 1;
-        attr[0].val.clusterDim.z = sm100::kMaxClusterSplitsNonPortable;
-        cfg.attrs = attr;
-        cfg.numAttrs = 1;
-        int clusters = 0;
-        const cudaError_t e = cudaOccupancyMaxActiveClusters(
-            &clusters, sm100::umma_gemm_kernel<sm100::GemmKind::kBF16x2, 32, detail::ResidualTileEpi>, &cfg);
-        if (e != cudaSuccess) {
-            (void)cudaGetLastError();
-            return sm100::kMaxClusterSplits;
-        }
-        return clusters >= 1 ? sm100::kMaxClusterSplitsNonPortable : sm100::kMaxClusterSplits;
-    }
+    // L2 prefetch of the next projection's weights by each decode GEMM: off
+    // by default (measured slower at C3: the prefetch competes with the
+    // running GEMM's own weight stream); OPWORKS_L2_PREFETCH=1 turns it on,
+    // =2 also lets the QKV GEMM pull the O weights across the attention kernel
+    int l2_prefetch_ = [] {
+        const char *e = std::getenv("OPWORKS_L2_PREFETCH");
+        return e ? std::atoi(e) : 0;
+    }();
+    bool l2_prefetch_qkv_o_ = l2_prefetch_ >= 2;
     // programmatic dependent launch between the kernels of a step
     // (OPWORKS_PDL=0 turns it off)
     bool pdl_ = [] {

@@ -90,6 +90,13 @@ __device__ __forceinline__ void prefetch_tmap(const CUtensorMap *tm) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tm)) : "memory");
 }
 
+// Bulk prefetch of [src, src + bytes) into L2 (no shared-memory destination,
+// no completion to wait for). src and bytes must be multiples of 16.
+__device__ __forceinline__ void bulk_prefetch_l2(const void *src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(src)), "r"(bytes)
+                 : "memory");
+}
+
 // 2D tiled TMA load of box (c0 = innermost coordinate, c1 = row) into smem,
 // completing `bytes` on `bar`. c0 * elem_size must be a multiple of 16.
 __device__ __forceinline__ void tma_load_2d(void *smem_dst, const CUtensorMap *tm, uint64_t *bar, int c0, int c1) {

@@ -47,6 +47,10 @@ struct GemmParams {
     int num_kb;           // K blocks of 128 bytes
     int splits;
     int *err;             // error word (bounded wait ran out)
+    // optional: bytes the next kernel will stream (its weights), pulled into
+    // L2 while this GEMM runs; every CTA prefetches its share
+    const uint8_t *l2_prefetch = nullptr;
+    uint64_t l2_prefetch_bytes = 0;
 };
 
 struct Identity {
@@ -98,8 +102,10 @@ template <GemmKind kKind, int BN> struct GemmShape {
     static constexpr uint32_t kBBytes = BN * kUmmaKBytes;
     static constexpr uint32_t kStageBytes =
         kSplit3 ? 2u * (kABytes + kBBytes) : (kSplitB ? kABytes + 2u * kBBytes : kABytes + kBBytes);
-    // narrow token tiles (decode) run two CTAs per SM so that a split-K grid
-    // of up to 2 x SMs CTAs is resident in one wave
+    // narrow token tiles (decode) run two CTAs per SM: the hardware keeps two
+    // tensor-memory CTAs of this size resident (the occupancy calculator
+    // reports one for any kernel that allocates tensor memory), and a second
+    // CTA overlaps one CTA's prologue / epilogue with the other's stream
     static constexpr int kCtasPerSm = BN <= 64 ? 2 : 1;
     static constexpr int kBudget = kCtasPerSm == 2 ? 98 * 1024 : 192 * 1024;
     static constexpr int kStagesRaw = kBudget / static_cast<int>(kStageBytes);
@@ -200,6 +206,17 @@ __global__ void __launch_bounds__(192, GemmShape<kKind, BN>::kCtasPerSm)
             for (int j = 0; j < pre; ++j) {
                 mbar_arrive_expect_tx(&full[j], S::kStageBytes);
                 load_a(kb_begin + j, j);
+            }
+            if (p.l2_prefetch_bytes > 0) {
+                // this CTA's share of the next kernel's stream, in 16-byte
+                // multiples and chunks of at most 64 KB
+                const uint64_t ctas = static_cast<uint64_t>(gridDim.x) * gridDim.y * gridDim.z;
+                const uint64_t cta = (static_cast<uint64_t>(blockIdx.z) * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
+                const uint64_t share = ((p.l2_prefetch_bytes + ctas - 1) / ctas + 15) & ~uint64_t(15);
+                const uint64_t lo = min(p.l2_prefetch_bytes, cta * share);
+                const uint64_t hi = min(p.l2_prefetch_bytes, lo + share);
+                for (uint64_t o = lo; o < hi; o += 65536)
+                    bulk_prefetch_l2(p.l2_prefetch + o, static_cast<uint32_t>(hi - o < 65536 ? hi - o : 65536));
             }
             pdl_wait();
             for (int j = 0; j < pre; ++j)
@@ -480,7 +497,8 @@ inline int gemm_pick_splits(int tiles, int num_kb, int slots, int min_kb = 2, in
 // so only the row strides need 16-byte alignment.
 template <GemmKind kKind, typename Epi = Identity>
 inline void gemm_tn(const GemmOperand &A, const GemmOperand &B, int k, float *out, int64_t ldo, int splits,
-                    int64_t split_stride, cudaStream_t stream, const Epi &epi = {}, int force_bn = 0) {
+                    int64_t split_stride, cudaStream_t stream, const Epi &epi = {}, int force_bn = 0,
+                    const void *l2_prefetch = nullptr, uint64_t l2_prefetch_bytes = 0) {
     constexpr bool kBf16 = kKind != GemmKind::kTF32x3;
     constexpr int kKElems = kBf16 ? 64 : 32;
     detail::require(k > 0, "gemm_tn: K must be positive");
@@ -494,6 +512,10 @@ inline void gemm_tn(const GemmOperand &A, const GemmOperand &B, int k, float *ou
     p.num_kb = (k + kKElems - 1) / kKElems;
     p.splits = splits < 1 ? 1 : (splits > p.num_kb ? p.num_kb : splits);
     p.err = device_error_word();
+    detail::require(l2_prefetch_bytes == 0 || (reinterpret_cast<uintptr_t>(l2_prefetch) % 16 == 0),
+                    "gemm_tn: L2 prefetch range must be 16-byte aligned");
+    p.l2_prefetch = static_cast<const uint8_t *>(l2_prefetch);
+    p.l2_prefetch_bytes = l2_prefetch_bytes & ~uint64_t(15);
     int bn = force_bn ? force_bn : gemm_pick_bn(kKind, B.rows);
     if (!force_bn && p.splits == 1) {
         // narrow the token tile while the grid is under one wave

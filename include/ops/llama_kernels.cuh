@@ -21,6 +21,7 @@
 #include "../core/cuda_utils.cuh"
 #include "attention_kernels.cuh"
 #include "detail/operand_prep.cuh"
+#include "gemm_sm100.cuh"
 
 namespace opworks::detail {
 
@@ -29,11 +30,33 @@ constexpr int kRowThreads = 256;
 // Sum of the squares of a row held as kPer values per thread, block-wide.
 __device__ __forceinline__ float row_sumsq_block(float ss) { return block_reduce_all<ReduceSum>(ss); }
 
-// One CTA per token row; cols == kRowThreads * kPer.
+// Deferred RMSNorm of the residual stream (fast path). The per-token factor
+// rsqrt(sum(h^2) / H + eps) commutes with the projection that consumes the
+// normalised row, W (h * g * r) = r (W (h * g)), so the producer of h writes
+// the GEMM operand h * g (no norm yet) plus one partial sum of squares per
+// 128-feature tile, part[tile][row], and the consuming GEMM's epilogue scales
+// its output by r, summing the tiles in order (deterministic).
+struct RowSumSq {
+    float *part = nullptr; // [tiles][ld]
+    int64_t ld = 0;
+    int tiles = 0;
+    int cols = 0; // H
+    float eps = 0.f;
+    __device__ __forceinline__ float inv_rms(int64_t row) const {
+        float s = 0.f;
+        for (int t = 0; t < tiles; ++t)
+            s += part[t * ld + row];
+        return rsqrtf(s / static_cast<float>(cols) + eps);
+    }
+};
+
+// One CTA per token row; cols == kRowThreads * kPer. With rs.part set the
+// norm is deferred (see RowSumSq): out = h * w and part[0][row] = sum(h^2),
+// the other tiles 0.
 template <int kPer, typename WT>
 __global__ void __launch_bounds__(kRowThreads)
     embed_rmsnorm_kernel(const WT *__restrict__ table, const int *__restrict__ ids, float *__restrict__ hidden,
-                         const float *__restrict__ w, float eps, ActOut out, int cols) {
+                         const float *__restrict__ w, float eps, ActOut out, int cols, RowSumSq rs) {
     pdl_trigger();
     pdl_wait();
     const int64_t row = blockIdx.x;
@@ -47,7 +70,18 @@ __global__ void __launch_bounds__(kRowThreads)
         hidden[row * cols + c] = v[i];
         ss += v[i] * v[i];
     }
-    const float inv = rsqrtf(row_sumsq_block(ss) / cols + eps);
+    const float total = row_sumsq_block(ss);
+    if (rs.part) {
+        for (int t = threadIdx.x; t < rs.tiles; t += blockDim.x)
+            rs.part[t * rs.ld + row] = t == 0 ? total : 0.f;
+#pragma unroll
+        for (int i = 0; i < kPer; ++i) {
+            const int c = threadIdx.x + i * kRowThreads;
+            out.put(row, c, v[i] * w[c]);
+        }
+        return;
+    }
+    const float inv = rsqrtf(total / cols + eps);
 #pragma unroll
     for (int i = 0; i < kPer; ++i) {
         const int c = threadIdx.x + i * kRowThreads;
@@ -169,34 +203,95 @@ static __global__ void silu_mul_kernel(const float *__restrict__ part, int split
 // threads (tid), after the split-K reduction, plus 2 KB of shared scratch
 // filled by their optional prepare().
 
-// hidden[tok][f] += value: the o and down projections' residual add.
+// hidden[tok][f] += value: the o and down projections' residual add. With
+// `gain` set it also writes the next projection's operand h * gain (two-term
+// bf16) and, per token, the tile's partial sum of squares of h (RowSumSq).
 struct ResidualTileEpi {
     static constexpr bool kTile = true;
     float *hidden;
     int64_t ld;
+    const float *gain = nullptr;
+    ActOut normed{};
+    RowSumSq rs{};
     __device__ __forceinline__ void operator()(const float *tile, int tok0, int ntok, int f0, int nfeat, int tid,
-                                               void *) const {
-        for (int idx = tid; idx < ntok * 128; idx += 128) {
-            const int t = idx >> 7, c = idx & 127;
-            if (c < nfeat)
-                hidden[static_cast<int64_t>(tok0 + t) * ld + f0 + c] += tile[idx];
+                                               void *scratch) const {
+        // thread tid owns column tid of every token row of the tile
+        float *red = static_cast<float *>(scratch); // [4 warps][ntok] partial sums of squares
+        const int c = tid;
+        const bool col_ok = c < nfeat;
+        const float g = (gain && col_ok) ? gain[f0 + c] : 0.f;
+        for (int t = 0; t < ntok; ++t) {
+            float h = 0.f;
+            if (col_ok) {
+                float *p = hidden + static_cast<int64_t>(tok0 + t) * ld + f0 + c;
+                h = *p + tile[t * 128 + c];
+                *p = h;
+                if (gain)
+                    normed.put(tok0 + t, f0 + c, h * g);
+            }
+            if (rs.part) {
+                float sq = h * h;
+#pragma unroll
+                for (int off = 16; off > 0; off >>= 1)
+                    sq += __shfl_xor_sync(kFullWarpMask, sq, off);
+                if ((tid & 31) == 0)
+                    red[(tid >> 5) * ntok + t] = sq;
+            }
+        }
+        if (rs.part) {
+            sm100::epilogue_bar();
+            for (int t = tid; t < ntok; t += 128)
+                rs.part[(f0 / 128) * rs.ld + tok0 + t] = ((red[t] + red[ntok + t]) + red[2 * ntok + t]) + red[3 * ntok + t];
         }
     }
 };
 
 // Interleaved gate/up columns (2j = gate_j, 2j + 1 = up_j) -> act[tok][j] =
 // silu(g) * u = g / (1 + exp(-g)) * u, the expression of silu_mul_kernel.
+// With rs.part set the operand was h * gain (deferred norm): both columns are
+// first scaled by the token's rsqrt(mean(h^2) + eps).
 struct SiluMulTileEpi {
     static constexpr bool kTile = true;
     ActOut act;
+    RowSumSq rs{};
+    __device__ __forceinline__ void prepare(int tok0, int ntok, int, int, int tid, void *scratch) const {
+        float *inv = static_cast<float *>(scratch);
+        for (int t = tid; t < ntok; t += 128)
+            inv[t] = rs.part ? rs.inv_rms(tok0 + t) : 1.f;
+    }
     __device__ __forceinline__ void operator()(const float *tile, int tok0, int ntok, int f0, int nfeat, int tid,
-                                               void *) const {
+                                               void *scratch) const {
+        const float *inv = static_cast<const float *>(scratch);
         for (int idx = tid; idx < ntok * 64; idx += 128) {
             const int t = idx >> 6, j = idx & 63;
             if (2 * j + 1 < nfeat) {
-                const float g = tile[t * 128 + 2 * j], u = tile[t * 128 + 2 * j + 1];
+                const float g = tile[t * 128 + 2 * j] * inv[t], u = tile[t * 128 + 2 * j + 1] * inv[t];
                 act.put(tok0 + t, f0 / 2 + j, g / (1.f + expf(-g)) * u);
             }
+        }
+    }
+};
+
+// LM head logits out[tok][f] = value * rsqrt(mean(h^2) + eps) of the token
+// (deferred final norm); ss_row0 maps tile tokens to RowSumSq rows.
+struct LogitsTileEpi {
+    static constexpr bool kTile = true;
+    float *out;
+    int64_t ld;
+    RowSumSq rs;
+    int64_t ss_row0 = 0;
+    __device__ __forceinline__ void prepare(int tok0, int ntok, int, int, int tid, void *scratch) const {
+        float *inv = static_cast<float *>(scratch);
+        for (int t = tid; t < ntok; t += 128)
+            inv[t] = rs.inv_rms(ss_row0 + tok0 + t);
+    }
+    __device__ __forceinline__ void operator()(const float *tile, int tok0, int ntok, int f0, int nfeat, int tid,
+                                               void *scratch) const {
+        const float *inv = static_cast<const float *>(scratch);
+        for (int idx = tid; idx < ntok * 128; idx += 128) {
+            const int t = idx >> 7, c = idx & 127;
+            if (c < nfeat)
+                out[static_cast<int64_t>(tok0 + t) * ld + f0 + c] = tile[idx] * inv[t];
         }
     }
 };
@@ -215,14 +310,16 @@ struct QkvTileEpi {
     float *kpool, *vpool;
     // per token of the slice: position, KV block and slot in it (loaded while
     // the GEMM main loop streams)
+    RowSumSq rs{}; // deferred input norm when rs.part is set
     __device__ __forceinline__ void prepare(int tok0, int ntok, int, int, int tid, void *scratch) const {
-        int *meta = static_cast<int *>(scratch);
+        int *meta = static_cast<int *>(scratch); // [ntok][4]: pos, block, slot, rsqrt scale (float bits)
         for (int t = tid; t < ntok; t += 128) {
             const int64_t row = tok0 + t;
             const int pos = tm.pos[row];
-            meta[3 * t] = pos;
-            meta[3 * t + 1] = kv.table[static_cast<int64_t>(tm.seq[row]) * kv.table_stride + pos / kKvChunk];
-            meta[3 * t + 2] = pos % kKvChunk;
+            meta[4 * t] = pos;
+            meta[4 * t + 1] = kv.table[static_cast<int64_t>(tm.seq[row]) * kv.table_stride + pos / kKvChunk];
+            meta[4 * t + 2] = pos % kKvChunk;
+            meta[4 * t + 3] = __float_as_int(rs.part ? rs.inv_rms(row) : 1.f);
         }
     }
     __device__ __forceinline__ void operator()(const float *tile, int tok0, int ntok, int f0, int nfeat, int tid,
@@ -234,8 +331,9 @@ struct QkvTileEpi {
                 continue;
             const int head = f0 / kAttnD + hh;
             const int64_t row = tok0 + t;
-            const float a = tile[t * 128 + hh * 64 + i], b = tile[t * 128 + hh * 64 + i + 32];
-            const int pos = meta[3 * t];
+            const float sc = __int_as_float(meta[4 * t + 3]);
+            const float a = tile[t * 128 + hh * 64 + i] * sc, b = tile[t * 128 + hh * 64 + i + 32] * sc;
+            const int pos = meta[4 * t];
             if (head < qh) {
                 const float2 r = rope[static_cast<int64_t>(pos) * (kAttnD / 2) + i];
                 float *q = q_out + row * qh * kAttnD + head * kAttnD;
@@ -243,8 +341,8 @@ struct QkvTileEpi {
                 q[i + kAttnD / 2] = b * r.x + a * r.y;
                 continue;
             }
-            const int blk = meta[3 * t + 1];
-            const int slot = meta[3 * t + 2];
+            const int blk = meta[4 * t + 1];
+            const int slot = meta[4 * t + 2];
             if (head < qh + kvh) {
                 const float2 r = rope[static_cast<int64_t>(pos) * (kAttnD / 2) + i];
                 float *k = kpool + ((static_cast<int64_t>(blk) * kvh + (head - qh)) * kKvChunk + slot) * kAttnD;
