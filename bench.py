@@ -64,6 +64,10 @@ def parse():
     ap.add_argument("--batch", type=int, default=BATCH, help="sequences per GPU (C3: 32; smaller for profiling)")
     ap.add_argument("--ctx", type=int, default=CTX, help="prefilled context (C3: 2048; smaller for profiling)")
     ap.add_argument("--profile-iters", type=int, default=3)
+    ap.add_argument("--workload", choices=["c3", "c5"], default="c3",
+                    help="c3: batched decode (default, the headline); c5: 256-request serving, "
+                         "request-partitioned over the ranks")
+    ap.add_argument("--c5-max-batch", type=int, default=64, help="KV slots per GPU for c5 continuous batching")
     return ap.parse_args()
 
 
@@ -552,12 +556,87 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def run_c5(args):
+    """BASELINE C5: 256 requests (prompt lengths U[256, 1024], 256 sampled
+    tokens each, T=0.7 top-p 0.9) split over the ranks by the deterministic
+    LPT partition (opworks_b200/serving.py); every rank serves its share with
+    continuous batching on its GPU, no collective on the data path. Timed
+    on the device (CUDA events on each engine stream, max over ranks); value =
+    generated tokens of all requests / that time."""
+    import torch
+    import torch.distributed as dist
+
+    from opworks_b200 import pack, serving
+    from opworks_b200.llama import LlamaBatch, Model
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+    if rank == 0:
+        pack.ensure_random_llama_pack()
+    if world > 1:
+        dist.barrier()
+    pack_path = pack.ensure_random_llama_pack()
+    reqs = serving.c5_requests()
+    model = Model(pack_path, weight_sets=1, device=local)
+    eng = LlamaBatch(model, args.c5_max_batch, 1024 + 256 + 16, "fast", prefill_rows=1024)
+    stream = torch.cuda.ExternalStream(eng.stream())
+    # warm-up: module loads and the decode graphs of every batch size used
+    warm = [serving.Request(10_000 + i, list(range(300)), 2, 0.7, 0.9, i) for i in range(args.c5_max_batch)]
+    serving.Server(eng, args.c5_max_batch).run(warm)
+    for n in range(1, args.c5_max_batch + 1):
+        eng.decode(list(range(n)), [0] * n, temperature=0.7, top_p=0.9)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.perf_counter()
+    a.record(stream)
+    server = serving.Server(eng, args.c5_max_batch)
+    out = serving.serve_partitioned(reqs, rank, world, lambda: server, gather=False)
+    b.record(stream)
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - t0
+    ms = a.elapsed_time(b)
+    gen = sum(len(v) for v in out.values())
+    if world > 1:
+        t = torch.tensor([ms, wall, float(gen), float(server.prefill_tokens)], dtype=torch.float64, device="cuda")
+        tm = t.clone()
+        dist.all_reduce(tm, op=dist.ReduceOp.MAX)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        ms, wall = float(tm[0].item()), float(tm[1].item())
+        gen, pre = int(t[2].item()), int(t[3].item())
+    else:
+        pre = server.prefill_tokens
+    if rank == 0:
+        line = {"metric": "C5 serving: generated tok/s (256 requests, prompts U[256,1024], 256 new tokens)",
+                "value": round(gen / (ms / 1e3), 1), "unit": UNIT, "n_gpus": world, "higher_is_better": True,
+                "scaling": "strong", "ms": round(ms, 1), "wall_s": round(wall, 2), "generated_tokens": gen,
+                "prefill_tokens": pre, "requests": len(reqs),
+                "config": {"workload": "C5", "max_batch_per_gpu": args.c5_max_batch,
+                           "parallelism": f"request-partitioned x{world} (LPT by prompt + new tokens, no collective)",
+                           "sampling": "T=0.7 top-p 0.9 on the device"},
+                "dtype": "bf16", "data": "synthetic: random-init weights, uniform random prompt ids"}
+        print(json.dumps(line), flush=True)
+    eng.close()
+    model.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main():
     global BATCH, CTX
     args = parse()
     BATCH, CTX = args.batch, args.ctx
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "c5":
+        run_c5(args)
     else:
         run_ours(args)
 
