@@ -42,6 +42,7 @@
 
 #include "../core/cuda_utils.cuh"
 #include "../ops/attention_kernels.cuh"
+#include "../ops/attention_prefill_tc.cuh"
 #include "../ops/gemm_sm100.cuh"
 #include "../ops/linear.cuh"
 #include "../ops/llama_kernels.cuh"
@@ -593,7 +594,8 @@ template <typename WT> class LlamaEngineT {
     }
 
     template <int kRep>
-    void attention(int rows, bool decode, int slot, int pos0, const detail::PagedKV &kv, const detail::ActOut &out) {
+    void attention(int layer, int rows, bool decode, int slot, int pos0, const detail::PagedKV &kv,
+                   const detail::ActOut &out) {
         const float scale = 1.f / std::sqrt(static_cast<float>(cfg_.head_dim));
         const int kvh = cfg_.num_kv_heads, qw = cfg_.q_width();
         if (decode) {
@@ -602,6 +604,17 @@ template <typename WT> class LlamaEngineT {
             detail::attn_decode_launch<detail::PagedKV, kRep, detail::ActOut>(
                 q_.data(), qw, kv, dev_at<int32_t>(layout_.lens), rows, kvh, tps, splits, scale, attn_po_.data(),
                 attn_pml_.data(), out, stream_);
+        } else if (fast() && tc_prefill_) {
+            // tensor-core (TF32) flash attention over the paged cache
+            if (kv_maps_.empty()) {
+                for (int l = 0; l < cfg_.num_layers; ++l) {
+                    kv_maps_.push_back(detail::make_kv_pool_tmap(kv_.k(l), kv_.num_blocks, kvh, false));
+                    kv_maps_.push_back(detail::make_kv_pool_tmap(kv_.v(l), kv_.num_blocks, kvh, true));
+                }
+            }
+            detail::attn_prefill_tc_launch<kRep, detail::ActOut>(
+                q_.data(), qw, cfg_.num_q_heads, kv_maps_[2 * layer], kv_maps_[2 * layer + 1], kv.table,
+                kv.table_stride, kvh, slot, rows, pos0, scale, out, stream_);
         } else {
             detail::attn_prefill_launch<detail::PagedKV, kRep, detail::ActOut>(q_.data(), qw, detail::kAttnD, out, kv,
                                                                                slot, rows, pos0, kvh, scale, stream_);
@@ -651,10 +664,10 @@ template <typename WT> class LlamaEngineT {
                 mark("qkv_rope_kv_write");
             }
             switch (cfg_.kv_rep()) {
-            case 1: attention<1>(rows, decode, slot, pos0, kv, attn_o); break;
-            case 2: attention<2>(rows, decode, slot, pos0, kv, attn_o); break;
-            case 4: attention<4>(rows, decode, slot, pos0, kv, attn_o); break;
-            default: attention<8>(rows, decode, slot, pos0, kv, attn_o); break;
+            case 1: attention<1>(l, rows, decode, slot, pos0, kv, attn_o); break;
+            case 2: attention<2>(l, rows, decode, slot, pos0, kv, attn_o); break;
+            case 4: attention<4>(l, rows, decode, slot, pos0, kv, attn_o); break;
+            default: attention<8>(l, rows, decode, slot, pos0, kv, attn_o); break;
             }
             mark("attention");
             if (fast()) {
@@ -757,6 +770,13 @@ template <typename WT> class LlamaEngineT {
     int32_t *out_host_ = nullptr;
     std::map<int, cudaGraphExec_t> graphs_;
     bool marks_enabled_ = false;
+    // tensor-core prefill attention on the fast path (OPWORKS_TC_PREFILL=0:
+    // the fp32 SIMT kernel instead); tensor maps of the layers' KV pools
+    bool tc_prefill_ = [] {
+        const char *e = std::getenv("OPWORKS_TC_PREFILL");
+        return !(e && e[0] == '0');
+    }();
+    std::vector<CUtensorMap> kv_maps_;
     // upper bound on the K splits (one cluster) of the fused GEMMs: the
     // portable 8 measured fastest at C3 (4 and 16 were slower);
     // OPWORKS_CLUSTER_SPLITS overrides it (up to 16, non-portable clusters)

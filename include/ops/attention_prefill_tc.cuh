@@ -1,0 +1,392 @@
+#pragma once
+
+// Causal GQA prefill attention on the 5th-generation tensor cores (sm_100a).
+//
+// One CTA owns 128 query rows of one KV head: 128 / kRep positions x the kRep
+// query heads that share the KV head (rows ordered position-major, exactly as
+// a 3-D TMA box {32 dims, kRep heads, 128 / kRep positions} lands them). It
+// walks the KV range in 128-key tiles staged by TMA straight from the paged
+// fp32 cache (16-token pages, one 2 KB box per page and 32-dim half).
+//
+//   S = Q K^T   tcgen05.mma kind::tf32, A = Q (K-major, smem), B = K (K-major,
+//               smem: the cache's [token][dim] rows), D in TMEM (128 x 128)
+//   P = softmax  4 warps, one TMEM lane (query row) per thread, scores in log2
+//               units (exp2 on the SFU), causal mask, running max / sum
+//   O += P V    tcgen05.mma kind::tf32, A = P (TMEM, written back over S),
+//               B = V (MN-major smem: the same [token][dim] rows), D in TMEM
+//               (128 x 64); the softmax warps fold each tile's P V into fp32
+//               registers with the running rescale
+//
+// Roles (192 threads): warp 0 TMA producer (one lane), warp 1 TMEM allocator
+// and single-thread MMA issuer, warps 2-5 softmax + epilogue. S is
+// double-buffered in TMEM, so QK^T of tile n+1 runs while tile n's softmax
+// does. Every mbarrier wait is bounded (device error word on timeout).
+//
+// Precision: TF32 operands (10-bit mantissa) with fp32 accumulation; used by
+// the fast (bf16-weight) model path only.
+
+#include "attention_kernels.cuh"
+#include "detail/sm100.cuh"
+
+namespace opworks::detail {
+
+constexpr int kPfKvTile = 128;   // keys per KV tile (8 pages)
+constexpr int kPfStages = 2;     // KV tiles in flight
+constexpr int kPfThreads = 192;  // warp 0 TMA, warp 1 MMA, warps 2-5 softmax
+constexpr uint32_t kPfTmemCols = 512; // S0 [0,128), S1 [128,256), O [256,320)
+
+struct PrefillTcSmem {
+    static constexpr uint32_t kSlab = 128 * 128;          // [128 rows][32 fp32], 16 KB
+    static constexpr uint32_t kQBytes = 2 * kSlab;         // dims 0-31, 32-63
+    static constexpr uint32_t kStageBytes = 4 * kSlab;     // K halves, V halves
+    static constexpr size_t kBytes = 1024 + kQBytes + kPfStages * kStageBytes + 256;
+};
+
+// Shared-memory descriptor of an MN-major tf32 operand: MN-major 32-bit
+// operands take the 128-byte swizzle with 32-byte atomicity (layout type 1,
+// SWIZZLE_128B_BASE32B; atoms of 4 K-rows x 128 bytes along MN, as a TMA load
+// with CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B writes them): `lbo` = bytes between
+// atoms adjacent along MN, `sbo` = bytes between 4-row groups along K.
+__device__ __forceinline__ uint64_t sdesc_mn128_32b(uint32_t smem_addr, uint32_t lbo, uint32_t sbo) {
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((smem_addr & 0x3FFFFu) >> 4);
+    d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+    d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
+    d |= static_cast<uint64_t>(1u) << 46;
+    d |= static_cast<uint64_t>(1u) << 61;
+    return d;
+}
+
+// D[tmem] (+)= A[tmem] * B[smem desc], tf32 (A from tensor memory, K-major).
+__device__ __forceinline__ void umma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                             uint32_t accumulate) {
+    asm volatile("{\n\t.reg .pred p;\n\t"
+                 "setp.ne.b32 p, %4, 0;\n\t"
+                 "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+                 "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_st_32x16(uint32_t taddr, const uint32_t (&r)[16]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+                 "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+                 "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+                 "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ void tma_load_3d(void *smem_dst, const CUtensorMap *tm, uint64_t *bar, int c0, int c1,
+                                            int c2) {
+    asm volatile("cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+                 " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(sm100::smem_u32(smem_dst)),
+                 "l"(reinterpret_cast<uint64_t>(tm)), "r"(sm100::smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+                 : "memory");
+}
+
+// Causal prefill of `T` query rows of sequence `b` (absolute positions
+// q_offset + t), grid = (ceil(T / (128 / kRep)), kvh); the heaviest query
+// tiles are scheduled first. tmQ covers q as {64 dims, qh heads, T rows};
+// tmK / tmV cover the KV pool as {64 dims, 16 tokens, blocks * kvh}.
+template <int kRep, typename Out>
+__global__ void __launch_bounds__(kPfThreads, 1)
+    attn_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                           const __grid_constant__ CUtensorMap tmV, const int *__restrict__ table, int table_stride,
+                           int kvh, int b, int T, int q_offset, float scale, Out out, int *err) {
+    using SM = PrefillTcSmem;
+    constexpr int kPos = 128 / kRep; // query positions per CTA
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *qs = smem;
+    uint8_t *stages = smem + SM::kQBytes;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(stages + kPfStages * SM::kStageBytes);
+    uint64_t *full_q = bars;
+    uint64_t *full_kv = bars + 1;              // [kPfStages]
+    uint64_t *empty_kv = full_kv + kPfStages;  // [kPfStages]
+    uint64_t *s_ready = empty_kv + kPfStages;  // [2]
+    uint64_t *p_ready = s_ready + 2;           // [2]
+    uint64_t *o_ready = p_ready + 2;
+    uint64_t *o_free = o_ready + 1;
+    uint64_t *drain = o_free + 1;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+
+    const int warp = threadIdx.x / kWarpSize, lane = threadIdx.x % kWarpSize;
+    const int qt = static_cast<int>(gridDim.x) - 1 - static_cast<int>(blockIdx.x); // heaviest first
+    const int h = blockIdx.y;
+    const int t0 = qt * kPos;
+    const int t_last = min(T, t0 + kPos) - 1;           // last query row of the tile
+    const int keys = q_offset + t_last + 1;             // keys any row of the tile may see
+    const int n_tiles = (keys + kPfKvTile - 1) / kPfKvTile;
+    const int last_page = (keys - 1) / kKvChunk;
+
+    if (threadIdx.x == 0) {
+        sm100::mbar_init(full_q, 1);
+        for (int s = 0; s < kPfStages; ++s) {
+            sm100::mbar_init(&full_kv[s], 1);
+            sm100::mbar_init(&empty_kv[s], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            sm100::mbar_init(&s_ready[i], 1);
+            sm100::mbar_init(&p_ready[i], 128);
+        }
+        sm100::mbar_init(o_ready, 1);
+        sm100::mbar_init(o_free, 128);
+        sm100::mbar_init(drain, 1);
+        sm100::fence_mbarrier_init();
+        sm100::prefetch_tmap(&tmQ);
+        sm100::prefetch_tmap(&tmK);
+        sm100::prefetch_tmap(&tmV);
+    }
+    if (warp == 1) {
+        sm100::tmem_alloc(tmem_slot, kPfTmemCols);
+        sm100::tmem_relinquish();
+    }
+    pdl_trigger();
+    sm100::tc_fence_before();
+    __syncthreads();
+    sm100::tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    bool ok = true;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            pdl_wait(); // q and the cache are written by earlier kernels
+            sm100::mbar_arrive_expect_tx(full_q, SM::kQBytes);
+            tma_load_3d(qs, &tmQ, full_q, 0, h * kRep, t0);
+            tma_load_3d(qs + SM::kSlab, &tmQ, full_q, 32, h * kRep, t0);
+            int issued = 0;
+            for (int n = 0; n < n_tiles; ++n, ++issued) {
+                const int s = n % kPfStages;
+                if (n >= kPfStages &&
+                    !sm100::mbar_wait(&empty_kv[s], static_cast<uint32_t>((n / kPfStages) - 1) & 1u)) {
+                    ok = false;
+                    break;
+                }
+                uint8_t *st = stages + s * SM::kStageBytes;
+                sm100::mbar_arrive_expect_tx(&full_kv[s], SM::kStageBytes);
+                for (int pg = 0; pg < kPfKvTile / kKvChunk; ++pg) {
+                    // pages past the last key still load (a valid page): their
+                    // keys are masked and P = 0 there
+                    const int page = min(n * (kPfKvTile / kKvChunk) + pg, last_page);
+                    const int blk = table[static_cast<int64_t>(b) * table_stride + page];
+                    const int row = blk * kvh + h;
+                    const uint32_t off = static_cast<uint32_t>(pg) * kKvChunk * 128;
+                    tma_load_3d(st + off, &tmK, &full_kv[s], 0, 0, row);
+                    tma_load_3d(st + SM::kSlab + off, &tmK, &full_kv[s], 32, 0, row);
+                    tma_load_3d(st + 2 * SM::kSlab + off, &tmV, &full_kv[s], 0, 0, row);
+                    tma_load_3d(st + 3 * SM::kSlab + off, &tmV, &full_kv[s], 32, 0, row);
+                }
+            }
+            // no copy may be in flight when the CTA exits
+            if (!sm100::mbar_wait(full_q, 0))
+                ok = false;
+            for (int j = (issued > kPfStages ? issued - kPfStages : 0); j < issued; ++j)
+                if (!sm100::mbar_wait(&full_kv[j % kPfStages], static_cast<uint32_t>(j / kPfStages) & 1u))
+                    ok = false;
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idesc_s = sm100::idesc_make(sm100::kFmtTF32, 128, kPfKvTile);
+            constexpr uint32_t idesc_o = sm100::idesc_make(sm100::kFmtTF32, 128, 64) | (1u << 16); // B MN-major
+            const uint32_t qa = sm100::smem_u32(qs);
+            auto issue_s = [&](int n) {
+                const int s = n % kPfStages;
+                const uint32_t kb = sm100::smem_u32(stages + s * SM::kStageBytes);
+                const uint32_t d = tmem + static_cast<uint32_t>((n & 1) * kPfKvTile);
+                for (int ks = 0; ks < 8; ++ks) { // 8 dims per step: 2 halves x 4 steps of 32 bytes
+                    const uint32_t o = static_cast<uint32_t>(ks / 4) * SM::kSlab + static_cast<uint32_t>(ks % 4) * 32u;
+                    sm100::umma_tf32(d, sm100::sdesc_k128(qa + o), sm100::sdesc_k128(kb + o), idesc_s, ks > 0);
+                }
+                sm100::umma_commit(&s_ready[n & 1]);
+            };
+            if (!sm100::mbar_wait(full_q, 0)) {
+                ok = false;
+            } else if (n_tiles > 0) {
+                if (!sm100::mbar_wait(&full_kv[0], 0)) {
+                    ok = false;
+                } else {
+                    sm100::tc_fence_after();
+                    issue_s(0);
+                }
+            }
+            for (int n = 0; ok && n < n_tiles; ++n) {
+                if (n + 1 < n_tiles) {
+                    const int s1 = (n + 1) % kPfStages;
+                    if (!sm100::mbar_wait(&full_kv[s1], static_cast<uint32_t>((n + 1) / kPfStages) & 1u)) {
+                        ok = false;
+                        break;
+                    }
+                    sm100::tc_fence_after();
+                    issue_s(n + 1);
+                }
+                if (!sm100::mbar_wait(&p_ready[n & 1], static_cast<uint32_t>(n >> 1) & 1u) ||
+                    (n > 0 && !sm100::mbar_wait(o_free, static_cast<uint32_t>(n - 1) & 1u))) {
+                    ok = false;
+                    break;
+                }
+                sm100::tc_fence_after();
+                const int s = n % kPfStages;
+                const uint32_t vb = sm100::smem_u32(stages + s * SM::kStageBytes + 2 * SM::kSlab);
+                const uint32_t pa = tmem + static_cast<uint32_t>((n & 1) * kPfKvTile);
+                for (int ks = 0; ks < kPfKvTile / 8; ++ks) // 8 keys per step = one 1 KB row group of V
+                    umma_tf32_ts(tmem + 256u, pa + static_cast<uint32_t>(ks * 8),
+                                 sdesc_mn128_32b(vb + static_cast<uint32_t>(ks) * 1024u, SM::kSlab, 512u), idesc_o, ks > 0);
+                sm100::umma_commit(o_ready);
+                sm100::umma_commit(&empty_kv[s]);
+            }
+            // every issued MMA completes before tensor memory is released
+            sm100::umma_commit(drain);
+            if (!sm100::mbar_wait(drain, 0))
+                ok = false;
+        }
+    } else {
+        // softmax warps: thread = TMEM lane = query row
+        const int quarter = warp & 3;
+        const int r = quarter * 32 + lane;
+        const int p = r / kRep, hh = r % kRep;
+        const int t = t0 + p;
+        const int qpos = q_offset + t;
+        const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
+        const float c = scale * kLog2e;
+        float m_run = kNegInf, l_run = 0.f;
+        float o[64];
+#pragma unroll
+        for (int i = 0; i < 64; ++i)
+            o[i] = 0.f;
+        for (int n = 0; n < n_tiles; ++n) {
+            const uint32_t sb = tmem + lane_addr + static_cast<uint32_t>((n & 1) * kPfKvTile);
+            if (!sm100::mbar_wait_warp(&s_ready[n & 1], static_cast<uint32_t>(n >> 1) & 1u)) {
+                ok = false;
+                break;
+            }
+            sm100::tc_fence_after();
+            const int k0 = n * kPfKvTile;
+            float mt = kNegInf;
+            uint32_t v[kPfKvTile];
+#pragma unroll
+            for (int cc = 0; cc < kPfKvTile / 16; ++cc) {
+                uint32_t rr[16];
+                sm100::tmem_ld_32x16(sb + static_cast<uint32_t>(cc * 16), rr);
+                sm100::tmem_wait_ld();
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    const int j = cc * 16 + i;
+                    const float sv = k0 + j <= qpos ? __uint_as_float(rr[i]) * c : kNegInf;
+                    v[j] = __float_as_uint(sv);
+                    mt = fmaxf(mt, sv);
+                }
+            }
+            const float m_new = fmaxf(m_run, mt);
+            const float alpha = m_run == kNegInf ? 0.f : exp2_approx(m_run - m_new);
+            float lsum = 0.f;
+#pragma unroll
+            for (int cc = 0; cc < kPfKvTile / 16; ++cc) {
+                uint32_t ww[16];
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    const float sv = __uint_as_float(v[cc * 16 + i]);
+                    const float pv = m_new == kNegInf ? 0.f : exp2_approx(sv - m_new);
+                    lsum += pv;
+                    ww[i] = __float_as_uint(pv);
+                }
+                tmem_st_32x16(sb + static_cast<uint32_t>(cc * 16), ww);
+            }
+            tmem_wait_st();
+            l_run = l_run * alpha + lsum;
+            m_run = m_new;
+            sm100::tc_fence_before();
+            sm100::mbar_arrive(&p_ready[n & 1]);
+            // fold this tile's P V into the running output
+            if (!sm100::mbar_wait_warp(o_ready, static_cast<uint32_t>(n) & 1u)) {
+                ok = false;
+                break;
+            }
+            sm100::tc_fence_after();
+#pragma unroll
+            for (int cc = 0; cc < 4; ++cc) {
+                uint32_t rr[16];
+                sm100::tmem_ld_32x16(tmem + lane_addr + 256u + static_cast<uint32_t>(cc * 16), rr);
+                sm100::tmem_wait_ld();
+#pragma unroll
+                for (int i = 0; i < 16; ++i)
+                    o[cc * 16 + i] = o[cc * 16 + i] * alpha + __uint_as_float(rr[i]);
+            }
+            sm100::tc_fence_before();
+            sm100::mbar_arrive(o_free);
+        }
+        if (ok && t < T) {
+            const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+#pragma unroll
+            for (int d = 0; d < 64; d += 4)
+                out.put4(t, h * kRep + hh, d, o[d] * inv, o[d + 1] * inv, o[d + 2] * inv, o[d + 3] * inv);
+        }
+    }
+    if (!ok)
+        atomicExch(err, 4);
+    sm100::tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        sm100::tc_fence_after();
+        sm100::tmem_dealloc(tmem, kPfTmemCols);
+    }
+}
+
+// 3-D fp32 tensor map with a 128-byte-wide innermost box (32 floats) and
+// 128B swizzle: dims / strides in elements / bytes, innermost first.
+inline CUtensorMap make_tmap_3d_f32(const void *base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t stride1_bytes,
+                                    uint64_t stride2_bytes, uint32_t box1, uint32_t box2,
+                                    CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
+    require(reinterpret_cast<uintptr_t>(base) % 16 == 0, "TMA base must be 16-byte aligned");
+    require(stride1_bytes % 16 == 0 && stride2_bytes % 16 == 0, "TMA strides must be multiples of 16 bytes");
+    CUtensorMap tm;
+    std::memset(&tm, 0, sizeof(tm));
+    const cuuint64_t dims[3] = {d0, d1, d2};
+    const cuuint64_t strides[2] = {stride1_bytes, stride2_bytes};
+    const cuuint32_t box[3] = {32, box1, box2};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    const CUresult r = sm100::tensor_map_encoder()(&tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void *>(base),
+                                                   dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                                   swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    require(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (3-D) failed");
+    return tm;
+}
+
+// Tensor maps of one K or V pool [blocks][kvh][16][64] fp32: K pages land in
+// the K-major 128B-swizzle layout, V pages in the MN-major one (32-byte
+// swizzle atoms).
+inline CUtensorMap make_kv_pool_tmap(const float *pool, int64_t blocks, int kvh, bool v_operand) {
+    return make_tmap_3d_f32(pool, kAttnD, kKvChunk, static_cast<uint64_t>(blocks) * kvh, kAttnD * 4,
+                            kKvChunk * kAttnD * 4, kKvChunk, 1,
+                            v_operand ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+template <int kRep, typename Out> inline void prepare_prefill_tc_kernel() {
+    static thread_local int done = -1;
+    int dev = 0;
+    OPWORKS_CUDA_CHECK(cudaGetDevice(&dev));
+    if (done != dev) {
+        OPWORKS_CUDA_CHECK(cudaFuncSetAttribute(attn_prefill_tc_kernel<kRep, Out>,
+                                                cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                static_cast<int>(PrefillTcSmem::kBytes)));
+        done = dev;
+    }
+}
+
+// q: [T][qh * 64] fp32 rows with row stride q_tok floats; kmap / vmap from
+// make_kv_pool_tmap of the layer's pools.
+template <int kRep, typename Out>
+inline void attn_prefill_tc_launch(const float *q, int64_t q_tok, int qh, const CUtensorMap &kmap,
+                                   const CUtensorMap &vmap, const int *table, int table_stride, int kvh, int b, int T,
+                                   int q_offset, float scale, const Out &out, cudaStream_t stream) {
+    static_assert(kRep == 1 || kRep == 2 || kRep == 4 || kRep == 8, "GQA ratio must divide 128 rows");
+    require(T > 0 && qh == kvh * kRep, "prefill attention: bad shape");
+    prepare_prefill_tc_kernel<kRep, Out>();
+    const CUtensorMap qmap = make_tmap_3d_f32(q, kAttnD, static_cast<uint64_t>(qh), static_cast<uint64_t>(T),
+                                              kAttnD * 4, static_cast<uint64_t>(q_tok) * 4, kRep, 128 / kRep);
+    const dim3 grid((T + 128 / kRep - 1) / (128 / kRep), kvh);
+    launch_ex(attn_prefill_tc_kernel<kRep, Out>, grid, dim3(kPfThreads), PrefillTcSmem::kBytes, stream, qmap, kmap,
+              vmap, table, table_stride, kvh, b, T, q_offset, scale, out, sm100::device_error_word());
+}
+
+} // namespace opworks::detail

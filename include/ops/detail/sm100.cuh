@@ -86,6 +86,13 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
     }
 }
 
+// mbar_wait by every lane of a warp, with a warp-uniform result: code that
+// follows a failed wait (and skips tcgen05 warp-collective instructions)
+// stays convergent even if the lanes' deadlines fell on both sides.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t *bar, uint32_t parity) {
+    return __all_sync(0xffffffffu, mbar_wait(bar, parity));
+}
+
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap *tm) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tm)) : "memory");
 }

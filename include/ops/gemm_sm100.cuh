@@ -321,7 +321,7 @@ __global__ void __launch_bounds__(192, GemmShape<kKind, BN>::kCtasPerSm)
                 acc[i] = 0.f;
             const int ngroups = (kb_end - kb_begin + S::kPromoteKb - 1) / S::kPromoteKb;
             for (int g = 0; g < ngroups; ++g) {
-                if (!mbar_wait(&ready[g & 1], static_cast<uint32_t>(g >> 1) & 1u)) {
+                if (!mbar_wait_warp(&ready[g & 1], static_cast<uint32_t>(g >> 1) & 1u)) {
                     ok = false;
                     break;
                 }
@@ -347,7 +347,7 @@ __global__ void __launch_bounds__(192, GemmShape<kKind, BN>::kCtasPerSm)
                     out[static_cast<int64_t>(tok) * p.ldo + feat] = apply_epilogue(epi, acc[i], tok, feat);
             }
         } else {
-        if (!mbar_wait(accum, 0)) {
+        if (!mbar_wait_warp(accum, 0)) {
             ok = false;
         }
         tc_fence_after();

@@ -120,6 +120,16 @@ OPW_API int opw_sample(const float *logits, int rows, int vocab, const float *te
 OPW_API int opw_paged_attention_decode(const float *q, const float *kpool, const float *vpool,
                                        const int32_t *block_table, int table_stride, const int32_t *lens, int B,
                                        int max_len, int num_q_heads, int num_kv_heads, float *out, void *stream);
+/* Causal GQA prefill attention of query rows [0, T) of sequence b (absolute
+ * positions q_offset + t) over a paged fp32 KV pool [num_blocks][kvh][16][64]
+ * with block_table[b * table_stride + page]; q and out are [T][num_q_heads *
+ * 64] fp32; head_dim 64, scale 1/8. tensor_cores = 1: TF32 tcgen05 flash
+ * attention (include/ops/attention_prefill_tc.cuh); 0: the fp32 SIMT kernel.
+ * Extension of this library (no reference counterpart; the reference's
+ * prefill attention is ops::attention_prefill_chunked over contiguous K/V). */
+OPW_API int opw_paged_attention_prefill(const float *q, const float *kpool, const float *vpool, const int32_t *block_table,
+                                        int table_stride, int num_blocks, int b, int T, int q_offset, int num_q_heads,
+                                        int num_kv_heads, float *out, int tensor_cores, void *stream);
 /* out[split][M][N] (fp32 partials) = W[N][K] (bf16) . (Xhi + Xlo)[M][K]^T with
  * the runtime's two-term bf16 activation GEMM; splits = 0 picks the runtime's
  * split-K plan. Returns the split count used, or -1. */

@@ -33,6 +33,10 @@ struct KvCache {
         : max_seq_len(max_seq_len_), num_layers(cfg.num_layers), kv_heads(cfg.num_kv_heads),
           head_dim(cfg.head_dim), num_blocks(num_blocks_) {
         pool = TypedDeviceBuffer<float>(static_cast<int64_t>(num_layers) * 2 * num_blocks * block_floats());
+        // tensor-core prefill stages whole 16-token pages, including slots
+        // past a sequence's end (masked, weight 0): they must hold finite values
+        if (pool.size() > 0)
+            OPWORKS_CUDA_CHECK(cudaMemset(pool.data(), 0, sizeof(float) * static_cast<size_t>(pool.size())));
     }
     KvCache(const KvCache &) = delete;
     KvCache &operator=(const KvCache &) = delete;

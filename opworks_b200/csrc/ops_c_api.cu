@@ -13,6 +13,7 @@
 #include "ops/argmax.cuh"
 #include "ops/attention_decode.cuh"
 #include "ops/attention_prefill.cuh"
+#include "ops/attention_prefill_tc.cuh"
 #include "ops/causal_scale.cuh"
 #include "ops/embedding.cuh"
 #include "ops/linear.cuh"
@@ -323,6 +324,41 @@ int opw_paged_attention_decode(const float *q, const float *kpool, const float *
         case 4: attn_decode_launch<PagedKV, 4>(q, num_q_heads * kAttnD, kv, lens, B, num_kv_heads, tps, splits, scale, part_o, part_ml, o, as_stream(stream)); break;
         case 8: attn_decode_launch<PagedKV, 8>(q, num_q_heads * kAttnD, kv, lens, B, num_kv_heads, tps, splits, scale, part_o, part_ml, o, as_stream(stream)); break;
         default: throw std::invalid_argument("paged attention: GQA ratio must be 1, 2, 4 or 8");
+        }
+    });
+}
+
+int opw_paged_attention_prefill(const float *q, const float *kpool, const float *vpool, const int32_t *block_table,
+                                int table_stride, int num_blocks, int b, int T, int q_offset, int num_q_heads,
+                                int num_kv_heads, float *out, int tensor_cores, void *stream) {
+    return guarded([&] {
+        using namespace opworks::detail;
+        require(T > 0 && q_offset >= 0 && num_kv_heads > 0 && num_q_heads % num_kv_heads == 0 && num_blocks > 0,
+                "paged prefill attention: bad shape");
+        require(q && kpool && vpool && block_table && out, "paged prefill attention: null pointer");
+        const int rep = num_q_heads / num_kv_heads;
+        const float scale = 0.125f;
+        const int64_t qw = static_cast<int64_t>(num_q_heads) * kAttnD;
+        const StridedOut<float> o{out, qw, kAttnD};
+        if (tensor_cores) {
+            const CUtensorMap km = make_kv_pool_tmap(kpool, num_blocks, num_kv_heads, false);
+            const CUtensorMap vm = make_kv_pool_tmap(vpool, num_blocks, num_kv_heads, true);
+            switch (rep) {
+            case 1: attn_prefill_tc_launch<1>(q, qw, num_q_heads, km, vm, block_table, table_stride, num_kv_heads, b, T, q_offset, scale, o, as_stream(stream)); break;
+            case 2: attn_prefill_tc_launch<2>(q, qw, num_q_heads, km, vm, block_table, table_stride, num_kv_heads, b, T, q_offset, scale, o, as_stream(stream)); break;
+            case 4: attn_prefill_tc_launch<4>(q, qw, num_q_heads, km, vm, block_table, table_stride, num_kv_heads, b, T, q_offset, scale, o, as_stream(stream)); break;
+            case 8: attn_prefill_tc_launch<8>(q, qw, num_q_heads, km, vm, block_table, table_stride, num_kv_heads, b, T, q_offset, scale, o, as_stream(stream)); break;
+            default: throw std::invalid_argument("paged prefill attention: GQA ratio must be 1, 2, 4 or 8");
+            }
+        } else {
+            const PagedKV kv{kpool, vpool, block_table, table_stride, num_kv_heads};
+            switch (rep) {
+            case 1: attn_prefill_launch<PagedKV, 1>(q, qw, kAttnD, o, kv, b, T, q_offset, num_kv_heads, scale, as_stream(stream)); break;
+            case 2: attn_prefill_launch<PagedKV, 2>(q, qw, kAttnD, o, kv, b, T, q_offset, num_kv_heads, scale, as_stream(stream)); break;
+            case 4: attn_prefill_launch<PagedKV, 4>(q, qw, kAttnD, o, kv, b, T, q_offset, num_kv_heads, scale, as_stream(stream)); break;
+            case 8: attn_prefill_launch<PagedKV, 8>(q, qw, kAttnD, o, kv, b, T, q_offset, num_kv_heads, scale, as_stream(stream)); break;
+            default: throw std::invalid_argument("paged prefill attention: GQA ratio must be 1, 2, 4 or 8");
+            }
         }
     });
 }
