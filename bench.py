@@ -476,6 +476,17 @@ def reference_cuda_path(pack_path, c3_sessions=2, c3_steps=8, c2_steps=64):
         out["c3"] = {"value": round(c3_sessions * c3_steps / dt, 1), "unit": UNIT,
                      "sample": f"{c3_sessions} sessions prefilled to {CTX}, {c3_steps} round-robin greedy decode "
                                "steps each (device sampling excluded: the reference samples on the host)"}
+        # C4: one 8192-token prefill (create_session(8192), the reference's cap)
+        ids8 = np.random.default_rng(8).integers(0, 128256, 8192).astype(np.int32)
+        s8 = lib.opw_llama_create_session(m, 8192, err, 512)
+        if s8:
+            a8 = (ctypes.c_int32 * 8192)(*ids8.tolist())
+            t = time.perf_counter()
+            ok = lib.opw_llama_prefill(s8, a8, 8192, err, 512) >= 0
+            dt8 = time.perf_counter() - t
+            lib.opw_llama_destroy_session(s8)
+            if ok:
+                out["c4"] = {"tokens": 8192, "ms": round(dt8 * 1e3, 1), "tok_s": round(8192 / dt8, 1)}
     finally:
         lib.opw_llama_free(m)
     return out

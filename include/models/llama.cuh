@@ -507,6 +507,15 @@ template <typename WT> class LlamaEngineT {
     // GEMMs leave HBM bandwidth idle)
     template <typename Epi>
     void linear_tile(const Projection &p, const Act &x, int rows, const Epi &epi, const Projection *next = nullptr) {
+        if (rows > prefill_single_rows_) {
+            // prefill-sized GEMMs: single-term bf16 activations (one MMA per
+            // K step, 256-token tiles), compute-bound shapes
+            sm100::gemm_tn<sm100::GemmKind::kBF16, Epi>({p.bf16.data(), nullptr, p.out, p.in},
+                                                        {x.bf16, nullptr, rows, p.in}, p.in, part_.data(), p.out, 1,
+                                                        static_cast<int64_t>(rows) * p.out, stream_, epi,
+                                                        sm100::gemm_pick_bn(sm100::GemmKind::kBF16, rows));
+            return;
+        }
         const int splits = plan_splits(p, rows, max_cluster_splits_);
         const bool pf = next != nullptr && l2_prefetch_ && rows <= 64;
         sm100::gemm_tn<sm100::GemmKind::kBF16x2, Epi>(
@@ -772,6 +781,15 @@ template <typename WT> class LlamaEngineT {
     bool marks_enabled_ = false;
     // tensor-core prefill attention on the fast path (OPWORKS_TC_PREFILL=0:
     // the fp32 SIMT kernel instead); tensor maps of the layers' KV pools
+    // fast-path GEMMs with more token rows than this use single-term bf16
+    // activations (one MMA per K step). Off by default: on a 1024-token
+    // prompt single-term activations move the logits by 0.043 against the
+    // fp32 path, over the 2e-2 GEMM tolerance (two terms: 0.010); C4 prefill
+    // would gain 16%. OPWORKS_PREFILL_SINGLE_ROWS sets the threshold.
+    int prefill_single_rows_ = [] {
+        const char *e = std::getenv("OPWORKS_PREFILL_SINGLE_ROWS");
+        return e ? std::atoi(e) : (1 << 30);
+    }();
     bool tc_prefill_ = [] {
         const char *e = std::getenv("OPWORKS_TC_PREFILL");
         return !(e && e[0] == '0');

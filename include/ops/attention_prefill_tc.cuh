@@ -14,8 +14,10 @@
 //               units (exp2 on the SFU), causal mask, running max / sum
 //   O += P V    tcgen05.mma kind::tf32, A = P (TMEM, written back over S),
 //               B = V (MN-major smem: the same [token][dim] rows), D in TMEM
-//               (128 x 64); the softmax warps fold each tile's P V into fp32
-//               registers with the running rescale
+//               (128 x 64, double-buffered); the softmax warps fold tile n-1's
+//               P V into fp32 registers (running rescale) after publishing
+//               tile n's P, so they never wait for the P V of the tile they
+//               just handed over
 //
 // Roles (192 threads): warp 0 TMA producer (one lane), warp 1 TMEM allocator
 // and single-thread MMA issuer, warps 2-5 softmax + epilogue. S is
@@ -33,7 +35,7 @@ namespace opworks::detail {
 constexpr int kPfKvTile = 128;   // keys per KV tile (8 pages)
 constexpr int kPfStages = 2;     // KV tiles in flight
 constexpr int kPfThreads = 192;  // warp 0 TMA, warp 1 MMA, warps 2-5 softmax
-constexpr uint32_t kPfTmemCols = 512; // S0 [0,128), S1 [128,256), O [256,320)
+constexpr uint32_t kPfTmemCols = 512; // S0 [0,128), S1 [128,256), O0 [256,320), O1 [320,384)
 
 struct PrefillTcSmem {
     static constexpr uint32_t kSlab = 128 * 128;          // [128 rows][32 fp32], 16 KB
@@ -105,9 +107,9 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     uint64_t *empty_kv = full_kv + kPfStages;  // [kPfStages]
     uint64_t *s_ready = empty_kv + kPfStages;  // [2]
     uint64_t *p_ready = s_ready + 2;           // [2]
-    uint64_t *o_ready = p_ready + 2;
-    uint64_t *o_free = o_ready + 1;
-    uint64_t *drain = o_free + 1;
+    uint64_t *o_ready = p_ready + 2;           // [2]
+    uint64_t *o_free = o_ready + 2;            // [2]
+    uint64_t *drain = o_free + 2;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
 
     const int warp = threadIdx.x / kWarpSize, lane = threadIdx.x % kWarpSize;
@@ -129,8 +131,10 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             sm100::mbar_init(&s_ready[i], 1);
             sm100::mbar_init(&p_ready[i], 128);
         }
-        sm100::mbar_init(o_ready, 1);
-        sm100::mbar_init(o_free, 128);
+        for (int i = 0; i < 2; ++i) {
+            sm100::mbar_init(&o_ready[i], 1);
+            sm100::mbar_init(&o_free[i], 128);
+        }
         sm100::mbar_init(drain, 1);
         sm100::fence_mbarrier_init();
         sm100::prefetch_tmap(&tmQ);
@@ -219,8 +223,9 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                     sm100::tc_fence_after();
                     issue_s(n + 1);
                 }
+                // O buffer n & 1 was last folded after P V of tile n - 2
                 if (!sm100::mbar_wait(&p_ready[n & 1], static_cast<uint32_t>(n >> 1) & 1u) ||
-                    (n > 0 && !sm100::mbar_wait(o_free, static_cast<uint32_t>(n - 1) & 1u))) {
+                    (n >= 2 && !sm100::mbar_wait(&o_free[n & 1], static_cast<uint32_t>((n >> 1) - 1) & 1u))) {
                     ok = false;
                     break;
                 }
@@ -228,10 +233,11 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 const int s = n % kPfStages;
                 const uint32_t vb = sm100::smem_u32(stages + s * SM::kStageBytes + 2 * SM::kSlab);
                 const uint32_t pa = tmem + static_cast<uint32_t>((n & 1) * kPfKvTile);
+                const uint32_t od = tmem + 256u + static_cast<uint32_t>((n & 1) * 64);
                 for (int ks = 0; ks < kPfKvTile / 8; ++ks) // 8 keys per step = one 1 KB row group of V
-                    umma_tf32_ts(tmem + 256u, pa + static_cast<uint32_t>(ks * 8),
+                    umma_tf32_ts(od, pa + static_cast<uint32_t>(ks * 8),
                                  sdesc_mn128_32b(vb + static_cast<uint32_t>(ks) * 1024u, SM::kSlab, 512u), idesc_o, ks > 0);
-                sm100::umma_commit(o_ready);
+                sm100::umma_commit(&o_ready[n & 1]);
                 sm100::umma_commit(&empty_kv[s]);
             }
             // every issued MMA completes before tensor memory is released
@@ -248,11 +254,31 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         const int qpos = q_offset + t;
         const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
         const float c = scale * kLog2e;
-        float m_run = kNegInf, l_run = 0.f;
+        float m_run = kNegInf, l_run = 0.f, alpha_prev = 0.f;
         float o[64];
 #pragma unroll
         for (int i = 0; i < 64; ++i)
             o[i] = 0.f;
+        // o = o * alpha + P V of tile k (tensor-memory buffer k & 1)
+        auto fold = [&](int k, float alpha) -> bool {
+            if (!sm100::mbar_wait_warp(&o_ready[k & 1], static_cast<uint32_t>(k >> 1) & 1u)) {
+                ok = false;
+                return false;
+            }
+            sm100::tc_fence_after();
+#pragma unroll
+            for (int cc = 0; cc < 4; ++cc) {
+                uint32_t rr[16];
+                sm100::tmem_ld_32x16(tmem + lane_addr + 256u + static_cast<uint32_t>((k & 1) * 64 + cc * 16), rr);
+                sm100::tmem_wait_ld();
+#pragma unroll
+                for (int i = 0; i < 16; ++i)
+                    o[cc * 16 + i] = o[cc * 16 + i] * alpha + __uint_as_float(rr[i]);
+            }
+            sm100::tc_fence_before();
+            sm100::mbar_arrive(&o_free[k & 1]);
+            return true;
+        };
         for (int n = 0; n < n_tiles; ++n) {
             const uint32_t sb = tmem + lane_addr + static_cast<uint32_t>((n & 1) * kPfKvTile);
             if (!sm100::mbar_wait_warp(&s_ready[n & 1], static_cast<uint32_t>(n >> 1) & 1u)) {
@@ -296,24 +322,14 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             m_run = m_new;
             sm100::tc_fence_before();
             sm100::mbar_arrive(&p_ready[n & 1]);
-            // fold this tile's P V into the running output
-            if (!sm100::mbar_wait_warp(o_ready, static_cast<uint32_t>(n) & 1u)) {
-                ok = false;
+            // fold the previous tile's P V (its MMA ran while this tile's
+            // softmax did)
+            if (n > 0 && !fold(n - 1, alpha_prev))
                 break;
-            }
-            sm100::tc_fence_after();
-#pragma unroll
-            for (int cc = 0; cc < 4; ++cc) {
-                uint32_t rr[16];
-                sm100::tmem_ld_32x16(tmem + lane_addr + 256u + static_cast<uint32_t>(cc * 16), rr);
-                sm100::tmem_wait_ld();
-#pragma unroll
-                for (int i = 0; i < 16; ++i)
-                    o[cc * 16 + i] = o[cc * 16 + i] * alpha + __uint_as_float(rr[i]);
-            }
-            sm100::tc_fence_before();
-            sm100::mbar_arrive(o_free);
+            alpha_prev = alpha;
         }
+        if (ok && n_tiles > 0)
+            fold(n_tiles - 1, alpha_prev);
         if (ok && t < T) {
             const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
 #pragma unroll

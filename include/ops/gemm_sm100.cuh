@@ -116,7 +116,9 @@ template <GemmKind kKind, int BN> struct GemmShape {
     // K blocks accumulated in TMEM before the epilogue promotes the partial
     // sum into fp32 registers (split-precision path only)
     static constexpr int kPromoteKb = 2;
-    static constexpr size_t kEpiScratchBytes = 2048; // tile epilogue metadata (prepare())
+    // tile epilogue scratch (prepare() metadata, per-token reductions): 16
+    // bytes per token row, at least 2 KB
+    static constexpr size_t kEpiScratchBytes = 16u * BN > 2048u ? 16u * BN : 2048u;
     static constexpr size_t kSmemBytes = 1024 + static_cast<size_t>(kStages) * kStageBytes + 256 + kEpiScratchBytes;
     static_assert(kStages >= 2, "GEMM tile does not fit two pipeline stages");
     static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N must be a multiple of 16 in [16, 256]");
@@ -130,8 +132,11 @@ __global__ void __launch_bounds__(192, GemmShape<kKind, BN>::kCtasPerSm)
     using S = GemmShape<kKind, BN>;
     constexpr int kStages = S::kStages;
     constexpr bool kTileEpi = is_tile_epilogue<Epi>::value;
-    static_assert(!kTileEpi || 2u * BN * kUmmaM * 4u <= kStages * S::kStageBytes,
-                  "tile epilogue: partial and reduced tiles must fit in the pipeline stages");
+    // the partial tile [BN][128] fp32 (and, for split K, the reduced slice)
+    // reuse the pipeline stages
+    static_assert(!kTileEpi || BN * kUmmaM * 4u <= kStages * S::kStageBytes,
+                  "tile epilogue: the partial tile must fit in the pipeline stages");
+    constexpr bool kFitsReduce = 2u * BN * kUmmaM * 4u <= kStages * S::kStageBytes;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + kStages * S::kStageBytes);
@@ -372,7 +377,7 @@ __global__ void __launch_bounds__(192, GemmShape<kKind, BN>::kCtasPerSm)
         // every thread of every CTA of the cluster takes both barriers, on
         // the error path too
         namespace cg = cooperative_groups;
-        const int nsplit = p.splits;
+        const int nsplit = kFitsReduce ? p.splits : 1; // the host splits only shapes that fit
         float *ptile = reinterpret_cast<float *>(smem);
         float *rtile = ptile + BN * kUmmaM;
         const int per = (BN + nsplit - 1) / nsplit;
@@ -538,8 +543,10 @@ inline void gemm_tn(const GemmOperand &A, const GemmOperand &B, int k, float *ou
     case 64: gemm_launch<kKind, 64, Epi>(ta, tb, ta_lo, tb_lo, p, epi, stream); break;
     case 128: gemm_launch<kKind, 128, Epi>(ta, tb, ta_lo, tb_lo, p, epi, stream); break;
     default:
-        // BN = 256 only for plain bf16 and elementwise epilogues
-        if constexpr (kKind == GemmKind::kTF32x3 || is_tile_epilogue<Epi>::value)
+        // BN = 256 for single-term bf16 (tile epilogues: unsplit only)
+        if constexpr (kKind != GemmKind::kBF16)
+            gemm_launch<kKind, 128, Epi>(ta, tb, ta_lo, tb_lo, p, epi, stream);
+        else if (is_tile_epilogue<Epi>::value && p.splits > 1)
             gemm_launch<kKind, 128, Epi>(ta, tb, ta_lo, tb_lo, p, epi, stream);
         else
             gemm_launch<kKind, 256, Epi>(ta, tb, ta_lo, tb_lo, p, epi, stream);

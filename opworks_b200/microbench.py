@@ -4,6 +4,7 @@ median over the timed launches.
 
     python -m opworks_b200.microbench c1        # BASELINE C1 operator configs
     python -m opworks_b200.microbench decode    # decode-step kernels (C3 shapes)
+    python -m opworks_b200.microbench prefill   # one 8192-token prefill (C4)
 
 `c1` times our operators and, when the reference was built from its own
 sources into oracle/_ref (libopworks_ops_ref.so), the reference's kernels on
@@ -197,13 +198,47 @@ def decode(only="all", iters=20):
     return res
 
 
+def prefill(T=8192, iters=2):
+    """BASELINE C4: one T-token prefill of the random-init Llama-3.2-1B on the
+    fast path (tensor-core GEMMs and attention), CUDA events on the engine
+    stream; returns ms and tokens/s."""
+    import torch
+
+    from opworks_b200 import pack
+    from opworks_b200.llama import LlamaBatch, Model
+
+    path = pack.ensure_random_llama_pack()
+    with Model(path, weight_sets=1, max_positions=max(8192, T)) as m, LlamaBatch(m, 1, T, "fast", prefill_rows=T) as eng:
+        ids = np.random.default_rng(8).integers(0, m.vocab, T).astype(np.int32)
+        eng.prefill(0, ids[:512])  # warm: module loads
+        st = torch.cuda.ExternalStream(eng.stream())
+        times = []
+        for _ in range(iters):
+            eng.reset(0)
+            torch.cuda.synchronize()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(st)
+            eng.prefill(0, ids)
+            b.record(st)
+            torch.cuda.synchronize()
+            times.append(a.elapsed_time(b))
+    ms = float(min(times))
+    return {"tokens": T, "ms": round(ms, 2), "tok_s": round(T / (ms / 1e3), 1)}
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["c1", "decode"])
+    ap.add_argument("what", choices=["c1", "decode", "prefill"])
+    ap.add_argument("--tokens", type=int, default=8192)
     ap.add_argument("--only", default="all", choices=["all", "attention", "gemm", "sample"])
     ap.add_argument("--iters", type=int, default=20)
     a = ap.parse_args()
-    r = c1(a.iters) if a.what == "c1" else decode(a.only, a.iters)
+    if a.what == "c1":
+        r = c1(a.iters)
+    elif a.what == "prefill":
+        r = prefill(a.tokens, max(1, min(a.iters, 3)))
+    else:
+        r = decode(a.only, a.iters)
     print(json.dumps(r))
 
 

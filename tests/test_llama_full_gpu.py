@@ -141,3 +141,23 @@ def test_batched_decode_equals_single(pack_path):
                 if i == 5:
                     err = np.max(np.abs(one.logits(0) - batch_logits))
                     assert err <= 2e-2, err
+
+
+def test_fast_path_long_prompt_logits_within_gemm_tolerance(pack_path):
+    """A 1024-token prompt: the fast path's prefill runs single-term bf16
+    activation GEMMs (more than 256 token rows) and tensor-core TF32
+    attention; its last-row logits stay within the BASELINE GEMM tolerance of
+    the accurate path (fp32 weights, split-TF32 GEMMs, fp32 attention)."""
+    from opworks_b200.llama import LlamaBatch, Model
+
+    prompt = np.random.default_rng(77).integers(0, 128256, 1024).astype(np.int32).tolist()
+    with Model(pack_path, weight_sets=7) as m:  # bf16 + fp32 + split-TF32 weights
+        with LlamaBatch(m, 1, 1100, "accurate", prefill_rows=1024) as acc:
+            t_acc = acc.prefill(0, prompt)
+            ref = acc.logits(0)
+        with LlamaBatch(m, 1, 1100, "fast", prefill_rows=1024) as fast:
+            t_fast = fast.prefill(0, prompt)
+            got = fast.logits(0)
+    err = np.max(np.abs(got - ref))
+    assert err <= 2e-2, err
+    assert t_fast == t_acc
