@@ -137,7 +137,7 @@ struct matmul_launcher {
                          g.b().data(), K, N, static_cast<int64_t>(N), bt_hi, bt_lo, ld);
         sm100::GemmOperand feat{bt_hi, bt_lo, K, ld};
         sm100::GemmOperand tok{a_hi, a_lo, M, ld};
-        sm100::gemm_tn<sm100::GemmKind::kTF32x3>(feat, tok, N, C, K, 1, 0, stream, epi);
+        sm100::gemm_tf32x3(feat, tok, N, C, K, stream, epi);
     }
 };
 

@@ -242,7 +242,10 @@ __global__ void __launch_bounds__(kDecodeThreads, kDecodeCtasPerSm)
     const int qh_total = gridDim.y * kRep;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     pdl_trigger();
-    pdl_wait();
+    // lens and the block table are step inputs (copied before the step's
+    // first kernel); q and the newest token's K/V come from the kernel
+    // before this one, so only the producer's first tiles of OLDER tokens
+    // may be fetched before the programmatic-launch wait
     const int len = lens[b];
     const int t_begin = split * tokens_per_split;
     const int t_end = min(len, t_begin + tokens_per_split);
@@ -264,6 +267,7 @@ __global__ void __launch_bounds__(kDecodeThreads, kDecodeCtasPerSm)
         // producer warp: the lanes look up 32 chunks' block offsets at a time,
         // lane 0 issues the copies
         int issued = 0;
+        bool waited = false;
         const int chunk0 = t_begin / kKvChunk;
         for (int base = 0; base < n_tiles && ok; base += 32 / kChunks) {
             const int my_chunk = chunk0 + base * kChunks + lane;
@@ -283,6 +287,13 @@ __global__ void __launch_bounds__(kDecodeThreads, kDecodeCtasPerSm)
                     ntok[c] = __shfl_sync(kFullWarpMask, my_tok, (tile - base) * kChunks + c);
                 }
                 const int s = tile % kDecodeStages;
+                // a tile that reaches the step's new token (position len - 1,
+                // written by the previous kernel) or needs a recycled stage
+                // waits for the previous kernel (warp-uniform condition)
+                if (!waited && (tile >= kDecodeStages || t_begin + (tile + 1) * kDecodeTile >= len)) {
+                    pdl_wait();
+                    waited = true;
+                }
                 bool go = true;
                 if (lane == 0) {
                     if (tile >= kDecodeStages)
@@ -305,6 +316,7 @@ __global__ void __launch_bounds__(kDecodeThreads, kDecodeCtasPerSm)
                 if (!sm100::mbar_wait(&full[j % kDecodeStages], static_cast<uint32_t>(j / kDecodeStages) & 1u))
                     ok = false;
     } else {
+        pdl_wait(); // q is the previous kernel's output
         // this lane's slice of the query heads, in registers, pre-scaled so
         // that scores come out in log2 units (softmax by exp2)
         const float qscale = scale * kLog2e;

@@ -266,14 +266,18 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 return false;
             }
             sm100::tc_fence_after();
+            // the four 16-column loads are in flight together: one wait
+            uint32_t rr[4][16];
+#pragma unroll
+            for (int cc = 0; cc < 4; ++cc)
+                sm100::tmem_ld_32x16(tmem + lane_addr + 256u + static_cast<uint32_t>((k & 1) * 64 + cc * 16), rr[cc]);
+            sm100::tmem_wait_ld();
 #pragma unroll
             for (int cc = 0; cc < 4; ++cc) {
-                uint32_t rr[16];
-                sm100::tmem_ld_32x16(tmem + lane_addr + 256u + static_cast<uint32_t>((k & 1) * 64 + cc * 16), rr);
-                sm100::tmem_wait_ld();
+                sm100::tmem_reg_fence(rr[cc]);
 #pragma unroll
                 for (int i = 0; i < 16; ++i)
-                    o[cc * 16 + i] = o[cc * 16 + i] * alpha + __uint_as_float(rr[i]);
+                    o[cc * 16 + i] = o[cc * 16 + i] * alpha + __uint_as_float(rr[cc][i]);
             }
             sm100::tc_fence_before();
             sm100::mbar_arrive(&o_free[k & 1]);
@@ -287,37 +291,51 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             }
             sm100::tc_fence_after();
             const int k0 = n * kPfKvTile;
-            float mt = kNegInf;
-            uint32_t v[kPfKvTile];
+            // all eight 16-column loads of the score row in flight, one wait
+            uint32_t v[kPfKvTile / 16][16];
+#pragma unroll
+            for (int cc = 0; cc < kPfKvTile / 16; ++cc)
+                sm100::tmem_ld_32x16(sb + static_cast<uint32_t>(cc * 16), v[cc]);
+            sm100::tmem_wait_ld();
+            // row max with one accumulator per 16-column group (short
+            // dependency chains), combined in a fixed order
+            float mg[kPfKvTile / 16];
 #pragma unroll
             for (int cc = 0; cc < kPfKvTile / 16; ++cc) {
-                uint32_t rr[16];
-                sm100::tmem_ld_32x16(sb + static_cast<uint32_t>(cc * 16), rr);
-                sm100::tmem_wait_ld();
+                sm100::tmem_reg_fence(v[cc]);
+                mg[cc] = kNegInf;
 #pragma unroll
                 for (int i = 0; i < 16; ++i) {
                     const int j = cc * 16 + i;
-                    const float sv = k0 + j <= qpos ? __uint_as_float(rr[i]) * c : kNegInf;
-                    v[j] = __float_as_uint(sv);
-                    mt = fmaxf(mt, sv);
+                    const float sv = k0 + j <= qpos ? __uint_as_float(v[cc][i]) * c : kNegInf;
+                    v[cc][i] = __float_as_uint(sv);
+                    mg[cc] = fmaxf(mg[cc], sv);
                 }
             }
+            float mt = kNegInf;
+#pragma unroll
+            for (int cc = 0; cc < kPfKvTile / 16; ++cc)
+                mt = fmaxf(mt, mg[cc]);
             const float m_new = fmaxf(m_run, mt);
             const float alpha = m_run == kNegInf ? 0.f : exp2_approx(m_run - m_new);
-            float lsum = 0.f;
+            float lg[kPfKvTile / 16];
 #pragma unroll
             for (int cc = 0; cc < kPfKvTile / 16; ++cc) {
-                uint32_t ww[16];
+                lg[cc] = 0.f;
 #pragma unroll
                 for (int i = 0; i < 16; ++i) {
-                    const float sv = __uint_as_float(v[cc * 16 + i]);
+                    const float sv = __uint_as_float(v[cc][i]);
                     const float pv = m_new == kNegInf ? 0.f : exp2_approx(sv - m_new);
-                    lsum += pv;
-                    ww[i] = __float_as_uint(pv);
+                    lg[cc] += pv;
+                    v[cc][i] = __float_as_uint(pv);
                 }
-                tmem_st_32x16(sb + static_cast<uint32_t>(cc * 16), ww);
+                tmem_st_32x16(sb + static_cast<uint32_t>(cc * 16), v[cc]);
             }
             tmem_wait_st();
+            float lsum = 0.f;
+#pragma unroll
+            for (int cc = 0; cc < kPfKvTile / 16; ++cc)
+                lsum += lg[cc];
             l_run = l_run * alpha + lsum;
             m_run = m_new;
             sm100::tc_fence_before();

@@ -89,11 +89,39 @@ inline int grid_for(int64_t n) {
 }
 
 // Stream-ordered scratch that is released after the work queued on `stream`.
+// Operand scratch from the stream-ordered allocator. The first use on a
+// device raises its default memory pool's release threshold to
+// kScratchKeepBytes, so scratch freed here stays mapped across stream
+// synchronisations (with the default threshold of 0 every synchronisation
+// returns it and the next call maps it again, which costs more than the GEMM
+// at C1 sizes). The setting is process-local and only affects the default pool.
+constexpr uint64_t kScratchKeepBytes = 1ull << 30;
+inline void keep_pool_scratch() {
+    static thread_local int done_mask = 0; // bit per device id < 32
+    int dev = 0;
+    OPWORKS_CUDA_CHECK(cudaGetDevice(&dev));
+    if (dev < 32 && (done_mask >> dev & 1))
+        return;
+    cudaMemPool_t pool;
+    uint64_t cur = 0, keep = kScratchKeepBytes;
+    cudaError_t rc = cudaDeviceGetDefaultMemPool(&pool, dev);
+    if (rc == cudaSuccess)
+        rc = cudaMemPoolGetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &cur);
+    if (rc == cudaSuccess && cur < keep)
+        rc = cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
+    if (rc != cudaSuccess)
+        cudaGetLastError(); // pools unsupported: keep the default behaviour
+    if (dev < 32)
+        done_mask |= 1 << dev;
+}
+
 class StreamScratch {
   public:
     StreamScratch(size_t bytes, cudaStream_t stream) : stream_(stream) {
-        if (bytes)
+        if (bytes) {
+            keep_pool_scratch();
             OPWORKS_CUDA_CHECK(cudaMallocAsync(&ptr_, bytes, stream));
+        }
     }
     ~StreamScratch() {
         if (ptr_)

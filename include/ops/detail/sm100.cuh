@@ -183,6 +183,19 @@ __device__ __forceinline__ void tmem_ld_32x16(uint32_t taddr, uint32_t (&r)[16])
 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// Registers loaded by tcgen05.ld are valid only after tcgen05.wait::ld. When
+// several loads are issued before one wait, this empty statement (placed
+// after the wait) redefines the registers so the compiler cannot move their
+// uses above the wait.
+__device__ __forceinline__ void tmem_reg_fence(uint32_t (&r)[16]) {
+    asm volatile(""
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                   "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                   "+r"(r[15])
+                 :
+                 : "memory");
+}
+
 // Shared-memory matrix descriptor for a K-major tile whose rows are 128 bytes
 // (one 128B swizzle atom per row, 8-row groups 1024 bytes apart), as written
 // by a TMA load with CU_TENSOR_MAP_SWIZZLE_128B. Fields: start address >> 4

@@ -311,9 +311,10 @@ __global__ void __launch_bounds__(192, GemmShape<kKind, BN>::kCtasPerSm)
         float *ptile = reinterpret_cast<float *>(smem);
         const int col = q * 32 + lane;
         if constexpr (kTileEpi && has_prepare<Epi>::value) {
+            const bool sliced = p.splits > 1; // this CTA's row slice of the cluster's tile
             const int per = (BN + p.splits - 1) / p.splits;
-            const int tb = p.splits > 1 ? min(BN, split * per) : 0;
-            const int nt = p.splits > 1 ? min(BN, tb + per) - tb : BN;
+            const int tb = sliced ? min(BN, split * per) : 0;
+            const int nt = sliced ? min(BN, tb + per) - tb : BN;
             epi.prepare(t0 + tb, max(0, min(nt, p.m_tok - (t0 + tb))), f0, min(kUmmaM, p.n_feat - f0),
                         static_cast<int>(threadIdx.x) - 64, epi_scratch);
         }
@@ -395,14 +396,24 @@ __global__ void __launch_bounds__(192, GemmShape<kKind, BN>::kCtasPerSm)
                 cg::cluster_group cluster = cg::this_cluster();
                 for (int idx = et; idx < (tl1 - tl0) * (kUmmaM / 4); idx += 128) {
                     const int t = tl0 + idx / (kUmmaM / 4), c4 = idx % (kUmmaM / 4);
+                    // eight remote loads in flight at a time, summed in rank
+                    // order
                     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-                    for (int r = 0; r < nsplit; ++r) {
-                        const float4 v =
-                            reinterpret_cast<const float4 *>(cluster.map_shared_rank(ptile, r))[t * (kUmmaM / 4) + c4];
-                        acc.x += v.x;
-                        acc.y += v.y;
-                        acc.z += v.z;
-                        acc.w += v.w;
+                    for (int r0 = 0; r0 < nsplit; r0 += 8) {
+                        float4 v[8];
+#pragma unroll
+                        for (int j = 0; j < 8; ++j)
+                            if (r0 + j < nsplit)
+                                v[j] = reinterpret_cast<const float4 *>(
+                                    cluster.map_shared_rank(ptile, r0 + j))[t * (kUmmaM / 4) + c4];
+#pragma unroll
+                        for (int j = 0; j < 8; ++j)
+                            if (r0 + j < nsplit) {
+                                acc.x += v[j].x;
+                                acc.y += v[j].y;
+                                acc.z += v[j].z;
+                                acc.w += v[j].w;
+                            }
                     }
                     reinterpret_cast<float4 *>(rtile)[(t - tl0) * (kUmmaM / 4) + c4] = acc;
                 }
@@ -552,6 +563,47 @@ inline void gemm_tn(const GemmOperand &A, const GemmOperand &B, int k, float *ou
             gemm_launch<kKind, 256, Epi>(ta, tb, ta_lo, tb_lo, p, epi, stream);
         break;
     }
+}
+
+// Tile epilogue that writes C[tok][feat] = epi(sum) from the reduced tile:
+// lets a plain element epilogue (which may be non-linear, e.g. ReLU) run
+// behind cluster split-K, where it sees the full sum.
+template <typename Epi> struct StoreTileEpi {
+    static constexpr bool kTile = true;
+    float *c;
+    int64_t ldc;
+    Epi epi;
+    __device__ void operator()(const float *tile, int tok0, int ntok, int f0, int nfeat, int tid, void *) const {
+        for (int i = tid; i < ntok * kUmmaM; i += 128) {
+            const int t = i / kUmmaM, f = i % kUmmaM;
+            if (f < nfeat)
+                c[static_cast<int64_t>(tok0 + t) * ldc + f0 + f] = apply_epilogue(epi, tile[i], tok0 + t, f0 + f);
+        }
+    }
+};
+
+// Split-precision (3xTF32) C[tok][feat] = epi(A . B^T) with the tile plan for
+// fp32 operator GEMMs: when 128 x 128 tiles leave most SMs idle and K is
+// long, the K range of each tile is split across a cluster of up to 8 CTAs
+// (reduced through distributed shared memory, epilogue on the full sum);
+// otherwise one unsplit launch with the token tile narrowed to fill a wave.
+template <typename Epi = Identity>
+inline void gemm_tf32x3(const GemmOperand &A, const GemmOperand &B, int k, float *C, int64_t ldc,
+                        cudaStream_t stream, const Epi &epi = {}) {
+    const int sms = detail::device_facts().sm_count;
+    const int tiles = ((A.rows + kUmmaM - 1) / kUmmaM) * ((B.rows + 127) / 128);
+    const int num_kb = (k + 31) / 32;
+    if (B.rows > 64 && tiles < sms / 2) {
+        int splits = sms / tiles;
+        splits = splits > kMaxClusterSplits ? kMaxClusterSplits : splits;
+        splits = splits > num_kb / 8 ? num_kb / 8 : splits;
+        if (splits >= 2) {
+            gemm_tn<GemmKind::kTF32x3, StoreTileEpi<Epi>>(A, B, k, nullptr, ldc, splits, 0, stream,
+                                                           StoreTileEpi<Epi>{C, ldc, epi}, 128);
+            return;
+        }
+    }
+    gemm_tn<GemmKind::kTF32x3, Epi>(A, B, k, C, ldc, 1, 0, stream, epi);
 }
 
 } // namespace opworks::sm100

@@ -208,7 +208,7 @@ inline void linear_f32_tc(const float *X, const float *W, float *Y, int rows, in
                  static_cast<int64_t>(in), w_hi, w_lo, ld);
     sm100::GemmOperand feat{w_hi, w_lo, out, ld};
     sm100::GemmOperand tok{x_hi, x_lo, rows, ld};
-    sm100::gemm_tn<sm100::GemmKind::kTF32x3>(feat, tok, in, Y, out, 1, 0, stream);
+    sm100::gemm_tf32x3(feat, tok, in, Y, out, stream);
 }
 
 } // namespace opworks::detail

@@ -215,27 +215,40 @@ struct ResidualTileEpi {
     RowSumSq rs{};
     __device__ __forceinline__ void operator()(const float *tile, int tok0, int ntok, int f0, int nfeat, int tid,
                                                void *scratch) const {
-        // thread tid owns column tid of every token row of the tile
+        // thread tid owns column tid of every token row of the tile; the
+        // residual values of kChunk tokens are loaded together (one memory
+        // latency per chunk, not per token)
+        constexpr int kChunk = 8;
         float *red = static_cast<float *>(scratch); // [4 warps][ntok] partial sums of squares
         const int c = tid;
         const bool col_ok = c < nfeat;
         const float g = (gain && col_ok) ? gain[f0 + c] : 0.f;
-        for (int t = 0; t < ntok; ++t) {
-            float h = 0.f;
-            if (col_ok) {
-                float *p = hidden + static_cast<int64_t>(tok0 + t) * ld + f0 + c;
-                h = *p + tile[t * 128 + c];
-                *p = h;
-                if (gain)
-                    normed.put(tok0 + t, f0 + c, h * g);
-            }
-            if (rs.part) {
-                float sq = h * h;
+        float *col = hidden + static_cast<int64_t>(tok0) * ld + f0 + c;
+        for (int tb = 0; tb < ntok; tb += kChunk) {
+            float hv[kChunk];
 #pragma unroll
-                for (int off = 16; off > 0; off >>= 1)
-                    sq += __shfl_xor_sync(kFullWarpMask, sq, off);
-                if ((tid & 31) == 0)
-                    red[(tid >> 5) * ntok + t] = sq;
+            for (int j = 0; j < kChunk; ++j)
+                hv[j] = (col_ok && tb + j < ntok) ? col[static_cast<int64_t>(tb + j) * ld] : 0.f;
+#pragma unroll
+            for (int j = 0; j < kChunk; ++j) {
+                const int t = tb + j;
+                if (t >= ntok) // the same for every thread
+                    break;
+                float h = 0.f;
+                if (col_ok) {
+                    h = hv[j] + tile[t * 128 + c];
+                    col[static_cast<int64_t>(t) * ld] = h;
+                    if (gain)
+                        normed.put(tok0 + t, f0 + c, h * g);
+                }
+                if (rs.part) {
+                    float sq = h * h;
+#pragma unroll
+                    for (int off = 16; off > 0; off >>= 1)
+                        sq += __shfl_xor_sync(kFullWarpMask, sq, off);
+                    if ((tid & 31) == 0)
+                        red[(tid >> 5) * ntok + t] = sq;
+                }
             }
         }
         if (rs.part) {
@@ -325,33 +338,50 @@ struct QkvTileEpi {
     __device__ __forceinline__ void operator()(const float *tile, int tok0, int ntok, int f0, int nfeat, int tid,
                                                void *scratch) const {
         const int *meta = static_cast<const int *>(scratch);
-        for (int idx = tid; idx < ntok * 64; idx += 128) {
-            const int t = idx >> 6, hh = (idx >> 5) & 1, i = idx & 31;
-            if (hh * 64 + 64 > nfeat)
-                continue;
-            const int head = f0 / kAttnD + hh;
-            const int64_t row = tok0 + t;
-            const float sc = __int_as_float(meta[4 * t + 3]);
-            const float a = tile[t * 128 + hh * 64 + i] * sc, b = tile[t * 128 + hh * 64 + i + 32] * sc;
-            const int pos = meta[4 * t];
-            if (head < qh) {
-                const float2 r = rope[static_cast<int64_t>(pos) * (kAttnD / 2) + i];
-                float *q = q_out + row * qh * kAttnD + head * kAttnD;
-                q[i] = a * r.x - b * r.y;
-                q[i + kAttnD / 2] = b * r.x + a * r.y;
-                continue;
+        // kChunk items per thread at a time: their cos/sin loads are issued
+        // together (one memory latency per chunk)
+        constexpr int kChunk = 8;
+        const int items = ntok * 64;
+        for (int base = 0; base < items; base += kChunk * 128) {
+            float2 rv[kChunk];
+#pragma unroll
+            for (int j = 0; j < kChunk; ++j) {
+                const int idx = base + j * 128 + tid;
+                rv[j] = make_float2(1.f, 0.f);
+                if (idx < items && f0 / kAttnD + ((idx >> 5) & 1) < qh + kvh)
+                    rv[j] = rope[static_cast<int64_t>(meta[4 * (idx >> 6)]) * (kAttnD / 2) + (idx & 31)];
             }
-            const int blk = meta[4 * t + 1];
-            const int slot = meta[4 * t + 2];
-            if (head < qh + kvh) {
-                const float2 r = rope[static_cast<int64_t>(pos) * (kAttnD / 2) + i];
-                float *k = kpool + ((static_cast<int64_t>(blk) * kvh + (head - qh)) * kKvChunk + slot) * kAttnD;
-                k[i] = a * r.x - b * r.y;
-                k[i + kAttnD / 2] = b * r.x + a * r.y;
-            } else {
-                float *v = vpool + ((static_cast<int64_t>(blk) * kvh + (head - qh - kvh)) * kKvChunk + slot) * kAttnD;
-                v[i] = a;
-                v[i + kAttnD / 2] = b;
+#pragma unroll
+            for (int j = 0; j < kChunk; ++j) {
+                const int idx = base + j * 128 + tid;
+                if (idx >= items)
+                    break;
+                const int t = idx >> 6, hh = (idx >> 5) & 1, i = idx & 31;
+                if (hh * 64 + 64 > nfeat)
+                    continue;
+                const int head = f0 / kAttnD + hh;
+                const int64_t row = tok0 + t;
+                const float sc = __int_as_float(meta[4 * t + 3]);
+                const float a = tile[t * 128 + hh * 64 + i] * sc, b = tile[t * 128 + hh * 64 + i + 32] * sc;
+                const float2 r = rv[j];
+                if (head < qh) {
+                    float *q = q_out + row * qh * kAttnD + head * kAttnD;
+                    q[i] = a * r.x - b * r.y;
+                    q[i + kAttnD / 2] = b * r.x + a * r.y;
+                    continue;
+                }
+                const int blk = meta[4 * t + 1];
+                const int slot = meta[4 * t + 2];
+                if (head < qh + kvh) {
+                    float *k = kpool + ((static_cast<int64_t>(blk) * kvh + (head - qh)) * kKvChunk + slot) * kAttnD;
+                    k[i] = a * r.x - b * r.y;
+                    k[i + kAttnD / 2] = b * r.x + a * r.y;
+                } else {
+                    float *v =
+                        vpool + ((static_cast<int64_t>(blk) * kvh + (head - qh - kvh)) * kKvChunk + slot) * kAttnD;
+                    v[i] = a;
+                    v[i + kAttnD / 2] = b;
+                }
             }
         }
     }

@@ -11,7 +11,9 @@
 // pre-pass writes the hi/lo halves of A and of B^T (B is N-major; the GEMM
 // wants both operands K-major) into stream-ordered scratch; the GEMM then
 // streams them through TMA into a 128 x BN TMEM accumulator and applies the
-// epilogue functor on the way out.
+// epilogue functor on the way out. Grids of few 128 x 128 tiles (e.g. 1024 x
+// 1024 outputs) split K across a thread-block cluster and reduce the partial
+// tiles on chip before the epilogue (sm100::gemm_tf32x3).
 
 #include "../core/cuda_utils.cuh"
 #include "detail/operand_prep.cuh"
@@ -54,7 +56,7 @@ inline void mat_mul(const float *A, const float *B, float *C, int M, int N, int 
 
     sm100::GemmOperand feat{bt_hi, bt_lo, K, ld};
     sm100::GemmOperand tok{a_hi, a_lo, M, ld};
-    sm100::gemm_tn<sm100::GemmKind::kTF32x3, Epilogue>(feat, tok, N, C, K, 1, 0, stream, epilogue);
+    sm100::gemm_tf32x3<Epilogue>(feat, tok, N, C, K, stream, epilogue);
 }
 
 } // namespace opworks::ops

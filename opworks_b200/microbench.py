@@ -36,11 +36,16 @@ def measured_peaks():
 
 
 class Timer:
-    """Median CUDA-event time (ms) of fn(), with an L2 flush before each launch."""
+    """Median CUDA-event time (ms) of fn(), with an L2 flush before each launch.
+
+    The flush READS a 256 MB buffer (twice the L2): the cache is left holding
+    clean lines, so the timed kernel pays no write-back of the flush's own
+    data (a write flush would leave ~126 MB of dirty lines behind)."""
 
     def __init__(self, torch):
         self.torch = torch
-        self.flush_buf = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device="cuda")  # 256 MB > L2
+        self.flush_buf = torch.ones(64 * 1024 * 1024, dtype=torch.float32, device="cuda")  # 256 MB > L2
+        self.flush_out = torch.empty(1, dtype=torch.float32, device="cuda")
 
     def __call__(self, fn, iters=20, warmup=3):
         torch = self.torch
@@ -49,7 +54,7 @@ class Timer:
         torch.cuda.synchronize()
         times = []
         for _ in range(iters):
-            self.flush_buf.fill_(1.0)
+            torch.sum(self.flush_buf, dim=0, keepdim=True, out=self.flush_out)
             s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             s.record()
             fn()

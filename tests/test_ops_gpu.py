@@ -85,8 +85,10 @@ def bf16_bits(x):
 # ------------------------------------------------------------------ matmul
 
 
+# (256, 1024, 200) and (300, 4096, 130) take the cluster split-K plan with
+# ragged feature / token tiles; (1024, 2048, 1024) is the C1 shape (2 splits)
 @pytest.mark.parametrize("M,N,K", [(1, 1, 1), (3, 5, 7), (37, 100, 129), (130, 257, 200), (64, 2048, 96),
-                                   (1024, 2048, 1024)])
+                                   (256, 1024, 200), (300, 4096, 130), (1024, 2048, 1024)])
 def test_mat_mul_3xtf32_vs_oracle(ops, M, N, K):
     rng = np.random.default_rng(M * 7 + N * 13 + K)
     a = (rng.standard_normal((M, N)) / math.sqrt(max(N, 1))).astype(np.float32)
@@ -112,10 +114,10 @@ def test_mat_mul_framework_cases(ops):
 
 
 @pytest.mark.parametrize("ta,tb,act,bias", [(0, 0, 0, False), (1, 0, 1, True), (0, 1, 2, True), (1, 1, 0, True)])
-def test_matmul_builder_launcher(ops, ta, tb, act, bias):
-    M, N, K = 45, 70, 33
+@pytest.mark.parametrize("M,N,K", [(45, 70, 33), (200, 1024, 150)])
+def test_matmul_builder_launcher(ops, ta, tb, act, bias, M, N, K):
     rng = np.random.default_rng(5)
-    a = rng.standard_normal((M, N)).astype(np.float32)
+    a = (rng.standard_normal((M, N)) / math.sqrt(N)).astype(np.float32)
     b = rng.standard_normal((N, K)).astype(np.float32)
     bv = rng.standard_normal(K).astype(np.float32)
     a_st = a.T.copy() if ta else a
