@@ -489,6 +489,9 @@ template <typename WT> class LlamaEngineT {
     bool fast() const { return prec_ == Precision::kFast; }
 
     int plan_bn(int rows) const { return sm100::gemm_pick_bn(sm100::GemmKind::kBF16x2, rows); }
+    // the fused GEMM of `rows` token rows runs narrow (BN <= 64) tiles, whose
+    // epilogue scratch can hold rows preloaded during the main loop
+    bool narrow_tile(int rows) const { return rows <= prefill_single_rows_ && plan_bn(rows) <= 64; }
 
     int plan_splits(const Projection &p, int rows, int max_splits = 64) const {
         if (!fast() && rows <= 4)
@@ -661,7 +664,7 @@ template <typename WT> class LlamaEngineT {
             const detail::RowSumSq rs = row_sumsq();
             if (fast()) {
                 linear_tile(L.qkv, normed, rows,
-                            detail::QkvTileEpi{q_.data(), qh, kvh, rope, tm, kv, kv_.k(l), kv_.v(l), rs},
+                            detail::QkvTileEpi{q_.data(), qh, kvh, rope, tm, kv, kv_.k(l), kv_.v(l), rs, narrow_tile(rows)},
                             l2_prefetch_qkv_o_ ? &L.o : nullptr);
                 mark("gemm_qkv_rope_kv_write");
             } else {
@@ -683,14 +686,14 @@ template <typename WT> class LlamaEngineT {
                 // the residual epilogues also emit the next projection's
                 // operand h * gain and the tiles' sums of squares; the
                 // consuming epilogues apply the norm's per-token scale
-                linear_tile(L.o, attn, rows, detail::ResidualTileEpi{hidden_.data(), H, L.post_norm.data(), normed_o, rs},
+                linear_tile(L.o, attn, rows, detail::ResidualTileEpi{hidden_.data(), H, L.post_norm.data(), normed_o, rs, narrow_tile(rows)},
                             &L.gu);
                 mark("gemm_o_residual");
                 linear_tile(L.gu, normed, rows, detail::SiluMulTileEpi{act_o, rs}, &L.down);
                 mark("gemm_gate_up_silu");
                 const float *next_gain =
                     l + 1 < cfg_.num_layers ? w_.layers[l + 1].input_norm.data() : w_.final_norm.data();
-                linear_tile(L.down, act, rows, detail::ResidualTileEpi{hidden_.data(), H, next_gain, normed_o, rs},
+                linear_tile(L.down, act, rows, detail::ResidualTileEpi{hidden_.data(), H, next_gain, normed_o, rs, narrow_tile(rows)},
                             l + 1 < cfg_.num_layers ? &w_.layers[l + 1].qkv : nullptr);
                 mark("gemm_down_residual");
             } else {

@@ -71,14 +71,16 @@ struct Identity {
 // A tile epilogue may also define
 //   prepare(tok0, ntok, f0, nfeat, tid, void *scratch)
 // which runs on the epilogue threads while the main loop streams, before the
-// accumulator is final (metadata loads such as token positions), with 2 KB of
-// shared scratch that stays valid for operator().
+// accumulator is final (metadata loads such as token positions, residual rows),
+// with shared scratch (kEpiScratchNarrow bytes for BN <= 64, else at least
+// max(2 KB, 16 bytes per token row)) that stays valid for operator().
 template <typename Epi, typename = void> struct is_tile_epilogue : std::false_type {};
 template <typename Epi> struct is_tile_epilogue<Epi, std::void_t<decltype(Epi::kTile)>> : std::true_type {};
 template <typename Epi, typename = void> struct has_prepare : std::false_type {};
 template <typename Epi>
 struct has_prepare<Epi, std::void_t<decltype(std::declval<const Epi &>().prepare(0, 0, 0, 0, 0, nullptr))>>
     : std::true_type {};
+constexpr size_t kEpiScratchNarrow = 8192; // epilogue scratch bytes of BN <= 64 tiles
 constexpr int kMaxClusterSplits = 8;           // portable cluster size
 constexpr int kMaxClusterSplitsNonPortable = 16; // with the non-portable opt-in
 
@@ -116,9 +118,10 @@ template <GemmKind kKind, int BN> struct GemmShape {
     // K blocks accumulated in TMEM before the epilogue promotes the partial
     // sum into fp32 registers (split-precision path only)
     static constexpr int kPromoteKb = 2;
-    // tile epilogue scratch (prepare() metadata, per-token reductions): 16
-    // bytes per token row, at least 2 KB
-    static constexpr size_t kEpiScratchBytes = 16u * BN > 2048u ? 16u * BN : 2048u;
+    // tile epilogue scratch (prepare() metadata, per-token reductions, rows
+    // preloaded during the main loop): 8 KB for narrow decode tiles (two
+    // CTAs still fit an SM), else 16 bytes per token row, at least 2 KB
+    static constexpr size_t kEpiScratchBytes = BN <= 64 ? kEpiScratchNarrow : (16u * BN > 2048u ? 16u * BN : 2048u);
     static constexpr size_t kSmemBytes = 1024 + static_cast<size_t>(kStages) * kStageBytes + 256 + kEpiScratchBytes;
     static_assert(kStages >= 2, "GEMM tile does not fit two pipeline stages");
     static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N must be a multiple of 16 in [16, 256]");

@@ -208,27 +208,55 @@ static __global__ void silu_mul_kernel(const float *__restrict__ part, int split
 // bf16) and, per token, the tile's partial sum of squares of h (RowSumSq).
 struct ResidualTileEpi {
     static constexpr bool kTile = true;
+    // scratch: [4 warps][kPreTok] sums of squares | gain[128] | rows[kPreTok][128]
+    static constexpr int kPreTok = static_cast<int>((sm100::kEpiScratchNarrow - 1024) / 512);
     float *hidden;
     int64_t ld;
     const float *gain = nullptr;
     ActOut normed{};
     RowSumSq rs{};
+    bool preload = false; // the GEMM's scratch is kEpiScratchNarrow bytes (BN <= 64)
+    // while the main loop streams: the slice's residual rows and the gains
+    // go to shared memory, so the epilogue does no global load
+    __device__ __forceinline__ void prepare(int tok0, int ntok, int f0, int nfeat, int tid, void *scratch) const {
+        if (!preload || ntok > kPreTok)
+            return;
+        float *sg = static_cast<float *>(scratch) + 4 * kPreTok;
+        float *sh = sg + 128;
+        const int c = tid;
+        const bool col_ok = c < nfeat;
+        sg[c] = (gain && col_ok) ? gain[f0 + c] : 0.f;
+        const float *col = hidden + static_cast<int64_t>(tok0) * ld + f0 + c;
+        float hv[kPreTok];
+#pragma unroll
+        for (int j = 0; j < kPreTok; ++j)
+            hv[j] = (col_ok && j < ntok) ? col[static_cast<int64_t>(j) * ld] : 0.f;
+#pragma unroll
+        for (int j = 0; j < kPreTok; ++j)
+            if (j < ntok)
+                sh[j * 128 + c] = hv[j];
+    }
     __device__ __forceinline__ void operator()(const float *tile, int tok0, int ntok, int f0, int nfeat, int tid,
                                                void *scratch) const {
-        // thread tid owns column tid of every token row of the tile; the
+        // thread tid owns column tid of every token row of the tile (each
+        // thread reads back only what it staged in prepare()); otherwise the
         // residual values of kChunk tokens are loaded together (one memory
         // latency per chunk, not per token)
         constexpr int kChunk = 8;
+        const bool staged = preload && ntok <= kPreTok;
         float *red = static_cast<float *>(scratch); // [4 warps][ntok] partial sums of squares
+        const float *sg = red + 4 * kPreTok;
+        const float *sh = sg + 128;
         const int c = tid;
         const bool col_ok = c < nfeat;
-        const float g = (gain && col_ok) ? gain[f0 + c] : 0.f;
+        const float g = staged ? sg[c] : ((gain && col_ok) ? gain[f0 + c] : 0.f);
         float *col = hidden + static_cast<int64_t>(tok0) * ld + f0 + c;
         for (int tb = 0; tb < ntok; tb += kChunk) {
             float hv[kChunk];
 #pragma unroll
             for (int j = 0; j < kChunk; ++j)
-                hv[j] = (col_ok && tb + j < ntok) ? col[static_cast<int64_t>(tb + j) * ld] : 0.f;
+                hv[j] = (col_ok && tb + j < ntok) ? (staged ? sh[(tb + j) * 128 + c] : col[static_cast<int64_t>(tb + j) * ld])
+                                                  : 0.f;
 #pragma unroll
             for (int j = 0; j < kChunk; ++j) {
                 const int t = tb + j;
@@ -324,6 +352,10 @@ struct QkvTileEpi {
     // per token of the slice: position, KV block and slot in it (loaded while
     // the GEMM main loop streams)
     RowSumSq rs{}; // deferred input norm when rs.part is set
+    // scratch: meta [ntok][4] | cos/sin [ntok][32] (staged when preload is
+    // set, the GEMM's scratch is kEpiScratchNarrow bytes and ntok fits)
+    static constexpr int kPreTok = static_cast<int>(sm100::kEpiScratchNarrow / (16 + 8 * (kAttnD / 2)));
+    bool preload = false;
     __device__ __forceinline__ void prepare(int tok0, int ntok, int, int, int tid, void *scratch) const {
         int *meta = static_cast<int *>(scratch); // [ntok][4]: pos, block, slot, rsqrt scale (float bits)
         for (int t = tid; t < ntok; t += 128) {
@@ -334,10 +366,19 @@ struct QkvTileEpi {
             meta[4 * t + 2] = pos % kKvChunk;
             meta[4 * t + 3] = __float_as_int(rs.part ? rs.inv_rms(row) : 1.f);
         }
+        if (preload && ntok <= kPreTok) {
+            // read in operator() by other threads: the cluster barrier (or
+            // the block barrier of an unsplit tile) orders these writes
+            float2 *cs = reinterpret_cast<float2 *>(meta + 4 * kPreTok);
+            for (int idx = tid; idx < ntok * 32; idx += 128)
+                cs[idx] = rope[static_cast<int64_t>(tm.pos[tok0 + (idx >> 5)]) * (kAttnD / 2) + (idx & 31)];
+        }
     }
     __device__ __forceinline__ void operator()(const float *tile, int tok0, int ntok, int f0, int nfeat, int tid,
                                                void *scratch) const {
         const int *meta = static_cast<const int *>(scratch);
+        const bool staged = preload && ntok <= kPreTok;
+        const float2 *cs = reinterpret_cast<const float2 *>(meta + 4 * kPreTok);
         // kChunk items per thread at a time: their cos/sin loads are issued
         // together (one memory latency per chunk)
         constexpr int kChunk = 8;
@@ -349,7 +390,8 @@ struct QkvTileEpi {
                 const int idx = base + j * 128 + tid;
                 rv[j] = make_float2(1.f, 0.f);
                 if (idx < items && f0 / kAttnD + ((idx >> 5) & 1) < qh + kvh)
-                    rv[j] = rope[static_cast<int64_t>(meta[4 * (idx >> 6)]) * (kAttnD / 2) + (idx & 31)];
+                    rv[j] = staged ? cs[(idx >> 6) * 32 + (idx & 31)]
+                                   : rope[static_cast<int64_t>(meta[4 * (idx >> 6)]) * (kAttnD / 2) + (idx & 31)];
             }
 #pragma unroll
             for (int j = 0; j < kChunk; ++j) {

@@ -8,7 +8,8 @@
 // writes Op::identity().
 //
 // B200 kernel: one pass. Up to 1024 blocks stream the input with 16-byte
-// loads and four independent accumulators per thread; each block publishes
+// loads (eight in flight per thread) into four independent accumulators per
+// thread; each block publishes
 // its partial, and the last block to arrive (arrival counter in the
 // workspace) folds the partials in block order, so the result is
 // deterministic. The counter is cleared with a 4-byte memset node before the
@@ -40,15 +41,23 @@ template <typename Op> __device__ __forceinline__ float reduce_range(const float
         acc1 = Op::combine(acc1, in[i]);
     const float4 *v4 = reinterpret_cast<const float4 *>(in + head);
     int64_t v = tid;
-    for (; v + stride < n_vec; v += 2 * stride) {
-        const float4 a = v4[v];
-        const float4 b = v4[v + stride];
-        acc0 = Op::combine(acc0, Op::combine(a.x, a.y));
-        acc1 = Op::combine(acc1, Op::combine(a.z, a.w));
-        acc2 = Op::combine(acc2, Op::combine(b.x, b.y));
-        acc3 = Op::combine(acc3, Op::combine(b.z, b.w));
+    // eight 16-byte loads in flight per thread per iteration (128 bytes):
+    // the grid is one wave, so each thread's iterations are round trips
+    constexpr int kUnroll = 8;
+    for (; v + (kUnroll - 1) * stride < n_vec; v += kUnroll * stride) {
+        float4 a[kUnroll];
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u)
+            a[u] = v4[v + u * stride];
+#pragma unroll
+        for (int u = 0; u < kUnroll; u += 2) {
+            acc0 = Op::combine(acc0, Op::combine(a[u].x, a[u].y));
+            acc1 = Op::combine(acc1, Op::combine(a[u].z, a[u].w));
+            acc2 = Op::combine(acc2, Op::combine(a[u + 1].x, a[u + 1].y));
+            acc3 = Op::combine(acc3, Op::combine(a[u + 1].z, a[u + 1].w));
+        }
     }
-    if (v < n_vec) {
+    for (; v < n_vec; v += stride) {
         const float4 a = v4[v];
         acc0 = Op::combine(acc0, Op::combine(a.x, a.y));
         acc1 = Op::combine(acc1, Op::combine(a.z, a.w));
