@@ -44,6 +44,7 @@
 #include "../ops/attention_kernels.cuh"
 #include "../ops/attention_prefill_tc.cuh"
 #include "../ops/gemm_sm100.cuh"
+#include "../ops/gemm_sm100_pair.cuh"
 #include "../ops/linear.cuh"
 #include "../ops/llama_kernels.cuh"
 #include "../runtime/kv_cache.cuh"
@@ -519,6 +520,12 @@ template <typename WT> class LlamaEngineT {
                                                         sm100::gemm_pick_bn(sm100::GemmKind::kBF16, rows));
             return;
         }
+        if (rows >= pair_min_rows_) {
+            // prefill-sized GEMMs: two-SM 256 x 256 tiles (cta_group::2)
+            sm100::gemm_pair_bf16x2<Epi>({p.bf16.data(), nullptr, p.out, p.in}, {x.bf16, x.bf16_lo, rows, p.in}, p.in,
+                                         stream_, epi);
+            return;
+        }
         const int splits = plan_splits(p, rows, max_cluster_splits_);
         const bool pf = next != nullptr && l2_prefetch_ && rows <= 64;
         sm100::gemm_tn<sm100::GemmKind::kBF16x2, Epi>(
@@ -792,6 +799,14 @@ template <typename WT> class LlamaEngineT {
     int prefill_single_rows_ = [] {
         const char *e = std::getenv("OPWORKS_PREFILL_SINGLE_ROWS");
         return e ? std::atoi(e) : (1 << 30);
+    }();
+    // fast-path GEMMs of at least this many token rows (and not taken by
+    // the single-term path) run the two-SM cta_group::2 kernel;
+    // OPWORKS_PAIR_GEMM_ROWS overrides the threshold (0: never)
+    int pair_min_rows_ = [] {
+        const char *e = std::getenv("OPWORKS_PAIR_GEMM_ROWS");
+        const int v = e ? std::atoi(e) : 512;
+        return v > 0 ? v : (1 << 30);
     }();
     bool tc_prefill_ = [] {
         const char *e = std::getenv("OPWORKS_TC_PREFILL");

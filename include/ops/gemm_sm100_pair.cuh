@@ -1,0 +1,306 @@
+#pragma once
+
+// Two-SM (cta_group::2) tcgen05 GEMM for prefill-sized projections of the
+// fast path: bf16 weights times two-term bf16 activations (kBF16x2), fp32
+// accumulate, tile epilogue fused.
+//
+//   out[tok][feat] = epi( sum_k W[feat][k] * (Xhi + Xlo)[tok][k] )
+//
+// A pair of CTAs (a cluster of 2 along the feature tiles) computes one
+// 256-feature x 256-token tile with tcgen05.mma.cta_group::2 (M = 256,
+// N = 256): CTA rank r stages the 128 weight rows f0 + 128 r .. and the 128
+// token rows t0 + 128 r .. (hi and lo) of every 64-element K block, and the
+// leader CTA (rank 0) issues the MMAs, which read both CTAs' shared memory
+// and leave rank r's 128 features x 256 tokens in rank r's tensor memory.
+// Per CTA and K block that is 48 KB of operands for 128 x 256 x 64 x 2 MACs:
+// half the shared-memory traffic per MAC of a one-CTA 128 x 128 tile, which
+// is what keeps the tensor cores fed from L2 at prefill sizes.
+//
+// Protocol (every wait bounded; on a timeout the error word is set and the
+// CTA still takes every cluster barrier):
+//   * both producers wait on their own empty[s]; the leader's producer
+//     posts the expected bytes of BOTH CTAs on the leader's full[s]; both
+//     CTAs' TMA loads (.cta_group::2) complete on the leader's full[s];
+//   * the leader's MMA thread waits full[s], issues 4 K steps x 2 terms,
+//     and commits to empty[s] of both CTAs (multicast commit); after the
+//     last block it commits to accum of both CTAs;
+//   * each CTA's epilogue warps read their own tensor memory into a
+//     [256][128] fp32 tile in shared memory and run the tile epilogue.
+// Loads carry no cluster multicast: each CTA fetches its own operands.
+
+#include "gemm_sm100.cuh"
+
+namespace opworks::sm100 {
+
+struct PairShape {
+    static constexpr int BN = 256;                   // tokens per pair tile (128 per CTA staged)
+    static constexpr uint32_t kABytes = kUmmaM * kUmmaKBytes; // 128 weight rows x 128 B
+    static constexpr uint32_t kBBytes = 128 * kUmmaKBytes;    // 128 token rows x 128 B (one term)
+    static constexpr uint32_t kStageBytes = kABytes + 2 * kBBytes;
+    static constexpr int kStages = 4;
+    static constexpr uint32_t kTmemCols = BN;
+    static constexpr size_t kEpiScratchBytes = 16u * BN;
+    static constexpr size_t kSmemBytes = 1024 + static_cast<size_t>(kStages) * kStageBytes + 256 + kEpiScratchBytes;
+    static_assert(static_cast<size_t>(BN) * kUmmaM * 4 <= static_cast<size_t>(kStages) * kStageBytes,
+                  "the fp32 output tile must fit in the pipeline stages");
+};
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+// Shared-memory address of the same variable in cluster CTA `rank`.
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t smem_addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
+    return r;
+}
+
+// 2D TMA load into this CTA's shared memory whose completion is counted on
+// an mbarrier of either CTA of the pair (shared::cluster address).
+__device__ __forceinline__ void tma_load_2d_pair(void *smem_dst, const CUtensorMap *tm, uint32_t bar_cluster, int c0,
+                                                 int c1) {
+    asm volatile("cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+                 " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(smem_dst)),
+                 "l"(reinterpret_cast<uint64_t>(tm)), "r"(bar_cluster), "r"(c0), "r"(c1)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t *slot_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot_smem)),
+                 "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// D[tmem] (+)= A * B^T over the CTA pair (M = 256 split across the pair,
+// N split across the pair's B halves), bf16 inputs.
+__device__ __forceinline__ void umma_bf16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                               uint32_t accumulate) {
+    asm volatile("{\n\t.reg .pred p;\n\t"
+                 "setp.ne.b32 p, %4, 0;\n\t"
+                 "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+                 "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+                 : "memory");
+}
+
+// Arrive once on `bar` (same shared-memory offset) of every CTA in `mask`
+// when the MMAs issued so far by this thread have completed.
+__device__ __forceinline__ void umma_commit_pair(uint64_t *bar, uint16_t mask) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+                     smem_u32(bar)),
+                 "h"(mask)
+                 : "memory");
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+    cluster_arrive();
+    cluster_wait();
+}
+
+// grid = (feature tiles rounded up to even, token tiles of 256), cluster
+// (2, 1, 1), 192 threads: warp 0 TMA producer, warp 1 TMEM + MMA issuer
+// (leader only), warps 2-5 epilogue.
+template <typename Epi>
+__global__ void __launch_bounds__(192, 1)
+    umma_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                          const __grid_constant__ CUtensorMap tmB_lo, GemmParams p, Epi epi) {
+    using S = PairShape;
+    constexpr int kStages = S::kStages;
+    static_assert(is_tile_epilogue<Epi>::value, "the pair GEMM runs tile epilogues");
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + kStages * S::kStageBytes);
+    uint64_t *empty = full + kStages;
+    uint64_t *accum = empty + kStages;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(accum + 1);
+    void *epi_scratch = smem + kStages * S::kStageBytes + 256;
+
+    const int warp = threadIdx.x / kWarpSize;
+    const int lane = threadIdx.x % kWarpSize;
+    const uint32_t rank = cluster_rank();
+    const bool leader = rank == 0;
+    const int f0 = blockIdx.x * kUmmaM;        // this CTA's 128 features
+    const int t0 = blockIdx.y * S::BN;         // the pair's 256 tokens
+    const int tb = t0 + static_cast<int>(rank) * 128; // this CTA's staged token rows
+
+    if (warp == 0 && lane == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(accum, 1);
+        fence_mbarrier_init();
+        prefetch_tmap(&tmA);
+        prefetch_tmap(&tmB);
+        prefetch_tmap(&tmB_lo);
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(tmem_slot, S::kTmemCols);
+        tmem_relinquish_pair();
+    }
+    pdl_trigger();
+    tc_fence_before();
+    cluster_sync_all(); // barriers initialised and tensor memory allocated in both CTAs
+    tc_fence_after();
+    const uint32_t tmem_d = *tmem_slot;
+    bool ok = true;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            const uint32_t full0 = map_to_rank(smem_u32(full), 0); // the leader's full[0]
+            auto bar = [&](int s) { return full0 + static_cast<uint32_t>(s) * 8u; };
+            auto load_a = [&](int kb, int s) {
+                tma_load_2d_pair(smem + s * S::kStageBytes, &tmA, bar(s), kb * 64, f0);
+            };
+            auto load_b = [&](int kb, int s) {
+                uint8_t *st = smem + s * S::kStageBytes;
+                tma_load_2d_pair(st + S::kABytes, &tmB, bar(s), kb * 64, tb);
+                tma_load_2d_pair(st + S::kABytes + S::kBBytes, &tmB_lo, bar(s), kb * 64, tb);
+            };
+            // weights of the first stages stream before the programmatic-
+            // launch wait; activations after it
+            const int pre = min(kStages, p.num_kb);
+            for (int j = 0; j < pre; ++j) {
+                if (leader)
+                    mbar_arrive_expect_tx(&full[j], 2u * S::kStageBytes);
+                load_a(j, j);
+            }
+            pdl_wait();
+            for (int j = 0; j < pre; ++j)
+                load_b(j, j);
+            for (int kb = pre; kb < p.num_kb; ++kb) {
+                const int s = kb % kStages;
+                const uint32_t ph = static_cast<uint32_t>(kb / kStages) & 1u;
+                if (!mbar_wait(&empty[s], ph ^ 1u)) {
+                    ok = false;
+                    break;
+                }
+                if (leader)
+                    mbar_arrive_expect_tx(&full[s], 2u * S::kStageBytes);
+                load_a(kb, s);
+                load_b(kb, s);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && leader) {
+            constexpr uint32_t idesc = idesc_make(kFmtBF16, 2 * kUmmaM, S::BN);
+            for (int kb = 0; kb < p.num_kb; ++kb) {
+                const int s = kb % kStages;
+                const uint32_t ph = static_cast<uint32_t>(kb / kStages) & 1u;
+                if (!mbar_wait(&full[s], ph)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t a = smem_u32(smem + s * S::kStageBytes);
+                const uint32_t b = a + S::kABytes;
+#pragma unroll
+                for (int k = 0; k < 4; ++k) { // four 32-byte K steps per 128-byte block
+                    const uint64_t ad = sdesc_k128(a + 32 * k);
+                    const uint64_t bd = sdesc_k128(b + 32 * k);
+                    const uint64_t bd_lo = sdesc_k128(b + S::kBBytes + 32 * k);
+                    umma_bf16_pair(tmem_d, ad, bd_lo, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+                    umma_bf16_pair(tmem_d, ad, bd, idesc, 1u);
+                }
+                umma_commit_pair(&empty[s], 0x3);
+            }
+            // also on the error path: the epilogues of both CTAs wait on it
+            umma_commit_pair(accum, 0x3);
+        }
+    } else {
+        pdl_wait(); // the output may still be read by an earlier kernel
+        const int q = warp & 3;
+        const int col = q * 32 + lane;
+        const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
+        const int ntok = max(0, min(S::BN, p.m_tok - t0));
+        const int nfeat = min(kUmmaM, p.n_feat - f0);
+        if constexpr (has_prepare<Epi>::value)
+            if (f0 < p.n_feat)
+                epi.prepare(t0, ntok, f0, nfeat, static_cast<int>(threadIdx.x) - 64, epi_scratch);
+        if (!mbar_wait_warp(accum, 0))
+            ok = false;
+        tc_fence_after();
+        // [256 tokens][128 features] fp32 over the idle stages (every MMA
+        // reading either CTA's stages has completed: accum follows them)
+        float *ptile = reinterpret_cast<float *>(smem);
+#pragma unroll 1
+        for (int c = 0; c < S::BN; c += 64) {
+            uint32_t r[4][16];
+#pragma unroll
+            for (int g = 0; g < 4; ++g)
+                tmem_ld_32x16(tmem_d + lane_base + static_cast<uint32_t>(c + 16 * g), r[g]);
+            tmem_wait_ld();
+#pragma unroll
+            for (int g = 0; g < 4; ++g) {
+                tmem_reg_fence(r[g]);
+#pragma unroll
+                for (int i = 0; i < 16; ++i)
+                    ptile[(c + 16 * g + i) * kUmmaM + col] = __uint_as_float(r[g][i]);
+            }
+        }
+    }
+    __syncthreads(); // the output tile is complete
+    if (warp >= 2 && f0 < p.n_feat) { // the last pair may hold one tile past the features
+        const int ntok = max(0, min(S::BN, p.m_tok - t0));
+        epi(reinterpret_cast<const float *>(smem), t0, ntok, f0, min(kUmmaM, p.n_feat - f0),
+            static_cast<int>(threadIdx.x) - 64, epi_scratch);
+    }
+    if (!ok)
+        atomicExch(p.err, 1);
+    // neither CTA frees tensor memory or exits while its peer may still use
+    // the pair's resources (MMA reads of shared memory, commits)
+    tc_fence_before();
+    cluster_sync_all();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem_d, S::kTmemCols);
+    }
+}
+
+template <typename Epi> inline void gemm_pair_prepare_kernel() {
+    static thread_local int done_device = -1;
+    int dev = 0;
+    OPWORKS_CUDA_CHECK(cudaGetDevice(&dev));
+    if (done_device != dev) {
+        OPWORKS_CUDA_CHECK(cudaFuncSetAttribute(umma_gemm_pair_kernel<Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                static_cast<int>(PairShape::kSmemBytes)));
+        done_device = dev;
+    }
+}
+
+// out via `epi` (a tile epilogue): W [n_feat][k] bf16, X = Xhi + Xlo
+// [m_tok][k] bf16 (K-major, row strides 16-byte aligned). One launch, no K
+// split; grids are pairs of 128-feature tiles by 256-token tiles.
+template <typename Epi>
+inline void gemm_pair_bf16x2(const GemmOperand &W, const GemmOperand &X, int k, cudaStream_t stream, const Epi &epi) {
+    static_assert(is_tile_epilogue<Epi>::value, "gemm_pair_bf16x2 runs tile epilogues");
+    detail::require(k > 0 && W.rows > 0 && X.rows > 0, "gemm_pair_bf16x2: empty operand");
+    GemmParams p{};
+    p.out = nullptr;
+    p.ldo = 0;
+    p.split_stride = 0;
+    p.n_feat = W.rows;
+    p.m_tok = X.rows;
+    p.num_kb = (k + 63) / 64;
+    p.splits = 1;
+    p.err = device_error_word();
+    const CUtensorMap ta = make_tmap_2d(W.hi, true, static_cast<uint64_t>(k), W.rows, W.ld, 64, kUmmaM);
+    const CUtensorMap tb = make_tmap_2d(X.hi, true, static_cast<uint64_t>(k), X.rows, X.ld, 64, 128);
+    const CUtensorMap tb_lo = make_tmap_2d(X.lo, true, static_cast<uint64_t>(k), X.rows, X.ld, 64, 128);
+    gemm_pair_prepare_kernel<Epi>();
+    const int ftiles = (W.rows + kUmmaM - 1) / kUmmaM;
+    const dim3 grid((ftiles + 1) / 2 * 2, (X.rows + PairShape::BN - 1) / PairShape::BN, 1);
+    detail::require(grid.y <= 65535, "gemm_pair_bf16x2: grid exceeds the CUDA limits");
+    launch_ex_cluster(umma_gemm_pair_kernel<Epi>, grid, dim3(2, 1, 1), dim3(192), PairShape::kSmemBytes, stream, ta,
+                      tb, tb_lo, p, epi);
+}
+
+} // namespace opworks::sm100

@@ -135,6 +135,12 @@ OPW_API int opw_paged_attention_prefill(const float *q, const float *kpool, cons
  * split-K plan. Returns the split count used, or -1. */
 OPW_API int opw_gemm_bf16x2(const uint16_t *W, const uint16_t *x_hi, const uint16_t *x_lo, float *out, int N, int K,
                             int M, int splits, void *stream);
+/* out[M][N] (fp32) = W[N][K] (bf16) . (Xhi + Xlo)[M][K]^T by the two-SM
+ * (tcgen05 cta_group::2) GEMM of the runtime's prefill projections: pairs of
+ * CTAs compute 256 x 256 tiles (include/ops/gemm_sm100_pair.cuh). K must be a
+ * multiple of 8. Extension of this library (no reference counterpart). */
+OPW_API int opw_gemm_bf16x2_pair(const uint16_t *W, const uint16_t *x_hi, const uint16_t *x_lo, float *out, int N,
+                                 int K, int M, void *stream);
 
 #ifdef __cplusplus
 }

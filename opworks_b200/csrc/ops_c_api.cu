@@ -14,6 +14,7 @@
 #include "ops/attention_decode.cuh"
 #include "ops/attention_prefill.cuh"
 #include "ops/attention_prefill_tc.cuh"
+#include "ops/gemm_sm100_pair.cuh"
 #include "ops/causal_scale.cuh"
 #include "ops/embedding.cuh"
 #include "ops/linear.cuh"
@@ -381,6 +382,17 @@ int opw_gemm_bf16x2(const uint16_t *W, const uint16_t *x_hi, const uint16_t *x_l
         used = splits;
     });
     return rc == 0 ? used : -1;
+}
+
+int opw_gemm_bf16x2_pair(const uint16_t *W, const uint16_t *x_hi, const uint16_t *x_lo, float *out, int N, int K,
+                         int M, void *stream) {
+    return guarded([&] {
+        using namespace opworks;
+        detail::require(W && x_hi && x_lo && out && N > 0 && K > 0 && M > 0, "gemm_bf16x2_pair: bad arguments");
+        detail::require(K % 8 == 0, "gemm_bf16x2_pair: K must be a multiple of 8 (16-byte rows)");
+        sm100::gemm_pair_bf16x2({as_bf16(W), nullptr, N, K}, {as_bf16(x_hi), as_bf16(x_lo), M, K}, K,
+                                as_stream(stream), sm100::StoreTileEpi<sm100::Identity>{out, N, {}});
+    });
 }
 
 int opw_sample(const float *logits, int rows, int vocab, const float *temperature, const float *top_p,

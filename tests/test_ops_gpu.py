@@ -132,6 +132,26 @@ def test_matmul_builder_launcher(ops, ta, tb, act, bias, M, N, K):
     close(host(c), e, 2e-5)
 
 
+# two-SM (cta_group::2) GEMM of the prefill projections: even pairs of
+# feature tiles, a padded last pair (384 features), ragged token and K tails,
+# a single K block
+@pytest.mark.parametrize("M,N,K", [(512, 512, 1024), (300, 384, 200), (256, 128, 64), (1024, 2048, 2048)])
+def test_gemm_bf16x2_pair_vs_fp64(ops, M, N, K):
+    rng = np.random.default_rng(M + 3 * N + 7 * K)
+    w = (rng.standard_normal((N, K)) / math.sqrt(K)).astype(np.float32)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    wb = torch.from_numpy(w).to(torch.bfloat16)
+    xh = torch.from_numpy(x).to(torch.bfloat16)
+    xl = (torch.from_numpy(x) - xh.float()).to(torch.bfloat16)
+    out = torch.full((M, N), float("nan"), device="cuda")
+    dw, dh, dl = (t.cuda().view(torch.int16) for t in (wb, xh, xl))  # alive until the sync
+    rc = ops.raw("gemm_bf16x2_pair")(dw, dh, dl, out, N, K, M, 0)
+    assert rc == 0
+    sync(ops)
+    e = (xh.double() + xl.double()).numpy() @ wb.double().numpy().T
+    close(host(out), e, 2e-5)
+
+
 @pytest.mark.parametrize("rows", [2, 3, 16, 32, 33, 64, 100, 128, 256, 300])
 def test_linear_bf16_tensor_cores(ops, rows):
     rng = np.random.default_rng(rows)
