@@ -83,6 +83,46 @@ struct ActOut {
             f32[i] = v;
         }
     }
+    // four consecutive columns col .. col + 3 (col and ld multiples of 4)
+    __device__ __forceinline__ void put4c(int64_t row, int col, float4 v) const {
+        const int64_t i = row * ld + col;
+        if (bf16) {
+            const __nv_bfloat162 h01 = __floats2bfloat162_rn(v.x, v.y), h23 = __floats2bfloat162_rn(v.z, v.w);
+            uint2 hv;
+            hv.x = *reinterpret_cast<const uint32_t *>(&h01);
+            hv.y = *reinterpret_cast<const uint32_t *>(&h23);
+            *reinterpret_cast<uint2 *>(bf16 + i) = hv;
+            if (bf16_lo) {
+                const float2 f01 = __bfloat1622float2(h01), f23 = __bfloat1622float2(h23);
+                const __nv_bfloat162 l01 = __floats2bfloat162_rn(v.x - f01.x, v.y - f01.y);
+                const __nv_bfloat162 l23 = __floats2bfloat162_rn(v.z - f23.x, v.w - f23.y);
+                uint2 lv;
+                lv.x = *reinterpret_cast<const uint32_t *>(&l01);
+                lv.y = *reinterpret_cast<const uint32_t *>(&l23);
+                *reinterpret_cast<uint2 *>(bf16_lo + i) = lv;
+            }
+        } else {
+            put(row, col, v.x);
+            put(row, col + 1, v.y);
+            put(row, col + 2, v.z);
+            put(row, col + 3, v.w);
+        }
+    }
+    // two consecutive columns col, col + 1 (col and ld even)
+    __device__ __forceinline__ void put2c(int64_t row, int col, float a, float b) const {
+        const int64_t i = row * ld + col;
+        if (bf16) {
+            const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+            *reinterpret_cast<__nv_bfloat162 *>(bf16 + i) = h;
+            if (bf16_lo) {
+                const float2 f = __bfloat1622float2(h);
+                *reinterpret_cast<__nv_bfloat162 *>(bf16_lo + i) = __floats2bfloat162_rn(a - f.x, b - f.y);
+            }
+        } else {
+            put(row, col, a);
+            put(row, col + 1, b);
+        }
+    }
     // attention-writer form (head-major columns)
     __device__ __forceinline__ void put(int64_t t, int h, int d, float v) const { put(t, h * 64 + d, v); }
     __device__ __forceinline__ void put4(int64_t t, int h, int d0, float a, float b, float c, float e) const {

@@ -238,51 +238,82 @@ struct ResidualTileEpi {
     }
     __device__ __forceinline__ void operator()(const float *tile, int tok0, int ntok, int f0, int nfeat, int tid,
                                                void *scratch) const {
-        // thread tid owns column tid of every token row of the tile (each
-        // thread reads back only what it staged in prepare()); otherwise the
-        // residual values of kChunk tokens are loaded together (one memory
-        // latency per chunk, not per token)
+        // warp w takes tokens w, w + 4, ...; lane l owns columns 4l .. 4l + 3
+        // (16-byte loads and stores), so a token's sum of squares is one warp
+        // reduction. The residual rows of kChunk tokens per warp are loaded
+        // together (one memory latency per chunk), from the rows staged in
+        // shared memory by prepare() when they fit.
         constexpr int kChunk = 8;
         const bool staged = preload && ntok <= kPreTok;
-        float *red = static_cast<float *>(scratch); // [4 warps][ntok] partial sums of squares
-        const float *sg = red + 4 * kPreTok;
+        const float *sg = static_cast<const float *>(scratch) + 4 * kPreTok;
         const float *sh = sg + 128;
-        const int c = tid;
-        const bool col_ok = c < nfeat;
-        const float g = staged ? sg[c] : ((gain && col_ok) ? gain[f0 + c] : 0.f);
-        float *col = hidden + static_cast<int64_t>(tok0) * ld + f0 + c;
-        for (int tb = 0; tb < ntok; tb += kChunk) {
-            float hv[kChunk];
-#pragma unroll
-            for (int j = 0; j < kChunk; ++j)
-                hv[j] = (col_ok && tb + j < ntok) ? (staged ? sh[(tb + j) * 128 + c] : col[static_cast<int64_t>(tb + j) * ld])
-                                                  : 0.f;
+        const int warp = tid >> 5, lane = tid & 31, c = 4 * lane;
+        const bool vec = c + 3 < nfeat; // whole vector in range (nfeat is 128 on the model's shapes)
+        float4 g = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (gain) {
+            if (staged)
+                g = *reinterpret_cast<const float4 *>(sg + c);
+            else if (vec)
+                g = *reinterpret_cast<const float4 *>(gain + f0 + c);
+            else {
+                g.x = c < nfeat ? gain[f0 + c] : 0.f;
+                g.y = c + 1 < nfeat ? gain[f0 + c + 1] : 0.f;
+                g.z = c + 2 < nfeat ? gain[f0 + c + 2] : 0.f;
+                g.w = c + 3 < nfeat ? gain[f0 + c + 3] : 0.f;
+            }
+        }
+        float *base = hidden + static_cast<int64_t>(tok0) * ld + f0 + c;
+        for (int tb = warp; tb < ntok; tb += 4 * kChunk) {
+            float4 hv[kChunk];
 #pragma unroll
             for (int j = 0; j < kChunk; ++j) {
-                const int t = tb + j;
-                if (t >= ntok) // the same for every thread
+                const int t = tb + 4 * j;
+                hv[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (t < ntok) {
+                    if (staged)
+                        hv[j] = *reinterpret_cast<const float4 *>(sh + t * 128 + c);
+                    else if (vec)
+                        hv[j] = *reinterpret_cast<const float4 *>(base + static_cast<int64_t>(t) * ld);
+                    else {
+                        const float *r = base + static_cast<int64_t>(t) * ld;
+                        hv[j].x = c < nfeat ? r[0] : 0.f;
+                        hv[j].y = c + 1 < nfeat ? r[1] : 0.f;
+                        hv[j].z = c + 2 < nfeat ? r[2] : 0.f;
+                        hv[j].w = c + 3 < nfeat ? r[3] : 0.f;
+                    }
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < kChunk; ++j) {
+                const int t = tb + 4 * j;
+                if (t >= ntok) // the same for every lane of the warp
                     break;
-                float h = 0.f;
-                if (col_ok) {
-                    h = hv[j] + tile[t * 128 + c];
-                    col[static_cast<int64_t>(t) * ld] = h;
+                const float4 v = *reinterpret_cast<const float4 *>(tile + t * 128 + c);
+                const float4 h = make_float4(hv[j].x + v.x, hv[j].y + v.y, hv[j].z + v.z, hv[j].w + v.w);
+                float *r = base + static_cast<int64_t>(t) * ld;
+                if (vec) {
+                    *reinterpret_cast<float4 *>(r) = h;
                     if (gain)
-                        normed.put(tok0 + t, f0 + c, h * g);
+                        normed.put4c(tok0 + t, f0 + c, make_float4(h.x * g.x, h.y * g.y, h.z * g.z, h.w * g.w));
+                } else {
+                    const float hh[4] = {h.x, h.y, h.z, h.w}, gg[4] = {g.x, g.y, g.z, g.w};
+                    for (int e = 0; e < 4; ++e)
+                        if (c + e < nfeat) {
+                            r[e] = hh[e];
+                            if (gain)
+                                normed.put(tok0 + t, f0 + c + e, hh[e] * gg[e]);
+                        }
                 }
                 if (rs.part) {
-                    float sq = h * h;
+                    // columns past nfeat hold 0 (zero-filled operands)
+                    float sq = (h.x * h.x + h.y * h.y) + (h.z * h.z + h.w * h.w);
 #pragma unroll
                     for (int off = 16; off > 0; off >>= 1)
                         sq += __shfl_xor_sync(kFullWarpMask, sq, off);
-                    if ((tid & 31) == 0)
-                        red[(tid >> 5) * ntok + t] = sq;
+                    if (lane == 0)
+                        rs.part[(f0 / 128) * rs.ld + tok0 + t] = sq;
                 }
             }
-        }
-        if (rs.part) {
-            sm100::epilogue_bar();
-            for (int t = tid; t < ntok; t += 128)
-                rs.part[(f0 / 128) * rs.ld + tok0 + t] = ((red[t] + red[ntok + t]) + red[2 * ntok + t]) + red[3 * ntok + t];
         }
     }
 };
@@ -302,12 +333,21 @@ struct SiluMulTileEpi {
     }
     __device__ __forceinline__ void operator()(const float *tile, int tok0, int ntok, int f0, int nfeat, int tid,
                                                void *scratch) const {
+        // warp w takes tokens w, w + 4, ...; lane l reads the 16-byte group
+        // (g, u, g, u) of outputs 2l, 2l + 1 and writes them as one pair
         const float *inv = static_cast<const float *>(scratch);
-        for (int idx = tid; idx < ntok * 64; idx += 128) {
-            const int t = idx >> 6, j = idx & 63;
-            if (2 * j + 1 < nfeat) {
-                const float g = tile[t * 128 + 2 * j] * inv[t], u = tile[t * 128 + 2 * j + 1] * inv[t];
-                act.put(tok0 + t, f0 / 2 + j, g / (1.f + expf(-g)) * u);
+        const int warp = tid >> 5, lane = tid & 31;
+        const bool vec = 4 * lane + 3 < nfeat;
+        for (int t = warp; t < ntok; t += 4) {
+            const float sc = inv[t];
+            const float4 v = *reinterpret_cast<const float4 *>(tile + t * 128 + 4 * lane);
+            const float g0 = v.x * sc, u0 = v.y * sc, g1 = v.z * sc, u1 = v.w * sc;
+            const float a0 = g0 / (1.f + expf(-g0)) * u0, a1 = g1 / (1.f + expf(-g1)) * u1;
+            if (vec) {
+                act.put2c(tok0 + t, f0 / 2 + 2 * lane, a0, a1);
+            } else {
+                if (4 * lane + 1 < nfeat)
+                    act.put(tok0 + t, f0 / 2 + 2 * lane, a0);
             }
         }
     }
@@ -381,7 +421,7 @@ struct QkvTileEpi {
         const float2 *cs = reinterpret_cast<const float2 *>(meta + 4 * kPreTok);
         // kChunk items per thread at a time: their cos/sin loads are issued
         // together (one memory latency per chunk)
-        constexpr int kChunk = 8;
+        constexpr int kChunk = 16;
         const int items = ntok * 64;
         for (int base = 0; base < items; base += kChunk * 128) {
             float2 rv[kChunk];

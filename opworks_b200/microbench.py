@@ -1,10 +1,11 @@
 """Kernel-level timings through the C ABIs: CUDA events on the launching
-stream, warm-up first, L2 flushed (a 256 MB write) before every timed launch,
+stream, warm-up first, L2 flushed (a 256 MB read) before every timed launch,
 median over the timed launches.
 
     python -m opworks_b200.microbench c1        # BASELINE C1 operator configs
     python -m opworks_b200.microbench decode    # decode-step kernels (C3 shapes)
     python -m opworks_b200.microbench prefill   # one 8192-token prefill (C4)
+    python -m opworks_b200.microbench pair      # two-SM prefill GEMMs at the C4 shapes
 
 `c1` times our operators and, when the reference was built from its own
 sources into oracle/_ref (libopworks_ops_ref.so), the reference's kernels on
@@ -203,6 +204,33 @@ def decode(only="all", iters=20):
     return res
 
 
+def pair(M=8192, iters=10):
+    """Two-SM bf16 x two-term-bf16 GEMM (the prefill projections' kernel) at
+    the C4 shapes: M token rows against the QKV, O, gate/up and down weights.
+    TFLOP/s counts the useful 2*M*N*K; the tensor cores execute twice that
+    (one MMA per activation term)."""
+    import torch
+
+    import opworks_b200
+
+    ops = opworks_b200.ops_lib()
+    _, tc, src = measured_peaks()
+    t = Timer(torch)
+    raw = ops.raw("gemm_bf16x2_pair")
+    res = []
+    for name, N, K in [("qkv", 3072, 2048), ("o", 2048, 2048), ("gate_up", 16384, 2048), ("down", 2048, 8192)]:
+        W = (torch.randn(N, K, device="cuda") / K**0.5).to(torch.bfloat16)
+        x = torch.randn(M, K, device="cuda")
+        xh = x.to(torch.bfloat16)
+        xl = (x - xh.float()).to(torch.bfloat16)
+        o = torch.empty(M, N, device="cuda")
+        ms = t(lambda: raw(W.view(torch.int16), xh.view(torch.int16), xl.view(torch.int16), o, N, K, M, 0), iters)
+        f = 2.0 * M * N * K
+        res.append({"gemm": name, "M": M, "N": N, "K": K, "us": round(ms * 1e3, 1),
+                    "useful_tflops": round(f / ms / 1e9, 1), "mma_frac_of_bf16_peak": round(2 * f / ms / 1e9 / tc, 3)})
+    return {"peak_source": src, "bf16_tflops": tc, "gemms": res}
+
+
 def prefill(T=8192, iters=2):
     """BASELINE C4: one T-token prefill of the random-init Llama-3.2-1B on the
     fast path (tensor-core GEMMs and attention), CUDA events on the engine
@@ -233,7 +261,7 @@ def prefill(T=8192, iters=2):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["c1", "decode", "prefill"])
+    ap.add_argument("what", choices=["c1", "decode", "prefill", "pair"])
     ap.add_argument("--tokens", type=int, default=8192)
     ap.add_argument("--only", default="all", choices=["all", "attention", "gemm", "sample"])
     ap.add_argument("--iters", type=int, default=20)
@@ -242,6 +270,8 @@ def main():
         r = c1(a.iters)
     elif a.what == "prefill":
         r = prefill(a.tokens, max(1, min(a.iters, 3)))
+    elif a.what == "pair":
+        r = pair(a.tokens, a.iters)
     else:
         r = decode(a.only, a.iters)
     print(json.dumps(r))
