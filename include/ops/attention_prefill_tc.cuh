@@ -10,8 +10,11 @@
 //
 //   S = Q K^T   tcgen05.mma kind::tf32, A = Q (K-major, smem), B = K (K-major,
 //               smem: the cache's [token][dim] rows), D in TMEM (128 x 128)
-//   P = softmax  4 warps, one TMEM lane (query row) per thread, scores in log2
-//               units (exp2 on the SFU), causal mask, running max / sum
+//   P = softmax  8 warps, two per TMEM lane quarter: a thread owns half of a
+//               query row (64 of the 128 keys), the pair exchanges half-row
+//               maxima; scores in log2 units (one FFMA + exp2 on the SFU per
+//               score), causal mask on diagonal tiles only, running max /
+//               sum; P rounded to tf32
 //   O += P V    tcgen05.mma kind::tf32, A = P (TMEM, written back over S),
 //               B = V (MN-major smem: the same [token][dim] rows), D in TMEM
 //               (128 x 64, double-buffered); the softmax warps fold tile n-1's
@@ -19,10 +22,12 @@
 //               tile n's P, so they never wait for the P V of the tile they
 //               just handed over
 //
-// Roles (192 threads): warp 0 TMA producer (one lane), warp 1 TMEM allocator
-// and single-thread MMA issuer, warps 2-5 softmax + epilogue. S is
+// Roles (320 threads): warp 0 TMA producer (four lanes), warp 1 TMEM
+// allocator and single-thread MMA issuer, warps 2-9 softmax + epilogue. S is
 // double-buffered in TMEM, so QK^T of tile n+1 runs while tile n's softmax
-// does. Every mbarrier wait is bounded (device error word on timeout).
+// does; three KV stages (226 KB of shared memory with Q) keep the reload of a
+// stage (PV commit, 32 page copies, their latency) off the softmax's path.
+// Every mbarrier wait is bounded (device error word on timeout).
 //
 // Precision: TF32 operands (10-bit mantissa) with fp32 accumulation; used by
 // the fast (bf16-weight) model path only.
@@ -33,15 +38,19 @@
 namespace opworks::detail {
 
 constexpr int kPfKvTile = 128;   // keys per KV tile (8 pages)
-constexpr int kPfStages = 2;     // KV tiles in flight
-constexpr int kPfThreads = 192;  // warp 0 TMA, warp 1 MMA, warps 2-5 softmax
+constexpr int kPfStages = 3;     // KV tiles in flight
+constexpr int kPfThreads = 320;  // warp 0 TMA, warp 1 MMA, warps 2-9 softmax
+constexpr int kPfSoftmaxThreads = 256;
 constexpr uint32_t kPfTmemCols = 512; // S0 [0,128), S1 [128,256), O0 [256,320), O1 [320,384)
 
 struct PrefillTcSmem {
     static constexpr uint32_t kSlab = 128 * 128;          // [128 rows][32 fp32], 16 KB
     static constexpr uint32_t kQBytes = 2 * kSlab;         // dims 0-31, 32-63
     static constexpr uint32_t kStageBytes = 4 * kSlab;     // K halves, V halves
-    static constexpr size_t kBytes = 1024 + kQBytes + kPfStages * kStageBytes + 256;
+    // Q | KV stages | barriers (256 B) | half-row max exchange [2][2][128]
+    // floats. No alignment slack: the kernel checks that the dynamic
+    // shared-memory base is 1024-byte aligned (128B-swizzled operands)
+    static constexpr size_t kBytes = kQBytes + kPfStages * kStageBytes + 256 + 4 * 128 * 4;
 };
 
 // Shared-memory descriptor of an MN-major tf32 operand: MN-major 32-bit
@@ -78,6 +87,14 @@ __device__ __forceinline__ void tmem_st_32x16(uint32_t taddr, const uint32_t (&r
 }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+__device__ __forceinline__ void tma_load_4d(void *smem_dst, const CUtensorMap *tm, uint64_t *bar, int c0, int c1,
+                                            int c2, int c3) {
+    asm volatile("cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+                 " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(sm100::smem_u32(smem_dst)),
+                 "l"(reinterpret_cast<uint64_t>(tm)), "r"(sm100::smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+                 : "memory");
+}
+
 __device__ __forceinline__ void tma_load_3d(void *smem_dst, const CUtensorMap *tm, uint64_t *bar, int c0, int c1,
                                             int c2) {
     asm volatile("cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
@@ -97,8 +114,13 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                            int kvh, int b, int T, int q_offset, float scale, Out out, int *err) {
     using SM = PrefillTcSmem;
     constexpr int kPos = 128 / kRep; // query positions per CTA
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    if ((sm100::smem_u32(smem_raw) & 1023u) != 0) { // never taken on sm_100a (no static shared memory)
+        if (threadIdx.x == 0)
+            atomicExch(err, 5);
+        return;
+    }
+    uint8_t *smem = smem_raw;
     uint8_t *qs = smem;
     uint8_t *stages = smem + SM::kQBytes;
     uint64_t *bars = reinterpret_cast<uint64_t *>(stages + kPfStages * SM::kStageBytes);
@@ -110,7 +132,10 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     uint64_t *o_ready = p_ready + 2;           // [2]
     uint64_t *o_free = o_ready + 2;            // [2]
     uint64_t *drain = o_free + 2;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+    uint64_t *xch = drain + 1;                 // [2 tile parities][4 quarters]: half-row max exchange
+    uint64_t *xch_l = xch + 8;                 // [4 quarters]: row-sum exchange
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(xch_l + 4);
+    float *xv = reinterpret_cast<float *>(bars + 32); // [2 parities][2 halves][128 rows]
 
     const int warp = threadIdx.x / kWarpSize, lane = threadIdx.x % kWarpSize;
     const int qt = static_cast<int>(gridDim.x) - 1 - static_cast<int>(blockIdx.x); // heaviest first
@@ -129,13 +154,17 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         }
         for (int i = 0; i < 2; ++i) {
             sm100::mbar_init(&s_ready[i], 1);
-            sm100::mbar_init(&p_ready[i], 128);
+            sm100::mbar_init(&p_ready[i], kPfSoftmaxThreads);
         }
         for (int i = 0; i < 2; ++i) {
             sm100::mbar_init(&o_ready[i], 1);
-            sm100::mbar_init(&o_free[i], 128);
+            sm100::mbar_init(&o_free[i], kPfSoftmaxThreads);
         }
         sm100::mbar_init(drain, 1);
+        for (int i = 0; i < 8; ++i)
+            sm100::mbar_init(&xch[i], 64);
+        for (int i = 0; i < 4; ++i)
+            sm100::mbar_init(&xch_l[i], 64);
         sm100::fence_mbarrier_init();
         sm100::prefetch_tmap(&tmQ);
         sm100::prefetch_tmap(&tmK);
@@ -153,11 +182,17 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     bool ok = true;
 
     if (warp == 0) {
-        if (lane == 0) {
+        // producer: lanes 0-3 each copy two of a tile's eight pages (K and V,
+        // two 32-dim halves each); lane 0 posts the tile's byte count
+        constexpr int kIssuers = 4;
+        constexpr int kPagesPerLane = kPfKvTile / kKvChunk / kIssuers;
+        if (lane < kIssuers) {
             pdl_wait(); // q and the cache are written by earlier kernels
-            sm100::mbar_arrive_expect_tx(full_q, SM::kQBytes);
-            tma_load_3d(qs, &tmQ, full_q, 0, h * kRep, t0);
-            tma_load_3d(qs + SM::kSlab, &tmQ, full_q, 32, h * kRep, t0);
+            if (lane == 0) {
+                sm100::mbar_arrive_expect_tx(full_q, SM::kQBytes);
+                tma_load_3d(qs, &tmQ, full_q, 0, h * kRep, t0);
+                tma_load_3d(qs + SM::kSlab, &tmQ, full_q, 32, h * kRep, t0);
+            }
             int issued = 0;
             for (int n = 0; n < n_tiles; ++n, ++issued) {
                 const int s = n % kPfStages;
@@ -167,26 +202,35 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                     break;
                 }
                 uint8_t *st = stages + s * SM::kStageBytes;
-                sm100::mbar_arrive_expect_tx(&full_kv[s], SM::kStageBytes);
-                for (int pg = 0; pg < kPfKvTile / kKvChunk; ++pg) {
-                    // pages past the last key still load (a valid page): their
-                    // keys are masked and P = 0 there
-                    const int page = min(n * (kPfKvTile / kKvChunk) + pg, last_page);
-                    const int blk = table[static_cast<int64_t>(b) * table_stride + page];
-                    const int row = blk * kvh + h;
-                    const uint32_t off = static_cast<uint32_t>(pg) * kKvChunk * 128;
+                // block-table entries first (their loads overlap; the copies
+                // are ordered after them); pages past the last key still load
+                // (a valid page): their keys are masked and P = 0 there
+                int rows[kPagesPerLane];
+#pragma unroll
+                for (int i = 0; i < kPagesPerLane; ++i)
+                    rows[i] = table[static_cast<int64_t>(b) * table_stride +
+                                    min(n * (kPfKvTile / kKvChunk) + lane * kPagesPerLane + i, last_page)] * kvh + h;
+                if (lane == 0)
+                    sm100::mbar_arrive_expect_tx(&full_kv[s], SM::kStageBytes);
+#pragma unroll
+                for (int i = 0; i < kPagesPerLane; ++i) {
+                    const int row = rows[i];
+                    const uint32_t off = static_cast<uint32_t>(lane * kPagesPerLane + i) * kKvChunk * 128;
                     tma_load_3d(st + off, &tmK, &full_kv[s], 0, 0, row);
                     tma_load_3d(st + SM::kSlab + off, &tmK, &full_kv[s], 32, 0, row);
-                    tma_load_3d(st + 2 * SM::kSlab + off, &tmV, &full_kv[s], 0, 0, row);
-                    tma_load_3d(st + 3 * SM::kSlab + off, &tmV, &full_kv[s], 32, 0, row);
+                    // V page: both 32-dim halves in one copy, [half][16 keys][32]
+                    tma_load_4d(st + 2 * SM::kSlab + 2 * off, &tmV, &full_kv[s], 0, 0, 0, row);
                 }
             }
-            // no copy may be in flight when the CTA exits
-            if (!sm100::mbar_wait(full_q, 0))
-                ok = false;
-            for (int j = (issued > kPfStages ? issued - kPfStages : 0); j < issued; ++j)
-                if (!sm100::mbar_wait(&full_kv[j % kPfStages], static_cast<uint32_t>(j / kPfStages) & 1u))
+            // no copy may be in flight when the CTA exits (each phase of a
+            // stage completes only when all four lanes' copies landed)
+            if (lane == 0) {
+                if (!sm100::mbar_wait(full_q, 0))
                     ok = false;
+                for (int j = (issued > kPfStages ? issued - kPfStages : 0); j < issued; ++j)
+                    if (!sm100::mbar_wait(&full_kv[j % kPfStages], static_cast<uint32_t>(j / kPfStages) & 1u))
+                        ok = false;
+            }
         }
     } else if (warp == 1) {
         if (lane == 0) {
@@ -234,9 +278,14 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 const uint32_t vb = sm100::smem_u32(stages + s * SM::kStageBytes + 2 * SM::kSlab);
                 const uint32_t pa = tmem + static_cast<uint32_t>((n & 1) * kPfKvTile);
                 const uint32_t od = tmem + 256u + static_cast<uint32_t>((n & 1) * 64);
-                for (int ks = 0; ks < kPfKvTile / 8; ++ks) // 8 keys per step = one 1 KB row group of V
+                // 8 keys per step: half a V page ([half][16 keys][32 dims],
+                // 4 KB per page, the 32-dim halves 2 KB apart)
+                for (int ks = 0; ks < kPfKvTile / 8; ++ks)
                     umma_tf32_ts(od, pa + static_cast<uint32_t>(ks * 8),
-                                 sdesc_mn128_32b(vb + static_cast<uint32_t>(ks) * 1024u, SM::kSlab, 512u), idesc_o, ks > 0);
+                                 sdesc_mn128_32b(vb + static_cast<uint32_t>(ks >> 1) * 4096u +
+                                                     static_cast<uint32_t>(ks & 1) * 1024u,
+                                                 2048u, 512u),
+                                 idesc_o, ks > 0);
                 sm100::umma_commit(&o_ready[n & 1]);
                 sm100::umma_commit(&empty_kv[s]);
             }
@@ -246,34 +295,41 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 ok = false;
         }
     } else {
-        // softmax warps: thread = TMEM lane = query row
+        // softmax warps 2-9: warp w reads TMEM lane quarter w % 4 (row
+        // r = 32 (w % 4) + lane) and column half (w - 2) / 4 of every tile:
+        // S / P columns [64 half, +64), O dims [32 half, +32). The two warps
+        // of a row exchange their half-row maxima through shared memory (an
+        // mbarrier per quarter and tile parity, bounded waits) so both use
+        // the same running max; each keeps its half of the row sum.
         const int quarter = warp & 3;
+        const int half = (warp - 2) >> 2;
         const int r = quarter * 32 + lane;
         const int p = r / kRep, hh = r % kRep;
         const int t = t0 + p;
         const int qpos = q_offset + t;
+        const int qpos_min = q_offset + t0; // first row of the CTA: tiles below it need no mask
         const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
-        const float c = scale * kLog2e;
+        const float c = scale * kLog2e; // scores in log2 units: p = 2^(s c - m c)
         float m_run = kNegInf, l_run = 0.f, alpha_prev = 0.f;
-        float o[64];
+        float o[32];
 #pragma unroll
-        for (int i = 0; i < 64; ++i)
+        for (int i = 0; i < 32; ++i)
             o[i] = 0.f;
-        // o = o * alpha + P V of tile k (tensor-memory buffer k & 1)
+        // o = o * alpha + (P V of tile k)[dims 32 half ..] (buffer k & 1)
         auto fold = [&](int k, float alpha) -> bool {
             if (!sm100::mbar_wait_warp(&o_ready[k & 1], static_cast<uint32_t>(k >> 1) & 1u)) {
                 ok = false;
                 return false;
             }
             sm100::tc_fence_after();
-            // the four 16-column loads are in flight together: one wait
-            uint32_t rr[4][16];
+            uint32_t rr[2][16];
 #pragma unroll
-            for (int cc = 0; cc < 4; ++cc)
-                sm100::tmem_ld_32x16(tmem + lane_addr + 256u + static_cast<uint32_t>((k & 1) * 64 + cc * 16), rr[cc]);
+            for (int cc = 0; cc < 2; ++cc)
+                sm100::tmem_ld_32x16(tmem + lane_addr + 256u + static_cast<uint32_t>((k & 1) * 64 + 32 * half + cc * 16),
+                                     rr[cc]);
             sm100::tmem_wait_ld();
 #pragma unroll
-            for (int cc = 0; cc < 4; ++cc) {
+            for (int cc = 0; cc < 2; ++cc) {
                 sm100::tmem_reg_fence(rr[cc]);
 #pragma unroll
                 for (int i = 0; i < 16; ++i)
@@ -284,59 +340,71 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             return true;
         };
         for (int n = 0; n < n_tiles; ++n) {
-            const uint32_t sb = tmem + lane_addr + static_cast<uint32_t>((n & 1) * kPfKvTile);
+            const uint32_t sb = tmem + lane_addr + static_cast<uint32_t>((n & 1) * kPfKvTile + 64 * half);
             if (!sm100::mbar_wait_warp(&s_ready[n & 1], static_cast<uint32_t>(n >> 1) & 1u)) {
                 ok = false;
                 break;
             }
             sm100::tc_fence_after();
-            const int k0 = n * kPfKvTile;
-            // all eight 16-column loads of the score row in flight, one wait
-            uint32_t v[kPfKvTile / 16][16];
+            const int k0 = n * kPfKvTile + 64 * half; // first key of this warp's columns
+            uint32_t v[4][16];
 #pragma unroll
-            for (int cc = 0; cc < kPfKvTile / 16; ++cc)
+            for (int cc = 0; cc < 4; ++cc)
                 sm100::tmem_ld_32x16(sb + static_cast<uint32_t>(cc * 16), v[cc]);
             sm100::tmem_wait_ld();
-            // row max with one accumulator per 16-column group (short
-            // dependency chains), combined in a fixed order
-            float mg[kPfKvTile / 16];
+            // raw-score max, one accumulator per 16 columns (short chains);
+            // the causal mask only on tiles that reach past the CTA's first row
+            const bool masked = n * kPfKvTile + kPfKvTile - 1 > qpos_min;
+            float mg[4];
 #pragma unroll
-            for (int cc = 0; cc < kPfKvTile / 16; ++cc) {
+            for (int cc = 0; cc < 4; ++cc) {
                 sm100::tmem_reg_fence(v[cc]);
                 mg[cc] = kNegInf;
+                if (masked) {
 #pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    const int j = cc * 16 + i;
-                    const float sv = k0 + j <= qpos ? __uint_as_float(v[cc][i]) * c : kNegInf;
-                    v[cc][i] = __float_as_uint(sv);
-                    mg[cc] = fmaxf(mg[cc], sv);
+                    for (int i = 0; i < 16; ++i) {
+                        const float sv = k0 + cc * 16 + i <= qpos ? __uint_as_float(v[cc][i]) : kNegInf;
+                        v[cc][i] = __float_as_uint(sv);
+                        mg[cc] = fmaxf(mg[cc], sv);
+                    }
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 16; ++i)
+                        mg[cc] = fmaxf(mg[cc], __uint_as_float(v[cc][i]));
                 }
             }
-            float mt = kNegInf;
-#pragma unroll
-            for (int cc = 0; cc < kPfKvTile / 16; ++cc)
-                mt = fmaxf(mt, mg[cc]);
+            float mt = fmaxf(fmaxf(mg[0], mg[1]), fmaxf(mg[2], mg[3]));
+            // exchange with the other half of the row
+            xv[((n & 1) * 2 + half) * 128 + r] = mt;
+            sm100::mbar_arrive(&xch[(n & 1) * 4 + quarter]);
+            if (!sm100::mbar_wait_warp(&xch[(n & 1) * 4 + quarter], static_cast<uint32_t>(n >> 1) & 1u)) {
+                ok = false;
+                break;
+            }
+            mt = fmaxf(mt, xv[((n & 1) * 2 + (half ^ 1)) * 128 + r]);
             const float m_new = fmaxf(m_run, mt);
-            const float alpha = m_run == kNegInf ? 0.f : exp2_approx(m_run - m_new);
-            float lg[kPfKvTile / 16];
+            const float alpha = m_run == kNegInf ? 0.f : exp2_approx((m_run - m_new) * c);
+            const float mc = m_new == kNegInf ? 0.f : m_new * c;
+            float lg[4];
 #pragma unroll
-            for (int cc = 0; cc < kPfKvTile / 16; ++cc) {
+            for (int cc = 0; cc < 4; ++cc) {
                 lg[cc] = 0.f;
 #pragma unroll
                 for (int i = 0; i < 16; ++i) {
-                    const float sv = __uint_as_float(v[cc][i]);
-                    const float pv = m_new == kNegInf ? 0.f : exp2_approx(sv - m_new);
-                    lg[cc] += pv;
-                    v[cc][i] = __float_as_uint(pv);
+                    // masked scores are -inf: 2^-inf = 0. P is rounded to
+                    // the nearest tf32 here (the MMA would truncate it), and
+                    // the row sum adds the rounded values, so the weights the
+                    // P V product uses are exactly the ones normalised
+                    const float pv = exp2_approx(fmaf(__uint_as_float(v[cc][i]), c, -mc));
+                    uint32_t u = __float_as_uint(pv);
+                    u = (u + 0xfffu + ((u >> 13) & 1u)) & 0xffffe000u;
+                    lg[cc] += __uint_as_float(u);
+                    v[cc][i] = u;
                 }
                 tmem_st_32x16(sb + static_cast<uint32_t>(cc * 16), v[cc]);
             }
             tmem_wait_st();
-            float lsum = 0.f;
-#pragma unroll
-            for (int cc = 0; cc < kPfKvTile / 16; ++cc)
-                lsum += lg[cc];
-            l_run = l_run * alpha + lsum;
+            l_run = l_run * alpha + ((lg[0] + lg[1]) + (lg[2] + lg[3]));
             m_run = m_new;
             sm100::tc_fence_before();
             sm100::mbar_arrive(&p_ready[n & 1]);
@@ -348,11 +416,20 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         }
         if (ok && n_tiles > 0)
             fold(n_tiles - 1, alpha_prev);
+        // row sum = half 0 + half 1 (the same order in both warps), through
+        // the exchange buffer of parity n_tiles & 1: its last readers (tile
+        // n_tiles - 2) finished before the partner arrived on tile n_tiles - 1
+        float *xl = xv + (n_tiles & 1) * 256;
+        xl[half * 128 + r] = l_run;
+        sm100::mbar_arrive(&xch_l[quarter]);
+        if (!sm100::mbar_wait_warp(&xch_l[quarter], 0))
+            ok = false;
         if (ok && t < T) {
-            const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+            const float l_tot = xl[r] + xl[128 + r];
+            const float inv = l_tot > 0.f ? 1.f / l_tot : 0.f;
 #pragma unroll
-            for (int d = 0; d < 64; d += 4)
-                out.put4(t, h * kRep + hh, d, o[d] * inv, o[d + 1] * inv, o[d + 2] * inv, o[d + 3] * inv);
+            for (int d = 0; d < 32; d += 4)
+                out.put4(t, h * kRep + hh, 32 * half + d, o[d] * inv, o[d + 1] * inv, o[d + 2] * inv, o[d + 3] * inv);
         }
     }
     if (!ok)
@@ -386,13 +463,28 @@ inline CUtensorMap make_tmap_3d_f32(const void *base, uint64_t d0, uint64_t d1, 
     return tm;
 }
 
-// Tensor maps of one K or V pool [blocks][kvh][16][64] fp32: K pages land in
-// the K-major 128B-swizzle layout, V pages in the MN-major one (32-byte
-// swizzle atoms).
+// Tensor maps of one K or V pool [blocks][kvh][16][64] fp32. K pages land in
+// the K-major 128B-swizzle layout, one copy per 32-dim half ({32 dims, 16
+// tokens, page}); V pages in the MN-major one (32-byte swizzle atoms), both
+// halves in one copy: dims {32 dims, 16 tokens (256 B apart), 2 halves
+// (128 B apart), page}, landing as [half][16 tokens][32].
 inline CUtensorMap make_kv_pool_tmap(const float *pool, int64_t blocks, int kvh, bool v_operand) {
-    return make_tmap_3d_f32(pool, kAttnD, kKvChunk, static_cast<uint64_t>(blocks) * kvh, kAttnD * 4,
-                            kKvChunk * kAttnD * 4, kKvChunk, 1,
-                            v_operand ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B);
+    if (!v_operand)
+        return make_tmap_3d_f32(pool, kAttnD, kKvChunk, static_cast<uint64_t>(blocks) * kvh, kAttnD * 4,
+                                kKvChunk * kAttnD * 4, kKvChunk, 1, CU_TENSOR_MAP_SWIZZLE_128B);
+    require(reinterpret_cast<uintptr_t>(pool) % 16 == 0, "TMA base must be 16-byte aligned");
+    CUtensorMap tm;
+    std::memset(&tm, 0, sizeof(tm));
+    const cuuint64_t dims[4] = {32, kKvChunk, 2, static_cast<cuuint64_t>(blocks) * kvh};
+    const cuuint64_t strides[3] = {kAttnD * 4, 32 * 4, kKvChunk * kAttnD * 4};
+    const cuuint32_t box[4] = {32, kKvChunk, 2, 1};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    const CUresult r = sm100::tensor_map_encoder()(&tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float *>(pool),
+                                                   dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                                   CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    require(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (4-D V pages) failed");
+    return tm;
 }
 
 template <int kRep, typename Out> inline void prepare_prefill_tc_kernel() {
