@@ -164,6 +164,17 @@ template <typename WT> class LlamaEngineT {
         for (const Projection *p : projs)
             part = std::max(part, static_cast<int64_t>(plan_splits(*p, rows_max_)) * rows_max_ * p->out);
         part_ = TypedDeviceBuffer<float>(part);
+        if (fast) {
+            // grouped split-K workspace: slices of up to kGroupTiles 32-token
+            // tiles x 2 groups; counters zero-initialised
+            groups_part_ = TypedDeviceBuffer<float>(static_cast<int64_t>(kGroupTiles) * 2 * 32 * kUmmaM);
+            groups_cnt_ = TypedDeviceBuffer<int32_t>(kGroupTiles * sm100::kMaxClusterSplits);
+            OPWORKS_CUDA_CHECK(cudaMemset(groups_cnt_.data(), 0, sizeof(int32_t) * kGroupTiles * sm100::kMaxClusterSplits));
+            groups_ws_.partials = groups_part_.data();
+            groups_ws_.floats = static_cast<size_t>(kGroupTiles) * 2 * 32 * kUmmaM;
+            groups_ws_.counters = reinterpret_cast<unsigned int *>(groups_cnt_.data());
+            groups_ws_.max_counters = kGroupTiles * sm100::kMaxClusterSplits;
+        }
         // split-KV partials of decode attention, for every batch size
         int64_t attn_rows = 0;
         for (int n = 1; n <= max_batch; ++n) {
@@ -526,8 +537,27 @@ template <typename WT> class LlamaEngineT {
                                          stream_, epi);
             return;
         }
-        const int splits = plan_splits(p, rows, max_cluster_splits_);
+        int splits = plan_splits(p, rows, max_cluster_splits_);
         const bool pf = next != nullptr && l2_prefetch_ && rows <= 64;
+        // grids of at most one CTA per SM (16 tiles x 8 splits at C3) double
+        // their splits as two clusters per tile, reduced across clusters
+        // through L2, so twice the weight bytes are in flight
+        int cluster = 0;
+        if (split_groups_ > 0 && plan_bn(rows) == 32 && splits == sm100::kMaxClusterSplits) {
+            const int tiles = (p.out + kUmmaM - 1) / kUmmaM;
+            const int kb = (p.in + 63) / 64;
+            if (tiles * 2 * splits <= 2 * sm_count_ && tiles * splits <= sm_count_ &&
+                kb >= (split_groups_ >= 2 ? 32 : 64) && tiles * 2 <= kGroupTiles) {
+                cluster = splits;
+                splits *= 2;
+            }
+        }
+        if (cluster > 0) {
+            sm100::gemm_tn<sm100::GemmKind::kBF16x2, Epi>(
+                {p.bf16.data(), nullptr, p.out, p.in}, {x.bf16, x.bf16_lo, rows, p.in}, p.in, part_.data(), p.out,
+                splits, static_cast<int64_t>(rows) * p.out, stream_, epi, 32, nullptr, 0, &groups_ws_, cluster);
+            return;
+        }
         sm100::gemm_tn<sm100::GemmKind::kBF16x2, Epi>(
             {p.bf16.data(), nullptr, p.out, p.in}, {x.bf16, x.bf16_lo, rows, p.in}, p.in, part_.data(), p.out, splits,
             static_cast<int64_t>(rows) * p.out, stream_, epi, plan_bn(rows), pf ? next->bf16.data() : nullptr,
@@ -779,6 +809,17 @@ template <typename WT> class LlamaEngineT {
     TypedDeviceBuffer<int32_t> table_dev_;
     bool table_dirty_ = true;
     TypedDeviceBuffer<float> hidden_, ss_, q_, part_, attn_po_, attn_pml_, logits_;
+    static constexpr int kGroupTiles = 64;
+    TypedDeviceBuffer<float> groups_part_;
+    TypedDeviceBuffer<int32_t> groups_cnt_;
+    sm100::SplitGroupWorkspace groups_ws_{};
+    // grouped split K for narrow decode GEMMs whose 8-split grid leaves SMs
+    // idle: 0 off, 1 long K only (>= 64 blocks: the down projection at C3),
+    // 2 also K >= 32 blocks (O); OPWORKS_SPLIT_GROUPS overrides
+    int split_groups_ = [] {
+        const char *e = std::getenv("OPWORKS_SPLIT_GROUPS");
+        return e ? std::atoi(e) : 1;
+    }();
     TypedDeviceBuffer<__nv_bfloat16> normed_bf_, attn_bf_, act_bf_, normed_bflo_, attn_bflo_, act_bflo_;
     TypedDeviceBuffer<float> normed_f_, normed_lo_, attn_f_, attn_lo_, act_f_, act_lo_;
     TypedDeviceBuffer<int32_t> tokens_;

@@ -51,6 +51,23 @@ struct GemmParams {
     // L2 while this GEMM runs; every CTA prefetches its share
     const uint8_t *l2_prefetch = nullptr;
     uint64_t l2_prefetch_bytes = 0;
+    // tile epilogues: CTAs per cluster (0 = splits). With splits = G x
+    // cluster, each of the G clusters of a tile reduces its partials through
+    // distributed shared memory, stores its row slices to red_ws, and the
+    // last cluster to arrive at red_cnt[tile][slice] sums the G slices in
+    // group order and runs the epilogue (counters are zero between launches:
+    // the last arrival resets its own)
+    int cluster = 0;
+    float *red_ws = nullptr;
+    unsigned int *red_cnt = nullptr;
+};
+
+// Workspace of grouped split-K tile epilogues (GemmParams::red_ws / red_cnt).
+struct SplitGroupWorkspace {
+    float *partials = nullptr;        // [tiles][groups][BN][128] fp32
+    size_t floats = 0;
+    unsigned int *counters = nullptr; // [tiles][cluster], zero-initialised
+    int max_counters = 0;
 };
 
 struct Identity {
@@ -315,8 +332,9 @@ __global__ void __launch_bounds__(192, GemmShape<kKind, BN>::kCtasPerSm)
         const int col = q * 32 + lane;
         if constexpr (kTileEpi && has_prepare<Epi>::value) {
             const bool sliced = p.splits > 1; // this CTA's row slice of the cluster's tile
-            const int per = (BN + p.splits - 1) / p.splits;
-            const int tb = sliced ? min(BN, split * per) : 0;
+            const int csz = p.cluster > 0 ? p.cluster : p.splits;
+            const int per = (BN + csz - 1) / csz;
+            const int tb = sliced ? min(BN, (split % csz) * per) : 0;
             const int nt = sliced ? min(BN, tb + per) - tb : BN;
             epi.prepare(t0 + tb, max(0, min(nt, p.m_tok - (t0 + tb))), f0, min(kUmmaM, p.n_feat - f0),
                         static_cast<int>(threadIdx.x) - 64, epi_scratch);
@@ -381,11 +399,16 @@ __global__ void __launch_bounds__(192, GemmShape<kKind, BN>::kCtasPerSm)
         // every thread of every CTA of the cluster takes both barriers, on
         // the error path too
         namespace cg = cooperative_groups;
-        const int nsplit = kFitsReduce ? p.splits : 1; // the host splits only shapes that fit
+        // nsplit = CTAs of this tile's cluster (the host splits only shapes
+        // that fit); groups = clusters per tile
+        const int nsplit = kFitsReduce ? (p.splits > 1 && p.cluster > 0 ? p.cluster : p.splits) : 1;
+        const int groups = kFitsReduce ? p.splits / nsplit : 1;
+        const int rank = split % nsplit, group = split / nsplit;
         float *ptile = reinterpret_cast<float *>(smem);
         float *rtile = ptile + BN * kUmmaM;
         const int per = (BN + nsplit - 1) / nsplit;
-        const int tl0 = min(BN, split * per), tl1 = min(BN, tl0 + per);
+        const int tl0 = min(BN, rank * per), tl1 = min(BN, tl0 + per);
+        __shared__ int run_epilogue;
         if (nsplit > 1) {
             cluster_arrive(); // this CTA's partial tile is published
             cluster_wait();   // and every peer's
@@ -421,11 +444,48 @@ __global__ void __launch_bounds__(192, GemmShape<kKind, BN>::kCtasPerSm)
                     reinterpret_cast<float4 *>(rtile)[(t - tl0) * (kUmmaM / 4) + c4] = acc;
                 }
                 epilogue_bar();
+                if (groups > 1) {
+                    // across the tile's clusters: publish this slice, count
+                    // arrivals; the last group's CTA sums the slices in group
+                    // order (deterministic) and runs the epilogue
+                    const int tile = blockIdx.y * gridDim.x + blockIdx.x;
+                    const int nf4 = (tl1 - tl0) * (kUmmaM / 4);
+                    float4 *ws = reinterpret_cast<float4 *>(p.red_ws) +
+                                 (static_cast<int64_t>(tile) * groups * BN + tl0) * (kUmmaM / 4);
+                    const int64_t gstride = static_cast<int64_t>(BN) * (kUmmaM / 4);
+                    for (int i = et; i < nf4; i += 128)
+                        __stcg(ws + group * gstride + i, reinterpret_cast<const float4 *>(rtile)[i]);
+                    __threadfence();
+                    epilogue_bar();
+                    if (et == 0) {
+                        unsigned int *cnt = p.red_cnt + tile * nsplit + rank;
+                        const bool last = atomicAdd(cnt, 1u) == static_cast<unsigned>(groups - 1);
+                        if (last)
+                            *cnt = 0u; // ready for the next launch
+                        run_epilogue = last;
+                    }
+                    epilogue_bar();
+                    if (run_epilogue) {
+                        __threadfence(); // the other groups' slices are visible
+                        for (int i = et; i < nf4; i += 128) {
+                            float4 acc = __ldcg(ws + i);
+                            for (int g = 1; g < groups; ++g) {
+                                const float4 v = __ldcg(ws + g * gstride + i);
+                                acc.x += v.x;
+                                acc.y += v.y;
+                                acc.z += v.z;
+                                acc.w += v.w;
+                            }
+                            reinterpret_cast<float4 *>(rtile)[i] = acc;
+                        }
+                        epilogue_bar();
+                    }
+                }
             }
             src = rtile;
             cluster_arrive(); // done reading the peers' tiles; the epilogue runs under the barrier
         }
-        if (warp >= 2) {
+        if (warp >= 2 && (groups == 1 || run_epilogue)) {
             const int tb = nsplit > 1 ? tl0 : 0;
             const int ntok = max(0, min(nsplit > 1 ? tl1 - tl0 : BN, p.m_tok - (t0 + tb)));
             epi(src, t0 + tb, ntok, f0, min(kUmmaM, p.n_feat - f0), static_cast<int>(threadIdx.x) - 64, epi_scratch);
@@ -467,8 +527,12 @@ inline void gemm_launch(const CUtensorMap &a, const CUtensorMap &b, const CUtens
     const dim3 grid((p.n_feat + kUmmaM - 1) / kUmmaM, (p.m_tok + BN - 1) / BN, p.splits);
     detail::require(grid.y <= 65535 && grid.z <= 65535, "GEMM grid exceeds the CUDA limits");
     if constexpr (is_tile_epilogue<Epi>::value) {
-        detail::require(p.splits >= 1 && p.splits <= kMaxClusterSplitsNonPortable, "tile epilogue: at most 16 K splits");
-        launch_ex_cluster(umma_gemm_kernel<kKind, BN, Epi>, grid, dim3(1, 1, p.splits), dim3(192), S::kSmemBytes,
+        const int csz = p.splits > 1 && p.cluster > 0 ? p.cluster : p.splits;
+        detail::require(csz >= 1 && csz <= kMaxClusterSplitsNonPortable && p.splits % csz == 0,
+                        "tile epilogue: at most 16 K splits per cluster, splits a multiple of the cluster");
+        detail::require(p.splits == csz || (p.red_ws != nullptr && p.red_cnt != nullptr),
+                        "tile epilogue: grouped split K needs a workspace");
+        launch_ex_cluster(umma_gemm_kernel<kKind, BN, Epi>, grid, dim3(1, 1, csz), dim3(192), S::kSmemBytes,
                           stream, a, b, a_lo, b_lo, p, epi);
     } else {
         launch_ex(umma_gemm_kernel<kKind, BN, Epi>, grid, dim3(192), S::kSmemBytes, stream, a, b, a_lo, b_lo, p, epi);
@@ -517,7 +581,8 @@ inline int gemm_pick_splits(int tiles, int num_kb, int slots, int min_kb = 2, in
 template <GemmKind kKind, typename Epi = Identity>
 inline void gemm_tn(const GemmOperand &A, const GemmOperand &B, int k, float *out, int64_t ldo, int splits,
                     int64_t split_stride, cudaStream_t stream, const Epi &epi = {}, int force_bn = 0,
-                    const void *l2_prefetch = nullptr, uint64_t l2_prefetch_bytes = 0) {
+                    const void *l2_prefetch = nullptr, uint64_t l2_prefetch_bytes = 0,
+                    const SplitGroupWorkspace *groups_ws = nullptr, int cluster = 0) {
     constexpr bool kBf16 = kKind != GemmKind::kTF32x3;
     constexpr int kKElems = kBf16 ? 64 : 32;
     detail::require(k > 0, "gemm_tn: K must be positive");
@@ -536,6 +601,18 @@ inline void gemm_tn(const GemmOperand &A, const GemmOperand &B, int k, float *ou
     p.l2_prefetch = static_cast<const uint8_t *>(l2_prefetch);
     p.l2_prefetch_bytes = l2_prefetch_bytes & ~uint64_t(15);
     int bn = force_bn ? force_bn : gemm_pick_bn(kKind, B.rows);
+    if (is_tile_epilogue<Epi>::value && cluster > 0 && p.splits > cluster) {
+        // grouped split K: the tile grid's partial slices must fit the workspace
+        const int tiles = ((A.rows + kUmmaM - 1) / kUmmaM) * ((B.rows + bn - 1) / bn);
+        detail::require(groups_ws != nullptr && force_bn != 0 && p.splits % cluster == 0,
+                        "gemm_tn: grouped split K needs a workspace, an explicit token tile and whole clusters");
+        detail::require(static_cast<size_t>(tiles) * (p.splits / cluster) * bn * kUmmaM <= groups_ws->floats &&
+                            tiles * cluster <= groups_ws->max_counters,
+                        "gemm_tn: grouped split-K workspace too small");
+        p.cluster = cluster;
+        p.red_ws = groups_ws->partials;
+        p.red_cnt = groups_ws->counters;
+    }
     if (!force_bn && p.splits == 1) {
         // narrow the token tile while the grid is under one wave
         const int sms = detail::device_facts().sm_count;
