@@ -34,6 +34,7 @@
 #include <cstring>
 #include <functional>
 #include <map>
+#include <tuple>
 #include <memory>
 #include <stdexcept>
 #include <string>
@@ -200,6 +201,8 @@ template <typename WT> class LlamaEngineT {
         cudaSetDevice(device_);
         for (auto &g : graphs_)
             cudaGraphExecDestroy(g.second);
+        for (auto &g : multi_graphs_)
+            cudaGraphExecDestroy(g.second);
         if (stream_)
             cudaStreamSynchronize(stream_);
         if (in_host_)
@@ -320,6 +323,91 @@ template <typename WT> class LlamaEngineT {
             slots_[slots[i]].length += 1;
             out[i] = out_host_[i];
         }
+    }
+
+    // `steps` decode tokens for each of n slots without a host round trip per
+    // step: the step's CUDA graph is replayed `steps` times with the sampled
+    // tokens fed back on the device (decode_advance_kernel); KV blocks for all
+    // steps are reserved up front. out[k * n + i] is row i's token of step k,
+    // or -1 after the row emitted `eos` (eos < 0: none); count[i] is the
+    // number of tokens row i produced up to and including its eos. uniforms
+    // (optional, [steps][n]) replace sa[i].uniform from the second step on.
+    void decode_multi(int n, const int32_t *slots, const int32_t *prev, const SampleArgs *sa, int steps,
+                      const double *uniforms, int eos, int32_t *out, int32_t *count) {
+        detail::require(n > 0 && n <= max_batch_ && n <= 1024, "decode batch size outside the engine capacity");
+        detail::require(steps > 0, "multi-step decode needs steps > 0");
+        OPWORKS_CUDA_CHECK(cudaSetDevice(device_));
+        validate_ids(prev, n);
+        use_layout(dec_, 0);
+        int32_t *h_ids = host_i32(layout_.ids), *h_seq = host_i32(layout_.seq), *h_pos = host_i32(layout_.pos);
+        int32_t *h_lens = host_i32(layout_.lens);
+        for (int i = 0; i < n; ++i) {
+            check_slot(slots[i]);
+            for (int j = 0; j < i; ++j)
+                detail::require(slots[j] != slots[i], "a slot appears twice in one decode step");
+            detail::require(slots_[slots[i]].length + steps <= max_seq_len_, "session capacity exhausted");
+        }
+        for (int i = 0; i < n; ++i) {
+            Slot &s = slots_[slots[i]];
+            ensure_blocks(slots[i], s.length + steps);
+            h_ids[i] = prev[i];
+            h_seq[i] = slots[i];
+            h_pos[i] = s.length;
+            h_lens[i] = s.length + 1;
+            stage_sampling(i, sa ? sa[i] : SampleArgs{});
+        }
+        flush_table();
+        if (multi_cap_ < static_cast<int64_t>(steps) * n) {
+            multi_cap_ = static_cast<int64_t>(steps) * n;
+            multi_out_ = TypedDeviceBuffer<int32_t>(multi_cap_);
+            multi_uni_ = TypedDeviceBuffer<uint8_t>(8 * multi_cap_);
+        }
+        if (multi_state_.size() == 0)
+            multi_state_ = TypedDeviceBuffer<int32_t>(2 * static_cast<int64_t>(max_batch_) + 1);
+        multi_steps_ = steps;
+        multi_eos_ = eos;
+        multi_has_uni_ = uniforms != nullptr;
+        OPWORKS_CUDA_CHECK(cudaMemcpyAsync(in_dev_.data(), in_host_, dec_.bytes, cudaMemcpyHostToDevice, stream_));
+        if (uniforms)
+            OPWORKS_CUDA_CHECK(cudaMemcpyAsync(multi_uni_.data(), uniforms, sizeof(double) * steps * n,
+                                               cudaMemcpyHostToDevice, stream_));
+        OPWORKS_CUDA_CHECK(cudaMemsetAsync(multi_state_.data(), 0, sizeof(int32_t) * (2 * max_batch_ + 1), stream_));
+        // the step graph bakes in steps, eos and whether uniforms are given
+        const MultiKey key{n, steps, eos, multi_has_uni_};
+        auto it = multi_graphs_.find(key);
+        if (it == multi_graphs_.end()) {
+            if (graphs_.count(n) == 0) {
+                // modules and kernel attributes load outside any capture
+                multi_body(n);
+                OPWORKS_CUDA_CHECK(cudaStreamSynchronize(stream_));
+                // undo that eager step: same inputs again, counter to 0
+                OPWORKS_CUDA_CHECK(cudaMemcpyAsync(in_dev_.data(), in_host_, dec_.bytes, cudaMemcpyHostToDevice,
+                                                   stream_));
+                OPWORKS_CUDA_CHECK(cudaMemsetAsync(multi_state_.data(), 0, sizeof(int32_t) * (2 * max_batch_ + 1),
+                                                   stream_));
+            }
+            cudaGraph_t graph = nullptr;
+            OPWORKS_CUDA_CHECK(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
+            multi_body(n);
+            OPWORKS_CUDA_CHECK(cudaStreamEndCapture(stream_, &graph));
+            cudaGraphExec_t exec = nullptr;
+            OPWORKS_CUDA_CHECK(cudaGraphInstantiate(&exec, graph, 0));
+            OPWORKS_CUDA_CHECK(cudaGraphDestroy(graph));
+            it = multi_graphs_.emplace(key, exec).first;
+        }
+        for (int k = 0; k < steps; ++k)
+            OPWORKS_CUDA_CHECK(cudaGraphLaunch(it->second, stream_));
+        OPWORKS_CUDA_CHECK(cudaMemcpyAsync(out, multi_out_.data(), sizeof(int32_t) * steps * n,
+                                           cudaMemcpyDeviceToHost, stream_));
+        OPWORKS_CUDA_CHECK(cudaMemcpyAsync(count, multi_state_.data() + max_batch_, sizeof(int32_t) * n,
+                                           cudaMemcpyDeviceToHost, stream_));
+        OPWORKS_CUDA_CHECK(cudaMemcpyAsync(out_host_ + max_batch_, err_word_, sizeof(int32_t), cudaMemcpyDeviceToHost,
+                                           stream_));
+        OPWORKS_CUDA_CHECK(cudaMemsetAsync(err_word_, 0, sizeof(int32_t), stream_));
+        OPWORKS_CUDA_CHECK(cudaStreamSynchronize(stream_));
+        check_device_error();
+        for (int i = 0; i < n; ++i)
+            slots_[slots[i]].length += steps;
     }
 
     // Logits of row `row` of the last step (prefill: row 0 = last position).
@@ -476,6 +564,19 @@ template <typename WT> class LlamaEngineT {
         OPWORKS_CUDA_CHECK(cudaMemcpyAsync(out_host_ + max_batch_, err_word_, sizeof(int32_t),
                                            cudaMemcpyDeviceToHost, stream_));
         OPWORKS_CUDA_CHECK(cudaMemsetAsync(err_word_, 0, sizeof(int32_t), stream_));
+    }
+
+    // one step of a multi-step decode: forward, sample, feed the tokens back
+    void multi_body(int n) {
+        forward(n, /*decode=*/true, 0, 0, nullptr);
+        sample(n);
+        int32_t *st = multi_state_.data(); // done[max_batch] | count[max_batch] | step counter
+        detail::decode_advance_kernel<<<1, 1024, 0, stream_>>>(
+            n, multi_steps_, tokens_.data(), dev_at<int32_t>(layout_.ids), dev_at<int32_t>(layout_.pos),
+            dev_at<int32_t>(layout_.lens), dev_at<int32_t>(layout_.step), dev_at<double>(layout_.uniform),
+            multi_has_uni_ ? reinterpret_cast<const double *>(multi_uni_.data()) : nullptr, multi_eos_, st,
+            st + max_batch_, multi_out_.data(), st + 2 * max_batch_);
+        OPWORKS_CUDA_CHECK(cudaGetLastError());
     }
 
     void fetch_tokens(int n) {
@@ -829,6 +930,20 @@ template <typename WT> class LlamaEngineT {
     void *in_host_ = nullptr;
     int32_t *out_host_ = nullptr;
     std::map<int, cudaGraphExec_t> graphs_;
+    // multi-step decode: graphs keyed by (rows, steps, eos, uniforms given)
+    struct MultiKey {
+        int n, steps, eos;
+        bool uni;
+        bool operator<(const MultiKey &o) const {
+            return std::tie(n, steps, eos, uni) < std::tie(o.n, o.steps, o.eos, o.uni);
+        }
+    };
+    std::map<MultiKey, cudaGraphExec_t> multi_graphs_;
+    TypedDeviceBuffer<int32_t> multi_out_, multi_state_;
+    TypedDeviceBuffer<uint8_t> multi_uni_;
+    int64_t multi_cap_ = 0;
+    int multi_steps_ = 0, multi_eos_ = -1;
+    bool multi_has_uni_ = false;
     bool marks_enabled_ = false;
     // tensor-core prefill attention on the fast path (OPWORKS_TC_PREFILL=0:
     // the fp32 SIMT kernel instead); tensor maps of the layers' KV pools

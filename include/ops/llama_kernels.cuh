@@ -469,6 +469,38 @@ struct QkvTileEpi {
     }
 };
 
+// Device-side step feedback of a multi-step decode (one block, n <= 1024
+// rows): step k = *counter. Row i's sampled token goes to out[k][i] (-1 once
+// the row has emitted `eos`, which ends its count) and becomes the row's next
+// input; position, length and the sampling step advance; the next step's
+// uniform comes from uniforms[k + 1][i] when given. The counter advances last.
+static __global__ void __launch_bounds__(1024)
+    decode_advance_kernel(int n, int steps, const int32_t *__restrict__ sampled, int32_t *ids, int32_t *pos,
+                          int32_t *lens, int32_t *step, double *uniform, const double *__restrict__ uniforms, int eos,
+                          int32_t *done, int32_t *count, int32_t *out, int32_t *counter) {
+    const int k = *counter;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const int32_t tok = sampled[i];
+        int32_t emitted = -1;
+        if (!done[i]) {
+            emitted = tok;
+            count[i] = k + 1;
+            if (tok == eos)
+                done[i] = 1;
+        }
+        out[static_cast<int64_t>(k) * n + i] = emitted;
+        ids[i] = tok;
+        pos[i] += 1;
+        lens[i] += 1;
+        step[i] += 1;
+        if (uniforms != nullptr && k + 1 < steps)
+            uniform[i] = uniforms[static_cast<int64_t>(k + 1) * n + i];
+    }
+    __syncthreads();
+    if (threadIdx.x == 0)
+        *counter = k + 1;
+}
+
 // cos/sin table of RoPE: table[pos][i] = (cosf(a), sinf(a)), a = fp32(pos) *
 // inv_freq[i], the same fp32 expression as ops::rope.
 static __global__ void rope_table_kernel(const float *__restrict__ inv_freq, int max_pos, int half, float2 *__restrict__ out) {

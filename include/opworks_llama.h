@@ -85,6 +85,19 @@ OPW_API int opw_llama_batch_prefill(void *batch, int slot, const int32_t *tokens
 OPW_API int opw_llama_batch_decode(void *batch, int n, const int32_t *slots, const int32_t *prev_tokens,
                            const float *temperature, const float *top_p, const double *uniforms,
                            const uint64_t *seeds, const int32_t *steps, int32_t *out_tokens, char *err, int err_len);
+/* `steps` decode steps for n slots with no host round trip per step (the
+ * host-sync-free multi-step decode the reference's blocking decode_step,
+ * include/models/llama.cuh:118-134, does not have): the sampled tokens are
+ * fed back on the device and KV blocks for all steps are reserved up front.
+ * out_tokens[k * n + i] = row i's token of step k, or -1 after the row
+ * emitted eos_id (eos_id < 0: none); out_counts[i] = tokens row i produced up
+ * to and including its eos. uniforms, when given, is [steps][n] (one uniform
+ * per step); the other arrays are as in opw_llama_batch_decode. The tokens
+ * equal those of `steps` single-step calls with the same arguments. */
+OPW_API int opw_llama_batch_decode_multi(void *batch, int n, const int32_t *slots, const int32_t *prev_tokens,
+                                         const float *temperature, const float *top_p, const double *uniforms,
+                                         const uint64_t *seeds, const int32_t *steps0, int steps, int eos_id,
+                                         int32_t *out_tokens, int32_t *out_counts, char *err, int err_len);
 /* Logits (vocab_size floats) of row `row` of the last step. */
 OPW_API int opw_llama_batch_logits(void *batch, int row, float *out, int n, char *err, int err_len);
 

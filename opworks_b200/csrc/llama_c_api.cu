@@ -383,6 +383,35 @@ int opw_llama_batch_decode(void *batch, int n, const int32_t *slots, const int32
         err, err_len);
 }
 
+int opw_llama_batch_decode_multi(void *batch, int n, const int32_t *slots, const int32_t *prev_tokens,
+                                 const float *temperature, const float *top_p, const double *uniforms,
+                                 const uint64_t *seeds, const int32_t *steps0, int steps, int eos_id,
+                                 int32_t *out_tokens, int32_t *out_counts, char *err, int err_len) {
+    return guard(
+        [&] {
+            if (!batch)
+                throw std::invalid_argument("null batch");
+            if (n <= 0 || steps <= 0 || !slots || !prev_tokens || !out_tokens || !out_counts)
+                throw std::invalid_argument("multi-step decode needs n > 0, steps > 0, slots, prev_tokens and outputs");
+            auto *b = static_cast<BatchHolder *>(batch);
+            set_device(b->owner);
+            std::vector<opworks::SampleArgs> sa(static_cast<size_t>(n));
+            for (int i = 0; i < n; ++i) {
+                sa[i].temperature = temperature ? temperature[i] : 0.f;
+                sa[i].top_p = top_p ? top_p[i] : 1.f;
+                sa[i].uniform = uniforms ? uniforms[i] : -1.0;
+                sa[i].seed = seeds ? seeds[i] : 0;
+                sa[i].step = steps0 ? steps0[i] : 0;
+            }
+            with_engine(b, [&](auto &e) {
+                e.decode_multi(n, slots, prev_tokens, sa.data(), steps, uniforms, eos_id, out_tokens, out_counts);
+                return 0;
+            });
+            return 0;
+        },
+        err, err_len);
+}
+
 int opw_llama_batch_logits(void *batch, int row, float *out, int n, char *err, int err_len) {
     return guard(
         [&] {

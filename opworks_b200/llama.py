@@ -60,6 +60,7 @@ def bind(lib):
         "opw_llama_batch_length": (I, [P, I]),
         "opw_llama_batch_prefill": (I, [P, I, I32P, I, F, F, D, U64, S, I]),
         "opw_llama_batch_decode": (I, [P, I, I32P, I32P, FP, FP, DP, U64P, I32P, I32P, S, I]),
+        "opw_llama_batch_decode_multi": (I, [P, I, I32P, I32P, FP, FP, DP, U64P, I32P, I, I, I32P, I32P, S, I]),
         "opw_llama_batch_logits": (I, [P, I, FP, I, S, I]),
         "opw_llama_batch_stream": (P, [P]),
         "opw_llama_batch_io_bytes": (I, [P, I, ctypes.POINTER(ctypes.c_int64)]),
@@ -164,6 +165,32 @@ class LlamaBatch:
             opt(uniforms, np.float64, DP), opt(seeds, np.uint64, U64P), opt(steps, np.int32, I32P),
             out.ctypes.data_as(I32P), self.err, _ERR_LEN), "decode")
         return out.copy()
+
+    def decode_multi(self, slots, prev, steps, temperature=None, top_p=None, uniforms=None, seeds=None, steps0=None,
+                     eos_id=-1):
+        """`steps` decode steps with no host round trip per step. Returns
+        (tokens [steps][n] with -1 after a row's eos, counts [n]). `uniforms`,
+        when given, is [steps][n]."""
+        slots_a, slots_p = _i32(slots)
+        prev_a, prev_p = _i32(prev)
+        n = slots_a.size
+        keep = []
+
+        def opt(a, dtype, ptype, shape):
+            if a is None:
+                return None
+            a = np.ascontiguousarray(np.broadcast_to(a, shape), dtype=dtype)
+            keep.append(a)
+            return a.ctypes.data_as(ptype)
+
+        out = np.empty((steps, n), np.int32)
+        counts = np.empty(n, np.int32)
+        self._check(self.lib.opw_llama_batch_decode_multi(
+            self.handle, n, slots_p, prev_p, opt(temperature, np.float32, FP, (n,)), opt(top_p, np.float32, FP, (n,)),
+            opt(uniforms, np.float64, DP, (steps, n)), opt(seeds, np.uint64, U64P, (n,)),
+            opt(steps0, np.int32, I32P, (n,)), steps, eos_id, out.ctypes.data_as(I32P), counts.ctypes.data_as(I32P),
+            self.err, _ERR_LEN), "decode_multi")
+        return out, counts
 
     def stream(self):
         """The engine's cudaStream_t as an integer."""

@@ -144,8 +144,8 @@ def test_batched_decode_equals_single(pack_path):
 
 
 def test_fast_path_long_prompt_logits_within_gemm_tolerance(pack_path):
-    """A 1024-token prompt: the fast path's prefill runs single-term bf16
-    activation GEMMs (more than 256 token rows) and tensor-core TF32
+    """A 1024-token prompt: the fast path's prefill runs the two-SM bf16 x
+    two-term-bf16 GEMMs (at least 512 token rows) and tensor-core TF32
     attention; its last-row logits stay within the BASELINE GEMM tolerance of
     the accurate path (fp32 weights, split-TF32 GEMMs, fp32 attention)."""
     from opworks_b200.llama import LlamaBatch, Model
