@@ -121,8 +121,7 @@ struct matmul_launcher {
         float *bt_hi = scratch.as<float>(2 * a_bytes), *bt_lo = scratch.as<float>(2 * a_bytes + b_bytes);
         // token operand: A as [M][N] K-major
         if (!g.transposed_a())
-            launch_async(stream, detail::split_rows_kernel, detail::grid_for(static_cast<int64_t>(M) * ld), kThreads,
-                         g.a().data(), M, N, static_cast<int64_t>(N), a_hi, a_lo, ld);
+            detail::split_rows_launch(stream, g.a().data(), M, N, static_cast<int64_t>(N), a_hi, a_lo, ld);
         else
             launch_async(stream, detail::split_cols_t_kernel,
                          dim3(detail::blocks_for(M, 32), detail::blocks_for(static_cast<int>(ld), 32)), dim3(32, 8),
@@ -133,8 +132,7 @@ struct matmul_launcher {
                          dim3(detail::blocks_for(K, 32), detail::blocks_for(static_cast<int>(ld), 32)), dim3(32, 8),
                          g.b().data(), N, K, bt_hi, bt_lo, ld);
         else
-            launch_async(stream, detail::split_rows_kernel, detail::grid_for(static_cast<int64_t>(K) * ld), kThreads,
-                         g.b().data(), K, N, static_cast<int64_t>(N), bt_hi, bt_lo, ld);
+            detail::split_rows_launch(stream, g.b().data(), K, N, static_cast<int64_t>(N), bt_hi, bt_lo, ld);
         sm100::GemmOperand feat{bt_hi, bt_lo, K, ld};
         sm100::GemmOperand tok{a_hi, a_lo, M, ld};
         sm100::gemm_tf32x3(feat, tok, N, C, K, stream, epi);

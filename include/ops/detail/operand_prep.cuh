@@ -25,17 +25,39 @@ __device__ __forceinline__ float tf32_round(float x) {
     return __uint_as_float(u & 0xffffe000u);
 }
 
+// One block per row (grid-stride over rows): 16-byte stores of the hi / lo
+// rows (ld is a multiple of 4), 16-byte loads when the source row allows.
 static __global__ void split_rows_kernel(const float *__restrict__ src, int rows, int cols, int64_t ld_src,
                                          float *__restrict__ hi, float *__restrict__ lo, int64_t ld) {
-    const int64_t total = static_cast<int64_t>(rows) * ld;
-    OPWORKS_GRID_LOOP(i, total) {
-        const int64_t r = i / ld;
-        const int64_t c = i % ld;
-        const float x = c < cols ? src[r * ld_src + c] : 0.f;
-        const float h = tf32_round(x);
-        hi[i] = h;
-        lo[i] = x - h;
+    const bool vec_src = (ld_src % 4 == 0) && (reinterpret_cast<uintptr_t>(src) % 16 == 0);
+    for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+        const float *s = src + r * ld_src;
+        float4 *h4 = reinterpret_cast<float4 *>(hi + r * ld);
+        float4 *l4 = reinterpret_cast<float4 *>(lo + r * ld);
+        for (int64_t c = 4 * static_cast<int64_t>(threadIdx.x); c < ld; c += 4 * static_cast<int64_t>(blockDim.x)) {
+            float4 x;
+            if (vec_src && c + 3 < cols) {
+                x = *reinterpret_cast<const float4 *>(s + c);
+            } else {
+                x.x = c < cols ? s[c] : 0.f;
+                x.y = c + 1 < cols ? s[c + 1] : 0.f;
+                x.z = c + 2 < cols ? s[c + 2] : 0.f;
+                x.w = c + 3 < cols ? s[c + 3] : 0.f;
+            }
+            const float4 h = make_float4(tf32_round(x.x), tf32_round(x.y), tf32_round(x.z), tf32_round(x.w));
+            h4[c / 4] = h;
+            l4[c / 4] = make_float4(x.x - h.x, x.y - h.y, x.z - h.z, x.w - h.w);
+        }
     }
+}
+
+// Launch of split_rows_kernel: ld must be a multiple of 4 (16-byte rows).
+inline void split_rows_launch(cudaStream_t stream, const float *src, int rows, int cols, int64_t ld_src, float *hi,
+                              float *lo, int64_t ld) {
+    require(ld % 4 == 0, "split_rows: the padded row stride must be a multiple of 4");
+    const int grid = rows < 65535 ? rows : 65535;
+    if (grid > 0)
+        launch_async(stream, split_rows_kernel, grid, kThreads, src, rows, cols, ld_src, hi, lo, ld);
 }
 
 // 32x32 tiles through shared memory so both the read of src rows and the

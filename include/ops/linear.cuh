@@ -202,10 +202,8 @@ inline void linear_f32_tc(const float *X, const float *W, float *Y, int rows, in
     StreamScratch scratch(2 * x_bytes + 2 * w_bytes, stream);
     float *x_hi = scratch.as<float>(0), *x_lo = scratch.as<float>(x_bytes);
     float *w_hi = scratch.as<float>(2 * x_bytes), *w_lo = scratch.as<float>(2 * x_bytes + w_bytes);
-    launch_async(stream, split_rows_kernel, grid_for(static_cast<int64_t>(rows) * ld), kThreads, X, rows, in,
-                 static_cast<int64_t>(in), x_hi, x_lo, ld);
-    launch_async(stream, split_rows_kernel, grid_for(static_cast<int64_t>(out) * ld), kThreads, W, out, in,
-                 static_cast<int64_t>(in), w_hi, w_lo, ld);
+    split_rows_launch(stream, X, rows, in, static_cast<int64_t>(in), x_hi, x_lo, ld);
+    split_rows_launch(stream, W, out, in, static_cast<int64_t>(in), w_hi, w_lo, ld);
     sm100::GemmOperand feat{w_hi, w_lo, out, ld};
     sm100::GemmOperand tok{x_hi, x_lo, rows, ld};
     sm100::gemm_tf32x3(feat, tok, in, Y, out, stream);

@@ -49,8 +49,7 @@ inline void mat_mul(const float *A, const float *B, float *C, int M, int N, int 
     float *bt_hi = scratch.as<float>(2 * a_bytes);
     float *bt_lo = scratch.as<float>(2 * a_bytes + b_bytes);
 
-    launch_async(stream, detail::split_rows_kernel, detail::grid_for(static_cast<int64_t>(M) * ld), kThreads, A, M,
-                 N, static_cast<int64_t>(N), a_hi, a_lo, ld);
+    detail::split_rows_launch(stream, A, M, N, static_cast<int64_t>(N), a_hi, a_lo, ld);
     const dim3 tgrid(detail::blocks_for(K, 32), detail::blocks_for(static_cast<int>(ld), 32));
     launch_async(stream, detail::split_cols_t_kernel, tgrid, dim3(32, 8), B, N, K, bt_hi, bt_lo, ld);
 
