@@ -64,6 +64,9 @@ def parse():
     ap.add_argument("--batch", type=int, default=BATCH, help="sequences per GPU (C3: 32; smaller for profiling)")
     ap.add_argument("--ctx", type=int, default=CTX, help="prefilled context (C3: 2048; smaller for profiling)")
     ap.add_argument("--profile-iters", type=int, default=3)
+    ap.add_argument("--parallel", choices=["rp", "tp"], default="rp",
+                    help="rp: request-partitioned replicas (default, weak scaling); tp: one tensor-parallel engine "
+                         "over all ranks (global batch fixed, strong scaling)")
     ap.add_argument("--workload", choices=["c3", "c5"], default="c3",
                     help="c3: batched decode (default, the headline); c5: 256-request serving, "
                          "request-partitioned over the ranks")
@@ -226,12 +229,21 @@ def run_ours(args):
     t_load = time.perf_counter() - t_load
     cfg = {"layers": model.layers, "hidden": model.hidden, "intermediate": model.intermediate,
            "q_heads": model.q_heads, "kv_heads": model.kv_heads, "head_dim": model.head_dim, "vocab": model.vocab}
-    eng = LlamaBatch(model, BATCH, max_seq, "fast", prefill_rows=CTX)
+    tp = args.parallel == "tp" and world > 1
+    if tp:
+        from opworks_b200.llama import nccl_unique_id
+
+        box = [nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(box, src=0)
+        eng = LlamaBatch(model, BATCH, max_seq, "fast", prefill_rows=CTX, tp=(rank, world, box[0]))
+    else:
+        eng = LlamaBatch(model, BATCH, max_seq, "fast", prefill_rows=CTX)
+    shard = 0 if tp else rank  # tensor-parallel ranks serve the same sequences
     stream = torch.cuda.ExternalStream(eng.stream())
 
-    rng = np.random.default_rng(6 + 1000 * rank)
+    rng = np.random.default_rng(6 + 1000 * shard)
     prompts = rng.integers(0, model.vocab, (BATCH, CTX)).astype(np.int32)
-    seeds = (7_000 + np.arange(BATCH) + 1_000_000 * rank).astype(np.uint64)
+    seeds = (7_000 + np.arange(BATCH) + 1_000_000 * shard).astype(np.uint64)
     slots = np.arange(BATCH, dtype=np.int32)
 
     # ---- prefill (C3: 32 x 2048 tokens), timed on the engine stream
@@ -274,8 +286,9 @@ def run_ours(args):
     wall = allmax(wall)
 
     ctx_mean = CTX + W + K / 2.0
-    value = BATCH * K * world / (dev_ms / 1e3)
-    e2e_value = BATCH * K * world / wall
+    groups = 1 if tp else world  # independent sequence groups across the ranks
+    value = BATCH * K * groups / (dev_ms / 1e3)
+    e2e_value = BATCH * K * groups / wall
     h2d, d2h = eng.io_bytes(BATCH)
 
     # ---- per-kernel device time of the last step (roofline)
@@ -301,7 +314,7 @@ def run_ours(args):
             multi_chunk()
         wall_m = allmax(time.perf_counter() - t0m)
         n_m = (MULTI // chunk - 1) * chunk
-        multi = {"value": round(BATCH * n_m * world / wall_m, 1), "unit": UNIT, "steps": n_m, "chunk": chunk,
+        multi = {"value": round(BATCH * n_m * groups / wall_m, 1), "unit": UNIT, "steps": n_m, "chunk": chunk,
                  "timing": "host wall clock around opw_llama_batch_decode_multi calls (one H2D before and one "
                            "D2H after each chunk)"}
     hbm_peak, tc_peak, peak_src = measured_peaks()
@@ -395,15 +408,17 @@ def run_ours(args):
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world, "steps": K, "warmup": W,
-            "ms_per_step": round(dev_ms / K, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "ms_per_step": round(dev_ms / K, 4), "higher_is_better": True, "scaling": "strong" if tp else "weak",
+            "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic: random-init weights N(0,0.02) (norm gains 1.0), uniform random token ids",
             "config": {"workload": f"C3 batched decode: Llama-3.2-1B random-init, {BATCH} sequences per GPU "
                                    f"prefilled to {CTX} random ids, T=0.7 top-p=0.9 device sampling, fp32 paged KV "
                                    "(16-token blocks)",
                        "model": "Llama-3.2-1B (16 layers, 2048 hidden, 32/8 heads, 128256 vocab)",
-                       "global_batch": BATCH * world, "seq_len": CTX, "ctx_range": [CTX + W, CTX + W + K],
-                       "parallelism": f"request-partitioned x{world} (no collective)",
+                       "global_batch": BATCH * groups, "seq_len": CTX, "ctx_range": [CTX + W, CTX + W + K],
+                       "parallelism": (f"tp{world}: tensor-parallel heads / MLP columns, NCCL all-reduce after o and "
+                                       "down" if tp else f"request-partitioned x{world} (no collective)"),
                        "precision": "bf16 weights + GEMM operands, fp32 residual / KV cache / attention / "
                                     "softmax / sampling (fp64)",
                        "l2": "inputs larger than L2: every step streams 2.47 GB of weights + ~4.5 GB of KV",
@@ -414,7 +429,7 @@ def run_ours(args):
             "gpu_launches": gpu_launches_per_step * K, "gpu_launches_per_step": gpu_launches_per_step,
             "clocks": clocks.summary(),
             "prefill": {"c3_tokens": BATCH * CTX, "c3_ms": round(prefill_ms, 1),
-                        "c3_tok_s": round(BATCH * CTX * world / (prefill_ms / 1e3), 1), "c4": prefill8k},
+                        "c3_tok_s": round(BATCH * CTX * groups / (prefill_ms / 1e3), 1), "c4": prefill8k},
             "kernels": rows, "load_s": round(t_load, 2),
         }
         if cpu is not None:

@@ -50,6 +50,7 @@
 #include "../ops/llama_kernels.cuh"
 #include "../runtime/kv_cache.cuh"
 #include "../runtime/model_config.cuh"
+#include "../runtime/nccl_lite.cuh"
 #include "../runtime/pack_reader.cuh"
 #include "../runtime/weights.cuh"
 
@@ -64,6 +65,17 @@ struct SampleArgs {
     double uniform = -1.0; // >= 0: use this uniform (parity tests); < 0: counter RNG (seed, step)
     uint64_t seed = 0;
     int step = 0;
+};
+
+// Tensor parallelism of a fast-path engine (one process per GPU): rank `rank`
+// of `world` owns query heads [rank * qh / world, ...), the matching KV heads,
+// and MLP columns [rank * I / world, ...); after the o and down projections
+// the ranks sum their partial outputs with one NCCL all-reduce each.
+// nccl_id: the 128-byte communicator id from opw_llama_nccl_unique_id on one
+// rank, shared with the others.
+struct TensorParallel {
+    int rank = 0, world = 1;
+    const char *nccl_id = nullptr;
 };
 
 namespace detail {
@@ -105,7 +117,7 @@ template <typename WT> class LlamaEngineT {
     // max_batch sequences of up to max_seq_len tokens; prefill runs in chunks
     // of at most prefill_rows tokens (0: max_seq_len).
     LlamaEngineT(const ModelConfig &cfg, const ModelWeights<WT> &w, int max_batch, int max_seq_len, Precision prec,
-                 int prefill_rows = 0)
+                 int prefill_rows = 0, const TensorParallel &tp = {})
         : cfg_(cfg), w_(w), prec_(prec), max_batch_(max_batch), max_seq_len_(max_seq_len) {
         detail::require(max_batch > 0, "batch capacity must be positive");
         detail::require(max_seq_len > 0, "max_seq_len must be positive");
@@ -128,7 +140,22 @@ template <typename WT> class LlamaEngineT {
         sm_count_ = detail::device_facts().sm_count;
         err_word_ = sm100::device_error_word();
 
-        kv_ = KvCache(cfg, max_seq_len, max_batch * blocks_per_seq_);
+        tp_rank_ = tp.rank;
+        tp_world_ = tp.world;
+        detail::require(tp_world_ >= 1 && tp_rank_ >= 0 && tp_rank_ < tp_world_, "bad tensor-parallel rank / world");
+        if (tp_world_ > 1) {
+            detail::require(prec == Precision::kFast, "tensor parallelism runs the fast (bf16) path");
+            detail::require(tp.nccl_id != nullptr, "tensor parallelism needs an NCCL id");
+            detail::require(cfg.num_kv_heads % tp_world_ == 0 && cfg.intermediate_size % (128 * tp_world_) == 0 &&
+                                cfg.hidden_size % 128 == 0,
+                            "tensor parallelism needs KV heads and 128-column MLP tiles divisible by the world size");
+        }
+        qh_l_ = cfg.num_q_heads / tp_world_;
+        kvh_l_ = cfg.num_kv_heads / tp_world_;
+        inter_l_ = cfg.intermediate_size / tp_world_;
+        ModelConfig kv_cfg = cfg;
+        kv_cfg.num_kv_heads = kvh_l_;
+        kv_ = KvCache(kv_cfg, max_seq_len, max_batch * blocks_per_seq_);
         alloc_ = BlockAllocator(kv_.num_blocks);
         slots_.resize(max_batch);
         table_host_.assign(static_cast<size_t>(max_batch) * blocks_per_seq_, 0);
@@ -165,6 +192,11 @@ template <typename WT> class LlamaEngineT {
         for (const Projection *p : projs)
             part = std::max(part, static_cast<int64_t>(plan_splits(*p, rows_max_)) * rows_max_ * p->out);
         part_ = TypedDeviceBuffer<float>(part);
+        make_views();
+        if (tp_world_ > 1) {
+            tp_y_ = TypedDeviceBuffer<float>(rows_max_ * H);
+            tp_comm_ = NcclLite::get().init(tp.nccl_id, tp_world_, tp_rank_);
+        }
         if (fast) {
             // grouped split-K workspace: slices of up to kGroupTiles 32-token
             // tiles x 2 groups; counters zero-initialised
@@ -203,6 +235,11 @@ template <typename WT> class LlamaEngineT {
             cudaGraphExecDestroy(g.second);
         for (auto &g : multi_graphs_)
             cudaGraphExecDestroy(g.second);
+        if (tp_comm_) {
+            if (stream_)
+                cudaStreamSynchronize(stream_);
+            NcclLite::get().destroy(tp_comm_);
+        }
         if (stream_)
             cudaStreamSynchronize(stream_);
         if (in_host_)
@@ -606,6 +643,64 @@ template <typename WT> class LlamaEngineT {
     // epilogue scratch can hold rows preloaded during the main loop
     bool narrow_tile(int rows) const { return rows <= prefill_single_rows_ && plan_bn(rows) <= 64; }
 
+    // A bf16 weight operand: `out` rows of `in` elements, row stride ld
+    // (a column slice of a wider matrix keeps the matrix's stride).
+    struct WView {
+        const __nv_bfloat16 *w = nullptr;
+        int out = 0, in = 0;
+        int64_t ld = 0;
+    };
+    static WView view(const Projection &p) { return {p.bf16.data(), p.out, p.in, p.in}; }
+
+    // this rank's slices of the fast path's projections: QKV rows of its q,
+    // k and v heads (a compact copy), O and down input-column slices (views),
+    // gate/up rows of its interleaved MLP pairs (a view)
+    void make_views() {
+        if (!fast())
+            return;
+        const int H = cfg_.hidden_size, I = cfg_.intermediate_size, D = cfg_.head_dim;
+        const int qh = cfg_.num_q_heads, kvh = cfg_.num_kv_heads;
+        for (int l = 0; l < cfg_.num_layers; ++l) {
+            const LayerWeights<WT> &L = w_.layers[l];
+            if (tp_world_ == 1) {
+                qkv_v_.push_back(view(L.qkv));
+                o_v_.push_back(view(L.o));
+                gu_v_.push_back(view(L.gu));
+                down_v_.push_back(view(L.down));
+                continue;
+            }
+            const int qrows = qh_l_ * D, kvrows = kvh_l_ * D;
+            tp_qkv_.emplace_back(static_cast<int64_t>(qrows + 2 * kvrows) * H);
+            __nv_bfloat16 *dst = tp_qkv_.back().data();
+            const __nv_bfloat16 *src = L.qkv.bf16.data();
+            const int64_t from[3] = {static_cast<int64_t>(tp_rank_) * qrows,
+                                     static_cast<int64_t>(qh) * D + static_cast<int64_t>(tp_rank_) * kvrows,
+                                     static_cast<int64_t>(qh + kvh) * D + static_cast<int64_t>(tp_rank_) * kvrows};
+            const int64_t count[3] = {qrows, kvrows, kvrows};
+            int64_t at = 0;
+            for (int i = 0; i < 3; ++i) {
+                OPWORKS_CUDA_CHECK(cudaMemcpy(dst + at * H, src + from[i] * H,
+                                              sizeof(__nv_bfloat16) * static_cast<size_t>(count[i] * H),
+                                              cudaMemcpyDeviceToDevice));
+                at += count[i];
+            }
+            qkv_v_.push_back({dst, qrows + 2 * kvrows, H, H});
+            o_v_.push_back({L.o.bf16.data() + static_cast<int64_t>(tp_rank_) * qrows, H, qrows, cfg_.q_width()});
+            gu_v_.push_back({L.gu.bf16.data() + static_cast<int64_t>(tp_rank_) * 2 * inter_l_ * H, 2 * inter_l_, H, H});
+            down_v_.push_back({L.down.bf16.data() + static_cast<int64_t>(tp_rank_) * inter_l_, H, inter_l_, I});
+        }
+    }
+
+    int plan_splits(const WView &p, int rows, int max_splits = 64) const {
+        if (!fast() && rows <= 4)
+            return 1;
+        const int bn = fast() ? plan_bn(rows) : sm100::gemm_pick_bn(sm100::GemmKind::kTF32x3, rows);
+        const int tiles = ((p.out + kUmmaM - 1) / kUmmaM) * ((rows + bn - 1) / bn);
+        const int kb = fast() ? (p.in + 63) / 64 : (p.in + 31) / 32;
+        return sm100::gemm_pick_splits(tiles, kb, sm_count_ * sm100::gemm_ctas_per_sm(bn), fast() ? 2 : 8,
+                                       max_splits);
+    }
+
     int plan_splits(const Projection &p, int rows, int max_splits = 64) const {
         if (!fast() && rows <= 4)
             return 1;
@@ -622,11 +717,11 @@ template <typename WT> class LlamaEngineT {
     // weights are pulled into L2 while this GEMM runs (latency-bound decode
     // GEMMs leave HBM bandwidth idle)
     template <typename Epi>
-    void linear_tile(const Projection &p, const Act &x, int rows, const Epi &epi, const Projection *next = nullptr) {
+    void linear_tile(const WView &p, const Act &x, int rows, const Epi &epi, const WView *next = nullptr) {
         if (rows > prefill_single_rows_) {
             // prefill-sized GEMMs: single-term bf16 activations (one MMA per
             // K step, 256-token tiles), compute-bound shapes
-            sm100::gemm_tn<sm100::GemmKind::kBF16, Epi>({p.bf16.data(), nullptr, p.out, p.in},
+            sm100::gemm_tn<sm100::GemmKind::kBF16, Epi>({p.w, nullptr, p.out, p.ld},
                                                         {x.bf16, nullptr, rows, p.in}, p.in, part_.data(), p.out, 1,
                                                         static_cast<int64_t>(rows) * p.out, stream_, epi,
                                                         sm100::gemm_pick_bn(sm100::GemmKind::kBF16, rows));
@@ -634,8 +729,8 @@ template <typename WT> class LlamaEngineT {
         }
         if (rows >= pair_min_rows_) {
             // prefill-sized GEMMs: two-SM 256 x 256 tiles (cta_group::2)
-            sm100::gemm_pair_bf16x2<Epi>({p.bf16.data(), nullptr, p.out, p.in}, {x.bf16, x.bf16_lo, rows, p.in}, p.in,
-                                         stream_, epi);
+            sm100::gemm_pair_bf16x2<Epi>({p.w, nullptr, p.out, p.ld}, {x.bf16, x.bf16_lo, rows, p.in}, p.in, stream_,
+                                         epi);
             return;
         }
         int splits = plan_splits(p, rows, max_cluster_splits_);
@@ -655,14 +750,14 @@ template <typename WT> class LlamaEngineT {
         }
         if (cluster > 0) {
             sm100::gemm_tn<sm100::GemmKind::kBF16x2, Epi>(
-                {p.bf16.data(), nullptr, p.out, p.in}, {x.bf16, x.bf16_lo, rows, p.in}, p.in, part_.data(), p.out,
-                splits, static_cast<int64_t>(rows) * p.out, stream_, epi, 32, nullptr, 0, &groups_ws_, cluster);
+                {p.w, nullptr, p.out, p.ld}, {x.bf16, x.bf16_lo, rows, p.in}, p.in, part_.data(), p.out, splits,
+                static_cast<int64_t>(rows) * p.out, stream_, epi, 32, nullptr, 0, &groups_ws_, cluster);
             return;
         }
         sm100::gemm_tn<sm100::GemmKind::kBF16x2, Epi>(
-            {p.bf16.data(), nullptr, p.out, p.in}, {x.bf16, x.bf16_lo, rows, p.in}, p.in, part_.data(), p.out, splits,
-            static_cast<int64_t>(rows) * p.out, stream_, epi, plan_bn(rows), pf ? next->bf16.data() : nullptr,
-            pf ? sizeof(__nv_bfloat16) * static_cast<uint64_t>(next->out) * next->in : 0);
+            {p.w, nullptr, p.out, p.ld}, {x.bf16, x.bf16_lo, rows, p.in}, p.in, part_.data(), p.out, splits,
+            static_cast<int64_t>(rows) * p.out, stream_, epi, plan_bn(rows), pf ? next->w : nullptr,
+            pf ? sizeof(__nv_bfloat16) * static_cast<uint64_t>(next->out) * next->ld : 0);
     }
 
     // part[s][rows][p.out] = x[rows][p.in] . W^T (partial over split s)
@@ -747,7 +842,7 @@ template <typename WT> class LlamaEngineT {
     void attention(int layer, int rows, bool decode, int slot, int pos0, const detail::PagedKV &kv,
                    const detail::ActOut &out) {
         const float scale = 1.f / std::sqrt(static_cast<float>(cfg_.head_dim));
-        const int kvh = cfg_.num_kv_heads, qw = cfg_.q_width();
+        const int kvh = kvh_l_, qw = qh_l_ * cfg_.head_dim; // this rank's heads
         if (decode) {
             const int tps = detail::decode_tokens_per_split(rows * kvh, max_seq_len_, sm_count_);
             const int splits = (max_seq_len_ + tps - 1) / tps;
@@ -763,7 +858,7 @@ template <typename WT> class LlamaEngineT {
                 }
             }
             detail::attn_prefill_tc_launch<kRep, detail::ActOut>(
-                q_.data(), qw, cfg_.num_q_heads, kv_maps_[2 * layer], kv_maps_[2 * layer + 1], kv.table,
+                q_.data(), qw, qh_l_, kv_maps_[2 * layer], kv_maps_[2 * layer + 1], kv.table,
                 kv.table_stride, kvh, slot, rows, pos0, scale, out, stream_);
         } else {
             detail::attn_prefill_launch<detail::PagedKV, kRep, detail::ActOut>(q_.data(), qw, detail::kAttnD, out, kv,
@@ -771,10 +866,18 @@ template <typename WT> class LlamaEngineT {
         }
     }
 
+    // sum tp_y_ over the ranks, then hidden += y, the next operand and the
+    // tiles' sums of squares (tp_residual_kernel)
+    void tp_residual(int rows, const float *gain, const detail::ActOut &normed_o, const detail::RowSumSq &rs) {
+        NcclLite::get().allreduce_sum(tp_y_.data(), static_cast<size_t>(rows) * cfg_.hidden_size, tp_comm_, stream_);
+        launch_ex(detail::tp_residual_kernel, dim3(rows), dim3(128), 0, stream_, hidden_.data(),
+                  static_cast<const float *>(tp_y_.data()), cfg_.hidden_size, gain, normed_o, rs);
+    }
+
     void forward(int rows, bool decode, int slot, int pos0, const std::function<void(int)> &hook) {
         const PdlScope pdl(pdl_);
-        const int H = cfg_.hidden_size, I = cfg_.intermediate_size, QW = cfg_.q_width();
-        const int qh = cfg_.num_q_heads, kvh = cfg_.num_kv_heads;
+        const int H = cfg_.hidden_size, I = inter_l_, QW = qh_l_ * cfg_.head_dim; // this rank's widths
+        const int qh = qh_l_, kvh = kvh_l_;
         const detail::ActOut normed_o =
             act_out(normed_bf_.data(), normed_bflo_.data(), normed_f_.data(), normed_lo_.data(), H, rows);
         const detail::ActOut attn_o =
@@ -801,9 +904,9 @@ template <typename WT> class LlamaEngineT {
             int s = 0;
             const detail::RowSumSq rs = row_sumsq();
             if (fast()) {
-                linear_tile(L.qkv, normed, rows,
+                linear_tile(qkv_v_[l], normed, rows,
                             detail::QkvTileEpi{q_.data(), qh, kvh, rope, tm, kv, kv_.k(l), kv_.v(l), rs, narrow_tile(rows)},
-                            l2_prefetch_qkv_o_ ? &L.o : nullptr);
+                            l2_prefetch_qkv_o_ ? &o_v_[l] : nullptr);
                 mark("gemm_qkv_rope_kv_write");
             } else {
                 s = linear(L.qkv, normed, rows);
@@ -824,16 +927,32 @@ template <typename WT> class LlamaEngineT {
                 // the residual epilogues also emit the next projection's
                 // operand h * gain and the tiles' sums of squares; the
                 // consuming epilogues apply the norm's per-token scale
-                linear_tile(L.o, attn, rows, detail::ResidualTileEpi{hidden_.data(), H, L.post_norm.data(), normed_o, rs, narrow_tile(rows)},
-                            &L.gu);
-                mark("gemm_o_residual");
-                linear_tile(L.gu, normed, rows, detail::SiluMulTileEpi{act_o, rs}, &L.down);
-                mark("gemm_gate_up_silu");
                 const float *next_gain =
                     l + 1 < cfg_.num_layers ? w_.layers[l + 1].input_norm.data() : w_.final_norm.data();
-                linear_tile(L.down, act, rows, detail::ResidualTileEpi{hidden_.data(), H, next_gain, normed_o, rs, narrow_tile(rows)},
-                            l + 1 < cfg_.num_layers ? &w_.layers[l + 1].qkv : nullptr);
-                mark("gemm_down_residual");
+                if (tp_world_ > 1) {
+                    // partial projection outputs, summed over the ranks,
+                    // then the residual step of the fused epilogue
+                    linear_tile(o_v_[l], attn, rows, sm100::StoreTileEpi<sm100::Identity>{tp_y_.data(), H, {}});
+                    tp_residual(rows, L.post_norm.data(), normed_o, rs);
+                    mark("gemm_o_allreduce_residual");
+                    linear_tile(gu_v_[l], normed, rows, detail::SiluMulTileEpi{act_o, rs});
+                    mark("gemm_gate_up_silu");
+                    linear_tile(down_v_[l], act, rows, sm100::StoreTileEpi<sm100::Identity>{tp_y_.data(), H, {}});
+                    tp_residual(rows, next_gain, normed_o, rs);
+                    mark("gemm_down_allreduce_residual");
+                } else {
+                    linear_tile(o_v_[l], attn, rows,
+                                detail::ResidualTileEpi{hidden_.data(), H, L.post_norm.data(), normed_o, rs,
+                                                        narrow_tile(rows)},
+                                &gu_v_[l]);
+                    mark("gemm_o_residual");
+                    linear_tile(gu_v_[l], normed, rows, detail::SiluMulTileEpi{act_o, rs}, &down_v_[l]);
+                    mark("gemm_gate_up_silu");
+                    linear_tile(down_v_[l], act, rows,
+                                detail::ResidualTileEpi{hidden_.data(), H, next_gain, normed_o, rs, narrow_tile(rows)},
+                                l + 1 < cfg_.num_layers ? &qkv_v_[l + 1] : nullptr);
+                    mark("gemm_down_residual");
+                }
             } else {
                 s = linear(L.o, attn, rows);
                 mark("gemm_o");
@@ -910,6 +1029,12 @@ template <typename WT> class LlamaEngineT {
     TypedDeviceBuffer<int32_t> table_dev_;
     bool table_dirty_ = true;
     TypedDeviceBuffer<float> hidden_, ss_, q_, part_, attn_po_, attn_pml_, logits_;
+    // tensor parallelism (tp_world_ == 1: the whole model on this GPU)
+    int tp_rank_ = 0, tp_world_ = 1, qh_l_ = 0, kvh_l_ = 0, inter_l_ = 0;
+    ncclComm_t tp_comm_ = nullptr;
+    TypedDeviceBuffer<float> tp_y_;
+    std::vector<TypedDeviceBuffer<__nv_bfloat16>> tp_qkv_;
+    std::vector<WView> qkv_v_, o_v_, gu_v_, down_v_;
     static constexpr int kGroupTiles = 64;
     TypedDeviceBuffer<float> groups_part_;
     TypedDeviceBuffer<int32_t> groups_cnt_;
@@ -1044,9 +1169,10 @@ template <typename WT> class LlamaModelT {
         return s;
     }
 
-    std::unique_ptr<Engine> create_engine(int max_batch, int max_seq_len, Precision prec, int prefill_rows) const {
+    std::unique_ptr<Engine> create_engine(int max_batch, int max_seq_len, Precision prec, int prefill_rows,
+                                          const TensorParallel &tp = {}) const {
         OPWORKS_CUDA_CHECK(cudaSetDevice(device_));
-        return std::make_unique<Engine>(cfg_, *weights_, max_batch, max_seq_len, prec, prefill_rows);
+        return std::make_unique<Engine>(cfg_, *weights_, max_batch, max_seq_len, prec, prefill_rows, tp);
     }
 
     int32_t prefill(Session &s, const std::vector<int32_t> &ids) {

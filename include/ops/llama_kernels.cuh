@@ -469,6 +469,45 @@ struct QkvTileEpi {
     }
 };
 
+// Tensor-parallel residual step: y is the projection's output summed over the
+// ranks (all-reduce). hidden[row] += y[row]; with `gain` set, normed[row] =
+// hidden[row] * gain (the next projection's two-term bf16 operand, deferred
+// norm) and rs.part[tile][row] = the tile's sum of squares of hidden, as the
+// fused residual epilogue writes them. One block of 128 threads per row: warp
+// w takes the 128-feature tiles w, w + 4, ...; lane l owns features 4l..4l+3.
+// cols must be a multiple of 128.
+static __global__ void __launch_bounds__(128)
+    tp_residual_kernel(float *__restrict__ hidden, const float *__restrict__ y, int cols,
+                       const float *__restrict__ gain, ActOut normed, RowSumSq rs) {
+    pdl_trigger();
+    pdl_wait();
+    const int64_t row = blockIdx.x;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int t = warp; t < cols / 128; t += 4) {
+        const int c = t * 128 + 4 * lane;
+        float4 *hp = reinterpret_cast<float4 *>(hidden + row * cols + c);
+        const float4 v = *reinterpret_cast<const float4 *>(y + row * cols + c);
+        float4 h = *hp;
+        h.x += v.x;
+        h.y += v.y;
+        h.z += v.z;
+        h.w += v.w;
+        *hp = h;
+        if (gain) {
+            const float4 g = *reinterpret_cast<const float4 *>(gain + c);
+            normed.put4c(row, c, make_float4(h.x * g.x, h.y * g.y, h.z * g.z, h.w * g.w));
+        }
+        if (rs.part) {
+            float sq = (h.x * h.x + h.y * h.y) + (h.z * h.z + h.w * h.w);
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1)
+                sq += __shfl_xor_sync(kFullWarpMask, sq, off);
+            if (lane == 0)
+                rs.part[t * rs.ld + row] = sq;
+        }
+    }
+}
+
 // Device-side step feedback of a multi-step decode (one block, n <= 1024
 // rows): step k = *counter. Row i's sampled token goes to out[k][i] (-1 once
 // the row has emitted `eos`, which ends its count) and becomes the row's next

@@ -70,6 +70,18 @@ OPW_API int opw_llama_model_info(void *model, int32_t *out8, char *err, int err_
 OPW_API void *opw_llama_create_batch(void *model, int max_batch, int max_seq_len, int precision, int prefill_rows, char *err,
                              int err_len);
 OPW_API void opw_llama_destroy_batch(void *batch);
+/* Tensor parallelism (extension): opw_llama_nccl_unique_id writes a 128-byte
+ * NCCL communicator id (one rank creates it and shares it with the others);
+ * opw_llama_create_batch_tp creates this rank's fast-path engine of a
+ * tp_world-way tensor-parallel group (one process per GPU, every rank loads
+ * the full model): rank r owns query heads [r qh / tp_world, ...), the
+ * matching KV heads and MLP columns [r I / tp_world, ...), and the ranks sum
+ * the o and down projections with one NCCL all-reduce each per layer. Every
+ * rank must make the same calls with the same arguments (prefill, decode),
+ * and returns the same tokens. Requires libnccl.so.2. */
+OPW_API int opw_llama_nccl_unique_id(char *out128, char *err, int err_len);
+OPW_API void *opw_llama_create_batch_tp(void *model, int max_batch, int max_seq_len, int prefill_rows, int tp_rank,
+                                        int tp_world, const char *nccl_id, char *err, int err_len);
 /* Frees the slot's KV blocks; the slot starts empty. */
 OPW_API int opw_llama_batch_reset(void *batch, int slot, char *err, int err_len);
 /* Current token count of a slot, or -1. */

@@ -299,6 +299,46 @@ void *opw_llama_create_batch(void *model, int max_batch, int max_seq_len, int pr
         err, err_len);
 }
 
+int opw_llama_nccl_unique_id(char *out, char *err, int err_len) {
+    return guard(
+        [&] {
+            if (!out)
+                throw std::invalid_argument("null output");
+            opworks::NcclLite::get().unique_id(out);
+            return 0;
+        },
+        err, err_len);
+}
+
+void *opw_llama_create_batch_tp(void *model, int max_batch, int max_seq_len, int prefill_rows, int tp_rank,
+                                int tp_world, const char *nccl_id, char *err, int err_len) {
+    return guard_ptr(
+        [&]() -> void * {
+            if (!model || !nccl_id)
+                throw std::invalid_argument("null model or NCCL id");
+            auto *m = static_cast<ModelHolder *>(model);
+            set_device(m);
+            auto *b = new BatchHolder{m, {}};
+            try {
+                opworks::TensorParallel tp;
+                tp.rank = tp_rank;
+                tp.world = tp_world;
+                tp.nccl_id = nccl_id;
+                std::visit(
+                    [&](auto &md) {
+                        b->engine = md.create_engine(max_batch, max_seq_len, opworks::Precision::kFast, prefill_rows,
+                                                     tp);
+                    },
+                    m->model);
+            } catch (...) {
+                delete b;
+                throw;
+            }
+            return b;
+        },
+        err, err_len);
+}
+
 void opw_llama_destroy_batch(void *batch) {
     auto *b = static_cast<BatchHolder *>(batch);
     if (b) {

@@ -55,6 +55,8 @@ def bind(lib):
         "opw_llama_set_device": (I, [I]),
         "opw_llama_model_info": (I, [P, I32P, S, I]),
         "opw_llama_create_batch": (P, [P, I, I, I, I, S, I]),
+        "opw_llama_create_batch_tp": (P, [P, I, I, I, I, I, ctypes.c_char_p, S, I]),
+        "opw_llama_nccl_unique_id": (I, [ctypes.c_char_p, S, I]),
         "opw_llama_destroy_batch": (None, [P]),
         "opw_llama_batch_reset": (I, [P, I, S, I]),
         "opw_llama_batch_length": (I, [P, I]),
@@ -115,17 +117,37 @@ class Model:
         self.close()
 
 
+def nccl_unique_id():
+    """A 128-byte NCCL communicator id for LlamaBatch(tp=(rank, world, id))."""
+    import opworks_b200
+
+    lib = opworks_b200.llama_lib()
+    out = ctypes.create_string_buffer(128)
+    err = ctypes.create_string_buffer(_ERR_LEN)
+    if lib.opw_llama_nccl_unique_id(out, err, _ERR_LEN) < 0:
+        raise RuntimeError(f"nccl id failed: {err.value.decode(errors='replace')}")
+    return out.raw
+
+
 class LlamaBatch:
     """Batched engine: slots 0..max_batch-1 share a paged KV cache."""
 
-    def __init__(self, model: Model, max_batch, max_seq_len, precision="fast", prefill_rows=0):
+    def __init__(self, model: Model, max_batch, max_seq_len, precision="fast", prefill_rows=0, tp=None):
+        """tp = (rank, world, nccl_id): this process's rank of a tensor-parallel
+        group (fast path; nccl_id from nccl_unique_id() on one rank)."""
         self.model = model
         self.lib = model.lib
         self.err = ctypes.create_string_buffer(_ERR_LEN)
         self.max_batch = max_batch
         self.max_seq_len = max_seq_len
-        self.handle = self.lib.opw_llama_create_batch(model.handle, max_batch, max_seq_len, PRECISION[precision],
-                                                      prefill_rows, self.err, _ERR_LEN)
+        if tp is not None:
+            rank, world, nccl_id = tp
+            assert precision == "fast" and len(nccl_id) == 128
+            self.handle = self.lib.opw_llama_create_batch_tp(model.handle, max_batch, max_seq_len, prefill_rows, rank,
+                                                             world, bytes(nccl_id), self.err, _ERR_LEN)
+        else:
+            self.handle = self.lib.opw_llama_create_batch(model.handle, max_batch, max_seq_len, PRECISION[precision],
+                                                          prefill_rows, self.err, _ERR_LEN)
         if not self.handle:
             raise RuntimeError(f"batch creation failed: {self.err.value.decode(errors='replace')}")
         self._out = np.zeros(max_batch, np.int32)
