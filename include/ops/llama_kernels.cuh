@@ -319,7 +319,8 @@ struct ResidualTileEpi {
 };
 
 // Interleaved gate/up columns (2j = gate_j, 2j + 1 = up_j) -> act[tok][j] =
-// silu(g) * u = g / (1 + exp(-g)) * u, the expression of silu_mul_kernel.
+// silu(g) * u = g / (1 + exp(-g)) * u, the expression of silu_mul_kernel
+// (evaluated with the SFU exponential and a fast division: fast path only).
 // With rs.part set the operand was h * gain (deferred norm): both columns are
 // first scaled by the token's rsqrt(mean(h^2) + eps).
 struct SiluMulTileEpi {
@@ -335,19 +336,37 @@ struct SiluMulTileEpi {
                                                void *scratch) const {
         // warp w takes tokens w, w + 4, ...; lane l reads the 16-byte group
         // (g, u, g, u) of outputs 2l, 2l + 1 and writes them as one pair
+        // four tokens per warp iteration (independent chains); SiLU by the
+        // SFU exponential and a fast reciprocal (the fast path's outputs are
+        // bf16 pairs: their rounding dwarfs these few-ulp differences)
         const float *inv = static_cast<const float *>(scratch);
         const int warp = tid >> 5, lane = tid & 31;
         const bool vec = 4 * lane + 3 < nfeat;
-        for (int t = warp; t < ntok; t += 4) {
-            const float sc = inv[t];
-            const float4 v = *reinterpret_cast<const float4 *>(tile + t * 128 + 4 * lane);
-            const float g0 = v.x * sc, u0 = v.y * sc, g1 = v.z * sc, u1 = v.w * sc;
-            const float a0 = g0 / (1.f + expf(-g0)) * u0, a1 = g1 / (1.f + expf(-g1)) * u1;
-            if (vec) {
-                act.put2c(tok0 + t, f0 / 2 + 2 * lane, a0, a1);
-            } else {
-                if (4 * lane + 1 < nfeat)
-                    act.put(tok0 + t, f0 / 2 + 2 * lane, a0);
+        constexpr int kU = 4;
+        for (int tb = warp; tb < ntok; tb += 4 * kU) {
+            float a0[kU], a1[kU];
+#pragma unroll
+            for (int j = 0; j < kU; ++j) {
+                const int t = tb + 4 * j;
+                a0[j] = a1[j] = 0.f;
+                if (t < ntok) {
+                    const float sc = inv[t];
+                    const float4 v = *reinterpret_cast<const float4 *>(tile + t * 128 + 4 * lane);
+                    const float g0 = v.x * sc, u0 = v.y * sc, g1 = v.z * sc, u1 = v.w * sc;
+                    a0[j] = __fdividef(g0, 1.f + __expf(-g0)) * u0;
+                    a1[j] = __fdividef(g1, 1.f + __expf(-g1)) * u1;
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < kU; ++j) {
+                const int t = tb + 4 * j;
+                if (t >= ntok)
+                    break;
+                if (vec) {
+                    act.put2c(tok0 + t, f0 / 2 + 2 * lane, a0[j], a1[j]);
+                } else if (4 * lane + 1 < nfeat) {
+                    act.put(tok0 + t, f0 / 2 + 2 * lane, a0[j]);
+                }
             }
         }
     }
