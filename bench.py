@@ -67,6 +67,8 @@ def parse():
     ap.add_argument("--parallel", choices=["rp", "tp"], default="rp",
                     help="rp: request-partitioned replicas (default, weak scaling); tp: one tensor-parallel engine "
                          "over all ranks (global batch fixed, strong scaling)")
+    ap.add_argument("--tp-reduce", choices=["nccl", "p2p"], default="p2p",
+                    help="--parallel tp: NCCL all-reduce, or peer stores from the GEMM epilogue + rank-order sum")
     ap.add_argument("--workload", choices=["c3", "c5"], default="c3",
                     help="c3: batched decode (default, the headline); c5: 256-request serving, "
                          "request-partitioned over the ranks")
@@ -236,6 +238,10 @@ def run_ours(args):
         box = [nccl_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(box, src=0)
         eng = LlamaBatch(model, BATCH, max_seq, "fast", prefill_rows=CTX, tp=(rank, world, box[0]))
+        if args.tp_reduce == "p2p":
+            handles = [None] * world
+            dist.all_gather_object(handles, eng.tp_ipc_handle())
+            eng.tp_open_peers(handles)
     else:
         eng = LlamaBatch(model, BATCH, max_seq, "fast", prefill_rows=CTX)
     shard = 0 if tp else rank  # tensor-parallel ranks serve the same sequences
@@ -417,8 +423,11 @@ def run_ours(args):
                                    "(16-token blocks)",
                        "model": "Llama-3.2-1B (16 layers, 2048 hidden, 32/8 heads, 128256 vocab)",
                        "global_batch": BATCH * groups, "seq_len": CTX, "ctx_range": [CTX + W, CTX + W + K],
-                       "parallelism": (f"tp{world}: tensor-parallel heads / MLP columns, NCCL all-reduce after o and "
-                                       "down" if tp else f"request-partitioned x{world} (no collective)"),
+                       "parallelism": (f"tp{world}: tensor-parallel heads / MLP columns, "
+                                       + ("NCCL all-reduce" if args.tp_reduce == "nccl" else
+                                          "peer stores from the GEMM epilogue + rank-order sum")
+                                       + " after o and down" if tp else
+                                       f"request-partitioned x{world} (no collective)"),
                        "precision": "bf16 weights + GEMM operands, fp32 residual / KV cache / attention / "
                                     "softmax / sampling (fp64)",
                        "l2": "inputs larger than L2: every step streams 2.47 GB of weights + ~4.5 GB of KV",

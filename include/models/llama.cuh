@@ -196,6 +196,11 @@ template <typename WT> class LlamaEngineT {
         if (tp_world_ > 1) {
             tp_y_ = TypedDeviceBuffer<float>(rows_max_ * H);
             tp_comm_ = NcclLite::get().init(tp.nccl_id, tp_world_, tp_rank_);
+            // receive slots and counters of the fused peer-to-peer reduction
+            // (used once every rank has opened the others' with tp_open_peers)
+            tp_recv_ = TypedDeviceBuffer<float>(2 * tp_world_ * rows_max_ * H);
+            tp_cnt_ = TypedDeviceBuffer<int32_t>(4);
+            OPWORKS_CUDA_CHECK(cudaMemset(tp_cnt_.data(), 0, 4 * sizeof(int32_t)));
         }
         if (fast) {
             // grouped split-K workspace: slices of up to kGroupTiles 32-token
@@ -240,6 +245,8 @@ template <typename WT> class LlamaEngineT {
                 cudaStreamSynchronize(stream_);
             NcclLite::get().destroy(tp_comm_);
         }
+        for (void *p : peer_maps_)
+            cudaIpcCloseMemHandle(p);
         if (stream_)
             cudaStreamSynchronize(stream_);
         if (in_host_)
@@ -866,12 +873,69 @@ template <typename WT> class LlamaEngineT {
         }
     }
 
+  public:
+    // CUDA IPC handles of this rank's receive buffer and counters (2 x 64
+    // bytes) for the fused peer-to-peer reduction of a tensor-parallel engine
+    void tp_ipc_handles(char *out) const {
+        detail::require(tp_world_ > 1, "not a tensor-parallel engine");
+        cudaIpcMemHandle_t h[2];
+        OPWORKS_CUDA_CHECK(cudaIpcGetMemHandle(&h[0], const_cast<float *>(tp_recv_.data())));
+        OPWORKS_CUDA_CHECK(cudaIpcGetMemHandle(&h[1], const_cast<int32_t *>(tp_cnt_.data())));
+        std::memcpy(out, h, sizeof(h));
+    }
+    // handles of every rank (world x 128 bytes, in rank order): maps the
+    // peers' buffers; the projections then reduce through peer stores
+    // instead of NCCL (OPWORKS_TP_P2P=0 keeps NCCL)
+    void tp_open_peers(const char *all) {
+        detail::require(tp_world_ > 1 && tp_world_ <= detail::kTpMaxWorld, "not a tensor-parallel engine");
+        OPWORKS_CUDA_CHECK(cudaSetDevice(device_));
+        OPWORKS_CUDA_CHECK(cudaStreamSynchronize(stream_)); // no captured step in flight
+        detail::TpPeers pe;
+        pe.world = tp_world_;
+        pe.rank = tp_rank_;
+        pe.slot_floats = static_cast<int64_t>(rows_max_) * cfg_.hidden_size;
+        for (int r = 0; r < tp_world_; ++r) {
+            if (r == tp_rank_) {
+                pe.recv[r] = tp_recv_.data();
+                pe.cnt[r] = reinterpret_cast<unsigned int *>(tp_cnt_.data());
+                continue;
+            }
+            cudaIpcMemHandle_t h[2];
+            std::memcpy(h, all + 128 * r, sizeof(h));
+            void *recv = nullptr, *cnt = nullptr;
+            OPWORKS_CUDA_CHECK(cudaIpcOpenMemHandle(&recv, h[0], cudaIpcMemLazyEnablePeerAccess));
+            OPWORKS_CUDA_CHECK(cudaIpcOpenMemHandle(&cnt, h[1], cudaIpcMemLazyEnablePeerAccess));
+            peer_maps_.push_back(recv);
+            peer_maps_.push_back(cnt);
+            pe.recv[r] = static_cast<float *>(recv);
+            pe.cnt[r] = static_cast<unsigned int *>(cnt);
+        }
+        tp_peers_ = pe;
+        const char *e = std::getenv("OPWORKS_TP_P2P");
+        tp_p2p_ = !(e && e[0] == '0');
+        for (auto &g : graphs_) // steps captured with NCCL are captured again
+            cudaGraphExecDestroy(g.second);
+        graphs_.clear();
+        for (auto &g : multi_graphs_)
+            cudaGraphExecDestroy(g.second);
+        multi_graphs_.clear();
+    }
+
+  private:
     // sum tp_y_ over the ranks, then hidden += y, the next operand and the
     // tiles' sums of squares (tp_residual_kernel)
     void tp_residual(int rows, const float *gain, const detail::ActOut &normed_o, const detail::RowSumSq &rs) {
         NcclLite::get().allreduce_sum(tp_y_.data(), static_cast<size_t>(rows) * cfg_.hidden_size, tp_comm_, stream_);
         launch_ex(detail::tp_residual_kernel, dim3(rows), dim3(128), 0, stream_, hidden_.data(),
                   static_cast<const float *>(tp_y_.data()), cfg_.hidden_size, gain, normed_o, rs);
+    }
+
+    void tp_p2p_residual(int rows, int parity, const float *gain, const detail::ActOut &normed_o,
+                         const detail::RowSumSq &rs) {
+        unsigned int *cnt = reinterpret_cast<unsigned int *>(tp_cnt_.data());
+        launch_ex(detail::tp_p2p_residual_kernel, dim3(rows), dim3(128), 0, stream_, hidden_.data(),
+                  static_cast<const float *>(tp_recv_.data()), cnt, cnt + 2, parity, tp_world_,
+                  tp_peers_.slot_floats, rows, cfg_.hidden_size, gain, normed_o, rs, err_word_);
     }
 
     void forward(int rows, bool decode, int slot, int pos0, const std::function<void(int)> &hook) {
@@ -929,7 +993,19 @@ template <typename WT> class LlamaEngineT {
                 // consuming epilogues apply the norm's per-token scale
                 const float *next_gain =
                     l + 1 < cfg_.num_layers ? w_.layers[l + 1].input_norm.data() : w_.final_norm.data();
-                if (tp_world_ > 1) {
+                if (tp_world_ > 1 && tp_p2p_) {
+                    // partial projection outputs stored into every rank's
+                    // receive slot by the GEMM epilogue (peer memory), then
+                    // the rank-order sum and the residual step
+                    linear_tile(o_v_[l], attn, rows, detail::PeerStoreTileEpi{tp_peers_, 0, H});
+                    tp_p2p_residual(rows, 0, L.post_norm.data(), normed_o, rs);
+                    mark("gemm_o_p2p_reduce_residual");
+                    linear_tile(gu_v_[l], normed, rows, detail::SiluMulTileEpi{act_o, rs});
+                    mark("gemm_gate_up_silu");
+                    linear_tile(down_v_[l], act, rows, detail::PeerStoreTileEpi{tp_peers_, 1, H});
+                    tp_p2p_residual(rows, 1, next_gain, normed_o, rs);
+                    mark("gemm_down_p2p_reduce_residual");
+                } else if (tp_world_ > 1) {
                     // partial projection outputs, summed over the ranks,
                     // then the residual step of the fused epilogue
                     linear_tile(o_v_[l], attn, rows, sm100::StoreTileEpi<sm100::Identity>{tp_y_.data(), H, {}});
@@ -1032,7 +1108,11 @@ template <typename WT> class LlamaEngineT {
     // tensor parallelism (tp_world_ == 1: the whole model on this GPU)
     int tp_rank_ = 0, tp_world_ = 1, qh_l_ = 0, kvh_l_ = 0, inter_l_ = 0;
     ncclComm_t tp_comm_ = nullptr;
-    TypedDeviceBuffer<float> tp_y_;
+    TypedDeviceBuffer<float> tp_y_, tp_recv_;
+    TypedDeviceBuffer<int32_t> tp_cnt_; // arrival counters [2] | done counters [2]
+    detail::TpPeers tp_peers_{};
+    bool tp_p2p_ = false;
+    std::vector<void *> peer_maps_;
     std::vector<TypedDeviceBuffer<__nv_bfloat16>> tp_qkv_;
     std::vector<WView> qkv_v_, o_v_, gu_v_, down_v_;
     static constexpr int kGroupTiles = 64;

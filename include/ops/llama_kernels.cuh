@@ -527,6 +527,134 @@ static __global__ void __launch_bounds__(128)
     }
 }
 
+// Tensor parallelism without a library collective: the o / down GEMM's tile
+// epilogue stores its partial tile straight into slot `rank` of every rank's
+// receive buffer (peer memory over NVLink, CUDA IPC mappings) and then adds
+// the tile's token count to every rank's arrival counter (system-scope
+// atomics after a system fence); tp_p2p_residual_kernel waits for the
+// counter to reach rows x (H / 128) x world, sums the slots in rank order
+// (the same order on every rank: identical results) and runs the residual
+// step. Receive buffers and counters are double-buffered by `parity` (o: 0,
+// down: 1), and the last block of the consumer re-arms the parity's counter.
+constexpr int kTpMaxWorld = 8;
+// The ranks' hosts drift apart by more than a kernel-local wait (first-launch
+// module loads, graph captures), so the cross-rank wait allows 10 s before it
+// reports error 6 and returns.
+constexpr unsigned long long kTpPeerWaitNs = 10000000000ull;
+struct TpPeers {
+    float *recv[kTpMaxWorld];        // each rank's receive buffer [2][world][rows_max][H]
+    unsigned int *cnt[kTpMaxWorld];  // each rank's counters [2]
+    int world = 1, rank = 0;
+    int64_t slot_floats = 0;         // rows_max * H
+};
+
+struct PeerStoreTileEpi {
+    static constexpr bool kTile = true;
+    TpPeers peers;
+    int parity = 0;
+    int64_t ld = 0; // H
+    __device__ __forceinline__ void operator()(const float *tile, int tok0, int ntok, int f0, int nfeat, int tid,
+                                               void *) const {
+        const int warp = tid >> 5, lane = tid & 31, c = 4 * lane;
+        const int64_t base = (static_cast<int64_t>(parity) * peers.world + peers.rank) * peers.slot_floats;
+        for (int t = warp; t < ntok; t += 4) {
+            const float4 v = *reinterpret_cast<const float4 *>(tile + t * 128 + c);
+            const int64_t off = base + static_cast<int64_t>(tok0 + t) * ld + f0 + c;
+            for (int r = 0; r < peers.world; ++r) {
+                if (c + 3 < nfeat) {
+                    *reinterpret_cast<float4 *>(peers.recv[r] + off) = v;
+                } else {
+                    const float vv[4] = {v.x, v.y, v.z, v.w};
+                    for (int e = 0; e < 4; ++e)
+                        if (c + e < nfeat)
+                            peers.recv[r][off + e] = vv[e];
+                }
+            }
+        }
+        sm100::epilogue_bar(); // every epilogue thread's stores are issued
+        if (tid == 0 && ntok > 0) {
+            __threadfence_system();
+            for (int r = 0; r < peers.world; ++r)
+                atomicAdd_system(peers.cnt[r] + parity, static_cast<unsigned>(ntok));
+        }
+    }
+};
+
+// One block of 128 threads per row (see tp_residual_kernel); waits (bounded)
+// for the partial tiles of all ranks, y = sum of the slots in rank order.
+static __global__ void __launch_bounds__(128)
+    tp_p2p_residual_kernel(float *__restrict__ hidden, const float *__restrict__ recv, unsigned int *cnt,
+                           unsigned int *done, int parity, int world, int64_t slot_floats, int rows, int cols,
+                           const float *__restrict__ gain, ActOut normed, RowSumSq rs, int *err) {
+    pdl_trigger();
+    pdl_wait();
+    __shared__ int ok;
+    if (threadIdx.x == 0) {
+        const unsigned target = static_cast<unsigned>(rows) * static_cast<unsigned>(cols / 128) * world;
+        const uint64_t start = sm100::global_timer_ns();
+        unsigned seen = 0;
+        bool good = true;
+        while (true) {
+            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(seen) : "l"(cnt + parity) : "memory");
+            if (seen >= target)
+                break;
+            if (sm100::global_timer_ns() - start > kTpPeerWaitNs) {
+                good = false;
+                break;
+            }
+        }
+        ok = good;
+        if (!good)
+            atomicExch(err, 6);
+    }
+    __syncthreads();
+    if (ok) {
+        const int64_t row = blockIdx.x;
+        const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+        const float *slots = recv + static_cast<int64_t>(parity) * world * slot_floats + row * cols;
+        for (int t = warp; t < cols / 128; t += 4) {
+            const int c = t * 128 + 4 * lane;
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int r = 0; r < world; ++r) {
+                const float4 x = __ldcv(reinterpret_cast<const float4 *>(slots + r * slot_floats + c));
+                v.x += x.x;
+                v.y += x.y;
+                v.z += x.z;
+                v.w += x.w;
+            }
+            float4 *hp = reinterpret_cast<float4 *>(hidden + row * cols + c);
+            float4 h = *hp;
+            h.x += v.x;
+            h.y += v.y;
+            h.z += v.z;
+            h.w += v.w;
+            *hp = h;
+            if (gain) {
+                const float4 g = *reinterpret_cast<const float4 *>(gain + c);
+                normed.put4c(row, c, make_float4(h.x * g.x, h.y * g.y, h.z * g.z, h.w * g.w));
+            }
+            if (rs.part) {
+                float sq = (h.x * h.x + h.y * h.y) + (h.z * h.z + h.w * h.w);
+#pragma unroll
+                for (int off = 16; off > 0; off >>= 1)
+                    sq += __shfl_xor_sync(kFullWarpMask, sq, off);
+                if (lane == 0)
+                    rs.part[t * rs.ld + row] = sq;
+            }
+        }
+    }
+    // the last block of the launch re-arms this parity's counter (no rank
+    // writes it again before this rank's next GEMM of the other parity ran)
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        if (atomicAdd(done + parity, 1u) == gridDim.x - 1) {
+            atomicExch(cnt + parity, 0u);
+            atomicExch(done + parity, 0u);
+        }
+    }
+}
+
 // Device-side step feedback of a multi-step decode (one block, n <= 1024
 // rows): step k = *counter. Row i's sampled token goes to out[k][i] (-1 once
 // the row has emitted `eos`, which ends its count) and becomes the row's next

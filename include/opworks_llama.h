@@ -82,6 +82,17 @@ OPW_API void opw_llama_destroy_batch(void *batch);
 OPW_API int opw_llama_nccl_unique_id(char *out128, char *err, int err_len);
 OPW_API void *opw_llama_create_batch_tp(void *model, int max_batch, int max_seq_len, int prefill_rows, int tp_rank,
                                         int tp_world, const char *nccl_id, char *err, int err_len);
+/* Fused peer-to-peer reduction of a tensor-parallel batch (extension; one
+ * GPU per rank, peers reachable over NVLink): opw_llama_batch_tp_ipc_handle
+ * writes 128 bytes (CUDA IPC handles of this rank's receive buffer and
+ * arrival counters); after every rank has them, each calls
+ * opw_llama_batch_tp_open_peers with the world's handles concatenated in rank
+ * order (world x 128 bytes). From then on the o and down projections store
+ * their partial tiles into every rank's receive buffer from the GEMM
+ * epilogue and one kernel per projection sums them in rank order, instead of
+ * an NCCL all-reduce (environment OPWORKS_TP_P2P=0 keeps NCCL). */
+OPW_API int opw_llama_batch_tp_ipc_handle(void *batch, char *out128, char *err, int err_len);
+OPW_API int opw_llama_batch_tp_open_peers(void *batch, const char *handles, char *err, int err_len);
 /* Frees the slot's KV blocks; the slot starts empty. */
 OPW_API int opw_llama_batch_reset(void *batch, int slot, char *err, int err_len);
 /* Current token count of a slot, or -1. */

@@ -339,6 +339,36 @@ void *opw_llama_create_batch_tp(void *model, int max_batch, int max_seq_len, int
         err, err_len);
 }
 
+int opw_llama_batch_tp_ipc_handle(void *batch, char *out128, char *err, int err_len) {
+    return guard(
+        [&] {
+            if (!batch || !out128)
+                throw std::invalid_argument("null batch or output");
+            auto *b = static_cast<BatchHolder *>(batch);
+            set_device(b->owner);
+            return with_engine(b, [&](auto &e) {
+                e.tp_ipc_handles(out128);
+                return 0;
+            });
+        },
+        err, err_len);
+}
+
+int opw_llama_batch_tp_open_peers(void *batch, const char *handles, char *err, int err_len) {
+    return guard(
+        [&] {
+            if (!batch || !handles)
+                throw std::invalid_argument("null batch or handles");
+            auto *b = static_cast<BatchHolder *>(batch);
+            set_device(b->owner);
+            return with_engine(b, [&](auto &e) {
+                e.tp_open_peers(handles);
+                return 0;
+            });
+        },
+        err, err_len);
+}
+
 void opw_llama_destroy_batch(void *batch) {
     auto *b = static_cast<BatchHolder *>(batch);
     if (b) {

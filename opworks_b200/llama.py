@@ -57,6 +57,8 @@ def bind(lib):
         "opw_llama_create_batch": (P, [P, I, I, I, I, S, I]),
         "opw_llama_create_batch_tp": (P, [P, I, I, I, I, I, ctypes.c_char_p, S, I]),
         "opw_llama_nccl_unique_id": (I, [ctypes.c_char_p, S, I]),
+        "opw_llama_batch_tp_ipc_handle": (I, [P, ctypes.c_char_p, S, I]),
+        "opw_llama_batch_tp_open_peers": (I, [P, ctypes.c_char_p, S, I]),
         "opw_llama_destroy_batch": (None, [P]),
         "opw_llama_batch_reset": (I, [P, I, S, I]),
         "opw_llama_batch_length": (I, [P, I]),
@@ -156,6 +158,20 @@ class LlamaBatch:
         if rc < 0:
             raise RuntimeError(f"{what} failed: {self.err.value.decode(errors='replace')}")
         return rc
+
+    def tp_ipc_handle(self):
+        """128 bytes: CUDA IPC handles of this rank's receive buffer and
+        counters (tensor-parallel batches), to be shared with the other ranks."""
+        out = ctypes.create_string_buffer(128)
+        self._check(self.lib.opw_llama_batch_tp_ipc_handle(self.handle, out, self.err, _ERR_LEN), "tp ipc handle")
+        return out.raw
+
+    def tp_open_peers(self, handles):
+        """handles: every rank's tp_ipc_handle() in rank order. Switches the
+        o / down reductions from NCCL to peer stores from the GEMM epilogue."""
+        blob = b"".join(bytes(h) for h in handles)
+        assert all(len(h) == 128 for h in handles)
+        self._check(self.lib.opw_llama_batch_tp_open_peers(self.handle, blob, self.err, _ERR_LEN), "tp open peers")
 
     def reset(self, slot):
         self._check(self.lib.opw_llama_batch_reset(self.handle, slot, self.err, _ERR_LEN), "reset")
