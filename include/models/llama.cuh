@@ -890,6 +890,17 @@ template <typename WT> class LlamaEngineT {
         detail::require(tp_world_ > 1 && tp_world_ <= detail::kTpMaxWorld, "not a tensor-parallel engine");
         OPWORKS_CUDA_CHECK(cudaSetDevice(device_));
         OPWORKS_CUDA_CHECK(cudaStreamSynchronize(stream_)); // no captured step in flight
+        // steps captured so far (NCCL, or earlier mappings) are captured again
+        for (auto &g : graphs_)
+            cudaGraphExecDestroy(g.second);
+        graphs_.clear();
+        for (auto &g : multi_graphs_)
+            cudaGraphExecDestroy(g.second);
+        multi_graphs_.clear();
+        tp_p2p_ = false;
+        for (void *p : peer_maps_) // a second call maps the handles afresh
+            OPWORKS_CUDA_CHECK(cudaIpcCloseMemHandle(p));
+        peer_maps_.clear();
         detail::TpPeers pe;
         pe.world = tp_world_;
         pe.rank = tp_rank_;
@@ -904,8 +915,8 @@ template <typename WT> class LlamaEngineT {
             std::memcpy(h, all + 128 * r, sizeof(h));
             void *recv = nullptr, *cnt = nullptr;
             OPWORKS_CUDA_CHECK(cudaIpcOpenMemHandle(&recv, h[0], cudaIpcMemLazyEnablePeerAccess));
-            OPWORKS_CUDA_CHECK(cudaIpcOpenMemHandle(&cnt, h[1], cudaIpcMemLazyEnablePeerAccess));
             peer_maps_.push_back(recv);
+            OPWORKS_CUDA_CHECK(cudaIpcOpenMemHandle(&cnt, h[1], cudaIpcMemLazyEnablePeerAccess));
             peer_maps_.push_back(cnt);
             pe.recv[r] = static_cast<float *>(recv);
             pe.cnt[r] = static_cast<unsigned int *>(cnt);
@@ -913,12 +924,6 @@ template <typename WT> class LlamaEngineT {
         tp_peers_ = pe;
         const char *e = std::getenv("OPWORKS_TP_P2P");
         tp_p2p_ = !(e && e[0] == '0');
-        for (auto &g : graphs_) // steps captured with NCCL are captured again
-            cudaGraphExecDestroy(g.second);
-        graphs_.clear();
-        for (auto &g : multi_graphs_)
-            cudaGraphExecDestroy(g.second);
-        multi_graphs_.clear();
     }
 
   private:
