@@ -859,14 +859,12 @@ template <typename WT> class LlamaEngineT {
         } else if (fast() && tc_prefill_) {
             // tensor-core (TF32) flash attention over the paged cache
             if (kv_maps_.empty()) {
-                for (int l = 0; l < cfg_.num_layers; ++l) {
-                    kv_maps_.push_back(detail::make_kv_pool_tmap(kv_.k(l), kv_.num_blocks, kvh, false));
-                    kv_maps_.push_back(detail::make_kv_pool_tmap(kv_.v(l), kv_.num_blocks, kvh, true));
-                }
+                for (int l = 0; l < cfg_.num_layers; ++l)
+                    kv_maps_.push_back(detail::make_kv_pool_maps(kv_.k(l), kv_.v(l), kv_.num_blocks, kvh));
             }
-            detail::attn_prefill_tc_launch<kRep, detail::ActOut>(
-                q_.data(), qw, qh_l_, kv_maps_[2 * layer], kv_maps_[2 * layer + 1], kv.table,
-                kv.table_stride, kvh, slot, rows, pos0, scale, out, stream_);
+            detail::attn_prefill_tc_launch<kRep, detail::ActOut>(q_.data(), qw, qh_l_, kv_maps_[layer], kv.table,
+                                                                 kv.table_stride, kvh, slot, rows, pos0, scale, out,
+                                                                 stream_);
         } else {
             detail::attn_prefill_launch<detail::PagedKV, kRep, detail::ActOut>(q_.data(), qw, detail::kAttnD, out, kv,
                                                                                slot, rows, pos0, kvh, scale, stream_);
@@ -1178,7 +1176,7 @@ template <typename WT> class LlamaEngineT {
         const char *e = std::getenv("OPWORKS_TC_PREFILL");
         return !(e && e[0] == '0');
     }();
-    std::vector<CUtensorMap> kv_maps_;
+    std::vector<detail::KvPoolMaps> kv_maps_;
     // upper bound on the K splits (one cluster) of the fused GEMMs: the
     // portable 8 measured fastest at C3 (4 and 16 were slower);
     // OPWORKS_CLUSTER_SPLITS overrides it (up to 16, non-portable clusters)

@@ -6,7 +6,12 @@
 // query heads that share the KV head (rows ordered position-major, exactly as
 // a 3-D TMA box {32 dims, kRep heads, 128 / kRep positions} lands them). It
 // walks the KV range in 128-key tiles staged by TMA straight from the paged
-// fp32 cache (16-token pages, one 2 KB box per page and 32-dim half).
+// fp32 cache (16-token pages, one 2 KB box per page and 32-dim half). A tile
+// whose eight pages are consecutive physical blocks (the block allocator
+// hands a prefill ascending blocks) is staged with three copies instead of
+// 24: one 8-page box per K half and one for V, through run tensor maps that
+// step over blocks instead of (block, head) rows; both land the same bytes at
+// the same shared-memory addresses.
 //
 //   S = Q K^T   tcgen05.mma kind::tf32, A = Q (K-major, smem), B = K (K-major,
 //               smem: the cache's [token][dim] rows), D in TMEM (128 x 128)
@@ -95,6 +100,15 @@ __device__ __forceinline__ void tma_load_4d(void *smem_dst, const CUtensorMap *t
                  : "memory");
 }
 
+__device__ __forceinline__ void tma_load_5d(void *smem_dst, const CUtensorMap *tm, uint64_t *bar, int c0, int c1,
+                                            int c2, int c3, int c4) {
+    asm volatile("cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+                 " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(sm100::smem_u32(smem_dst)),
+                 "l"(reinterpret_cast<uint64_t>(tm)), "r"(sm100::smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3),
+                 "r"(c4)
+                 : "memory");
+}
+
 __device__ __forceinline__ void tma_load_3d(void *smem_dst, const CUtensorMap *tm, uint64_t *bar, int c0, int c1,
                                             int c2) {
     asm volatile("cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
@@ -106,11 +120,13 @@ __device__ __forceinline__ void tma_load_3d(void *smem_dst, const CUtensorMap *t
 // Causal prefill of `T` query rows of sequence `b` (absolute positions
 // q_offset + t), grid = (ceil(T / (128 / kRep)), kvh); the heaviest query
 // tiles are scheduled first. tmQ covers q as {64 dims, qh heads, T rows};
-// tmK / tmV cover the KV pool as {64 dims, 16 tokens, blocks * kvh}.
+// tmK / tmV cover the KV pool as {64 dims, 16 tokens, blocks * kvh}; tmKr /
+// tmVr (the run maps) as {64 dims, 16 tokens, kvh, blocks} with 8-block boxes.
 template <int kRep, typename Out>
 __global__ void __launch_bounds__(kPfThreads, 1)
     attn_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                           const __grid_constant__ CUtensorMap tmV, const int *__restrict__ table, int table_stride,
+                           const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmKr,
+                           const __grid_constant__ CUtensorMap tmVr, const int *__restrict__ table, int table_stride,
                            int kvh, int b, int T, int q_offset, float scale, Out out, int *err) {
     using SM = PrefillTcSmem;
     constexpr int kPos = 128 / kRep; // query positions per CTA
@@ -169,6 +185,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         sm100::prefetch_tmap(&tmQ);
         sm100::prefetch_tmap(&tmK);
         sm100::prefetch_tmap(&tmV);
+        sm100::prefetch_tmap(&tmKr);
+        sm100::prefetch_tmap(&tmVr);
     }
     if (warp == 1) {
         sm100::tmem_alloc(tmem_slot, kPfTmemCols);
@@ -196,8 +214,9 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             int issued = 0;
             for (int n = 0; n < n_tiles; ++n, ++issued) {
                 const int s = n % kPfStages;
-                if (n >= kPfStages &&
-                    !sm100::mbar_wait(&empty_kv[s], static_cast<uint32_t>((n / kPfStages) - 1) & 1u)) {
+                const bool freed =
+                    n < kPfStages || sm100::mbar_wait(&empty_kv[s], static_cast<uint32_t>((n / kPfStages) - 1) & 1u);
+                if (!__all_sync(0xFu, freed)) { // the four lanes leave together (they shuffle below)
                     ok = false;
                     break;
                 }
@@ -210,16 +229,34 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 for (int i = 0; i < kPagesPerLane; ++i)
                     rows[i] = table[static_cast<int64_t>(b) * table_stride +
                                     min(n * (kPfKvTile / kKvChunk) + lane * kPagesPerLane + i, last_page)] * kvh + h;
+                // a run: the tile's eight pages are consecutive blocks, all
+                // at or before the last page (rows[] = block * kvh + h)
+                const int row0 = __shfl_sync(0xFu, rows[0], 0);
+                bool mine = n * (kPfKvTile / kKvChunk) + kPfKvTile / kKvChunk - 1 <= last_page;
+#pragma unroll
+                for (int i = 0; i < kPagesPerLane; ++i)
+                    mine = mine && rows[i] == row0 + (lane * kPagesPerLane + i) * kvh;
+                const bool run = __all_sync(0xFu, mine);
                 if (lane == 0)
                     sm100::mbar_arrive_expect_tx(&full_kv[s], SM::kStageBytes);
+                if (run) {
+                    const int blk0 = (row0 - h) / kvh;
+                    if (lane == 0)
+                        tma_load_4d(st, &tmKr, &full_kv[s], 0, 0, h, blk0);
+                    else if (lane == 1)
+                        tma_load_4d(st + SM::kSlab, &tmKr, &full_kv[s], 32, 0, h, blk0);
+                    else if (lane == 2) // [block][half][16 keys][32], as the page copies land
+                        tma_load_5d(st + 2 * SM::kSlab, &tmVr, &full_kv[s], 0, 0, 0, h, blk0);
+                } else {
 #pragma unroll
-                for (int i = 0; i < kPagesPerLane; ++i) {
-                    const int row = rows[i];
-                    const uint32_t off = static_cast<uint32_t>(lane * kPagesPerLane + i) * kKvChunk * 128;
-                    tma_load_3d(st + off, &tmK, &full_kv[s], 0, 0, row);
-                    tma_load_3d(st + SM::kSlab + off, &tmK, &full_kv[s], 32, 0, row);
-                    // V page: both 32-dim halves in one copy, [half][16 keys][32]
-                    tma_load_4d(st + 2 * SM::kSlab + 2 * off, &tmV, &full_kv[s], 0, 0, 0, row);
+                    for (int i = 0; i < kPagesPerLane; ++i) {
+                        const int row = rows[i];
+                        const uint32_t off = static_cast<uint32_t>(lane * kPagesPerLane + i) * kKvChunk * 128;
+                        tma_load_3d(st + off, &tmK, &full_kv[s], 0, 0, row);
+                        tma_load_3d(st + SM::kSlab + off, &tmK, &full_kv[s], 32, 0, row);
+                        // V page: both 32-dim halves in one copy, [half][16 keys][32]
+                        tma_load_4d(st + 2 * SM::kSlab + 2 * off, &tmV, &full_kv[s], 0, 0, 0, row);
+                    }
                 }
             }
             // no copy may be in flight when the CTA exits (each phase of a
@@ -487,6 +524,47 @@ inline CUtensorMap make_kv_pool_tmap(const float *pool, int64_t blocks, int kvh,
     return tm;
 }
 
+// Run maps of the same pool: K as {64 dims, 16 tokens, kvh, blocks} with box
+// {32, 16, 1, 8} (eight consecutive blocks of one head land as [128 keys][32],
+// one copy per 32-dim half), V as {32 dims, 16 tokens, 2 halves, kvh, blocks}
+// with box {32, 16, 2, 1, 8} (landing as [block][half][16 keys][32]).
+inline CUtensorMap make_kv_run_tmap(const float *pool, int64_t blocks, int kvh, bool v_operand) {
+    require(reinterpret_cast<uintptr_t>(pool) % 16 == 0, "TMA base must be 16-byte aligned");
+    CUtensorMap tm;
+    std::memset(&tm, 0, sizeof(tm));
+    const cuuint64_t page_bytes = kKvChunk * kAttnD * 4;
+    CUresult r;
+    if (!v_operand) {
+        const cuuint64_t dims[4] = {kAttnD, kKvChunk, static_cast<cuuint64_t>(kvh), static_cast<cuuint64_t>(blocks)};
+        const cuuint64_t strides[3] = {kAttnD * 4, page_bytes, page_bytes * static_cast<cuuint64_t>(kvh)};
+        const cuuint32_t box[4] = {32, kKvChunk, 1, kPfKvTile / kKvChunk};
+        const cuuint32_t estr[4] = {1, 1, 1, 1};
+        r = sm100::tensor_map_encoder()(&tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float *>(pool), dims,
+                                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    } else {
+        const cuuint64_t dims[5] = {32, kKvChunk, 2, static_cast<cuuint64_t>(kvh), static_cast<cuuint64_t>(blocks)};
+        const cuuint64_t strides[4] = {kAttnD * 4, 32 * 4, page_bytes, page_bytes * static_cast<cuuint64_t>(kvh)};
+        const cuuint32_t box[5] = {32, kKvChunk, 2, 1, kPfKvTile / kKvChunk};
+        const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+        r = sm100::tensor_map_encoder()(&tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 5, const_cast<float *>(pool), dims,
+                                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                        CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    }
+    require(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (KV run map) failed");
+    return tm;
+}
+
+// The four tensor maps of one layer's K and V pools.
+struct KvPoolMaps {
+    CUtensorMap k, v, k_run, v_run;
+};
+inline KvPoolMaps make_kv_pool_maps(const float *kpool, const float *vpool, int64_t blocks, int kvh) {
+    return {make_kv_pool_tmap(kpool, blocks, kvh, false), make_kv_pool_tmap(vpool, blocks, kvh, true),
+            make_kv_run_tmap(kpool, blocks, kvh, false), make_kv_run_tmap(vpool, blocks, kvh, true)};
+}
+
 template <int kRep, typename Out> inline void prepare_prefill_tc_kernel() {
     static thread_local int done = -1;
     int dev = 0;
@@ -499,20 +577,21 @@ template <int kRep, typename Out> inline void prepare_prefill_tc_kernel() {
     }
 }
 
-// q: [T][qh * 64] fp32 rows with row stride q_tok floats; kmap / vmap from
-// make_kv_pool_tmap of the layer's pools.
+// q: [T][qh * 64] fp32 rows with row stride q_tok floats; maps from
+// make_kv_pool_maps of the layer's pools.
 template <int kRep, typename Out>
-inline void attn_prefill_tc_launch(const float *q, int64_t q_tok, int qh, const CUtensorMap &kmap,
-                                   const CUtensorMap &vmap, const int *table, int table_stride, int kvh, int b, int T,
-                                   int q_offset, float scale, const Out &out, cudaStream_t stream) {
+inline void attn_prefill_tc_launch(const float *q, int64_t q_tok, int qh, const KvPoolMaps &maps, const int *table,
+                                   int table_stride, int kvh, int b, int T, int q_offset, float scale, const Out &out,
+                                   cudaStream_t stream) {
     static_assert(kRep == 1 || kRep == 2 || kRep == 4 || kRep == 8, "GQA ratio must divide 128 rows");
     require(T > 0 && qh == kvh * kRep, "prefill attention: bad shape");
     prepare_prefill_tc_kernel<kRep, Out>();
     const CUtensorMap qmap = make_tmap_3d_f32(q, kAttnD, static_cast<uint64_t>(qh), static_cast<uint64_t>(T),
                                               kAttnD * 4, static_cast<uint64_t>(q_tok) * 4, kRep, 128 / kRep);
     const dim3 grid((T + 128 / kRep - 1) / (128 / kRep), kvh);
-    launch_ex(attn_prefill_tc_kernel<kRep, Out>, grid, dim3(kPfThreads), PrefillTcSmem::kBytes, stream, qmap, kmap,
-              vmap, table, table_stride, kvh, b, T, q_offset, scale, out, sm100::device_error_word());
+    launch_ex(attn_prefill_tc_kernel<kRep, Out>, grid, dim3(kPfThreads), PrefillTcSmem::kBytes, stream, qmap, maps.k,
+              maps.v, maps.k_run, maps.v_run, table, table_stride, kvh, b, T, q_offset, scale, out,
+              sm100::device_error_word());
 }
 
 } // namespace opworks::detail

@@ -342,13 +342,12 @@ int opw_paged_attention_prefill(const float *q, const float *kpool, const float 
         const int64_t qw = static_cast<int64_t>(num_q_heads) * kAttnD;
         const StridedOut<float> o{out, qw, kAttnD};
         if (tensor_cores) {
-            const CUtensorMap km = make_kv_pool_tmap(kpool, num_blocks, num_kv_heads, false);
-            const CUtensorMap vm = make_kv_pool_tmap(vpool, num_blocks, num_kv_heads, true);
+            const KvPoolMaps maps = make_kv_pool_maps(kpool, vpool, num_blocks, num_kv_heads);
             switch (rep) {
-            case 1: attn_prefill_tc_launch<1>(q, qw, num_q_heads, km, vm, block_table, table_stride, num_kv_heads, b, T, q_offset, scale, o, as_stream(stream)); break;
-            case 2: attn_prefill_tc_launch<2>(q, qw, num_q_heads, km, vm, block_table, table_stride, num_kv_heads, b, T, q_offset, scale, o, as_stream(stream)); break;
-            case 4: attn_prefill_tc_launch<4>(q, qw, num_q_heads, km, vm, block_table, table_stride, num_kv_heads, b, T, q_offset, scale, o, as_stream(stream)); break;
-            case 8: attn_prefill_tc_launch<8>(q, qw, num_q_heads, km, vm, block_table, table_stride, num_kv_heads, b, T, q_offset, scale, o, as_stream(stream)); break;
+            case 1: attn_prefill_tc_launch<1>(q, qw, num_q_heads, maps, block_table, table_stride, num_kv_heads, b, T, q_offset, scale, o, as_stream(stream)); break;
+            case 2: attn_prefill_tc_launch<2>(q, qw, num_q_heads, maps, block_table, table_stride, num_kv_heads, b, T, q_offset, scale, o, as_stream(stream)); break;
+            case 4: attn_prefill_tc_launch<4>(q, qw, num_q_heads, maps, block_table, table_stride, num_kv_heads, b, T, q_offset, scale, o, as_stream(stream)); break;
+            case 8: attn_prefill_tc_launch<8>(q, qw, num_q_heads, maps, block_table, table_stride, num_kv_heads, b, T, q_offset, scale, o, as_stream(stream)); break;
             default: throw std::invalid_argument("paged prefill attention: GQA ratio must be 1, 2, 4 or 8");
             }
         } else {

@@ -2,7 +2,9 @@
 KV cache (include/ops/attention_prefill_tc.cuh, through opw_paged_attention_
 prefill) against a float64 reference and against the fp32 SIMT kernel on the
 same seeded inputs: ragged lengths (partial query tiles, partial pages), a
-non-zero cached prefix (chunked prefill) and every GQA ratio. Tolerance: TF32
+non-zero cached prefix (chunked prefill), every GQA ratio, and block tables
+whose 128-key tiles are runs of consecutive blocks (staged by the 8-page run
+copies) mixed with scattered pages (staged page by page). Tolerance: TF32
 operands (10-bit mantissa) with fp32 accumulation, |err| <= 4e-3 (outputs are
 convex combinations of V entries ~N(0,1))."""
 
@@ -20,7 +22,7 @@ def ops():
     return opworks_b200.ops_lib()
 
 
-def make_case(T, q_offset, qh, kvh, seed, extra_blocks=3):
+def make_case(T, q_offset, qh, kvh, seed, extra_blocks=3, layout="scattered"):
     g = torch.Generator().manual_seed(seed)
     S = q_offset + T
     pages = (S + 15) // 16
@@ -28,6 +30,14 @@ def make_case(T, q_offset, qh, kvh, seed, extra_blocks=3):
     kpool = torch.randn(nblk, kvh, 16, 64, generator=g)
     vpool = torch.randn(nblk, kvh, 16, 64, generator=g)
     perm = torch.randperm(nblk, generator=g)[:pages].int()
+    if layout == "runs":  # ascending blocks from an offset: every full tile is a run
+        perm = torch.arange(extra_blocks - 1, extra_blocks - 1 + pages, dtype=torch.int32)
+    elif layout == "mixed":  # runs, one tile broken by a swap, a scattered tail
+        perm = torch.arange(1, 1 + pages, dtype=torch.int32)
+        if pages > 20:
+            perm[9], perm[12] = perm[12].item(), perm[9].item()
+            tail = perm[24:].clone()
+            perm[24:] = tail[torch.randperm(tail.numel(), generator=g)]
     stride = pages + 1
     table = torch.full((2, stride), -1, dtype=torch.int32)
     table[1, :pages] = perm  # sequence slot 1
@@ -79,6 +89,17 @@ def test_tc_prefill_matches_reference(ops, T, q_offset):
 def test_tc_prefill_gqa_ratios(ops, qh, kvh):
     T, q_offset = 77, 20
     case = make_case(T, q_offset, qh, kvh, seed=qh)
+    want = reference(case[0], case[1], case[2], case[3], T, q_offset, qh, kvh)
+    got = run(ops, *case, T, q_offset, qh, kvh, tc=1)
+    assert torch.isfinite(got).all()
+    assert (got.double() - want).abs().max().item() <= 4e-3
+
+
+@pytest.mark.parametrize("layout", ["runs", "mixed"])
+@pytest.mark.parametrize("T,q_offset", [(1000, 0), (129, 37), (64, 300), (300, 129), (5, 0)])
+def test_tc_prefill_page_runs(ops, layout, T, q_offset):
+    qh, kvh = 32, 8
+    case = make_case(T, q_offset, qh, kvh, seed=T + q_offset + len(layout), layout=layout)
     want = reference(case[0], case[1], case[2], case[3], T, q_offset, qh, kvh)
     got = run(ops, *case, T, q_offset, qh, kvh, tc=1)
     assert torch.isfinite(got).all()
