@@ -168,15 +168,18 @@ def step_bytes(cfg, batch, ctx_mean):
     return tot
 
 
-def scaled_traffic(label, tr, batch, ctx):
+def scaled_traffic(label, tr, batch, ctx, kv_share=1.0):
     """DRAM bytes per launch from an ncu capture (profiles/traffic.json),
     scaled to this launch by the units it processes: attention traffic grows
-    with batch x context (KV tokens read), a GEMM's does not change."""
+    with batch x context x the KV heads this GPU holds (kv_share of them), a
+    GEMM's does not change."""
     if not isinstance(tr, dict) or "dram_bytes_per_launch" not in tr:
         return None
     b = float(tr["dram_bytes_per_launch"])
     if label == "attention":
-        b *= (batch * ctx) / float(tr["batch"] * tr["ctx"])
+        b *= (batch * ctx) / float(tr["batch"] * tr["ctx"]) * kv_share
+    elif kv_share != 1.0:
+        return None  # the capture holds the full weight matrices
     return int(b)
 
 
@@ -232,6 +235,12 @@ def run_ours(args):
     cfg = {"layers": model.layers, "hidden": model.hidden, "intermediate": model.intermediate,
            "q_heads": model.q_heads, "kv_heads": model.kv_heads, "head_dim": model.head_dim, "vocab": model.vocab}
     tp = args.parallel == "tp" and world > 1
+    # bytes this GPU moves: a tensor-parallel rank holds 1 / world of the
+    # heads and MLP columns (embedding and LM head stay whole)
+    rcfg = dict(cfg)
+    if tp:
+        for key in ("q_heads", "kv_heads", "intermediate"):
+            rcfg[key] = cfg[key] // world
     if tp:
         from opworks_b200.llama import nccl_unique_id
 
@@ -328,7 +337,7 @@ def run_ours(args):
     traffic = load_traffic()
     rows = []
     for label, ms, launches in kernels:
-        b = algorithmic_bytes(label, cfg, BATCH, ctx_now)
+        b = algorithmic_bytes(label, rcfg, BATCH, ctx_now)
         rows.append({"kernel": label, "ms_per_step": round(ms, 4), "launches_per_step": launches,
                      "gbs": round(b / (ms / 1e3) / 1e9, 1) if b and ms > 0 else None})
     # launch groups: attention = split-KV partial (+ combine kernel when the
@@ -337,16 +346,16 @@ def run_ours(args):
     attn_kernels = 1 if (2 * sms) // (BATCH * cfg["kv_heads"]) <= 1 else 2
     gpu_launches_per_step = sum(k[2] * (attn_kernels if k[0] == "attention" else 1) for k in kernels)
     dom = max((r for r in rows if r["gbs"] is not None), key=lambda r: r["ms_per_step"])
-    dom_bytes = algorithmic_bytes(dom["kernel"], cfg, BATCH, ctx_now) / dom["launches_per_step"]
+    dom_bytes = algorithmic_bytes(dom["kernel"], rcfg, BATCH, ctx_now) / dom["launches_per_step"]
     dom_ms = dom["ms_per_step"] / dom["launches_per_step"]
     achieved = dom_bytes / (dom_ms / 1e3) / 1e9
     tr = traffic.get(dom["kernel"])
     roofline = {"bound": "hbm", "kernel": dom["kernel"], "achieved": round(achieved, 1), "peak": hbm_peak,
                 "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
-                "traffic": scaled_traffic(dom["kernel"], tr, BATCH, ctx_now),
+                "traffic": scaled_traffic(dom["kernel"], tr, BATCH, ctx_now, rcfg["kv_heads"] / cfg["kv_heads"]),
                 "algorithmic_bytes_per_launch": int(dom_bytes), "avg_launch_ms": round(dom_ms, 5),
                 "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)"}
-    sb = step_bytes(cfg, BATCH, ctx_mean)
+    sb = step_bytes(rcfg, BATCH, ctx_mean)
     step_roofline = {"bytes_per_step": int(sb), "achieved_gbs": round(sb / (dev_ms / K / 1e3) / 1e9, 1),
                      "frac_of_hbm": round(sb / (dev_ms / K / 1e3) / 1e9 / hbm_peak, 4)}
 
