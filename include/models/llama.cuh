@@ -1153,8 +1153,6 @@ template <typename WT> class LlamaEngineT {
     int multi_steps_ = 0, multi_eos_ = -1;
     bool multi_has_uni_ = false;
     bool marks_enabled_ = false;
-    // tensor-core prefill attention on the fast path (OPWORKS_TC_PREFILL=0:
-    // the fp32 SIMT kernel instead); tensor maps of the layers' KV pools
     // fast-path GEMMs with more token rows than this use single-term bf16
     // activations (one MMA per K step). Off by default: on a 1024-token
     // prompt single-term activations move the logits by 0.043 against the
@@ -1172,6 +1170,8 @@ template <typename WT> class LlamaEngineT {
         const int v = e ? std::atoi(e) : 512;
         return v > 0 ? v : (1 << 30);
     }();
+    // tensor-core prefill attention on the fast path (OPWORKS_TC_PREFILL=0:
+    // the fp32 SIMT kernel instead); tensor maps of the layers' KV pools
     bool tc_prefill_ = [] {
         const char *e = std::getenv("OPWORKS_TC_PREFILL");
         return !(e && e[0] == '0');
