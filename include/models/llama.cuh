@@ -281,6 +281,7 @@ template <typename WT> class LlamaEngineT {
     int32_t prefill(int slot, const int32_t *ids, int n, const SampleArgs &sa,
                     const std::function<void(int)> &hook = nullptr) {
         check_slot(slot);
+        check_usable();
         detail::require(n > 0, "prefill requires at least one token");
         detail::require(ids != nullptr, "null token buffer");
         validate_ids(ids, n);
@@ -322,6 +323,7 @@ template <typename WT> class LlamaEngineT {
     // token appended to slots[i]; out[i] receives the next token.
     void decode(int n, const int32_t *slots, const int32_t *prev, const SampleArgs *sa, int32_t *out) {
         detail::require(n > 0 && n <= max_batch_, "decode batch size outside the engine capacity");
+        check_usable();
         OPWORKS_CUDA_CHECK(cudaSetDevice(device_));
         validate_ids(prev, n);
         use_layout(dec_, 0);
@@ -380,6 +382,7 @@ template <typename WT> class LlamaEngineT {
                       const double *uniforms, int eos, int32_t *out, int32_t *count) {
         detail::require(n > 0 && n <= max_batch_ && n <= 1024, "decode batch size outside the engine capacity");
         detail::require(steps > 0, "multi-step decode needs steps > 0");
+        check_usable();
         OPWORKS_CUDA_CHECK(cudaSetDevice(device_));
         validate_ids(prev, n);
         use_layout(dec_, 0);
@@ -533,7 +536,79 @@ template <typename WT> class LlamaEngineT {
         OPWORKS_CUDA_CHECK(cudaStreamSynchronize(stream_));
     }
 
+    // KV inspection. Physical block ids of `slot`, as the kernels see them
+    // (the device copy of the block table); writes min(count, cap) ids and
+    // returns the slot's mapped block count.
+    int kv_blocks(int slot, int32_t *out, int cap) {
+        check_slot(slot);
+        const int count = static_cast<int>(slots_[slot].blocks.size());
+        const std::vector<int32_t> table = device_table_row(slot);
+        for (int i = 0; i < std::min(count, cap); ++i)
+            out[i] = table[i];
+        return count;
+    }
+
+    // K and V of positions [pos0, pos0 + n) of `slot` in `layer`, gathered
+    // through the device block table, as [n][kv_heads][head_dim] floats each
+    // (post-RoPE K, as attention reads it). Positions may run past the slot's
+    // length up to the end of its last mapped block.
+    void read_kv(int slot, int layer, int pos0, int n, float *k_out, float *v_out) {
+        check_slot(slot);
+        detail::require(layer >= 0 && layer < kv_.num_layers, "layer index out of range");
+        detail::require(pos0 >= 0 && n >= 0, "negative position or count");
+        detail::require(static_cast<int64_t>(pos0) + n <=
+                            static_cast<int64_t>(slots_[slot].blocks.size()) * kKvBlockTokens,
+                        "positions past the slot's mapped KV blocks");
+        const std::vector<int32_t> table = device_table_row(slot);
+        const int64_t bf = kv_.block_floats(), D = kv_.head_dim, kvh = kv_.kv_heads;
+        std::vector<float> kb(static_cast<size_t>(bf)), vb(static_cast<size_t>(bf));
+        for (int lb = pos0 / kKvBlockTokens; lb * kKvBlockTokens < pos0 + n; ++lb) {
+            const int phys = table[lb];
+            detail::require(phys >= 0 && phys < kv_.num_blocks, "block table holds an invalid block id");
+            copy_pool_block(layer, phys, kb.data(), vb.data());
+            const int p_lo = std::max(pos0, lb * kKvBlockTokens), p_hi = std::min(pos0 + n, (lb + 1) * kKvBlockTokens);
+            for (int p = p_lo; p < p_hi; ++p)
+                for (int64_t h = 0; h < kvh; ++h) {
+                    const int64_t src = (h * kKvBlockTokens + p % kKvBlockTokens) * D;
+                    const int64_t dst = ((static_cast<int64_t>(p) - pos0) * kvh + h) * D;
+                    std::memcpy(k_out + dst, kb.data() + src, sizeof(float) * D);
+                    std::memcpy(v_out + dst, vb.data() + src, sizeof(float) * D);
+                }
+        }
+    }
+
+    // Raw pool blocks [block0, block0 + nblocks) of `layer` in pool order
+    // ([block][kv_heads][16][head_dim] floats each for K and V). Returns the
+    // pool's block count (nblocks = 0 only asks for it).
+    int read_kv_pool(int layer, int block0, int nblocks, float *k_out, float *v_out) {
+        detail::require(layer >= 0 && layer < kv_.num_layers, "layer index out of range");
+        detail::require(block0 >= 0 && nblocks >= 0 && static_cast<int64_t>(block0) + nblocks <= kv_.num_blocks,
+                        "block range outside the KV pool");
+        const int64_t bf = kv_.block_floats();
+        for (int b = 0; b < nblocks; ++b)
+            copy_pool_block(layer, block0 + b, k_out + b * bf, v_out + b * bf);
+        return kv_.num_blocks;
+    }
+
   private:
+    std::vector<int32_t> device_table_row(int slot) {
+        std::vector<int32_t> row(static_cast<size_t>(blocks_per_seq_));
+        OPWORKS_CUDA_CHECK(cudaSetDevice(device_));
+        OPWORKS_CUDA_CHECK(cudaMemcpyAsync(row.data(), table_dev_.data() + static_cast<int64_t>(slot) * blocks_per_seq_,
+                                           sizeof(int32_t) * row.size(), cudaMemcpyDeviceToHost, stream_));
+        OPWORKS_CUDA_CHECK(cudaStreamSynchronize(stream_));
+        return row;
+    }
+    void copy_pool_block(int layer, int block, float *k_host, float *v_host) {
+        const int64_t bf = kv_.block_floats();
+        OPWORKS_CUDA_CHECK(cudaSetDevice(device_));
+        OPWORKS_CUDA_CHECK(cudaMemcpyAsync(k_host, kv_.k(layer) + block * bf, sizeof(float) * bf,
+                                           cudaMemcpyDeviceToHost, stream_));
+        OPWORKS_CUDA_CHECK(cudaMemcpyAsync(v_host, kv_.v(layer) + block * bf, sizeof(float) * bf,
+                                           cudaMemcpyDeviceToHost, stream_));
+        OPWORKS_CUDA_CHECK(cudaStreamSynchronize(stream_));
+    }
+
     struct Slot {
         int length = 0;
         std::vector<int> blocks;
@@ -554,6 +629,10 @@ template <typename WT> class LlamaEngineT {
         marks_.emplace_back(label, e);
     }
 
+    void check_usable() const {
+        if (!failed_.empty())
+            throw std::runtime_error(failed_);
+    }
     void check_slot(int slot) const {
         detail::require(slot >= 0 && slot < max_batch_, "slot outside the engine capacity");
     }
@@ -636,6 +715,8 @@ template <typename WT> class LlamaEngineT {
         if (out_host_[max_batch_] != 0) {
             const int code = out_host_[max_batch_];
             out_host_[max_batch_] = 0;
+            if (code == detail::kErrTpPeerTimeout)
+                failed_ = "a tensor-parallel peer exchange timed out; recreate the batch on every rank";
             throw std::runtime_error("a device-side wait timed out in the forward pass (code " +
                                      std::to_string(code) + ")");
         }
@@ -938,7 +1019,7 @@ template <typename WT> class LlamaEngineT {
         unsigned int *cnt = reinterpret_cast<unsigned int *>(tp_cnt_.data());
         launch_ex(detail::tp_p2p_residual_kernel, dim3(rows), dim3(128), 0, stream_, hidden_.data(),
                   static_cast<const float *>(tp_recv_.data()), cnt, cnt + 2, parity, tp_world_,
-                  tp_peers_.slot_floats, rows, cfg_.hidden_size, gain, normed_o, rs, err_word_);
+                  tp_peers_.slot_floats, rows, cfg_.hidden_size, gain, normed_o, rs, err_word_, tp_wait_ns_);
     }
 
     void forward(int rows, bool decode, int slot, int pos0, const std::function<void(int)> &hook) {
@@ -1115,6 +1196,13 @@ template <typename WT> class LlamaEngineT {
     TypedDeviceBuffer<int32_t> tp_cnt_; // arrival counters [2] | done counters [2]
     detail::TpPeers tp_peers_{};
     bool tp_p2p_ = false;
+    std::string failed_; // set when the engine can take no further step
+    // limit of the cross-rank wait of the peer-store reduction
+    unsigned long long tp_wait_ns_ = [] {
+        const char *e = std::getenv("OPWORKS_TP_WAIT_MS");
+        const long long ms = e ? std::atoll(e) : 0;
+        return ms > 0 ? static_cast<unsigned long long>(ms) * 1000000ull : detail::kTpPeerWaitNs;
+    }();
     std::vector<void *> peer_maps_;
     std::vector<TypedDeviceBuffer<__nv_bfloat16>> tp_qkv_;
     std::vector<WView> qkv_v_, o_v_, gu_v_, down_v_;

@@ -19,6 +19,7 @@
 #include <cstdint>
 #include <cstring>
 #include <mutex>
+#include <vector>
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
@@ -260,13 +261,16 @@ inline CUtensorMap make_tmap_2d(const void *base, bool bf16, uint64_t cols, uint
 
 // Per-device error word written by kernels whose bounded waits ran out.
 inline int *device_error_word() {
-    constexpr int kSlots = 16;
-    static int *words[kSlots] = {};
+    static std::vector<int *> words; // one word per device index
     static std::mutex mu;
-    int dev = 0;
+    int dev = 0, count = 0;
     OPWORKS_CUDA_CHECK(cudaGetDevice(&dev));
+    OPWORKS_CUDA_CHECK(cudaGetDeviceCount(&count));
     std::lock_guard<std::mutex> lock(mu);
-    int *&w = words[dev % kSlots];
+    if (words.size() < static_cast<size_t>(count))
+        words.resize(static_cast<size_t>(count), nullptr);
+    detail::require(dev >= 0 && dev < count, "device index outside the visible devices");
+    int *&w = words[static_cast<size_t>(dev)];
     if (w == nullptr) {
         OPWORKS_CUDA_CHECK(cudaMalloc(reinterpret_cast<void **>(&w), sizeof(int)));
         OPWORKS_CUDA_CHECK(cudaMemset(w, 0, sizeof(int)));

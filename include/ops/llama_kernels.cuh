@@ -538,9 +538,13 @@ static __global__ void __launch_bounds__(128)
 // down: 1), and the last block of the consumer re-arms the parity's counter.
 constexpr int kTpMaxWorld = 8;
 // The ranks' hosts drift apart by more than a kernel-local wait (first-launch
-// module loads, graph captures), so the cross-rank wait allows 10 s before it
-// reports error 6 and returns.
+// module loads, graph captures), so the cross-rank wait allows 10 s by
+// default before it reports error 6 and returns. After error 6 the receive
+// counters are left as they are (partial tiles of slow ranks may still
+// arrive), and the engine that launched the wait refuses further steps: its
+// tensor-parallel exchange must be rebuilt (a new batch on every rank).
 constexpr unsigned long long kTpPeerWaitNs = 10000000000ull;
+constexpr int kErrTpPeerTimeout = 6;
 struct TpPeers {
     float *recv[kTpMaxWorld];        // each rank's receive buffer [2][world][rows_max][H]
     unsigned int *cnt[kTpMaxWorld];  // each rank's counters [2]
@@ -585,7 +589,8 @@ struct PeerStoreTileEpi {
 static __global__ void __launch_bounds__(128)
     tp_p2p_residual_kernel(float *__restrict__ hidden, const float *__restrict__ recv, unsigned int *cnt,
                            unsigned int *done, int parity, int world, int64_t slot_floats, int rows, int cols,
-                           const float *__restrict__ gain, ActOut normed, RowSumSq rs, int *err) {
+                           const float *__restrict__ gain, ActOut normed, RowSumSq rs, int *err,
+                           unsigned long long wait_ns) {
     pdl_trigger();
     pdl_wait();
     __shared__ int ok;
@@ -600,14 +605,14 @@ static __global__ void __launch_bounds__(128)
                 break;
             // a wait that already ran out (this launch or an earlier one of
             // the step) ends the others at once: one 10 s stall per step
-            if (*static_cast<volatile int *>(err) == 6 || sm100::global_timer_ns() - start > kTpPeerWaitNs) {
+            if (*static_cast<volatile int *>(err) == kErrTpPeerTimeout || sm100::global_timer_ns() - start > wait_ns) {
                 good = false;
                 break;
             }
         }
         ok = good;
         if (!good)
-            atomicExch(err, 6);
+            atomicExch(err, kErrTpPeerTimeout);
     }
     __syncthreads();
     if (ok) {
@@ -646,9 +651,11 @@ static __global__ void __launch_bounds__(128)
         }
     }
     // the last block of the launch re-arms this parity's counter (no rank
-    // writes it again before this rank's next GEMM of the other parity ran)
+    // writes it again before this rank's next GEMM of the other parity ran);
+    // a block whose wait ran out takes no part, so the counters stay as the
+    // ranks left them
     __syncthreads();
-    if (threadIdx.x == 0) {
+    if (threadIdx.x == 0 && ok) {
         __threadfence();
         if (atomicAdd(done + parity, 1u) == gridDim.x - 1) {
             atomicExch(cnt + parity, 0u);

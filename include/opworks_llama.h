@@ -124,6 +124,25 @@ OPW_API int opw_llama_batch_decode_multi(void *batch, int n, const int32_t *slot
 /* Logits (vocab_size floats) of row `row` of the last step. */
 OPW_API int opw_llama_batch_logits(void *batch, int row, float *out, int n, char *err, int err_len);
 
+/* KV-cache inspection (extension; the reference's contiguous cache needs
+ * none, include/runtime/kv_cache.cuh:11-35 there). The pool holds 16-token
+ * blocks; a per-slot block table maps logical to physical blocks.
+ * opw_llama_batch_kv_blocks: physical block ids of `slot` as the kernels see
+ * them (the device copy of the table); writes min(count, cap) ids, returns
+ * the count or -1.
+ * opw_llama_batch_kv_read: K (post-RoPE) and V of positions [pos0, pos0 + n)
+ * of `slot` in `layer`, gathered through the device block table, as
+ * [n][kv_heads][head_dim] floats each; positions may run up to the end of the
+ * slot's last mapped block. Returns 0 / -1.
+ * opw_llama_batch_kv_pool: raw physical blocks [block0, block0 + nblocks) of
+ * `layer`, [block][kv_heads][16][head_dim] floats each for K and V; returns
+ * the pool's block count (nblocks = 0 only asks for it) or -1. */
+OPW_API int opw_llama_batch_kv_blocks(void *batch, int slot, int32_t *out, int cap, char *err, int err_len);
+OPW_API int opw_llama_batch_kv_read(void *batch, int slot, int layer, int pos0, int n, float *k_out, float *v_out,
+                                    char *err, int err_len);
+OPW_API int opw_llama_batch_kv_pool(void *batch, int layer, int block0, int nblocks, float *k_out, float *v_out,
+                                    char *err, int err_len);
+
 /* The engine's CUDA stream (cudaStream_t), e.g. to record timing events. */
 OPW_API void *opw_llama_batch_stream(void *batch);
 /* Bytes copied host->device and device->host around one decode step of n

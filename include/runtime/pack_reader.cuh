@@ -72,7 +72,10 @@ class PackReader {
             throw std::runtime_error(path + ": unsupported dtype " + dtype_);
         for (const auto &[name, meta] : manifest_.at("tensors").as_object()) {
             TensorMeta t;
-            t.offset = static_cast<uint64_t>(meta.at("offset").as_int());
+            const int64_t offset = meta.at("offset").as_int();
+            if (offset < 0)
+                throw std::runtime_error(path + ": negative offset of " + name);
+            t.offset = static_cast<uint64_t>(offset);
             t.numel = 1;
             for (const auto &d : meta.at("shape").as_array()) {
                 const int64_t dim = d.as_int();
@@ -83,7 +86,8 @@ class PackReader {
                     throw std::runtime_error(path + ": absurd tensor size in " + name);
                 t.shape.push_back(dim);
             }
-            if (t.offset + static_cast<uint64_t>(t.numel) * elem_size_ > blob_size_)
+            const uint64_t bytes = static_cast<uint64_t>(t.numel) * elem_size_;
+            if (t.offset > blob_size_ || bytes > blob_size_ - t.offset) // no wrap-around
                 throw std::runtime_error(path + ": tensor " + name + " overruns the data blob");
             tensors_.emplace(name, std::move(t));
         }

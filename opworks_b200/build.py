@@ -6,9 +6,9 @@
 Outputs live next to the sources so they travel with the repository:
     opworks_b200/lib/libopworks_ops.so     operator C ABI   (include/opworks_ops.h)
     opworks_b200/lib/libopworks_llama.so   Llama C ABI      (include/opworks_llama.h)
-    oracle/liboracle.so                    CPU checker (test infrastructure)
-    oracle/_ref/*                          reference built from its own sources,
-                                           only when the reference tree is present
+
+The test checkers (CPU oracle, reference builds) have their own recipe,
+oracle/build_ref.py; __graft_entry__.build() runs both.
 """
 
 from __future__ import annotations
@@ -53,11 +53,6 @@ def _targets():
         out.append((os.path.join(LIBDIR, "libopworks_llama.so"),
                     [NVCC] + NVCC_FLAGS + ["-I", INC] + llama_srcs + ["-o", os.path.join(LIBDIR, "libopworks_llama.so")],
                     hdrs + llama_srcs))
-    orc = os.path.join(ROOT, "oracle", "oracle.cpp")
-    out.append((os.path.join(ROOT, "oracle", "liboracle.so"),
-                ["g++", "-O3", "-march=x86-64-v3", "-fopenmp", "-std=c++17", "-shared", "-fPIC", orc, "-o",
-                 os.path.join(ROOT, "oracle", "liboracle.so")],
-                [orc]))
     return out
 
 
@@ -82,16 +77,6 @@ def build(force=False, verbose=True):
         raise RuntimeError("build failed: " + ", ".join(os.path.basename(t) for t, _ in failed))
     if verbose and jobs:
         print(f"build: {len(jobs)} target(s) in {time.time() - t0:.1f}s", file=sys.stderr)
-    # reference builds (checker only) when the reference tree is mounted
-    ref = os.environ.get("OPWORKS_REFERENCE", "/root/reference")
-    if os.path.isdir(os.path.join(ref, "include")):
-        sys.path.insert(0, os.path.join(ROOT, "oracle"))
-        try:
-            import build_ref  # noqa: E402
-
-            build_ref.build(ref, force=force, verbose=verbose)
-        finally:
-            sys.path.pop(0)
 
 
 if __name__ == "__main__":

@@ -66,6 +66,9 @@ def bind(lib):
         "opw_llama_batch_decode": (I, [P, I, I32P, I32P, FP, FP, DP, U64P, I32P, I32P, S, I]),
         "opw_llama_batch_decode_multi": (I, [P, I, I32P, I32P, FP, FP, DP, U64P, I32P, I, I, I32P, I32P, S, I]),
         "opw_llama_batch_logits": (I, [P, I, FP, I, S, I]),
+        "opw_llama_batch_kv_blocks": (I, [P, I, I32P, I, S, I]),
+        "opw_llama_batch_kv_read": (I, [P, I, I, I, I, FP, FP, S, I]),
+        "opw_llama_batch_kv_pool": (I, [P, I, I, I, FP, FP, S, I]),
         "opw_llama_batch_stream": (P, [P]),
         "opw_llama_batch_io_bytes": (I, [P, I, ctypes.POINTER(ctypes.c_int64)]),
         "opw_llama_batch_profile": (I, [P, I, I, FP, I32P, S, I, S, I]),
@@ -142,6 +145,7 @@ class LlamaBatch:
         self.err = ctypes.create_string_buffer(_ERR_LEN)
         self.max_batch = max_batch
         self.max_seq_len = max_seq_len
+        self.tp_world = 1 if tp is None else int(tp[1])
         if tp is not None:
             rank, world, nccl_id = tp
             assert precision == "fast" and len(nccl_id) == 128
@@ -257,6 +261,37 @@ class LlamaBatch:
         self._check(self.lib.opw_llama_batch_logits(self.handle, row, out.ctypes.data_as(FP), out.size, self.err,
                                                     _ERR_LEN), "logits")
         return out
+
+    def kv_blocks(self, slot):
+        """Physical KV block ids of `slot` (the device copy of its block table)."""
+        cap = (self.max_seq_len + 15) // 16
+        out = np.zeros(cap, np.int32)
+        n = self._check(self.lib.opw_llama_batch_kv_blocks(self.handle, slot, out.ctypes.data_as(I32P), cap, self.err,
+                                                           _ERR_LEN), "kv blocks")
+        return out[:n].copy()
+
+    def kv_read(self, slot, layer, pos0, n):
+        """(K, V) of positions [pos0, pos0 + n) of `slot` in `layer`, read
+        through the block table: two [n][kv_heads][head_dim] float32 arrays."""
+        shape = (n, self.model.kv_heads // self.tp_world, self.model.head_dim)
+        k = np.empty(shape, np.float32)
+        v = np.empty(shape, np.float32)
+        self._check(self.lib.opw_llama_batch_kv_read(self.handle, slot, layer, pos0, n, k.ctypes.data_as(FP),
+                                                     v.ctypes.data_as(FP), self.err, _ERR_LEN), "kv read")
+        return k, v
+
+    def kv_pool(self, layer, block0=0, nblocks=None):
+        """Raw physical blocks of `layer`: (K, V) as [blocks][kv_heads][16][head_dim]."""
+        total = self._check(self.lib.opw_llama_batch_kv_pool(self.handle, layer, 0, 0, None, None, self.err, _ERR_LEN),
+                            "kv pool")
+        if nblocks is None:
+            nblocks = total - block0
+        shape = (nblocks, self.model.kv_heads // self.tp_world, 16, self.model.head_dim)
+        k = np.empty(shape, np.float32)
+        v = np.empty(shape, np.float32)
+        self._check(self.lib.opw_llama_batch_kv_pool(self.handle, layer, block0, nblocks, k.ctypes.data_as(FP),
+                                                     v.ctypes.data_as(FP), self.err, _ERR_LEN), "kv pool")
+        return k, v
 
     def close(self):
         if self.handle:

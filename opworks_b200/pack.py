@@ -166,13 +166,16 @@ def default_pack_dir():
     return os.environ.get("OPWORKS_PACK_DIR", "/tmp/opworks_packs")
 
 
-def ensure_random_llama_pack(cfg=None, seed=1234, name=None):
-    """Path of a cached random-init pack, generating it on first use."""
+def ensure_random_llama_pack(cfg=None, seed=1234, name=None, bf16_grid=True):
+    """Path of a cached random-init pack, generating it on first use. With
+    bf16_grid=False the weights keep all fp32 bits (BASELINE's plain
+    N(0, 0.02) draw), so the fast path's bf16 weight copy is a rounding."""
     cfg = cfg or LLAMA_3_2_1B
     d = default_pack_dir()
     os.makedirs(d, exist_ok=True)
-    tag = name or f"llama_L{cfg['num_hidden_layers']}_H{cfg['hidden_size']}_V{cfg['vocab_size']}_s{seed}_bf16grid"
+    grid = "bf16grid" if bf16_grid else "fp32"
+    tag = name or f"llama_L{cfg['num_hidden_layers']}_H{cfg['hidden_size']}_V{cfg['vocab_size']}_s{seed}_{grid}"
     path = os.path.join(d, tag + ".pack")
     if not os.path.exists(path):
-        random_llama_pack(path, cfg, seed)
+        random_llama_pack(path, cfg, seed, bf16_grid=bf16_grid)
     return path

@@ -143,12 +143,78 @@ static inline double dot_f64(const float *x, const float *w, int n) {
 
 // Y[rows, out] = X[rows, in] @ W[out, in]^T (include/ops/linear.cuh:18-121).
 // Each weight row is streamed once for all rows of X.
+// Four dot products of one x row against four weight rows, each summed in
+// exactly dot_f64's order (same lanes, same tree), so the blocked linear
+// below is bit-identical to the unblocked one; one x load feeds four FMAs.
+// (A float x float product is exact in double, so a fused multiply-add of
+// the widened operands rounds exactly like the scalar multiply and add.) The
+// weight rows come pre-widened to double (wd, 4 x n), converted once per
+// block of outputs.
+typedef double v4d __attribute__((vector_size(32)));
+typedef float v4f __attribute__((vector_size(16)));
+static inline v4d load4d(const float *p) {
+    v4f f;
+    std::memcpy(&f, p, sizeof(f));
+    return __builtin_convertvector(f, v4d);
+}
+static inline v4d load4dd(const double *p) {
+    v4d d;
+    std::memcpy(&d, p, sizeof(d));
+    return d;
+}
+static inline v4d fma4(v4d a, v4d b, v4d c) {
+#if defined(__FMA__)
+    return __builtin_ia32_vfmaddpd256(a, b, c);
+#else
+    return a * b + c;
+#endif
+}
+static inline void dot4_f64(const float *x, const double *wd, int n, double out[4]) {
+    v4d lo[4] = {}, hi[4] = {}; // lanes 0-3 and 4-7 of dot_f64's eight partial sums
+    int i = 0;
+    for (; i + 8 <= n; i += 8) {
+        const v4d x0 = load4d(x + i), x1 = load4d(x + i + 4);
+        for (int k = 0; k < 4; ++k) {
+            lo[k] = fma4(x0, load4dd(wd + static_cast<int64_t>(k) * n + i), lo[k]);
+            hi[k] = fma4(x1, load4dd(wd + static_cast<int64_t>(k) * n + i + 4), hi[k]);
+        }
+    }
+    for (int k = 0; k < 4; ++k) {
+        double a[8];
+        for (int j = 0; j < 4; ++j) {
+            a[j] = lo[k][j];
+            a[j + 4] = hi[k][j];
+        }
+        for (int t = i; t < n; ++t)
+            a[0] += static_cast<double>(x[t]) * wd[static_cast<int64_t>(k) * n + t];
+        out[k] = ((a[0] + a[1]) + (a[2] + a[3])) + ((a[4] + a[5]) + (a[6] + a[7]));
+    }
+}
+
 void orc_linear(const float *X, const float *W, float *Y, int rows, int in, int out) {
-#pragma omp parallel for schedule(static)
-    for (int o = 0; o < out; ++o) {
-        const float *w = W + static_cast<int64_t>(o) * in;
-        for (int r = 0; r < rows; ++r)
-            Y[static_cast<int64_t>(r) * out + o] = static_cast<float>(dot_f64(X + static_cast<int64_t>(r) * in, w, in));
+    const int blocks = (out + 3) / 4;
+#pragma omp parallel for schedule(dynamic, 4)
+    for (int b = 0; b < blocks; ++b) {
+        const int o0 = b * 4;
+        if (o0 + 4 <= out) {
+            thread_local std::vector<double> wd;
+            wd.resize(static_cast<size_t>(4) * in);
+            for (int64_t i = 0; i < static_cast<int64_t>(4) * in; ++i)
+                wd[i] = W[static_cast<int64_t>(o0) * in + i];
+            for (int r = 0; r < rows; ++r) {
+                double d[4];
+                dot4_f64(X + static_cast<int64_t>(r) * in, wd.data(), in, d);
+                for (int k = 0; k < 4; ++k)
+                    Y[static_cast<int64_t>(r) * out + o0 + k] = static_cast<float>(d[k]);
+            }
+        } else {
+            for (int o = o0; o < out; ++o) {
+                const float *w = W + static_cast<int64_t>(o) * in;
+                for (int r = 0; r < rows; ++r)
+                    Y[static_cast<int64_t>(r) * out + o] =
+                        static_cast<float>(dot_f64(X + static_cast<int64_t>(r) * in, w, in));
+            }
+        }
     }
 }
 
@@ -236,13 +302,16 @@ void orc_attention(const float *q, const float *k, const float *v, float *out, i
                 sc[s] = std::exp(sc[s] - m);
                 z += sc[s];
             }
+            // every output dim sums its terms in key order s = 0..last
             float *o = out + (static_cast<int64_t>(t) * qh + h) * D;
-            for (int i = 0; i < D; ++i) {
-                double acc = 0.0;
-                for (int s = 0; s <= last; ++s)
-                    acc += sc[s] * v[(static_cast<int64_t>(s) * kvh + g) * D + i];
-                o[i] = static_cast<float>(acc / z);
+            std::vector<double> acc(D, 0.0);
+            for (int s = 0; s <= last; ++s) {
+                const float *vr = v + (static_cast<int64_t>(s) * kvh + g) * D;
+                for (int i = 0; i < D; ++i)
+                    acc[i] += sc[s] * vr[i];
             }
+            for (int i = 0; i < D; ++i)
+                o[i] = static_cast<float>(acc[i] / z);
         }
 }
 

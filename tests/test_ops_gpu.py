@@ -337,6 +337,38 @@ def test_swiglu_add_split_merge_causal(ops):
     assert np.array_equal(host(dsc), want.astype(np.float32))
 
 
+@pytest.mark.parametrize("rows,heads,head_dim,off", [(33, 32, 64, 0), (7, 3, 6, 0), (5, 4, 64, 1), (3, 2, 4200, 0)])
+def test_rope_split_merge_causal_vector_and_scalar_paths(ops, rows, heads, head_dim, off):
+    """Both access widths of the standalone layout ops: 16-byte vectors
+    (head_dim / 2 a multiple of 4, aligned rows) and single floats (odd
+    halves, a pointer one float off 16-byte alignment), and RoPE's per-pair
+    trig path for halves too long for the shared-memory table."""
+    rng = np.random.default_rng(rows * 1000 + head_dim)
+    x = rng.standard_normal((rows, heads * head_dim)).astype(np.float32)
+    inv = (1.0 / (500000.0 ** (np.arange(head_dim // 2) * 2.0 / head_dim))).astype(np.float32)
+    buf = torch.zeros(x.size + off, device="cuda")
+    buf[off:] = torch.from_numpy(x.ravel()).cuda()
+    ops.rope(buf[off:], dev(inv), rows, heads, head_dim, 41, 0)
+    close(host(buf[off:]).reshape(rows, -1), oracle.rope(x, inv, heads, head_dim, 41))
+    stride, first = rows + 3, 2
+    slabs = torch.zeros(heads * stride * head_dim + off, device="cuda")
+    ops.split_heads(buf[off:], slabs[off:], rows, heads, head_dim, stride, first, 0)
+    rot = host(buf[off:]).reshape(rows, heads, head_dim)
+    s = host(slabs[off:]).reshape(heads, stride, head_dim)
+    assert np.array_equal(s[:, first:first + rows, :], rot.transpose(1, 0, 2))
+    assert not s[:, :first, :].any() and not s[:, first + rows:, :].any()
+    back = torch.empty(rows * heads * head_dim + off, device="cuda")
+    ops.merge_heads(slabs[off:], back[off:], rows, heads, head_dim, stride, first, 0)
+    assert np.array_equal(host(back[off:]).reshape(rows, heads, head_dim), rot)
+    for r, c in ((rows, rows + 8 * head_dim % 13), (rows, 4 * rows + 4)):
+        sc = rng.standard_normal((r, c)).astype(np.float32)
+        d = torch.empty(sc.size + off, device="cuda")
+        d[off:] = torch.from_numpy(sc.ravel()).cuda()
+        ops.causal_scale(d[off:], r, c, 0.125, 0)
+        want = np.where(np.arange(c)[None, :] <= (c - r + np.arange(r))[:, None], sc * np.float32(0.125), -np.inf)
+        assert np.array_equal(host(d[off:]).reshape(r, c), want.astype(np.float32))
+
+
 def test_argmax_exact(ops):
     g = np.load(os.path.join(GOLD, "ops_golden.npz"))
     x = inputs.op_inputs()["argmax.x"]

@@ -1,0 +1,223 @@
+"""Parity at the sizes the benchmark runs (BASELINE configs C2-C4), on the
+full-size random-init Llama-3.2-1B pack.
+
+* C3: 32 sequences prefilled to 2048 random ids, then 8 sampled decode steps
+  (T 0.7, top-p 0.9). For rows {0, 17, 31} the fast path's logits at every
+  step stay within the GEMM tolerance (2e-2 max-abs) of the accurate path fed
+  the same tokens; every sampled token equals the oracle sampler's draw on the
+  fast path's own logits with the same uniform; the accurate path's logits of
+  row 17 (prefill and last step) are within 1e-3 of the CPU oracle.
+* C4: one 8192-token prefill; last-row logits of the fast path (two-SM GEMMs,
+  tensor-core attention) within 2e-2 of the accurate path, same greedy token.
+* Weights off the bf16 grid: the C2 check (128-token prompt, 32 greedy steps)
+  on a pack whose fp32 weights are a plain N(0, 0.02) draw, so the fast path's
+  bf16 weights are a rounding of the accurate path's.
+* KV-cache writes: after a 37-token prefill plus 3 decode steps, K (post-RoPE)
+  and V read back through the block table match the oracle's cache; blocks and
+  positions nothing wrote are still exactly zero; and a second engine whose
+  block allocation runs in a different physical order holds bit-identical K/V
+  at every logical position (and gives bit-identical logits).
+
+Each test prints one "PARITY ..." line with the measured maximum errors.
+"""
+
+import numpy as np
+import pytest
+
+import oracle
+
+pytestmark = pytest.mark.gpu
+torch = pytest.importorskip("torch")
+
+TOL_GEMM = 2e-2  # BASELINE: logits of the bf16/TF32 tensor-core path, max-abs
+TOL_ORACLE = 1e-3  # accurate (fp32 / split-TF32) path against the double-accumulated oracle
+V = 128256
+ALL_SETS = 7  # bf16 + fp32 + split-TF32 weights
+
+
+@pytest.fixture(scope="module")
+def pack_path():
+    from opworks_b200 import pack
+
+    return pack.ensure_random_llama_pack()
+
+
+@pytest.fixture(scope="module")
+def model(pack_path):
+    from opworks_b200.llama import Model
+
+    with Model(pack_path, weight_sets=ALL_SETS) as m:
+        yield m
+
+
+@pytest.fixture(scope="module")
+def oracle_model(pack_path):
+    from opworks_b200 import pack
+
+    manifest, tensors = pack.read_pack(pack_path)
+    return oracle.Llama(manifest["config"], tensors)
+
+
+def test_c3_bs32_ctx2048_fast_vs_accurate_vs_oracle(model, oracle_model):
+    from opworks_b200.llama import LlamaBatch
+
+    B, CTX, STEPS, T, TOP_P = 32, 2048, 8, 0.7, 0.9
+    rows = (0, 17, 31)
+    prompts = np.random.default_rng(6).integers(0, V, (B, CTX)).astype(np.int32)
+    uni = np.random.default_rng(7).random((STEPS + 1, B))  # row 0: the prefill draws
+    tokens = np.zeros((STEPS + 1, B), np.int32)
+    fast = {r: [] for r in rows}
+    with LlamaBatch(model, B, CTX + STEPS + 8, "fast", prefill_rows=CTX) as fb:
+        for i in range(B):
+            tokens[0, i] = fb.prefill(i, prompts[i], T, TOP_P, float(uni[0, i]))
+            if i in fast:
+                fast[i].append(fb.logits(0))
+        for k in range(STEPS):
+            tokens[k + 1] = fb.decode(list(range(B)), tokens[k], temperature=T, top_p=TOP_P, uniforms=uni[k + 1])
+            for r in rows:
+                fast[r].append(fb.logits(r))
+    # the device sampler draws what the reference's host rule draws on the same logits
+    for r in rows:
+        for k in range(STEPS + 1):
+            assert oracle.top_p_sample(fast[r][k], T, TOP_P, uni[k, r]) == tokens[k, r], (r, k)
+    worst = 0.0
+    acc17 = []
+    with LlamaBatch(model, 1, CTX + STEPS + 8, "accurate", prefill_rows=CTX) as ab:
+        for r in rows:
+            ab.reset(0)
+            ab.prefill(0, prompts[r])
+            acc = [ab.logits(0)]
+            for k in range(STEPS):
+                ab.decode([0], [tokens[k, r]])
+                acc.append(ab.logits(0))
+            for k in range(STEPS + 1):
+                err = float(np.max(np.abs(fast[r][k] - acc[k])))
+                worst = max(worst, err)
+                assert err <= TOL_GEMM, (r, k, err)
+            if r == 17:
+                acc17 = acc
+    kc, vc = oracle_model.new_cache(CTX + STEPS + 1)
+    want = oracle_model.forward(prompts[17], 0, kc, vc)
+    err_pre = float(np.max(np.abs(acc17[0] - want)))
+    for k in range(STEPS):
+        want = oracle_model.forward([int(tokens[k, 17])], CTX + k, kc, vc)
+    err_last = float(np.max(np.abs(acc17[-1] - want)))
+    print(f"PARITY c3 fast_vs_accurate_max_abs={worst:.3e} accurate_vs_oracle_prefill={err_pre:.3e} "
+          f"accurate_vs_oracle_last_step={err_last:.3e}")
+    assert err_pre <= TOL_ORACLE, err_pre
+    assert err_last <= TOL_ORACLE, err_last
+
+
+def test_c4_8192_prefill_fast_vs_accurate(model):
+    from opworks_b200.llama import LlamaBatch
+
+    prompt = np.random.default_rng(8).integers(0, V, 8192).astype(np.int32)
+    with LlamaBatch(model, 1, 8192, "fast", prefill_rows=8192) as fb:
+        t_fast = fb.prefill(0, prompt)
+        got = fb.logits(0)
+    with LlamaBatch(model, 1, 8192, "accurate", prefill_rows=8192) as ab:
+        t_acc = ab.prefill(0, prompt)
+        ref = ab.logits(0)
+    err = float(np.max(np.abs(got - ref)))
+    print(f"PARITY c4 fast_vs_accurate_max_abs={err:.3e} tokens={t_fast},{t_acc}")
+    assert err <= TOL_GEMM, err
+    assert t_fast == t_acc
+
+
+def test_unrounded_weights_c2_fast_vs_accurate():
+    """The fast path reads bf16 copies of fp32 weights that are not on the
+    bf16 grid (BASELINE's plain N(0, 0.02) weights)."""
+    from opworks_b200 import pack
+    from opworks_b200.llama import LlamaBatch, Model
+
+    path = pack.ensure_random_llama_pack(bf16_grid=False)
+    prompt = np.random.default_rng(5).integers(0, V, 128).astype(np.int32)
+    steps = 32
+    with Model(path, weight_sets=ALL_SETS) as m:
+        with LlamaBatch(m, 1, 256, "accurate", prefill_rows=128) as ab:
+            toks = [ab.prefill(0, prompt)]
+            acc = [ab.logits(0)]
+            while len(toks) < steps:
+                toks.append(int(ab.decode([0], [toks[-1]])[0]))
+                acc.append(ab.logits(0))
+        with LlamaBatch(m, 1, 256, "fast", prefill_rows=128) as fb:
+            ftoks = [fb.prefill(0, prompt)]
+            errs = [float(np.max(np.abs(fb.logits(0) - acc[0])))]
+            for k in range(1, steps):
+                ftoks.append(int(fb.decode([0], [toks[k - 1]])[0]))  # fed the accurate path's tokens
+                errs.append(float(np.max(np.abs(fb.logits(0) - acc[k]))))
+    same = sum(int(a == b) for a, b in zip(toks, ftoks))
+    print(f"PARITY c2_unrounded fast_vs_accurate_max_abs={max(errs):.3e} mean_step_max_abs={np.mean(errs):.3e} "
+          f"greedy_agree={same}/{steps}")
+    assert max(errs) <= TOL_GEMM, max(errs)
+
+
+def _run_kv_script(b, prompts):
+    """37-token prefill of slot 1 (beside slots 0 and 2) and 3 decode steps of
+    all three; returns the tokens fed to slot 1 after its prompt and the last
+    step's logits of slot 1."""
+    first = [b.prefill(s, prompts[s]) for s in range(3)]
+    fed = [first[1]]
+    prev = first
+    for _ in range(3):
+        prev = b.decode([0, 1, 2], prev)
+        fed.append(int(prev[1]))
+    return fed[:3], b.logits(1)
+
+
+def _pool_unwritten_is_zero(b, layers, lengths):
+    """Every pool float that no slot's first `length` positions map to is 0."""
+    owned = {}
+    for s, n in lengths.items():
+        for i, blk in enumerate(b.kv_blocks(s)):
+            owned[int(blk)] = max(0, min(16, n - 16 * i))  # written positions of that block
+    for layer in layers:
+        k, v = b.kv_pool(layer)
+        for blk in range(k.shape[0]):
+            used = owned.get(blk, 0)
+            if np.any(k[blk, :, used:, :] != 0) or np.any(v[blk, :, used:, :] != 0):
+                return False
+    return True
+
+
+@pytest.mark.parametrize("precision", ["accurate", "fast"])
+def test_kv_cache_writes_bit_exact(model, oracle_model, precision):
+    from opworks_b200.llama import LlamaBatch
+
+    rng = np.random.default_rng(41)
+    prompts = [rng.integers(0, V, n).astype(np.int32) for n in (20, 37, 5)]
+    L = model.layers
+    with LlamaBatch(model, 3, 96, precision, prefill_rows=96) as a:
+        fed, logits_a = _run_kv_script(a, prompts)
+        blocks_a = a.kv_blocks(1)
+        kv_a = [a.kv_read(1, l, 0, 40) for l in range(L)]
+        assert _pool_unwritten_is_zero(a, range(L), {0: 23, 1: 40, 2: 8})
+    with LlamaBatch(model, 3, 96, precision, prefill_rows=96) as b:
+        # a 70-token sequence takes and frees blocks 0..4 first, so this
+        # engine's later blocks come out of the free list in reverse order
+        b.prefill(2, rng.integers(0, V, 70).astype(np.int32))
+        b.reset(2)
+        fed_b, logits_b = _run_kv_script(b, prompts)
+        blocks_b = b.kv_blocks(1)
+        kv_b = [b.kv_read(1, l, 0, 40) for l in range(L)]
+    assert fed_b == fed
+    assert not np.array_equal(blocks_a, blocks_b), (blocks_a, blocks_b)
+    for l in range(L):
+        for x, y in zip(kv_a[l], kv_b[l]):
+            assert np.array_equal(x.view(np.uint32), y.view(np.uint32)), l
+    assert np.array_equal(logits_a.view(np.uint32), logits_b.view(np.uint32))
+    # values: the oracle's post-RoPE K and V of the same 40 positions
+    kc, vc = oracle_model.new_cache(48)
+    oracle_model.forward(prompts[1], 0, kc, vc)
+    for k, t in enumerate(fed):
+        oracle_model.forward([t], 37 + k, kc, vc)
+    tol = 1e-4 if precision == "accurate" else TOL_GEMM
+    worst = 0.0
+    for l in range(L):
+        k_got, v_got = kv_a[l]
+        k_want = kc[l, :, :40, :].transpose(1, 0, 2)
+        v_want = vc[l, :, :40, :].transpose(1, 0, 2)
+        worst = max(worst, float(np.max(np.abs(k_got - k_want))), float(np.max(np.abs(v_got - v_want))))
+    print(f"PARITY kv_{precision} max_abs_vs_oracle={worst:.3e} blocks_a={blocks_a.tolist()} "
+          f"blocks_b={blocks_b.tolist()}")
+    assert worst <= tol, worst
