@@ -7,7 +7,7 @@ Workload (one batch per GPU, request-partitioned so
 N GPUs run N independent batches with no collective on the data path):
   * weights: OPWPACK1 float32 pack, N(0, 0.02) projections / embedding,
     RMSNorm gains 1.0, tied LM head (generated once per box under
-    $OPWORKS_PACK_DIR, default /tmp/opworks_packs); the engine uses the bf16
+    $OPWORKS_PACK_DIR, default /tmp/opworks_packs); the engine uses the fp16
     copy made at load (fast path), the fp32 KV cache is paged (16-token blocks)
   * 32 sequences per GPU, each prefilled with 2048 uniform random token ids
   * W warm-up + K timed decode steps, every sequence sampling with T = 0.7,
@@ -25,6 +25,8 @@ Reported (one JSON line from rank 0):
   cpu_baseline  the C++ oracle's batched decode step on the host cores
              (bounded sample: a few steps), rank 0 at N = 1
   prefill    C3 prefill (32 x 2048 tokens) and C4 (one 8192-token prompt)
+  c5         BASELINE C5 serving at this N: 256 requests partitioned over the
+             ranks (strong scaling: total generated tok/s, per-rank busy time)
 `--impl reference` times the reference algorithm's CPU restatement (the
 OpWorks reference has no CPU path of its own) on the same workload.
 """
@@ -73,6 +75,7 @@ def parse():
                     help="c3: batched decode (default, the headline); c5: 256-request serving, "
                          "request-partitioned over the ranks")
     ap.add_argument("--c5-max-batch", type=int, default=64, help="KV slots per GPU for c5 continuous batching")
+    ap.add_argument("--no-c5", action="store_true", help="skip the C5 serving block of the c3 line")
     return ap.parse_args()
 
 
@@ -147,7 +150,7 @@ def algorithmic_bytes(label, cfg, batch, ctx_mean):
         "gemm_o": L * (H * qw * 2 + act(qw) * 2 + act(H) * 4),
         "gemm_gate_up": L * (2 * I * H * 2 + act(H) * 2 + act(2 * I) * 4),
         "gemm_down": L * (H * I * 2 + act(I) * 2 + act(H) * 4),
-        # fused fast path: bf16 weights, two-term bf16 activations in (4 bytes
+        # fused fast path: 16-bit weights, two-term 16-bit activations in (4 bytes
         # per element), fused epilogue traffic out
         "gemm_qkv_rope_kv_write": L * ((qw + 2 * kvw) * H * 2 + act(H) * 4 + act(qw + 2 * kvw) * 4),
         # residual epilogues: hidden read + write, next operand h * gain out
@@ -383,6 +386,12 @@ def run_ours(args):
                      "frac_of_bf16_peak": round((gemm_flop + attn_flop) / (ms8 / 1e3) / 1e12 / tc_peak, 4)}
         eng8.close()
 
+    # ---- C5: 256-request serving, strong scaling over the ranks (every
+    # rank; request-partitioned, no collective on the data path)
+    c5 = None
+    if not args.no_c5 and not tp:
+        c5 = c5_serve(model, args, rank, world, torch.device("cuda", local))
+
     # ---- C2: batch 1, 128-token prompt, then greedy decode (fast path, our
     # batched ABI with one slot; host wall clock per blocking call)
     c2 = None
@@ -400,7 +409,7 @@ def run_ours(args):
                 tok = int(e2.decode([0], [tok])[0])
             dec = time.perf_counter() - t
         c2 = {"prompt": 128, "ttft_ms": round(ttft * 1e3, 2), "decode_steps": 128,
-              "decode_tok_s": round(128 / dec, 1), "precision": "fast (bf16 weights)",
+              "decode_tok_s": round(128 / dec, 1), "precision": "fast (fp16 weights)",
               "timing": "host wall clock per blocking call"}
 
     # ---- C1 operator configs, ours and the reference's kernels (rank 0, N = 1)
@@ -425,7 +434,7 @@ def run_ours(args):
             "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world, "steps": K, "warmup": W,
             "ms_per_step": round(dev_ms / K, 4), "higher_is_better": True, "scaling": "strong" if tp else "weak",
             "vs_baseline": None,
-            "dtype": "bf16",
+            "dtype": "f16",
             "data": "synthetic: random-init weights N(0,0.02) (norm gains 1.0), uniform random token ids",
             "config": {"workload": f"C3 batched decode: Llama-3.2-1B random-init, {BATCH} sequences per GPU "
                                    f"prefilled to {CTX} random ids, T=0.7 top-p=0.9 device sampling, fp32 paged KV "
@@ -437,8 +446,8 @@ def run_ours(args):
                                           "peer stores from the GEMM epilogue + rank-order sum")
                                        + " after o and down" if tp else
                                        f"request-partitioned x{world} (no collective)"),
-                       "precision": "bf16 weights + GEMM operands, fp32 residual / KV cache / attention / "
-                                    "softmax / sampling (fp64)",
+                       "precision": "fp16 weights (rounded from the fp32 pack) and two-term fp16 GEMM operands, "
+                                    "fp32 accumulation / residual / KV cache / attention / softmax, sampling fp64",
                        "l2": "inputs larger than L2: every step streams 2.47 GB of weights + ~4.5 GB of KV",
                        "cuda_graph": True},
             "roofline": roofline, "step_roofline": step_roofline,
@@ -456,6 +465,8 @@ def run_ours(args):
             line["c1_ops"] = c1
         if c2 is not None:
             line["c2"] = c2
+        if c5 is not None:
+            line["c5"] = c5
         if multi is not None:
             line["multi_step_decode"] = multi
         if ref_cuda is not None:
@@ -627,34 +638,21 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
-def run_c5(args):
-    """BASELINE C5: 256 requests (prompt lengths U[256, 1024], 256 sampled
-    tokens each, T=0.7 top-p 0.9) split over the ranks by the deterministic
-    LPT partition (opworks_b200/serving.py); every rank serves its share with
-    continuous batching on its GPU, no collective on the data path. Timed
-    on the device (CUDA events on each engine stream, max over ranks); value =
-    generated tokens of all requests / that time."""
+def c5_serve(model, args, rank, world, device_id):
+    """BASELINE C5 on an already loaded model: 256 requests (prompt lengths
+    U[256, 1024], 256 sampled tokens each, T=0.7 top-p 0.9) split over the
+    ranks by the deterministic LPT partition (opworks_b200/serving.py); every
+    rank serves its share with continuous batching on its GPU, no collective
+    on the data path. Timed on the device (CUDA events on each engine stream,
+    max over ranks); returns (on every rank) the strong-scaling record: total
+    generated tokens / that time, plus each rank's busy time."""
     import torch
     import torch.distributed as dist
 
-    from opworks_b200 import pack, serving
-    from opworks_b200.llama import LlamaBatch, Model
+    from opworks_b200 import serving
+    from opworks_b200.llama import LlamaBatch
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    if world > 1:
-        import datetime
-
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
-    if rank == 0:
-        pack.ensure_random_llama_pack()
-    if world > 1:
-        dist.barrier()
-    pack_path = pack.ensure_random_llama_pack()
     reqs = serving.c5_requests()
-    model = Model(pack_path, weight_sets=1, device=local)
     eng = LlamaBatch(model, args.c5_max_batch, 1024 + 256 + 16, "fast", prefill_rows=1024)
     stream = torch.cuda.ExternalStream(eng.stream())
     # warm-up: module loads and the decode graphs of every batch size used
@@ -675,26 +673,57 @@ def run_c5(args):
     wall = time.perf_counter() - t0
     ms = a.elapsed_time(b)
     gen = sum(len(v) for v in out.values())
+    my = [ms, float(gen), float(server.prefill_tokens)]
+    busy = [my]
     if world > 1:
-        t = torch.tensor([ms, wall, float(gen), float(server.prefill_tokens)], dtype=torch.float64, device="cuda")
-        tm = t.clone()
-        dist.all_reduce(tm, op=dist.ReduceOp.MAX)
-        dist.all_reduce(t, op=dist.ReduceOp.SUM)
-        ms, wall = float(tm[0].item()), float(tm[1].item())
-        gen, pre = int(t[2].item()), int(t[3].item())
-    else:
-        pre = server.prefill_tokens
-    if rank == 0:
-        line = {"metric": "C5 serving: generated tok/s (256 requests, prompts U[256,1024], 256 new tokens)",
-                "value": round(gen / (ms / 1e3), 1), "unit": UNIT, "n_gpus": world, "higher_is_better": True,
-                "scaling": "strong", "ms": round(ms, 1), "wall_s": round(wall, 2), "generated_tokens": gen,
-                "prefill_tokens": pre, "requests": len(reqs),
-                "config": {"workload": "C5", "max_batch_per_gpu": args.c5_max_batch,
-                           "parallelism": f"request-partitioned x{world} (LPT by prompt + new tokens, no collective)",
-                           "sampling": "T=0.7 top-p 0.9 on the device"},
-                "dtype": "bf16", "data": "synthetic: random-init weights, uniform random prompt ids"}
-        print(json.dumps(line), flush=True)
+        t = torch.tensor(my, dtype=torch.float64, device=device_id)
+        allt = [torch.zeros_like(t) for _ in range(world)]
+        dist.all_gather(allt, t)
+        busy = [x.tolist() for x in allt]
+        w = torch.tensor([wall], dtype=torch.float64, device=device_id)
+        dist.all_reduce(w, op=dist.ReduceOp.MAX)
+        wall = float(w.item())
     eng.close()
+    ms_max = max(r[0] for r in busy)
+    gen = int(sum(r[1] for r in busy))
+    pre = int(sum(r[2] for r in busy))
+    return {"metric": "C5 serving: generated tok/s (256 requests, prompts U[256,1024], 256 new tokens)",
+            "value": round(gen / (ms_max / 1e3), 1), "unit": UNIT, "n_gpus": world, "scaling": "strong",
+            "ms": round(ms_max, 1), "wall_s": round(wall, 2), "generated_tokens": gen, "prefill_tokens": pre,
+            "requests": len(reqs), "rank_busy_ms": [round(r[0], 1) for r in busy],
+            "rank_generated_tokens": [int(r[1]) for r in busy],
+            "config": {"max_batch_per_gpu": args.c5_max_batch,
+                       "parallelism": f"request-partitioned x{world} (LPT by prompt + new tokens, no collective)",
+                       "sampling": "T=0.7 top-p 0.9 on the device"}}
+
+
+def run_c5(args):
+    """`--workload c5`: the C5 serving run alone (c5_serve) as the line."""
+    import torch
+    import torch.distributed as dist
+
+    from opworks_b200 import pack
+    from opworks_b200.llama import Model
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+    if rank == 0:
+        pack.ensure_random_llama_pack()
+    if world > 1:
+        dist.barrier()
+    pack_path = pack.ensure_random_llama_pack()
+    model = Model(pack_path, weight_sets=1, device=local)
+    line = c5_serve(model, args, rank, world, torch.device("cuda", local))
+    if rank == 0:
+        line.update({"higher_is_better": True, "dtype": "f16",
+                     "data": "synthetic: random-init weights, uniform random prompt ids"})
+        print(json.dumps(line), flush=True)
     model.close()
     if world > 1:
         dist.destroy_process_group()

@@ -1,7 +1,8 @@
 #pragma once
 
 // RAII device allocation for the runtime's element types (float, int32_t,
-// __nv_bfloat16, plus uint8_t for raw byte pools), 64-bit sizes. API of
+// __nv_bfloat16, uint16_t for 16-bit tensor-core operands whose format is
+// kept beside them, uint8_t for raw byte pools), 64-bit sizes. API of
 // OpWorks include/core/typed_device_buffer.cuh:15-92.
 
 #include <cstdint>
@@ -16,8 +17,8 @@ namespace opworks {
 
 template <typename T> class TypedDeviceBuffer {
     static_assert(std::is_same_v<T, float> || std::is_same_v<T, int32_t> || std::is_same_v<T, __nv_bfloat16> ||
-                      std::is_same_v<T, uint8_t>,
-                  "TypedDeviceBuffer supports float, int32_t, __nv_bfloat16 and uint8_t");
+                      std::is_same_v<T, uint16_t> || std::is_same_v<T, uint8_t>,
+                  "TypedDeviceBuffer supports float, int32_t, __nv_bfloat16, uint16_t and uint8_t");
 
   public:
     TypedDeviceBuffer() = default;

@@ -21,7 +21,8 @@
 // captured once per batch size as a CUDA graph (input H2D, forward, sampler,
 // token D2H), so a step costs one graph launch and one stream sync.
 //
-// Precision: kFast = bf16 weights and GEMM operands, fp32 residual stream,
+// Precision: kFast = 16-bit weights and two-term 16-bit GEMM activations
+// (fp16 for float32 packs, bf16 for bfloat16 packs), fp32 residual stream,
 // fp32 KV cache, fp32 attention and softmax; kAccurate = fp32 end to end
 // (shared-weight fp32 GEMV for <= 4 rows, split-precision TF32 tensor-core
 // GEMM otherwise) — the fp32 model's default, for parity with the reference.
@@ -53,6 +54,7 @@
 #include "../runtime/nccl_lite.cuh"
 #include "../runtime/pack_reader.cuh"
 #include "../runtime/weights.cuh"
+#include "tp_plan.cuh"
 
 namespace opworks {
 
@@ -128,7 +130,7 @@ template <typename WT> class LlamaEngineT {
         const int rep = cfg.kv_rep();
         detail::require(rep == 1 || rep == 2 || rep == 4 || rep == 8, "GQA ratio must be 1, 2, 4 or 8");
         if (prec == Precision::kFast)
-            detail::require(w.sets & kWeightsBF16, "bf16 weights were not loaded");
+            detail::require(w.sets & kWeights16, "16-bit (fast path) weights were not loaded");
         else
             detail::require((w.sets & kWeightsF32) && (w.sets & kWeightsSplit),
                             "fp32 weights (accurate path) were not loaded");
@@ -144,15 +146,13 @@ template <typename WT> class LlamaEngineT {
         tp_world_ = tp.world;
         detail::require(tp_world_ >= 1 && tp_rank_ >= 0 && tp_rank_ < tp_world_, "bad tensor-parallel rank / world");
         if (tp_world_ > 1) {
-            detail::require(prec == Precision::kFast, "tensor parallelism runs the fast (bf16) path");
+            detail::require(prec == Precision::kFast, "tensor parallelism runs the fast (16-bit) path");
             detail::require(tp.nccl_id != nullptr, "tensor parallelism needs an NCCL id");
-            detail::require(cfg.num_kv_heads % tp_world_ == 0 && cfg.intermediate_size % (128 * tp_world_) == 0 &&
-                                cfg.hidden_size % 128 == 0,
-                            "tensor parallelism needs KV heads and 128-column MLP tiles divisible by the world size");
         }
-        qh_l_ = cfg.num_q_heads / tp_world_;
-        kvh_l_ = cfg.num_kv_heads / tp_world_;
-        inter_l_ = cfg.intermediate_size / tp_world_;
+        shard_ = tp_shard(cfg, tp_rank_, tp_world_);
+        qh_l_ = shard_.q_heads;
+        kvh_l_ = shard_.kv_heads;
+        inter_l_ = shard_.inter;
         ModelConfig kv_cfg = cfg;
         kv_cfg.num_kv_heads = kvh_l_;
         kv_ = KvCache(kv_cfg, max_seq_len, max_batch * blocks_per_seq_);
@@ -168,12 +168,12 @@ template <typename WT> class LlamaEngineT {
         ss_ = TypedDeviceBuffer<float>(rows_max_ * ((H + kUmmaM - 1) / kUmmaM));
         q_ = TypedDeviceBuffer<float>(rows_max_ * QW);
         if (fast) {
-            normed_bf_ = TypedDeviceBuffer<__nv_bfloat16>(rows_max_ * H);
-            attn_bf_ = TypedDeviceBuffer<__nv_bfloat16>(rows_max_ * QW);
-            act_bf_ = TypedDeviceBuffer<__nv_bfloat16>(rows_max_ * I);
-            normed_bflo_ = TypedDeviceBuffer<__nv_bfloat16>(rows_max_ * H);
-            attn_bflo_ = TypedDeviceBuffer<__nv_bfloat16>(rows_max_ * QW);
-            act_bflo_ = TypedDeviceBuffer<__nv_bfloat16>(rows_max_ * I);
+            normed_h_ = TypedDeviceBuffer<uint16_t>(rows_max_ * H);
+            attn_h_ = TypedDeviceBuffer<uint16_t>(rows_max_ * QW);
+            act_h_ = TypedDeviceBuffer<uint16_t>(rows_max_ * I);
+            normed_hlo_ = TypedDeviceBuffer<uint16_t>(rows_max_ * H);
+            attn_hlo_ = TypedDeviceBuffer<uint16_t>(rows_max_ * QW);
+            act_hlo_ = TypedDeviceBuffer<uint16_t>(rows_max_ * I);
         } else {
             normed_f_ = TypedDeviceBuffer<float>(rows_max_ * H);
             normed_lo_ = TypedDeviceBuffer<float>(rows_max_ * H);
@@ -614,8 +614,8 @@ template <typename WT> class LlamaEngineT {
         std::vector<int> blocks;
     };
     struct Act {
-        const __nv_bfloat16 *bf16;
-        const __nv_bfloat16 *bf16_lo;
+        const uint16_t *h16;    // 16-bit operand (format: w_.f16), hi term
+        const uint16_t *h16_lo; // remainder term
         const float *f32;
         const float *lo;
     };
@@ -731,14 +731,19 @@ template <typename WT> class LlamaEngineT {
     // epilogue scratch can hold rows preloaded during the main loop
     bool narrow_tile(int rows) const { return rows <= prefill_single_rows_ && plan_bn(rows) <= 64; }
 
-    // A bf16 weight operand: `out` rows of `in` elements, row stride ld
+    // A 16-bit weight operand: `out` rows of `in` elements, row stride ld
     // (a column slice of a wider matrix keeps the matrix's stride).
     struct WView {
-        const __nv_bfloat16 *w = nullptr;
+        const uint16_t *w = nullptr;
         int out = 0, in = 0;
         int64_t ld = 0;
     };
-    static WView view(const Projection &p) { return {p.bf16.data(), p.out, p.in, p.in}; }
+    static WView view(const Projection &p) { return {p.w16.data(), p.out, p.in, p.in}; }
+    // GEMM operands in the model's 16-bit format
+    sm100::GemmOperand wop(const WView &p) const { return {p.w, nullptr, p.out, p.ld, w_.f16}; }
+    sm100::GemmOperand xop(const Act &x, int rows, int64_t ld, bool two_term = true) const {
+        return {x.h16, two_term ? x.h16_lo : nullptr, rows, ld, w_.f16};
+    }
 
     // this rank's slices of the fast path's projections: QKV rows of its q,
     // k and v heads (a compact copy), O and down input-column slices (views),
@@ -746,8 +751,7 @@ template <typename WT> class LlamaEngineT {
     void make_views() {
         if (!fast())
             return;
-        const int H = cfg_.hidden_size, I = cfg_.intermediate_size, D = cfg_.head_dim;
-        const int qh = cfg_.num_q_heads, kvh = cfg_.num_kv_heads;
+        const int H = cfg_.hidden_size, I = cfg_.intermediate_size;
         for (int l = 0; l < cfg_.num_layers; ++l) {
             const LayerWeights<WT> &L = w_.layers[l];
             if (tp_world_ == 1) {
@@ -757,25 +761,24 @@ template <typename WT> class LlamaEngineT {
                 down_v_.push_back(view(L.down));
                 continue;
             }
-            const int qrows = qh_l_ * D, kvrows = kvh_l_ * D;
+            const TpShard &sh = shard_;
+            const int qrows = static_cast<int>(sh.q_rows), kvrows = static_cast<int>(sh.kv_rows);
             tp_qkv_.emplace_back(static_cast<int64_t>(qrows + 2 * kvrows) * H);
-            __nv_bfloat16 *dst = tp_qkv_.back().data();
-            const __nv_bfloat16 *src = L.qkv.bf16.data();
-            const int64_t from[3] = {static_cast<int64_t>(tp_rank_) * qrows,
-                                     static_cast<int64_t>(qh) * D + static_cast<int64_t>(tp_rank_) * kvrows,
-                                     static_cast<int64_t>(qh + kvh) * D + static_cast<int64_t>(tp_rank_) * kvrows};
+            uint16_t *dst = tp_qkv_.back().data();
+            const uint16_t *src = L.qkv.w16.data();
+            const int64_t from[3] = {sh.q_row0, sh.k_row0, sh.v_row0};
             const int64_t count[3] = {qrows, kvrows, kvrows};
             int64_t at = 0;
             for (int i = 0; i < 3; ++i) {
                 OPWORKS_CUDA_CHECK(cudaMemcpy(dst + at * H, src + from[i] * H,
-                                              sizeof(__nv_bfloat16) * static_cast<size_t>(count[i] * H),
+                                              sizeof(uint16_t) * static_cast<size_t>(count[i] * H),
                                               cudaMemcpyDeviceToDevice));
                 at += count[i];
             }
             qkv_v_.push_back({dst, qrows + 2 * kvrows, H, H});
-            o_v_.push_back({L.o.bf16.data() + static_cast<int64_t>(tp_rank_) * qrows, H, qrows, cfg_.q_width()});
-            gu_v_.push_back({L.gu.bf16.data() + static_cast<int64_t>(tp_rank_) * 2 * inter_l_ * H, 2 * inter_l_, H, H});
-            down_v_.push_back({L.down.bf16.data() + static_cast<int64_t>(tp_rank_) * inter_l_, H, inter_l_, I});
+            o_v_.push_back({L.o.w16.data() + sh.o_col0, H, qrows, cfg_.q_width()});
+            gu_v_.push_back({L.gu.w16.data() + sh.gu_row0 * H, static_cast<int>(sh.gu_rows), H, H});
+            down_v_.push_back({L.down.w16.data() + sh.down_col0, H, sh.inter, I});
         }
     }
 
@@ -807,18 +810,16 @@ template <typename WT> class LlamaEngineT {
     template <typename Epi>
     void linear_tile(const WView &p, const Act &x, int rows, const Epi &epi, const WView *next = nullptr) {
         if (rows > prefill_single_rows_) {
-            // prefill-sized GEMMs: single-term bf16 activations (one MMA per
-            // K step, 256-token tiles), compute-bound shapes
-            sm100::gemm_tn<sm100::GemmKind::kBF16, Epi>({p.w, nullptr, p.out, p.ld},
-                                                        {x.bf16, nullptr, rows, p.in}, p.in, part_.data(), p.out, 1,
+            // prefill-sized GEMMs: single-term 16-bit activations (one MMA
+            // per K step, 256-token tiles), compute-bound shapes
+            sm100::gemm_tn<sm100::GemmKind::kBF16, Epi>(wop(p), xop(x, rows, p.in, false), p.in, part_.data(), p.out, 1,
                                                         static_cast<int64_t>(rows) * p.out, stream_, epi,
                                                         sm100::gemm_pick_bn(sm100::GemmKind::kBF16, rows));
             return;
         }
         if (rows >= pair_min_rows_) {
             // prefill-sized GEMMs: two-SM 256 x 256 tiles (cta_group::2)
-            sm100::gemm_pair_bf16x2<Epi>({p.w, nullptr, p.out, p.ld}, {x.bf16, x.bf16_lo, rows, p.in}, p.in, stream_,
-                                         epi);
+            sm100::gemm_pair_bf16x2<Epi>(wop(p), xop(x, rows, p.in), p.in, stream_, epi);
             return;
         }
         int splits = plan_splits(p, rows, max_cluster_splits_);
@@ -838,22 +839,21 @@ template <typename WT> class LlamaEngineT {
         }
         if (cluster > 0) {
             sm100::gemm_tn<sm100::GemmKind::kBF16x2, Epi>(
-                {p.w, nullptr, p.out, p.ld}, {x.bf16, x.bf16_lo, rows, p.in}, p.in, part_.data(), p.out, splits,
+                wop(p), xop(x, rows, p.in), p.in, part_.data(), p.out, splits,
                 static_cast<int64_t>(rows) * p.out, stream_, epi, 32, nullptr, 0, &groups_ws_, cluster);
             return;
         }
         sm100::gemm_tn<sm100::GemmKind::kBF16x2, Epi>(
-            {p.w, nullptr, p.out, p.ld}, {x.bf16, x.bf16_lo, rows, p.in}, p.in, part_.data(), p.out, splits,
+            wop(p), xop(x, rows, p.in), p.in, part_.data(), p.out, splits,
             static_cast<int64_t>(rows) * p.out, stream_, epi, plan_bn(rows), pf ? next->w : nullptr,
-            pf ? sizeof(__nv_bfloat16) * static_cast<uint64_t>(next->out) * next->ld : 0);
+            pf ? sizeof(uint16_t) * static_cast<uint64_t>(next->out) * next->ld : 0);
     }
 
     // part[s][rows][p.out] = x[rows][p.in] . W^T (partial over split s)
     int linear(const Projection &p, const Act &x, int rows) {
         const int splits = plan_splits(p, rows);
         if (fast()) {
-            sm100::gemm_tn<sm100::GemmKind::kBF16x2>({p.bf16.data(), nullptr, p.out, p.in},
-                                                     {x.bf16, x.bf16_lo, rows, p.in}, p.in, part_.data(), p.out,
+            sm100::gemm_tn<sm100::GemmKind::kBF16x2>(wop(view(p)), xop(x, rows, p.in), p.in, part_.data(), p.out,
                                                      splits, static_cast<int64_t>(rows) * p.out, stream_,
                                                      sm100::Identity{}, plan_bn(rows));
         } else if (rows <= 4) {
@@ -868,13 +868,13 @@ template <typename WT> class LlamaEngineT {
         return splits;
     }
 
-    detail::ActOut act_out(__nv_bfloat16 *bf, __nv_bfloat16 *bflo, float *f, float *lo, int64_t ld,
-                           int rows) const {
+    detail::ActOut act_out(uint16_t *h, uint16_t *hlo, float *f, float *lo, int64_t ld, int rows) const {
         detail::ActOut o;
         o.ld = ld;
         if (fast()) {
-            o.bf16 = bf;
-            o.bf16_lo = bflo;
+            o.h16 = h;
+            o.h16_lo = hlo;
+            o.f16 = w_.f16;
         } else {
             o.f32 = f;
             o.lo = rows > 4 ? lo : nullptr;
@@ -1027,18 +1027,17 @@ template <typename WT> class LlamaEngineT {
         const int H = cfg_.hidden_size, I = inter_l_, QW = qh_l_ * cfg_.head_dim; // this rank's widths
         const int qh = qh_l_, kvh = kvh_l_;
         const detail::ActOut normed_o =
-            act_out(normed_bf_.data(), normed_bflo_.data(), normed_f_.data(), normed_lo_.data(), H, rows);
-        const detail::ActOut attn_o =
-            act_out(attn_bf_.data(), attn_bflo_.data(), attn_f_.data(), attn_lo_.data(), QW, rows);
-        const detail::ActOut act_o = act_out(act_bf_.data(), act_bflo_.data(), act_f_.data(), act_lo_.data(), I, rows);
-        const Act normed{normed_o.bf16, normed_o.bf16_lo, normed_o.f32, normed_o.lo};
-        const Act attn{attn_o.bf16, attn_o.bf16_lo, attn_o.f32, attn_o.lo};
-        const Act act{act_o.bf16, act_o.bf16_lo, act_o.f32, act_o.lo};
+            act_out(normed_h_.data(), normed_hlo_.data(), normed_f_.data(), normed_lo_.data(), H, rows);
+        const detail::ActOut attn_o = act_out(attn_h_.data(), attn_hlo_.data(), attn_f_.data(), attn_lo_.data(), QW, rows);
+        const detail::ActOut act_o = act_out(act_h_.data(), act_hlo_.data(), act_f_.data(), act_lo_.data(), I, rows);
+        const Act normed{normed_o.h16, normed_o.h16_lo, normed_o.f32, normed_o.lo};
+        const Act attn{attn_o.h16, attn_o.h16_lo, attn_o.f32, attn_o.lo};
+        const Act act{act_o.h16, act_o.h16_lo, act_o.f32, act_o.lo};
 
         if (w_.embed_f32.size() > 0)
             embed(rows, w_.embed_f32.data(), normed_o);
-        else
-            embed(rows, w_.embed_bf16.data(), normed_o);
+        else // bfloat16 packs: the table's words are bf16
+            embed(rows, reinterpret_cast<const __nv_bfloat16 *>(w_.embed_w16.data()), normed_o);
         mark("embed_rmsnorm");
         if (hook) {
             OPWORKS_CUDA_CHECK(cudaStreamSynchronize(stream_));
@@ -1151,9 +1150,9 @@ template <typename WT> class LlamaEngineT {
         if (fast()) {
             // deferred final norm: the epilogue scales each row's logits
             sm100::gemm_tn<sm100::GemmKind::kBF16x2, detail::LogitsTileEpi>(
-                {w_.embed_bf16.data(), nullptr, V, H},
-                {normed_bf_.data() + first * H, normed_bflo_.data() + first * H, lrows, H}, H, logits_.data(), V, 1,
-                0, stream_, detail::LogitsTileEpi{logits_.data(), V, row_sumsq(), first}, plan_bn(lrows));
+                {w_.embed_w16.data(), nullptr, V, H, w_.f16},
+                {normed_h_.data() + first * H, normed_hlo_.data() + first * H, lrows, H, w_.f16}, H, logits_.data(), V,
+                1, 0, stream_, detail::LogitsTileEpi{logits_.data(), V, row_sumsq(), first}, plan_bn(lrows));
         } else {
             for (int r0 = 0; r0 < lrows; r0 += 4) {
                 const int r = std::min(4, lrows - r0);
@@ -1191,6 +1190,7 @@ template <typename WT> class LlamaEngineT {
     TypedDeviceBuffer<float> hidden_, ss_, q_, part_, attn_po_, attn_pml_, logits_;
     // tensor parallelism (tp_world_ == 1: the whole model on this GPU)
     int tp_rank_ = 0, tp_world_ = 1, qh_l_ = 0, kvh_l_ = 0, inter_l_ = 0;
+    TpShard shard_;
     ncclComm_t tp_comm_ = nullptr;
     TypedDeviceBuffer<float> tp_y_, tp_recv_;
     TypedDeviceBuffer<int32_t> tp_cnt_; // arrival counters [2] | done counters [2]
@@ -1204,7 +1204,7 @@ template <typename WT> class LlamaEngineT {
         return ms > 0 ? static_cast<unsigned long long>(ms) * 1000000ull : detail::kTpPeerWaitNs;
     }();
     std::vector<void *> peer_maps_;
-    std::vector<TypedDeviceBuffer<__nv_bfloat16>> tp_qkv_;
+    std::vector<TypedDeviceBuffer<uint16_t>> tp_qkv_;
     std::vector<WView> qkv_v_, o_v_, gu_v_, down_v_;
     static constexpr int kGroupTiles = 64;
     TypedDeviceBuffer<float> groups_part_;
@@ -1217,7 +1217,8 @@ template <typename WT> class LlamaEngineT {
         const char *e = std::getenv("OPWORKS_SPLIT_GROUPS");
         return e ? std::atoi(e) : 1;
     }();
-    TypedDeviceBuffer<__nv_bfloat16> normed_bf_, attn_bf_, act_bf_, normed_bflo_, attn_bflo_, act_bflo_;
+    // fast path: two-term 16-bit operands (format w_.f16)
+    TypedDeviceBuffer<uint16_t> normed_h_, attn_h_, act_h_, normed_hlo_, attn_hlo_, act_hlo_;
     TypedDeviceBuffer<float> normed_f_, normed_lo_, attn_f_, attn_lo_, act_f_, act_lo_;
     TypedDeviceBuffer<int32_t> tokens_;
     detail::StepLayout layout_{}, dec_{}, pre_{};
@@ -1241,11 +1242,11 @@ template <typename WT> class LlamaEngineT {
     int multi_steps_ = 0, multi_eos_ = -1;
     bool multi_has_uni_ = false;
     bool marks_enabled_ = false;
-    // fast-path GEMMs with more token rows than this use single-term bf16
+    // fast-path GEMMs with more token rows than this use single-term 16-bit
     // activations (one MMA per K step). Off by default: on a 1024-token
-    // prompt single-term activations move the logits by 0.043 against the
-    // fp32 path, over the 2e-2 GEMM tolerance (two terms: 0.010); C4 prefill
-    // would gain 16%. OPWORKS_PREFILL_SINGLE_ROWS sets the threshold.
+    // prompt single-term bf16 activations moved the logits by 0.043 against
+    // the fp32 path, over the 2e-2 GEMM tolerance (two terms: 0.010); C4
+    // prefill would gain 16%. OPWORKS_PREFILL_SINGLE_ROWS sets the threshold.
     int prefill_single_rows_ = [] {
         const char *e = std::getenv("OPWORKS_PREFILL_SINGLE_ROWS");
         return e ? std::atoi(e) : (1 << 30);
@@ -1309,13 +1310,13 @@ template <typename WT> class LlamaModelT {
     };
 
     // sets: which weight precisions to keep on the device (0 = default: all
-    // for fp32 packs, bf16 for bf16 packs).
+    // for fp32 packs, the 16-bit set for bf16 packs).
     static LlamaModelT load(const std::string &pack_path, unsigned sets = 0, int max_positions = 8192) {
         PackReader pack(pack_path);
         LlamaModelT m;
         m.cfg_ = ModelConfig::from_manifest(pack.manifest());
         if (sets == 0)
-            sets = std::is_same_v<WT, float> ? (kWeightsBF16 | kWeightsF32 | kWeightsSplit) : kWeightsBF16;
+            sets = std::is_same_v<WT, float> ? (kWeights16 | kWeightsF32 | kWeightsSplit) : kWeights16;
         OPWORKS_CUDA_CHECK(cudaGetDevice(&m.device_));
         m.weights_ = std::make_unique<ModelWeights<WT>>(ModelWeights<WT>::load(pack, m.cfg_, sets, max_positions));
         m.default_precision_ = std::is_same_v<WT, float> ? Precision::kAccurate : Precision::kFast;

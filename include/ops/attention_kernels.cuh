@@ -25,42 +25,35 @@
 
 #include "../core/block_reduce.cuh"
 #include "../core/cuda_utils.cuh"
+#include "detail/operand16.cuh"
 #include "detail/sm100.cuh"
 
 namespace opworks::detail {
 
 constexpr int kAttnD = 64;      // head dim supported by these kernels
 
-// Attention output writers: out(t, head, d) = v for query token t.
+// Attention output writer into fp32 memory: out(t, head, d) = v for query
+// token t (the operator API's layouts).
 template <typename T> struct StridedOut {
+    static_assert(std::is_same_v<T, float>, "attention outputs of the operator API are fp32");
     T *p;
     int64_t tok, head; // element strides
-    __device__ __forceinline__ void put(int64_t t, int h, int d, float v) const {
-        if constexpr (std::is_same_v<T, float>)
-            p[t * tok + h * head + d] = v;
-        else
-            p[t * tok + h * head + d] = __float2bfloat16_rn(v);
-    }
+    __device__ __forceinline__ void put(int64_t t, int h, int d, float v) const { p[t * tok + h * head + d] = v; }
     __device__ __forceinline__ void put4(int64_t t, int h, int d0, float a, float b, float c, float e) const {
-        T *dst = p + t * tok + h * head + d0;
-        if constexpr (std::is_same_v<T, float>) {
-            *reinterpret_cast<float4 *>(dst) = make_float4(a, b, c, e);
-        } else {
-            __nv_bfloat162 *d2 = reinterpret_cast<__nv_bfloat162 *>(dst);
-            d2[0] = __floats2bfloat162_rn(a, b);
-            d2[1] = __floats2bfloat162_rn(c, e);
-        }
+        *reinterpret_cast<float4 *>(p + t * tok + h * head + d0) = make_float4(a, b, c, e);
     }
 };
 
-// Row-major activation [tokens][qh * 64] for the next GEMM: bf16 (optionally
-// with the bf16 remainder term), or fp32 (optionally split into tf32 hi/lo).
+// Row-major activation [tokens][cols] written as the next GEMM's operand:
+// 16-bit words (fp16 when f16, else bf16; with h16_lo also the remainder
+// term r(x - hi)), or fp32 (with lo: split into a tf32 hi part and x - hi).
 struct ActOut {
-    __nv_bfloat16 *bf16 = nullptr;    // hi part when bf16_lo != nullptr
-    __nv_bfloat16 *bf16_lo = nullptr; // bf16(x - hi)
-    float *f32 = nullptr;             // tf32 hi part when lo != nullptr
-    float *lo = nullptr;              // x - tf32(x)
-    int64_t ld = 0;                   // row stride (elements)
+    uint16_t *h16 = nullptr;    // hi term of a 16-bit operand
+    uint16_t *h16_lo = nullptr; // optional remainder term
+    bool f16 = false;           // format of the 16-bit terms
+    float *f32 = nullptr;       // tf32 hi part when lo != nullptr
+    float *lo = nullptr;        // x - tf32(x)
+    int64_t ld = 0;             // row stride (elements)
     __device__ __forceinline__ static float tf32_rn(float x) {
         uint32_t u = __float_as_uint(x);
         if ((u & 0x7f800000u) == 0x7f800000u)
@@ -70,11 +63,11 @@ struct ActOut {
     }
     __device__ __forceinline__ void put(int64_t row, int col, float v) const {
         const int64_t i = row * ld + col;
-        if (bf16) {
-            const __nv_bfloat16 h = __float2bfloat16_rn(v);
-            bf16[i] = h;
-            if (bf16_lo)
-                bf16_lo[i] = __float2bfloat16_rn(v - __bfloat162float(h));
+        if (h16) {
+            const uint16_t h = to16(v, f16);
+            h16[i] = h;
+            if (h16_lo)
+                h16_lo[i] = to16(v - from16(h, f16), f16);
         } else if (lo) {
             const float h = tf32_rn(v);
             f32[i] = h;
@@ -83,23 +76,31 @@ struct ActOut {
             f32[i] = v;
         }
     }
+    // two consecutive columns col, col + 1 (col and ld even)
+    __device__ __forceinline__ void put2c(int64_t row, int col, float a, float b) const {
+        const int64_t i = row * ld + col;
+        if (h16) {
+            const uint32_t h = pack16x2(a, b, f16);
+            *reinterpret_cast<uint32_t *>(h16 + i) = h;
+            if (h16_lo) {
+                const float2 f = unpack16x2(h, f16);
+                *reinterpret_cast<uint32_t *>(h16_lo + i) = pack16x2(a - f.x, b - f.y, f16);
+            }
+        } else {
+            put(row, col, a);
+            put(row, col + 1, b);
+        }
+    }
     // four consecutive columns col .. col + 3 (col and ld multiples of 4)
     __device__ __forceinline__ void put4c(int64_t row, int col, float4 v) const {
         const int64_t i = row * ld + col;
-        if (bf16) {
-            const __nv_bfloat162 h01 = __floats2bfloat162_rn(v.x, v.y), h23 = __floats2bfloat162_rn(v.z, v.w);
-            uint2 hv;
-            hv.x = *reinterpret_cast<const uint32_t *>(&h01);
-            hv.y = *reinterpret_cast<const uint32_t *>(&h23);
-            *reinterpret_cast<uint2 *>(bf16 + i) = hv;
-            if (bf16_lo) {
-                const float2 f01 = __bfloat1622float2(h01), f23 = __bfloat1622float2(h23);
-                const __nv_bfloat162 l01 = __floats2bfloat162_rn(v.x - f01.x, v.y - f01.y);
-                const __nv_bfloat162 l23 = __floats2bfloat162_rn(v.z - f23.x, v.w - f23.y);
-                uint2 lv;
-                lv.x = *reinterpret_cast<const uint32_t *>(&l01);
-                lv.y = *reinterpret_cast<const uint32_t *>(&l23);
-                *reinterpret_cast<uint2 *>(bf16_lo + i) = lv;
+        if (h16) {
+            const uint32_t h01 = pack16x2(v.x, v.y, f16), h23 = pack16x2(v.z, v.w, f16);
+            *reinterpret_cast<uint2 *>(h16 + i) = make_uint2(h01, h23);
+            if (h16_lo) {
+                const float2 f01 = unpack16x2(h01, f16), f23 = unpack16x2(h23, f16);
+                *reinterpret_cast<uint2 *>(h16_lo + i) =
+                    make_uint2(pack16x2(v.x - f01.x, v.y - f01.y, f16), pack16x2(v.z - f23.x, v.w - f23.y, f16));
             }
         } else {
             put(row, col, v.x);
@@ -108,28 +109,18 @@ struct ActOut {
             put(row, col + 3, v.w);
         }
     }
-    // two consecutive columns col, col + 1 (col and ld even)
-    __device__ __forceinline__ void put2c(int64_t row, int col, float a, float b) const {
-        const int64_t i = row * ld + col;
-        if (bf16) {
-            const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
-            *reinterpret_cast<__nv_bfloat162 *>(bf16 + i) = h;
-            if (bf16_lo) {
-                const float2 f = __bfloat1622float2(h);
-                *reinterpret_cast<__nv_bfloat162 *>(bf16_lo + i) = __floats2bfloat162_rn(a - f.x, b - f.y);
-            }
-        } else {
-            put(row, col, a);
-            put(row, col + 1, b);
-        }
-    }
     // attention-writer form (head-major columns)
     __device__ __forceinline__ void put(int64_t t, int h, int d, float v) const { put(t, h * 64 + d, v); }
     __device__ __forceinline__ void put4(int64_t t, int h, int d0, float a, float b, float c, float e) const {
-        put(t, h * 64 + d0, a);
-        put(t, h * 64 + d0 + 1, b);
-        put(t, h * 64 + d0 + 2, c);
-        put(t, h * 64 + d0 + 3, e);
+        const int col = h * 64 + d0;
+        if ((col & 3) == 0 && (ld & 3) == 0) {
+            put4c(t, col, make_float4(a, b, c, e));
+        } else {
+            put(t, col, a);
+            put(t, col + 1, b);
+            put(t, col + 2, c);
+            put(t, col + 3, e);
+        }
     }
 };
 constexpr int kKvChunk = 16;    // tokens per chunk / paged block
@@ -258,14 +249,15 @@ __device__ __forceinline__ void stage_kv_tile_offsets(const KV &kv, const int64_
     }
 }
 
-// q: [B][q_stride] with heads at h*64. grid = (splits, kvh, B). With one
+// q: [B][q_stride] with heads at h*64; sequence b holds lens[b] tokens (or
+// len_all when lens is null). grid = (splits, kvh, B). With one
 // split the normalised result goes straight to `out`; otherwise part_o
 // [B][qh][splits][64] and part_ml [B][qh][splits][2] (running max in log2 units, running
 // sum) hold the split partials for attn_decode_combine_kernel.
 template <class KV, int kRep, typename Out>
 __global__ void __launch_bounds__(kDecodeThreads, kDecodeCtasPerSm)
     attn_decode_partial_kernel(const float *__restrict__ q, int64_t q_stride, KV kv, const int *__restrict__ lens,
-                               int tokens_per_split, float scale, float *__restrict__ part_o,
+                               int len_all, int tokens_per_split, float scale, float *__restrict__ part_o,
                                float *__restrict__ part_ml, Out out, int *err) {
     using G = DecodeGeo<kRep>;
     constexpr int kChunks = kDecodeTile / kKvChunk;
@@ -286,7 +278,7 @@ __global__ void __launch_bounds__(kDecodeThreads, kDecodeCtasPerSm)
     // first kernel); q and the newest token's K/V come from the kernel
     // before this one, so only the producer's first tiles of OLDER tokens
     // may be fetched before the programmatic-launch wait
-    const int len = lens[b];
+    const int len = lens != nullptr ? lens[b] : len_all;
     const int t_begin = split * tokens_per_split;
     const int t_end = min(len, t_begin + tokens_per_split);
     const int n_tiles = t_end > t_begin ? (t_end - t_begin + kDecodeTile - 1) / kDecodeTile : 0;
@@ -787,11 +779,11 @@ inline int decode_tokens_per_split(int pairs, int max_len, int sm_count) {
 template <class KV, int kRep, typename Out>
 inline void attn_decode_launch(const float *q, int64_t q_stride, const KV &kv, const int *lens, int batch, int kvh,
                                int tokens_per_split, int splits, float scale, float *part_o, float *part_ml,
-                               const Out &out, cudaStream_t stream) {
+                               const Out &out, cudaStream_t stream, int len_all = 0) {
     prepare_decode_kernel<KV, kRep, Out>();
     const dim3 grid(splits, kvh, batch);
     launch_ex(attn_decode_partial_kernel<KV, kRep, Out>, grid, dim3(kDecodeThreads), DecodeGeo<kRep>::kBytes, stream, q,
-              q_stride, kv, lens, tokens_per_split, scale, part_o, part_ml, out, sm100::device_error_word());
+              q_stride, kv, lens, len_all, tokens_per_split, scale, part_o, part_ml, out, sm100::device_error_word());
     if (splits > 1)
         launch_ex(attn_decode_combine_kernel<Out>, dim3(kvh * kRep, batch), dim3(64), 0, stream,
                   static_cast<const float *>(part_o), static_cast<const float *>(part_ml), splits, out);

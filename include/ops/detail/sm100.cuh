@@ -213,12 +213,13 @@ __device__ __forceinline__ uint64_t sdesc_k128(uint32_t smem_addr) {
     return d;
 }
 
-// Instruction descriptor: D fp32, A/B format (1 = bf16, 2 = tf32), both
-// K-major, N >> 3 at [17,23), M >> 4 at [24,29).
+// Instruction descriptor: D fp32, A/B format (kind::f16: 0 = fp16, 1 = bf16;
+// kind::tf32: 2), both K-major, N >> 3 at [17,23), M >> 4 at [24,29).
 __host__ __device__ constexpr uint32_t idesc_make(uint32_t ab_format, int m, int n) {
     return (1u << 4) | (ab_format << 7) | (ab_format << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
            (static_cast<uint32_t>(m >> 4) << 24);
 }
+constexpr uint32_t kFmtF16 = 0;
 constexpr uint32_t kFmtBF16 = 1;
 constexpr uint32_t kFmtTF32 = 2;
 
@@ -239,9 +240,12 @@ inline PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 
 // 2D row-major tensor [rows][cols] with row stride `ld` elements, loaded as
 // boxes of box_cols x box_rows with 128B swizzle (box_cols * elem == 128).
-inline CUtensorMap make_tmap_2d(const void *base, bool bf16, uint64_t cols, uint64_t rows, uint64_t ld,
+// 2-D tiled map of 16-bit (word16) or 32-bit elements. Tiled copies move
+// bytes without conversion, so 16-bit words of either format (bf16 or fp16)
+// use the one 16-bit map type.
+inline CUtensorMap make_tmap_2d(const void *base, bool word16, uint64_t cols, uint64_t rows, uint64_t ld,
                                 uint32_t box_cols, uint32_t box_rows) {
-    const size_t elem = bf16 ? 2 : 4;
+    const size_t elem = word16 ? 2 : 4;
     detail::require(reinterpret_cast<uintptr_t>(base) % 16 == 0, "TMA base must be 16-byte aligned");
     detail::require((ld * elem) % 16 == 0, "TMA row stride must be a multiple of 16 bytes");
     detail::require(box_cols * elem == 128, "TMA box must be one 128-byte swizzle atom wide");
@@ -252,7 +256,7 @@ inline CUtensorMap make_tmap_2d(const void *base, bool bf16, uint64_t cols, uint
     const cuuint32_t box[2] = {box_cols, box_rows};
     const cuuint32_t estr[2] = {1, 1};
     const CUresult r = tensor_map_encoder()(
-        &tm, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void *>(base),
+        &tm, word16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void *>(base),
         dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     detail::require(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed");

@@ -20,10 +20,14 @@
 // epilogue.
 //
 // Precision kinds:
-//   kBF16   one kind::f16 MMA per 16-wide K step (bf16 x bf16 -> fp32)
-//   kBF16x2 bf16 weights times a two-term bf16 activation (x = hi + lo, lo =
-//           bf16(x - hi)): two kind::f16 MMAs per K step, so activations keep
-//           ~16 mantissa bits while the weight stream stays 2 bytes/element
+//   kBF16   one kind::f16 MMA per 16-wide K step (16-bit x 16-bit -> fp32)
+//   kBF16x2 16-bit weights times a two-term 16-bit activation (x = hi + lo,
+//           lo = r(x - hi)): two kind::f16 MMAs per K step, so activations
+//           keep about twice the format's mantissa bits while the weight
+//           stream stays 2 bytes/element
+//   The 16-bit format of both kinds is bf16 or fp16 (GemmOperand::f16, the
+//   instruction descriptor's A/B format at run time); the kind names keep
+//   the bf16 spelling of their first format.
 //   kTF32x3 split-precision fp32: operands pre-split into tf32 hi/lo parts,
 //           three kind::tf32 MMAs per K step (hi*hi + hi*lo + lo*hi) give
 //           ~fp32 accuracy on the tensor cores.
@@ -60,6 +64,8 @@ struct GemmParams {
     int cluster = 0;
     float *red_ws = nullptr;
     unsigned int *red_cnt = nullptr;
+    // A/B format of the 16-bit kinds (kFmtBF16 or kFmtF16; both operands share it)
+    uint32_t ab_fmt = kFmtBF16;
 };
 
 // Workspace of grouped split-K tile epilogues (GemmParams::red_ws / red_cnt).
@@ -267,8 +273,7 @@ __global__ void __launch_bounds__(192, GemmShape<kKind, BN>::kCtasPerSm)
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            constexpr uint32_t idesc = idesc_make(S::kSplit3 ? kFmtTF32 : kFmtBF16, kUmmaM, BN);
-            (void)idesc;
+            const uint32_t idesc = idesc_make(S::kSplit3 ? kFmtTF32 : p.ab_fmt, kUmmaM, BN);
             int it = 0;
             for (int kb = kb_begin; kb < kb_end; ++kb, ++it) {
                 const int s = it % kStages;
@@ -541,11 +546,18 @@ inline void gemm_launch(const CUtensorMap &a, const CUtensorMap &b, const CUtens
 
 // Operand description for the host launcher.
 struct GemmOperand {
-    const void *hi;     // bf16 or fp32 (tf32 hi part)
-    const void *lo;     // tf32 lo part (kTF32x3 only)
+    const void *hi;     // 16-bit words (bf16, or fp16 with f16) or fp32 (tf32 hi part)
+    const void *lo;     // tf32 lo part (kTF32x3), remainder term (token operand of kBF16x2)
     int rows;
     int64_t ld;         // row stride in elements; K extent is the GEMM's k
+    bool f16 = false;   // 16-bit words are fp16 (both operands of a GEMM agree)
 };
+
+// A/B format code of a 16-bit GEMM from its operands.
+inline uint32_t gemm_ab_format(const GemmOperand &A, const GemmOperand &B) {
+    detail::require(A.f16 == B.f16, "GEMM operands must share one 16-bit format");
+    return A.f16 ? kFmtF16 : kFmtBF16;
+}
 
 inline int gemm_pick_bn(GemmKind kind, int m_tok) {
     if (m_tok <= 32)
@@ -596,6 +608,8 @@ inline void gemm_tn(const GemmOperand &A, const GemmOperand &B, int k, float *ou
     p.num_kb = (k + kKElems - 1) / kKElems;
     p.splits = splits < 1 ? 1 : (splits > p.num_kb ? p.num_kb : splits);
     p.err = device_error_word();
+    if constexpr (kBf16)
+        p.ab_fmt = gemm_ab_format(A, B);
     detail::require(l2_prefetch_bytes == 0 || (reinterpret_cast<uintptr_t>(l2_prefetch) % 16 == 0),
                     "gemm_tn: L2 prefetch range must be 16-byte aligned");
     p.l2_prefetch = static_cast<const uint8_t *>(l2_prefetch);

@@ -191,7 +191,7 @@ __global__ void __launch_bounds__(192, 1)
         }
     } else if (warp == 1) {
         if (lane == 0 && leader) {
-            constexpr uint32_t idesc = idesc_make(kFmtBF16, 2 * kUmmaM, S::BN);
+            const uint32_t idesc = idesc_make(p.ab_fmt, 2 * kUmmaM, S::BN);
             for (int kb = 0; kb < p.num_kb; ++kb) {
                 const int s = kb % kStages;
                 const uint32_t ph = static_cast<uint32_t>(kb / kStages) & 1u;
@@ -292,6 +292,7 @@ inline void gemm_pair_bf16x2(const GemmOperand &W, const GemmOperand &X, int k, 
     p.num_kb = (k + 63) / 64;
     p.splits = 1;
     p.err = device_error_word();
+    p.ab_fmt = gemm_ab_format(W, X);
     const CUtensorMap ta = make_tmap_2d(W.hi, true, static_cast<uint64_t>(k), W.rows, W.ld, 64, kUmmaM);
     const CUtensorMap tb = make_tmap_2d(X.hi, true, static_cast<uint64_t>(k), X.rows, X.ld, 64, 128);
     const CUtensorMap tb_lo = make_tmap_2d(X.lo, true, static_cast<uint64_t>(k), X.rows, X.ld, 64, 128);

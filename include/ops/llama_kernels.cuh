@@ -10,9 +10,10 @@
 //   silu_mul        sum partials of the interleaved gate/up GEMM -> silu(g) * u
 //   sample          greedy argmax or exact top-p (float64) per sequence
 //
-// "normed"/"act" outputs go to an ActOut: bf16 (fast path, the GEMM operand
-// directly) or fp32, optionally with the tf32 hi/lo split of the accurate
-// (split-precision) GEMM path.
+// "normed"/"act" outputs go to an ActOut: two-term 16-bit words (fast path,
+// the GEMM operand directly; fp16 or bf16 by the model's format) or fp32,
+// optionally with the tf32 hi/lo split of the accurate (split-precision) GEMM
+// path.
 
 #include <cooperative_groups.h>
 #include <cuda_bf16.h>
@@ -205,7 +206,7 @@ static __global__ void silu_mul_kernel(const float *__restrict__ part, int split
 
 // hidden[tok][f] += value: the o and down projections' residual add. With
 // `gain` set it also writes the next projection's operand h * gain (two-term
-// bf16) and, per token, the tile's partial sum of squares of h (RowSumSq).
+// 16-bit) and, per token, the tile's partial sum of squares of h (RowSumSq).
 struct ResidualTileEpi {
     static constexpr bool kTile = true;
     // scratch: [4 warps][kPreTok] sums of squares | gain[128] | rows[kPreTok][128]
@@ -338,7 +339,7 @@ struct SiluMulTileEpi {
         // (g, u, g, u) of outputs 2l, 2l + 1 and writes them as one pair
         // four tokens per warp iteration (independent chains); SiLU by the
         // SFU exponential and a fast reciprocal (the fast path's outputs are
-        // bf16 pairs: their rounding dwarfs these few-ulp differences)
+        // 16-bit pairs: their rounding dwarfs these few-ulp differences)
         const float *inv = static_cast<const float *>(scratch);
         const int warp = tid >> 5, lane = tid & 31;
         const bool vec = 4 * lane + 3 < nfeat;
@@ -490,7 +491,7 @@ struct QkvTileEpi {
 
 // Tensor-parallel residual step: y is the projection's output summed over the
 // ranks (all-reduce). hidden[row] += y[row]; with `gain` set, normed[row] =
-// hidden[row] * gain (the next projection's two-term bf16 operand, deferred
+// hidden[row] * gain (the next projection's two-term 16-bit operand, deferred
 // norm) and rs.part[tile][row] = the tile's sum of squares of hidden, as the
 // fused residual epilogue writes them. One block of 128 threads per row: warp
 // w takes the 128-feature tiles w, w + 4, ...; lane l owns features 4l..4l+3.
@@ -706,16 +707,17 @@ static __global__ void rope_table_kernel(const float *__restrict__ inv_freq, int
     }
 }
 
-// fp32 weight -> bf16 copy with optional row interleave of two sources:
-// dst row 2j = a[j], 2j + 1 = b[j] (b == nullptr: plain copy of a).
-static __global__ void weights_to_bf16_kernel(const float *__restrict__ a, const float *__restrict__ b, int rows, int cols,
-                                       __nv_bfloat16 *__restrict__ dst) {
+// fp32 weight -> 16-bit operand copy (fp16 when f16, else bf16; nearest even)
+// with optional row interleave of two sources: dst row 2j = a[j], 2j + 1 =
+// b[j] (b == nullptr: plain copy of a).
+static __global__ void weights_to_16_kernel(const float *__restrict__ a, const float *__restrict__ b, int rows, int cols,
+                                            uint16_t *__restrict__ dst, bool f16) {
     const int64_t total = static_cast<int64_t>(b ? 2 * rows : rows) * cols;
     OPWORKS_GRID_LOOP(i, total) {
         const int64_t r = i / cols, c = i % cols;
         const float *src = b ? ((r & 1) ? b : a) : a;
         const int64_t sr = b ? (r >> 1) : r;
-        dst[i] = __float2bfloat16_rn(src[sr * cols + c]);
+        dst[i] = to16(src[sr * cols + c], f16);
     }
 }
 
@@ -744,9 +746,9 @@ static __global__ void weights_interleave_kernel(const float *__restrict__ a, co
     }
 }
 
-// bf16 weight rows interleave (bf16 packs): dst 2j = a[j], 2j+1 = b[j].
-static __global__ void bf16_interleave_kernel(const __nv_bfloat16 *__restrict__ a, const __nv_bfloat16 *__restrict__ b,
-                                       int rows, int cols, __nv_bfloat16 *__restrict__ dst) {
+// 16-bit weight rows interleave (bf16 packs): dst 2j = a[j], 2j+1 = b[j].
+static __global__ void interleave16_kernel(const uint16_t *__restrict__ a, const uint16_t *__restrict__ b, int rows,
+                                           int cols, uint16_t *__restrict__ dst) {
     const int64_t total = static_cast<int64_t>(2 * rows) * cols;
     OPWORKS_GRID_LOOP(i, total) {
         const int64_t r = i / cols, c = i % cols;

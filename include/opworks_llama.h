@@ -55,8 +55,10 @@ OPW_API const char *opw_llama_last_error(void);
 
 /* Select the CUDA device used by subsequent loads on this thread. */
 OPW_API int opw_llama_set_device(int device);
-/* Load keeping only some weight precisions: bit 1 = bf16 (fast path),
- * 2 = fp32 (accurate GEMV), 4 = tf32 hi/lo (accurate GEMM); 0 = default.
+/* Load keeping only some weight precisions: bit 1 = 16-bit (fast path: fp16
+ * words for float32 packs, or bf16 with OPWORKS_FAST_WEIGHTS=bf16; the pack's
+ * bf16 words for bfloat16 packs), 2 = fp32 (accurate GEMV), 4 = tf32 hi/lo
+ * (accurate GEMM); 0 = default.
  * max_positions sizes the RoPE table (>= the longest session). */
 OPW_API void *opw_llama_load_ex(const char *pack_path, unsigned weight_sets, int max_positions, char *err, int err_len);
 /* Model hyper-parameters: out[0..7] = layers, hidden, intermediate, q heads,
@@ -65,7 +67,8 @@ OPW_API int opw_llama_model_info(void *model, int32_t *out8, char *err, int err_
 
 /* Batched engine: max_batch sequences (slots) of up to max_seq_len tokens
  * each over one paged KV cache. precision: 0 = accurate (fp32), 1 = fast
- * (bf16 weights and GEMM operands, fp32 residual / KV / softmax).
+ * (16-bit weights and two-term 16-bit GEMM activations, fp32 residual / KV /
+ * softmax).
  * prefill_rows: prefill chunk size (0 = max_seq_len). */
 OPW_API void *opw_llama_create_batch(void *model, int max_batch, int max_seq_len, int precision, int prefill_rows, char *err,
                              int err_len);
@@ -93,6 +96,13 @@ OPW_API void *opw_llama_create_batch_tp(void *model, int max_batch, int max_seq_
  * an NCCL all-reduce (environment OPWORKS_TP_P2P=0 keeps NCCL). */
 OPW_API int opw_llama_batch_tp_ipc_handle(void *batch, char *out128, char *err, int err_len);
 OPW_API int opw_llama_batch_tp_open_peers(void *batch, const char *handles, char *err, int err_len);
+/* The shard plan of tensor-parallel rank `rank` of `world` (pure host
+ * arithmetic; include/models/tp_plan.cuh): cfg5 = hidden, intermediate, q
+ * heads, kv heads, head dim; out12 = this rank's q heads, kv heads, MLP
+ * columns, first QKV rows of its q / k / v heads, q rows, kv rows, first O
+ * input column, first interleaved gate/up row, gate/up rows, first down input
+ * column. Returns 0, or -1 when the model does not shard `world` ways. */
+OPW_API int opw_llama_tp_shard(const int32_t *cfg5, int rank, int world, int64_t *out12, char *err, int err_len);
 /* Frees the slot's KV blocks; the slot starts empty. */
 OPW_API int opw_llama_batch_reset(void *batch, int slot, char *err, int err_len);
 /* Current token count of a slot, or -1. */

@@ -10,13 +10,18 @@
 //   gu   = interleaved gate/up rows  [2 I, H]   (row 2j = gate_j, 2j+1 = up_j)
 //   o    = [H, qh * D], down = [H, I]
 // in up to three precisions:
-//   bf16  (fast path: tcgen05 kind::f16 GEMM / bf16 GEMV)
-//   f32   (accurate path, few rows: shared-weight GEMV)
-//   hi/lo (accurate path, many rows: split-precision tf32 GEMM)
-// bf16 packs load the bf16 set only.
+//   16-bit (fast path: tcgen05 kind::f16 GEMMs) — fp16 for float32 packs
+//          (11 significant bits at 2 bytes per weight), the pack's own bf16
+//          values for bfloat16 packs; OPWORKS_FAST_WEIGHTS=bf16 makes
+//          float32 packs round to bf16 instead
+//   f32    (accurate path, few rows: shared-weight GEMV)
+//   hi/lo  (accurate path, many rows: split-precision tf32 GEMM)
+// bf16 packs load the 16-bit set only.
 
 #include <cuda_bf16.h>
 
+#include <cstdlib>
+#include <cstring>
 #include <memory>
 #include <stdexcept>
 #include <string>
@@ -29,12 +34,12 @@
 
 namespace opworks {
 
-enum WeightSets : unsigned { kWeightsBF16 = 1u, kWeightsF32 = 2u, kWeightsSplit = 4u };
+enum WeightSets : unsigned { kWeights16 = 1u, kWeightsF32 = 2u, kWeightsSplit = 4u };
 
 // One fused projection in every precision that was loaded.
 struct Projection {
     int out = 0, in = 0;
-    TypedDeviceBuffer<__nv_bfloat16> bf16;
+    TypedDeviceBuffer<uint16_t> w16; // format: ModelWeights::f16
     TypedDeviceBuffer<float> f32, hi, lo;
 };
 
@@ -46,13 +51,14 @@ template <typename WT> struct LayerWeights {
 
 template <typename WT> struct ModelWeights {
     TypedDeviceBuffer<float> embed_f32;           // [V, H] fp32 packs
-    TypedDeviceBuffer<__nv_bfloat16> embed_bf16;  // [V, H] (tied LM head, fast path)
+    TypedDeviceBuffer<uint16_t> embed_w16;        // [V, H] (tied LM head, fast path)
     TypedDeviceBuffer<float> final_norm;          // [H]
     std::vector<LayerWeights<WT>> layers;
     TypedDeviceBuffer<float> rope_inv_freq;       // [D / 2]
     TypedDeviceBuffer<float> rope_table;          // [max_pos][D / 2][2] (cos, sin)
     int rope_max_pos = 0;
     unsigned sets = 0;
+    bool f16 = false; // the 16-bit set holds fp16 words (else bf16)
 
     static ModelWeights load(const PackReader &pack, const ModelConfig &cfg, unsigned sets,
                              int rope_max_pos = 8192, cudaStream_t stream = nullptr) {
@@ -63,12 +69,14 @@ template <typename WT> struct ModelWeights {
         } else {
             if (f32_pack)
                 throw std::runtime_error("bf16 model requires a bfloat16 pack");
-            sets = kWeightsBF16;
+            sets = kWeights16;
         }
         if (sets == 0)
-            sets = kWeightsBF16;
+            sets = kWeights16;
         ModelWeights w;
         w.sets = sets;
+        const char *fmt = std::getenv("OPWORKS_FAST_WEIGHTS");
+        w.f16 = f32_pack && !(fmt && std::strcmp(fmt, "bf16") == 0);
         const int64_t H = cfg.hidden_size, I = cfg.intermediate_size;
         const int64_t qw = cfg.q_width(), kw = cfg.kv_width();
         const int64_t V = cfg.vocab_size;
@@ -100,26 +108,26 @@ template <typename WT> struct ModelWeights {
         if (f32_pack) {
             w.embed_f32 = TypedDeviceBuffer<float>(V * H);
             upload("model.embed_tokens.weight", w.embed_f32.data(), V * H);
-            if (sets & kWeightsBF16) {
-                w.embed_bf16 = TypedDeviceBuffer<__nv_bfloat16>(V * H);
-                detail::weights_to_bf16_kernel<<<grid, 256, 0, stream>>>(w.embed_f32.data(), nullptr,
-                                                                         static_cast<int>(V), static_cast<int>(H),
-                                                                         w.embed_bf16.data());
+            if (sets & kWeights16) {
+                w.embed_w16 = TypedDeviceBuffer<uint16_t>(V * H);
+                detail::weights_to_16_kernel<<<grid, 256, 0, stream>>>(w.embed_f32.data(), nullptr,
+                                                                       static_cast<int>(V), static_cast<int>(H),
+                                                                       w.embed_w16.data(), w.f16);
                 OPWORKS_CUDA_CHECK(cudaGetLastError());
             }
         } else {
-            w.embed_bf16 = TypedDeviceBuffer<__nv_bfloat16>(V * H);
-            upload("model.embed_tokens.weight", w.embed_bf16.data(), V * H);
+            w.embed_w16 = TypedDeviceBuffer<uint16_t>(V * H);
+            upload("model.embed_tokens.weight", w.embed_w16.data(), V * H);
         }
         w.final_norm = norm("model.norm.weight");
 
         // fp32 source matrix (already on the device) -> the loaded precisions
         auto finish_f32 = [&](Projection &p, float *src_f32, const float *interleave_b) {
             const int rows = interleave_b ? p.out / 2 : p.out;
-            if (sets & kWeightsBF16) {
-                p.bf16 = TypedDeviceBuffer<__nv_bfloat16>(static_cast<int64_t>(p.out) * p.in);
-                detail::weights_to_bf16_kernel<<<grid, 256, 0, stream>>>(src_f32, interleave_b, rows, p.in,
-                                                                         p.bf16.data());
+            if (sets & kWeights16) {
+                p.w16 = TypedDeviceBuffer<uint16_t>(static_cast<int64_t>(p.out) * p.in);
+                detail::weights_to_16_kernel<<<grid, 256, 0, stream>>>(src_f32, interleave_b, rows, p.in,
+                                                                       p.w16.data(), w.f16);
                 OPWORKS_CUDA_CHECK(cudaGetLastError());
             }
             if (sets & kWeightsSplit) {
@@ -181,25 +189,25 @@ template <typename WT> struct ModelWeights {
                 // using them first
                 OPWORKS_CUDA_CHECK(cudaStreamSynchronize(stream));
             } else {
-                auto bf = [&](Projection &p) {
-                    p.bf16 = TypedDeviceBuffer<__nv_bfloat16>(static_cast<int64_t>(p.out) * p.in);
+                auto alloc16 = [&](Projection &p) {
+                    p.w16 = TypedDeviceBuffer<uint16_t>(static_cast<int64_t>(p.out) * p.in);
                 };
-                bf(lw.qkv);
-                upload(pre + "self_attn.q_proj.weight", lw.qkv.bf16.data(), qw * H);
-                upload(pre + "self_attn.k_proj.weight", lw.qkv.bf16.data() + qw * H, kw * H);
-                upload(pre + "self_attn.v_proj.weight", lw.qkv.bf16.data() + (qw + kw) * H, kw * H);
-                bf(lw.o);
-                upload(pre + "self_attn.o_proj.weight", lw.o.bf16.data(), H * qw);
-                bf(lw.gu);
-                __nv_bfloat16 *gate = reinterpret_cast<__nv_bfloat16 *>(stage.data());
-                __nv_bfloat16 *up = reinterpret_cast<__nv_bfloat16 *>(stage2.data());
+                alloc16(lw.qkv);
+                upload(pre + "self_attn.q_proj.weight", lw.qkv.w16.data(), qw * H);
+                upload(pre + "self_attn.k_proj.weight", lw.qkv.w16.data() + qw * H, kw * H);
+                upload(pre + "self_attn.v_proj.weight", lw.qkv.w16.data() + (qw + kw) * H, kw * H);
+                alloc16(lw.o);
+                upload(pre + "self_attn.o_proj.weight", lw.o.w16.data(), H * qw);
+                alloc16(lw.gu);
+                uint16_t *gate = reinterpret_cast<uint16_t *>(stage.data());
+                uint16_t *up = reinterpret_cast<uint16_t *>(stage2.data());
                 upload(pre + "mlp.gate_proj.weight", gate, I * H);
                 upload(pre + "mlp.up_proj.weight", up, I * H);
-                detail::bf16_interleave_kernel<<<grid, 256, 0, stream>>>(gate, up, static_cast<int>(I),
-                                                                         static_cast<int>(H), lw.gu.bf16.data());
+                detail::interleave16_kernel<<<grid, 256, 0, stream>>>(gate, up, static_cast<int>(I),
+                                                                      static_cast<int>(H), lw.gu.w16.data());
                 OPWORKS_CUDA_CHECK(cudaGetLastError());
-                bf(lw.down);
-                upload(pre + "mlp.down_proj.weight", lw.down.bf16.data(), H * I);
+                alloc16(lw.down);
+                upload(pre + "mlp.down_proj.weight", lw.down.w16.data(), H * I);
                 OPWORKS_CUDA_CHECK(cudaStreamSynchronize(stream));
             }
         }

@@ -412,6 +412,27 @@ int opw_llama_batch_logits(void *batch, int row, float *out, int n, char *err, i
     });
 }
 
+int opw_llama_tp_shard(const int32_t *cfg5, int rank, int world, int64_t *out12, char *err, int err_len) {
+    return shielded(-1, err, err_len, [&] {
+        if (!cfg5 || !out12)
+            throw std::invalid_argument("null argument");
+        opworks::ModelConfig c;
+        c.hidden_size = cfg5[0];
+        c.intermediate_size = cfg5[1];
+        c.num_q_heads = cfg5[2];
+        c.num_kv_heads = cfg5[3];
+        c.head_dim = cfg5[4];
+        if (c.hidden_size <= 0 || c.intermediate_size <= 0 || c.num_q_heads <= 0 || c.num_kv_heads <= 0 ||
+            c.head_dim <= 0)
+            throw std::invalid_argument("model dimensions must be positive");
+        const opworks::TpShard sh = opworks::tp_shard(c, rank, world);
+        const int64_t v[12] = {sh.q_heads, sh.kv_heads, sh.inter,  sh.q_row0, sh.k_row0,  sh.v_row0,
+                               sh.q_rows,  sh.kv_rows,  sh.o_col0, sh.gu_row0, sh.gu_rows, sh.down_col0};
+        std::copy(v, v + 12, out12);
+        return 0;
+    });
+}
+
 int opw_llama_batch_kv_blocks(void *batch, int slot, int32_t *out, int cap, char *err, int err_len) {
     return shielded(-1, err, err_len, [&] {
         auto &b = deref<BatchHandle>(batch, "batch");

@@ -363,35 +363,59 @@ int opw_paged_attention_prefill(const float *q, const float *kpool, const float 
     });
 }
 
-int opw_gemm_bf16x2(const uint16_t *W, const uint16_t *x_hi, const uint16_t *x_lo, float *out, int N, int K, int M,
-                    int splits, void *stream) {
+namespace {
+// Two-term 16-bit GEMM out[M][N] = W[N][K] . (x_hi + x_lo)[M][K]^T with the
+// 16-bit words read as fp16 (f16) or bf16.
+int gemm_16x2(const uint16_t *W, const uint16_t *x_hi, const uint16_t *x_lo, float *out, int N, int K, int M,
+              int splits, bool f16, void *stream) {
     int used = -1;
     const int rc = guarded([&] {
         using namespace opworks;
-        detail::require(W && x_hi && x_lo && out && N > 0 && K > 0 && M > 0, "gemm_bf16x2: bad arguments");
+        detail::require(W && x_hi && x_lo && out && N > 0 && K > 0 && M > 0, "gemm_16x2: bad arguments");
         const int bn = sm100::gemm_pick_bn(sm100::GemmKind::kBF16x2, M);
         if (splits <= 0) {
             const int tiles = ((N + kUmmaM - 1) / kUmmaM) * ((M + bn - 1) / bn);
             splits = sm100::gemm_pick_splits(tiles, (K + 63) / 64,
                                              detail::device_facts().sm_count * sm100::gemm_ctas_per_sm(bn));
         }
-        sm100::gemm_tn<sm100::GemmKind::kBF16x2>({as_bf16(W), nullptr, N, K}, {as_bf16(x_hi), as_bf16(x_lo), M, K},
-                                                 K, out, N, splits, static_cast<int64_t>(M) * N, as_stream(stream),
-                                                 sm100::Identity{}, bn);
+        sm100::gemm_tn<sm100::GemmKind::kBF16x2>({W, nullptr, N, K, f16}, {x_hi, x_lo, M, K, f16}, K, out, N, splits,
+                                                 static_cast<int64_t>(M) * N, as_stream(stream), sm100::Identity{},
+                                                 bn);
         used = splits;
     });
     return rc == 0 ? used : -1;
 }
 
-int opw_gemm_bf16x2_pair(const uint16_t *W, const uint16_t *x_hi, const uint16_t *x_lo, float *out, int N, int K,
-                         int M, void *stream) {
+int gemm_16x2_pair(const uint16_t *W, const uint16_t *x_hi, const uint16_t *x_lo, float *out, int N, int K, int M,
+                   bool f16, void *stream) {
     return guarded([&] {
         using namespace opworks;
-        detail::require(W && x_hi && x_lo && out && N > 0 && K > 0 && M > 0, "gemm_bf16x2_pair: bad arguments");
-        detail::require(K % 8 == 0, "gemm_bf16x2_pair: K must be a multiple of 8 (16-byte rows)");
-        sm100::gemm_pair_bf16x2({as_bf16(W), nullptr, N, K}, {as_bf16(x_hi), as_bf16(x_lo), M, K}, K,
-                                as_stream(stream), sm100::StoreTileEpi<sm100::Identity>{out, N, {}});
+        detail::require(W && x_hi && x_lo && out && N > 0 && K > 0 && M > 0, "gemm_16x2_pair: bad arguments");
+        detail::require(K % 8 == 0, "gemm_16x2_pair: K must be a multiple of 8 (16-byte rows)");
+        sm100::gemm_pair_bf16x2({W, nullptr, N, K, f16}, {x_hi, x_lo, M, K, f16}, K, as_stream(stream),
+                                sm100::StoreTileEpi<sm100::Identity>{out, N, {}});
     });
+}
+} // namespace
+
+int opw_gemm_bf16x2(const uint16_t *W, const uint16_t *x_hi, const uint16_t *x_lo, float *out, int N, int K, int M,
+                    int splits, void *stream) {
+    return gemm_16x2(W, x_hi, x_lo, out, N, K, M, splits, false, stream);
+}
+
+int opw_gemm_f16x2(const uint16_t *W, const uint16_t *x_hi, const uint16_t *x_lo, float *out, int N, int K, int M,
+                   int splits, void *stream) {
+    return gemm_16x2(W, x_hi, x_lo, out, N, K, M, splits, true, stream);
+}
+
+int opw_gemm_bf16x2_pair(const uint16_t *W, const uint16_t *x_hi, const uint16_t *x_lo, float *out, int N, int K,
+                         int M, void *stream) {
+    return gemm_16x2_pair(W, x_hi, x_lo, out, N, K, M, false, stream);
+}
+
+int opw_gemm_f16x2_pair(const uint16_t *W, const uint16_t *x_hi, const uint16_t *x_lo, float *out, int N, int K, int M,
+                        void *stream) {
+    return gemm_16x2_pair(W, x_hi, x_lo, out, N, K, M, true, stream);
 }
 
 int opw_sample(const float *logits, int rows, int vocab, const float *temperature, const float *top_p,

@@ -47,6 +47,8 @@ SIGNATURES = {
     "opw_paged_attention_decode": [P, P, P, P, I, P, I, I, I, I, P, P],
     "opw_gemm_bf16x2": [P, P, P, P, I, I, I, I, P],
     "opw_gemm_bf16x2_pair": [P, P, P, P, I, I, I, P],
+    "opw_gemm_f16x2": [P, P, P, P, I, I, I, I, P],
+    "opw_gemm_f16x2_pair": [P, P, P, P, I, I, I, P],
     "opw_paged_attention_prefill": [P, P, P, P, I, I, I, I, I, I, I, P, I, P],
 }
 

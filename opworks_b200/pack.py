@@ -166,10 +166,11 @@ def default_pack_dir():
     return os.environ.get("OPWORKS_PACK_DIR", "/tmp/opworks_packs")
 
 
-def ensure_random_llama_pack(cfg=None, seed=1234, name=None, bf16_grid=True):
-    """Path of a cached random-init pack, generating it on first use. With
-    bf16_grid=False the weights keep all fp32 bits (BASELINE's plain
-    N(0, 0.02) draw), so the fast path's bf16 weight copy is a rounding."""
+def ensure_random_llama_pack(cfg=None, seed=1234, name=None, bf16_grid=False):
+    """Path of a cached random-init pack, generating it on first use. By
+    default the weights keep every fp32 bit of the N(0, 0.02) draw (the fast
+    path's 16-bit copy is then a rounding of them); bf16_grid=True rounds them
+    to the bf16 grid first."""
     cfg = cfg or LLAMA_3_2_1B
     d = default_pack_dir()
     os.makedirs(d, exist_ok=True)

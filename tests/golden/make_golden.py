@@ -12,7 +12,8 @@ afterwards):
                      (examples/llama/generate.py:83-109) with a seeded
                      numpy Generator, logits served by a stand-in for the C ABI
 
-Usage: python tests/golden/make_golden.py [/root/reference]
+Usage: python tests/golden/make_golden.py [<reference root>]
+(default: OPWORKS_REFERENCE, else a `reference` directory beside the repository)
 """
 
 from __future__ import annotations
@@ -128,7 +129,12 @@ def sampler_golden(ref):
 
 
 if __name__ == "__main__":
-    ref = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    sys.path.insert(0, os.path.join(HERE, "..", "..", "oracle"))
+    import build_ref  # noqa: E402
+
+    ref = build_ref.reference_root(sys.argv[1] if len(sys.argv) > 1 else None)
+    if ref is None:
+        sys.exit("reference tree not found: pass its path or set OPWORKS_REFERENCE")
     ops_golden(ref)
     tiny_llama_golden()
     sampler_golden(ref)

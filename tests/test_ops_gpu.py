@@ -152,6 +152,35 @@ def test_gemm_bf16x2_pair_vs_fp64(ops, M, N, K):
     close(host(out), e, 2e-5)
 
 
+# the fp16 operand format of both GEMM kernels (the fast path of float32
+# packs): the instruction descriptor's A/B format switches at run time, so a
+# wrong format would read every word with the other layout and miss by O(1)
+@pytest.mark.parametrize("kernel,M,N,K", [("gemm_f16x2", 32, 2048, 2048), ("gemm_f16x2", 7, 384, 200),
+                                          ("gemm_f16x2", 200, 256, 1024), ("gemm_f16x2_pair", 512, 512, 1024),
+                                          ("gemm_f16x2_pair", 300, 384, 200)])
+def test_gemm_f16x2_vs_fp64(ops, kernel, M, N, K):
+    rng = np.random.default_rng(M + 5 * N + 11 * K)
+    w = (rng.standard_normal((N, K)) / math.sqrt(K)).astype(np.float32)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    wh = torch.from_numpy(w).to(torch.float16)
+    xh = torch.from_numpy(x).to(torch.float16)
+    xl = (torch.from_numpy(x) - xh.float()).to(torch.float16)
+    dw, dh, dl = (t.cuda().view(torch.int16) for t in (wh, xh, xl))  # alive until the sync
+    if kernel == "gemm_f16x2":
+        part = torch.full((64, M, N), float("nan"), device="cuda")
+        splits = ops.raw(kernel)(dw, dh, dl, part, N, K, M, 0, 0)
+        assert splits >= 1
+        sync(ops)
+        got = host(part[:splits]).sum(axis=0)
+    else:
+        out = torch.full((M, N), float("nan"), device="cuda")
+        assert ops.raw(kernel)(dw, dh, dl, out, N, K, M, 0) == 0
+        sync(ops)
+        got = host(out)
+    e = (xh.double() + xl.double()).numpy() @ wh.double().numpy().T
+    close(got, e, 2e-5)
+
+
 @pytest.mark.parametrize("rows", [2, 3, 16, 32, 33, 64, 100, 128, 256, 300])
 def test_linear_bf16_tensor_cores(ops, rows):
     rng = np.random.default_rng(rows)
@@ -462,6 +491,30 @@ def test_graph_capture_replay(ops):
     assert host(out)[0] == 8198
     g.replay()
     assert host(out)[0] == 16396
+
+
+def test_attention_decode_is_async_and_capturable(ops):
+    """ops::attention_decode allocates nothing, copies nothing from the host
+    and never synchronises (the reference op's contract,
+    include/ops/attention_decode.cuh:99-109), so it records into a CUDA graph;
+    the replay reads the caches' current contents."""
+    rng = np.random.default_rng(5)
+    QH, rep, L, cap = 32, 4, 3000, 3001
+    k = rng.uniform(-1, 1, (QH // rep, cap, 64)).astype(np.float32)
+    v = rng.uniform(-1, 1, (QH // rep, cap, 64)).astype(np.float32)
+    q = rng.uniform(-1, 1, (QH, 64)).astype(np.float32)
+    dq, dk, dv = dev(q), dev(k), dev(v)
+    out = torch.empty(QH, 64, device="cuda")
+    ops.attention_decode(dq, dk, dv, out, QH, rep, 64, L, cap, 0)  # module load outside capture
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        ops.attention_decode(dq, dk, dv, out, QH, rep, 64, L, cap, torch.cuda.current_stream().cuda_stream)
+    dv.mul_(2.0)
+    out.zero_()
+    g.replay()
+    want = oracle.attention(q[None], k[:, :L].transpose(1, 0, 2), 2 * v[:, :L].transpose(1, 0, 2))[0]
+    model_close(host(out), want)
 
 
 # ------------------------------------------------- vs the reference kernels
