@@ -27,6 +27,8 @@ Reported (one JSON line from rank 0):
   prefill    C3 prefill (32 x 2048 tokens) and C4 (one 8192-token prompt)
   c5         BASELINE C5 serving at this N: 256 requests partitioned over the
              ranks (strong scaling: total generated tok/s, per-rank busy time)
+  c2_session C2 through the 11-symbol session ABI (our library and the
+             reference's, float32 and bfloat16 packs)
 `--impl reference` times the reference algorithm's CPU restatement (the
 OpWorks reference has no CPU path of its own) on the same workload.
 """
@@ -421,13 +423,17 @@ def run_ours(args):
 
     cpu = None
     ref_cuda = None
+    c2_session = None
     if rank == 0 and world == 1:
         eng.close()
         model.close()
         if not args.no_extras:
             ref_cuda = reference_cuda_path(pack_path)
+            c2_session = session_c2_block(pack_path)
         if not args.no_cpu_baseline:
-            cpu = cpu_baseline(pack_path, steps=2)
+            cpu = cpu_baseline(pack_path)
+            if not args.no_extras:
+                cpu["other_configs"] = cpu_extras(pack_path)
 
     if rank == 0:
         line = {
@@ -471,6 +477,8 @@ def run_ours(args):
             line["multi_step_decode"] = multi
         if ref_cuda is not None:
             line["reference_cuda"] = ref_cuda
+        if c2_session is not None:
+            line["c2_session"] = c2_session
         print(json.dumps(line), flush=True)
     try:
         eng.close()
@@ -484,6 +492,73 @@ def run_ours(args):
 # ------------------------------------- the reference's own CUDA path (same GPU)
 
 REF_LLAMA = os.path.join(ROOT, "oracle", "_ref", "libopworks_llama_ref.so")
+
+
+def session_c2(lib, pack_path, steps=64, reps=3):
+    """C2 through the reference's 11-symbol session ABI, timed the way the
+    reference's scripts/llama/benchmark.py:53-68 times it: reset, prefill of
+    a 128-token prompt (TTFT, host wall clock), then `steps` blocking
+    decode_step calls (tokens/s); the median of `reps` repetitions. `lib` is
+    a ctypes library with the ABI (ours or the reference's)."""
+    import ctypes
+    import statistics
+
+    P, I, S = ctypes.c_void_p, ctypes.c_int, ctypes.c_char_p
+    for name, res, args in (("opw_llama_load", P, [S, S, I]), ("opw_llama_create_session", P, [P, I, S, I]),
+                            ("opw_llama_reset_session", I, [P, S, I]),
+                            ("opw_llama_prefill", ctypes.c_int32, [P, ctypes.POINTER(ctypes.c_int32), I, S, I]),
+                            ("opw_llama_decode_step", ctypes.c_int32, [P, ctypes.c_int32, S, I]),
+                            ("opw_llama_destroy_session", None, [P]), ("opw_llama_free", None, [P])):
+        fn = getattr(lib, name)
+        fn.restype, fn.argtypes = res, args
+    err = ctypes.create_string_buffer(512)
+    t = time.perf_counter()
+    m = lib.opw_llama_load(pack_path.encode(), err, 512)
+    load_s = time.perf_counter() - t
+    if not m:
+        return {"unavailable": err.value.decode(errors="replace")}
+    prompt = np.random.default_rng(5).integers(0, 128256, 128).astype(np.int32)
+    arr = (ctypes.c_int32 * 128)(*prompt.tolist())
+    s = lib.opw_llama_create_session(m, 128 + steps + 8, err, 512)
+    ttfts, rates = [], []
+    try:
+        for _ in range(reps + 1):  # the first repetition warms up
+            lib.opw_llama_reset_session(s, err, 512)
+            t0 = time.perf_counter()
+            tok = lib.opw_llama_prefill(s, arr, 128, err, 512)
+            t1 = time.perf_counter()
+            for _ in range(steps):
+                tok = lib.opw_llama_decode_step(s, tok, err, 512)
+            t2 = time.perf_counter()
+            if tok < 0:
+                return {"unavailable": err.value.decode(errors="replace")}
+            ttfts.append(t1 - t0)
+            rates.append(steps / (t2 - t1))
+    finally:
+        lib.opw_llama_destroy_session(s)
+        lib.opw_llama_free(m)
+    return {"ttft_ms": round(statistics.median(ttfts[1:]) * 1e3, 2),
+            "decode_tok_s": round(statistics.median(rates[1:]), 1), "load_s": round(load_s, 2),
+            "prompt": 128, "decode_steps": steps, "reps": reps}
+
+
+def session_c2_block(fp32_pack):
+    """C2 via the session ABI: our library and the reference's, on the float32
+    pack (our session default: the accurate fp32 path) and on a bfloat16 pack
+    of the same draw (LlamaModelBF16: our fast path)."""
+    import ctypes
+
+    from opworks_b200 import llama, pack
+
+    bf16_pack = pack.ensure_random_llama_pack(dtype="bfloat16")
+    out = {"method": "reference scripts/llama/benchmark.py:53-68 (host wall clock, blocking calls), median of 3",
+           "ours_fp32_pack": session_c2(llama.lib(), fp32_pack),
+           "ours_bf16_pack": session_c2(llama.lib(), bf16_pack)}
+    if os.path.exists(REF_LLAMA):
+        ref = ctypes.CDLL(REF_LLAMA)
+        out["reference_fp32_pack"] = session_c2(ref, fp32_pack)
+        out["reference_bf16_pack"] = session_c2(ref, bf16_pack)
+    return out
 
 
 def reference_cuda_path(pack_path, c3_sessions=2, c3_steps=8, c2_steps=64):
@@ -598,11 +673,90 @@ def cpu_decode_steps(pack_path, batch, steps, warmup, ctx=CTX):
     return float(np.mean(times)), oracle.lib().orc_num_threads()
 
 
-def cpu_baseline(pack_path, steps=2):
-    sec, threads = cpu_decode_steps(pack_path, BATCH, steps, warmup=1)
-    return {"value": round(BATCH / sec, 3), "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": f"{steps} batched decode steps (32 sequences, context {CTX}, random KV) of the C++/OpenMP "
-                      f"restatement, {sec:.2f} s per step"}
+CPU_STEP_BUDGET_S = 1.5  # one CPU sample step: a batched decode step of at most this long
+
+
+def cpu_sample_batch(pack_path):
+    """Sequences per CPU sample step: all 32 of C3 unless one 32-sequence step
+    (probed once) takes longer than CPU_STEP_BUDGET_S, then proportionally
+    fewer. Returns (batch, probe seconds of the full step)."""
+    probe, _ = cpu_decode_steps(pack_path, BATCH, 1, warmup=0)
+    batch = BATCH if probe <= CPU_STEP_BUDGET_S else max(1, int(BATCH * CPU_STEP_BUDGET_S / probe))
+    return batch, probe
+
+
+def cpu_measure(pack_path, steps, warmup):
+    """The one CPU measurement method of this file (the cpu_baseline leg and
+    the --impl reference arm): `steps` timed batched decode steps of the
+    oracle after `warmup` untimed ones, each step the sample of
+    cpu_sample_batch at context 2048; value = sequences per step / seconds per
+    step (tok/s)."""
+    batch, probe = cpu_sample_batch(pack_path)
+    sec, threads = cpu_decode_steps(pack_path, batch, steps, warmup=warmup)
+    return {"value": round(batch / sec, 3), "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{steps} timed decode steps (after {warmup} untimed) of {batch} sequences at context {CTX}, "
+                      f"random KV; C++/OpenMP restatement of the reference math; one 32-sequence step took "
+                      f"{probe:.2f} s", "batch": batch, "sec_per_step": sec}
+
+
+def cpu_extras(pack_path):
+    """The CPU numbers BASELINE.md promises beside the C3 one, on the host
+    cores (the C++/OpenMP oracle, double accumulation): C1 operators timed in
+    full; C2 = a 128-token prefill timed in full and 8 greedy decode steps
+    (per token); C4 (8192-token prefill) extrapolated from the measured
+    per-token projection cost and the measured causal-attention cost at 1024
+    tokens scaled by (8192 / 1024)^2, labelled as such."""
+    import oracle
+
+    rng = np.random.default_rng(1)
+
+    def timed(fn, reps=1):
+        best = float("inf")
+        for _ in range(reps):
+            t = time.perf_counter()
+            fn()
+            best = min(best, time.perf_counter() - t)
+        return best
+
+    x = (rng.standard_normal((4096, 1024)) * 4).astype(np.float32)
+    ln = rng.standard_normal((4096, 2048)).astype(np.float32)
+    g, b = rng.uniform(0.5, 1.5, 2048).astype(np.float32), (rng.standard_normal(2048) * 0.1).astype(np.float32)
+    A = (rng.standard_normal((1024, 2048)) / 2048 ** 0.5).astype(np.float32)
+    B = (rng.standard_normal((2048, 1024)) / 2048 ** 0.5).astype(np.float32)
+    s24 = rng.uniform(-1, 1, 1 << 24).astype(np.float32)
+    c1 = {"softmax_4096x1024_ms": round(timed(lambda: oracle.softmax(x), 3) * 1e3, 2),
+          "layer_norm_4096x2048_ms": round(timed(lambda: oracle.layer_norm(ln, g, b), 3) * 1e3, 2),
+          "mat_mul_relu_1024x2048x1024_ms": round(timed(lambda: oracle.mat_mul(A, B, epilogue=1), 2) * 1e3, 2),
+          "sum_2e24_ms": round(timed(lambda: oracle.reduce_sum(s24), 3) * 1e3, 2)}
+    m, _ = _oracle_model(pack_path)
+    prompt = np.random.default_rng(5).integers(0, m.V, 128).astype(np.int32)
+    kc, vc = m.new_cache(128 + 9)
+    t = time.perf_counter()
+    logits = m.forward(prompt, 0, kc, vc)
+    prefill_s = time.perf_counter() - t
+    tok = oracle.argmax(logits)
+    t = time.perf_counter()
+    for k in range(8):
+        tok = oracle.argmax(m.forward([tok], 128 + k, kc, vc))
+    decode_s = (time.perf_counter() - t) / 8
+    q = rng.standard_normal((1024, m.qh, m.D)).astype(np.float32)
+    kv = rng.standard_normal((1024, m.kvh, m.D)).astype(np.float32)
+    attn1k = timed(lambda: oracle.attention(q, kv, kv))
+    per_tok = prefill_s / 128  # attention is < 1% of a 128-token prefill
+    c4_s = per_tok * 8192 + attn1k * 64 * m.L
+    return {"threads": oracle.lib().orc_num_threads(), "c1": c1,
+            "c2": {"prefill_128_ms": round(prefill_s * 1e3, 1), "ttft_tok_s": round(128 / prefill_s, 1),
+                   "decode_tok_s": round(1 / decode_s, 2), "decode_steps": 8},
+            "c4_extrapolated": {"ms": round(c4_s * 1e3), "tok_s": round(8192 / c4_s, 1),
+                                "method": "128-token prefill cost per token x 8192 + 1024-token causal attention "
+                                          "x 64 x layers (extrapolated, not run)"}}
+
+
+def cpu_baseline(pack_path, steps=6):
+    out = cpu_measure(pack_path, steps, warmup=1)
+    out.pop("batch")
+    out["sec_per_step"] = round(out["sec_per_step"], 3)
+    return out
 
 
 def run_reference(args):
@@ -614,14 +768,9 @@ def run_reference(args):
 
     pack_path = pack.ensure_random_llama_pack()
     K, W = args.steps, args.warmup
-    # bound the whole run to a few minutes: measure one full step, then size
-    # the per-step sample (sequences per step) so W + K steps fit ~150 s
-    probe, threads = cpu_decode_steps(pack_path, BATCH, 1, warmup=0)
-    budget = 150.0
-    per_step = budget / max(1, K + W)
-    batch = BATCH if probe <= per_step else max(1, int(BATCH * per_step / probe))
-    sec, threads = cpu_decode_steps(pack_path, batch, K, warmup=W)
-    value = batch / sec
+    # the same sample step as the cpu_baseline leg of our arm (cpu_measure)
+    m = cpu_measure(pack_path, K, W)
+    batch, sec, threads, value = m["batch"], m["sec_per_step"], m["cores"], m["value"]
     line = {
         "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": K, "warmup": W,
         "ms_per_step": round(sec * 1e3, 2), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
@@ -631,8 +780,7 @@ def run_reference(args):
                                "OpenMP; OpWorks has no CPU path of its own)", "global_batch": batch,
                    "seq_len": CTX, "parallelism": "host threads"},
         "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": threads, "kind": "port",
-                         "sample": f"{K} decode steps of {batch} sequences at context {CTX} (1 full 32-sequence "
-                                   f"step took {probe:.2f} s)"},
+                         "sample": m["sample"]},
         "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)

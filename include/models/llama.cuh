@@ -134,6 +134,8 @@ template <typename WT> class LlamaEngineT {
         else
             detail::require((w.sets & kWeightsF32) && (w.sets & kWeightsSplit),
                             "fp32 weights (accurate path) were not loaded");
+        if (prefill_single_rows_ < 0)
+            prefill_single_rows_ = w.f16 && pair_min_rows_ < (1 << 30) ? pair_min_rows_ - 1 : (1 << 30);
         prefill_rows_ = prefill_rows > 0 ? std::min(prefill_rows, max_seq_len) : max_seq_len;
         rows_max_ = std::max(prefill_rows_, max_batch);
         blocks_per_seq_ = (max_seq_len + kKvBlockTokens - 1) / kKvBlockTokens;
@@ -807,23 +809,32 @@ template <typename WT> class LlamaEngineT {
     // `next` (optional): the projection that streams after this one; its
     // weights are pulled into L2 while this GEMM runs (latency-bound decode
     // GEMMs leave HBM bandwidth idle)
+    // `which` (0 QKV, 1 O, 2 gate/up, 3 down) selects a per-projection cap
+    // on the K splits (OPWORKS_SPLITS_QKV / _O / _GU / _DOWN; default: the
+    // cluster bound)
     template <typename Epi>
-    void linear_tile(const WView &p, const Act &x, int rows, const Epi &epi, const WView *next = nullptr) {
-        if (rows > prefill_single_rows_) {
-            // prefill-sized GEMMs: single-term 16-bit activations (one MMA
-            // per K step, 256-token tiles), compute-bound shapes
+    void linear_tile(const WView &p, const Act &x, int rows, const Epi &epi, const WView *next = nullptr,
+                     int which = -1) {
+        const bool single = rows > prefill_single_rows_;
+        if (rows >= pair_min_rows_) {
+            // prefill-sized GEMMs: two-SM 256 x 256 tiles (cta_group::2);
+            // one activation term (one MMA per K step) above the threshold
+            sm100::gemm_pair_bf16x2<Epi>(wop(p), xop(x, rows, p.in, !single), p.in, stream_, epi);
+            return;
+        }
+        if (single) {
+            // single-term 16-bit activations (one MMA per K step, 256-token
+            // tiles), compute-bound shapes
             sm100::gemm_tn<sm100::GemmKind::kBF16, Epi>(wop(p), xop(x, rows, p.in, false), p.in, part_.data(), p.out, 1,
                                                         static_cast<int64_t>(rows) * p.out, stream_, epi,
                                                         sm100::gemm_pick_bn(sm100::GemmKind::kBF16, rows));
             return;
         }
-        if (rows >= pair_min_rows_) {
-            // prefill-sized GEMMs: two-SM 256 x 256 tiles (cta_group::2)
-            sm100::gemm_pair_bf16x2<Epi>(wop(p), xop(x, rows, p.in), p.in, stream_, epi);
-            return;
-        }
-        int splits = plan_splits(p, rows, max_cluster_splits_);
+        const int cap = which >= 0 && split_cap_[which] > 0 ? std::min(split_cap_[which], max_cluster_splits_)
+                                                            : max_cluster_splits_;
+        int splits = plan_splits(p, rows, cap);
         const bool pf = next != nullptr && l2_prefetch_ && rows <= 64;
+        const uint64_t pf_bytes = pf ? sizeof(uint16_t) * static_cast<uint64_t>(next->out) * next->ld : 0;
         // grids of at most one CTA per SM (16 tiles x 8 splits at C3) double
         // their splits as two clusters per tile, reduced across clusters
         // through L2, so twice the weight bytes are in flight
@@ -840,13 +851,14 @@ template <typename WT> class LlamaEngineT {
         if (cluster > 0) {
             sm100::gemm_tn<sm100::GemmKind::kBF16x2, Epi>(
                 wop(p), xop(x, rows, p.in), p.in, part_.data(), p.out, splits,
-                static_cast<int64_t>(rows) * p.out, stream_, epi, 32, nullptr, 0, &groups_ws_, cluster);
+                static_cast<int64_t>(rows) * p.out, stream_, epi, 32, pf ? next->w : nullptr, pf_bytes, &groups_ws_,
+                cluster, l2_prefetch_tail_);
             return;
         }
         sm100::gemm_tn<sm100::GemmKind::kBF16x2, Epi>(
             wop(p), xop(x, rows, p.in), p.in, part_.data(), p.out, splits,
-            static_cast<int64_t>(rows) * p.out, stream_, epi, plan_bn(rows), pf ? next->w : nullptr,
-            pf ? sizeof(uint16_t) * static_cast<uint64_t>(next->out) * next->ld : 0);
+            static_cast<int64_t>(rows) * p.out, stream_, epi, plan_bn(rows), pf ? next->w : nullptr, pf_bytes, nullptr,
+            0, l2_prefetch_tail_);
     }
 
     // part[s][rows][p.out] = x[rows][p.in] . W^T (partial over split s)
@@ -1053,7 +1065,7 @@ template <typename WT> class LlamaEngineT {
             if (fast()) {
                 linear_tile(qkv_v_[l], normed, rows,
                             detail::QkvTileEpi{q_.data(), qh, kvh, rope, tm, kv, kv_.k(l), kv_.v(l), rs, narrow_tile(rows)},
-                            l2_prefetch_qkv_o_ ? &o_v_[l] : nullptr);
+                            l2_prefetch_qkv_o_ ? &o_v_[l] : nullptr, 0);
                 mark("gemm_qkv_rope_kv_write");
             } else {
                 s = linear(L.qkv, normed, rows);
@@ -1103,13 +1115,13 @@ template <typename WT> class LlamaEngineT {
                     linear_tile(o_v_[l], attn, rows,
                                 detail::ResidualTileEpi{hidden_.data(), H, L.post_norm.data(), normed_o, rs,
                                                         narrow_tile(rows)},
-                                &gu_v_[l]);
+                                &gu_v_[l], 1);
                     mark("gemm_o_residual");
-                    linear_tile(gu_v_[l], normed, rows, detail::SiluMulTileEpi{act_o, rs}, &down_v_[l]);
+                    linear_tile(gu_v_[l], normed, rows, detail::SiluMulTileEpi{act_o, rs}, &down_v_[l], 2);
                     mark("gemm_gate_up_silu");
                     linear_tile(down_v_[l], act, rows,
                                 detail::ResidualTileEpi{hidden_.data(), H, next_gain, normed_o, rs, narrow_tile(rows)},
-                                l + 1 < cfg_.num_layers ? &qkv_v_[l + 1] : nullptr);
+                                l + 1 < cfg_.num_layers ? &qkv_v_[l + 1] : nullptr, 3);
                     mark("gemm_down_residual");
                 }
             } else {
@@ -1152,7 +1164,8 @@ template <typename WT> class LlamaEngineT {
             sm100::gemm_tn<sm100::GemmKind::kBF16x2, detail::LogitsTileEpi>(
                 {w_.embed_w16.data(), nullptr, V, H, w_.f16},
                 {normed_h_.data() + first * H, normed_hlo_.data() + first * H, lrows, H, w_.f16}, H, logits_.data(), V,
-                1, 0, stream_, detail::LogitsTileEpi{logits_.data(), V, row_sumsq(), first}, plan_bn(lrows));
+                lm_head_splits_, 0, stream_, detail::LogitsTileEpi{logits_.data(), V, row_sumsq(), first},
+                plan_bn(lrows));
         } else {
             for (int r0 = 0; r0 < lrows; r0 += 4) {
                 const int r = std::min(4, lrows - r0);
@@ -1243,13 +1256,17 @@ template <typename WT> class LlamaEngineT {
     bool multi_has_uni_ = false;
     bool marks_enabled_ = false;
     // fast-path GEMMs with more token rows than this use single-term 16-bit
-    // activations (one MMA per K step). Off by default: on a 1024-token
-    // prompt single-term bf16 activations moved the logits by 0.043 against
-    // the fp32 path, over the 2e-2 GEMM tolerance (two terms: 0.010); C4
-    // prefill would gain 16%. OPWORKS_PREFILL_SINGLE_ROWS sets the threshold.
+    // activations (one MMA per K step). Default: fp16 models from the
+    // two-SM threshold on (every prefill GEMM of at least pair_min_rows_
+    // rows), bf16 models never. Measured on the float32 pack: fp16 single
+    // term keeps the logits within 1.65e-2 of the fp32 path at C3 and C4
+    // (two terms: 1.23e-2) and makes the C4 prefill 19% faster; bf16 single
+    // term moved them by 0.043 on a 1024-token prompt, over the 2e-2 GEMM
+    // tolerance. OPWORKS_PREFILL_SINGLE_ROWS sets the threshold (resolved in
+    // the constructor).
     int prefill_single_rows_ = [] {
         const char *e = std::getenv("OPWORKS_PREFILL_SINGLE_ROWS");
-        return e ? std::atoi(e) : (1 << 30);
+        return e ? std::atoi(e) : -1;
     }();
     // fast-path GEMMs of at least this many token rows (and not taken by
     // the single-term path) run the two-SM cta_group::2 kernel;
@@ -1269,6 +1286,10 @@ template <typename WT> class LlamaEngineT {
     // upper bound on the K splits (one cluster) of the fused GEMMs: the
     // portable 8 measured fastest at C3 (4 and 16 were slower);
     // OPWORKS_CLUSTER_SPLITS overrides it (up to 16, non-portable clusters)
+    int split_cap_[4] = {std::getenv("OPWORKS_SPLITS_QKV") ? std::atoi(std::getenv("OPWORKS_SPLITS_QKV")) : 0,
+                         std::getenv("OPWORKS_SPLITS_O") ? std::atoi(std::getenv("OPWORKS_SPLITS_O")) : 0,
+                         std::getenv("OPWORKS_SPLITS_GU") ? std::atoi(std::getenv("OPWORKS_SPLITS_GU")) : 0,
+                         std::getenv("OPWORKS_SPLITS_DOWN") ? std::atoi(std::getenv("OPWORKS_SPLITS_DOWN")) : 0};
     int max_cluster_splits_ = [] {
         const char *e = std::getenv("OPWORKS_CLUSTER_SPLITS");
         const int want = e ? std::atoi(e) : sm100::kMaxClusterSplits;
@@ -1283,6 +1304,19 @@ template <typename WT> class LlamaEngineT {
         return e ? std::atoi(e) : 0;
     }();
     bool l2_prefetch_qkv_o_ = l2_prefetch_ >= 2;
+    // K splits of the LM head GEMM (a cluster per vocabulary tile when > 1:
+    // smaller CTAs, so the last wave of 1002 tiles leaves fewer SMs idle)
+    int lm_head_splits_ = [] {
+        const char *e = std::getenv("OPWORKS_LMHEAD_SPLITS");
+        const int v = e ? std::atoi(e) : 1;
+        return v >= 1 && v <= 8 ? v : 1;
+    }();
+    // where a GEMM issues that prefetch: after its own last load
+    // (OPWORKS_L2_PREFETCH_AT=tail) or at its start
+    bool l2_prefetch_tail_ = [] {
+        const char *e = std::getenv("OPWORKS_L2_PREFETCH_AT");
+        return e && std::strcmp(e, "tail") == 0;
+    }();
     // programmatic dependent launch between the kernels of a step
     // (OPWORKS_PDL=0 turns it off)
     bool pdl_ = [] {

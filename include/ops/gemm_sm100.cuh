@@ -52,9 +52,13 @@ struct GemmParams {
     int splits;
     int *err;             // error word (bounded wait ran out)
     // optional: bytes the next kernel will stream (its weights), pulled into
-    // L2 while this GEMM runs; every CTA prefetches its share
+    // L2 while this GEMM runs; every CTA prefetches its share, either at its
+    // start (l2_prefetch_tail false) or once its producer has issued its own
+    // last load, so the prefetch fills the HBM time the MMA drain and the
+    // epilogue leave idle instead of competing with this GEMM's stream
     const uint8_t *l2_prefetch = nullptr;
     uint64_t l2_prefetch_bytes = 0;
+    bool l2_prefetch_tail = false;
     // tile epilogues: CTAs per cluster (0 = splits). With splits = G x
     // cluster, each of the G clusters of a tile reduces its partials through
     // distributed shared memory, stores its row slices to red_ws, and the
@@ -238,9 +242,9 @@ __global__ void __launch_bounds__(192, GemmShape<kKind, BN>::kCtasPerSm)
                 mbar_arrive_expect_tx(&full[j], S::kStageBytes);
                 load_a(kb_begin + j, j);
             }
-            if (p.l2_prefetch_bytes > 0) {
-                // this CTA's share of the next kernel's stream, in 16-byte
-                // multiples and chunks of at most 64 KB
+            // this CTA's share of the next kernel's stream, in 16-byte
+            // multiples and chunks of at most 64 KB
+            auto prefetch_next = [&]() {
                 const uint64_t ctas = static_cast<uint64_t>(gridDim.x) * gridDim.y * gridDim.z;
                 const uint64_t cta = (static_cast<uint64_t>(blockIdx.z) * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
                 const uint64_t share = ((p.l2_prefetch_bytes + ctas - 1) / ctas + 15) & ~uint64_t(15);
@@ -248,7 +252,9 @@ __global__ void __launch_bounds__(192, GemmShape<kKind, BN>::kCtasPerSm)
                 const uint64_t hi = min(p.l2_prefetch_bytes, lo + share);
                 for (uint64_t o = lo; o < hi; o += 65536)
                     bulk_prefetch_l2(p.l2_prefetch + o, static_cast<uint32_t>(hi - o < 65536 ? hi - o : 65536));
-            }
+            };
+            if (p.l2_prefetch_bytes > 0 && !p.l2_prefetch_tail)
+                prefetch_next();
             pdl_wait();
             for (int j = 0; j < pre; ++j)
                 load_b(kb_begin + j, j);
@@ -264,6 +270,8 @@ __global__ void __launch_bounds__(192, GemmShape<kKind, BN>::kCtasPerSm)
                 load_a(kb, s);
                 load_b(kb, s);
             }
+            if (ok && p.l2_prefetch_bytes > 0 && p.l2_prefetch_tail)
+                prefetch_next();
             // never leave the CTA with copies in flight: the last issued
             // phase of every slot must have landed (returns at once when the
             // MMA warp already consumed it)
@@ -594,7 +602,7 @@ template <GemmKind kKind, typename Epi = Identity>
 inline void gemm_tn(const GemmOperand &A, const GemmOperand &B, int k, float *out, int64_t ldo, int splits,
                     int64_t split_stride, cudaStream_t stream, const Epi &epi = {}, int force_bn = 0,
                     const void *l2_prefetch = nullptr, uint64_t l2_prefetch_bytes = 0,
-                    const SplitGroupWorkspace *groups_ws = nullptr, int cluster = 0) {
+                    const SplitGroupWorkspace *groups_ws = nullptr, int cluster = 0, bool l2_prefetch_tail = false) {
     constexpr bool kBf16 = kKind != GemmKind::kTF32x3;
     constexpr int kKElems = kBf16 ? 64 : 32;
     detail::require(k > 0, "gemm_tn: K must be positive");
@@ -614,6 +622,7 @@ inline void gemm_tn(const GemmOperand &A, const GemmOperand &B, int k, float *ou
                     "gemm_tn: L2 prefetch range must be 16-byte aligned");
     p.l2_prefetch = static_cast<const uint8_t *>(l2_prefetch);
     p.l2_prefetch_bytes = l2_prefetch_bytes & ~uint64_t(15);
+    p.l2_prefetch_tail = l2_prefetch_tail;
     int bn = force_bn ? force_bn : gemm_pick_bn(kKind, B.rows);
     if (is_tile_epilogue<Epi>::value && cluster > 0 && p.splits > cluster) {
         // grouped split K: the tile grid's partial slices must fit the workspace

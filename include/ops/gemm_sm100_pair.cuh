@@ -32,12 +32,14 @@
 
 namespace opworks::sm100 {
 
-struct PairShape {
+// kTerms = 2: activations as hi + lo terms (two MMAs per K step); 1: one
+// term (one MMA per K step, 32 KB stages, so the ring is 6 deep).
+template <int kTerms> struct PairShape {
     static constexpr int BN = 256;                   // tokens per pair tile (128 per CTA staged)
     static constexpr uint32_t kABytes = kUmmaM * kUmmaKBytes; // 128 weight rows x 128 B
     static constexpr uint32_t kBBytes = 128 * kUmmaKBytes;    // 128 token rows x 128 B (one term)
-    static constexpr uint32_t kStageBytes = kABytes + 2 * kBBytes;
-    static constexpr int kStages = 4;
+    static constexpr uint32_t kStageBytes = kABytes + kTerms * kBBytes;
+    static constexpr int kStages = kTerms == 2 ? 4 : 6;
     static constexpr uint32_t kTmemCols = BN;
     static constexpr size_t kEpiScratchBytes = 16u * BN;
     static constexpr size_t kSmemBytes = 1024 + static_cast<size_t>(kStages) * kStageBytes + 256 + kEpiScratchBytes;
@@ -108,11 +110,11 @@ __device__ __forceinline__ void cluster_sync_all() {
 // grid = (feature tiles rounded up to even, token tiles of 256), cluster
 // (2, 1, 1), 192 threads: warp 0 TMA producer, warp 1 TMEM + MMA issuer
 // (leader only), warps 2-5 epilogue.
-template <typename Epi>
+template <typename Epi, int kTerms>
 __global__ void __launch_bounds__(192, 1)
     umma_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                           const __grid_constant__ CUtensorMap tmB_lo, GemmParams p, Epi epi) {
-    using S = PairShape;
+    using S = PairShape<kTerms>;
     constexpr int kStages = S::kStages;
     static_assert(is_tile_epilogue<Epi>::value, "the pair GEMM runs tile epilogues");
     extern __shared__ uint8_t smem_raw[];
@@ -140,7 +142,8 @@ __global__ void __launch_bounds__(192, 1)
         fence_mbarrier_init();
         prefetch_tmap(&tmA);
         prefetch_tmap(&tmB);
-        prefetch_tmap(&tmB_lo);
+        if constexpr (kTerms == 2)
+            prefetch_tmap(&tmB_lo);
     }
     if (warp == 1) {
         tmem_alloc_pair(tmem_slot, S::kTmemCols);
@@ -163,7 +166,8 @@ __global__ void __launch_bounds__(192, 1)
             auto load_b = [&](int kb, int s) {
                 uint8_t *st = smem + s * S::kStageBytes;
                 tma_load_2d_pair(st + S::kABytes, &tmB, bar(s), kb * 64, tb);
-                tma_load_2d_pair(st + S::kABytes + S::kBBytes, &tmB_lo, bar(s), kb * 64, tb);
+                if constexpr (kTerms == 2)
+                    tma_load_2d_pair(st + S::kABytes + S::kBBytes, &tmB_lo, bar(s), kb * 64, tb);
             };
             // weights of the first stages stream before the programmatic-
             // launch wait; activations after it
@@ -206,9 +210,14 @@ __global__ void __launch_bounds__(192, 1)
                 for (int k = 0; k < 4; ++k) { // four 32-byte K steps per 128-byte block
                     const uint64_t ad = sdesc_k128(a + 32 * k);
                     const uint64_t bd = sdesc_k128(b + 32 * k);
-                    const uint64_t bd_lo = sdesc_k128(b + S::kBBytes + 32 * k);
-                    umma_bf16_pair(tmem_d, ad, bd_lo, idesc, (kb > 0 || k > 0) ? 1u : 0u);
-                    umma_bf16_pair(tmem_d, ad, bd, idesc, 1u);
+                    const uint32_t acc = (kb > 0 || k > 0) ? 1u : 0u;
+                    if constexpr (kTerms == 2) {
+                        const uint64_t bd_lo = sdesc_k128(b + S::kBBytes + 32 * k);
+                        umma_bf16_pair(tmem_d, ad, bd_lo, idesc, acc);
+                        umma_bf16_pair(tmem_d, ad, bd, idesc, 1u);
+                    } else {
+                        umma_bf16_pair(tmem_d, ad, bd, idesc, acc);
+                    }
                 }
                 umma_commit_pair(&empty[s], 0x3);
             }
@@ -265,20 +274,22 @@ __global__ void __launch_bounds__(192, 1)
     }
 }
 
-template <typename Epi> inline void gemm_pair_prepare_kernel() {
+template <typename Epi, int kTerms> inline void gemm_pair_prepare_kernel() {
     static thread_local int done_device = -1;
     int dev = 0;
     OPWORKS_CUDA_CHECK(cudaGetDevice(&dev));
     if (done_device != dev) {
-        OPWORKS_CUDA_CHECK(cudaFuncSetAttribute(umma_gemm_pair_kernel<Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                static_cast<int>(PairShape::kSmemBytes)));
+        OPWORKS_CUDA_CHECK(cudaFuncSetAttribute(umma_gemm_pair_kernel<Epi, kTerms>,
+                                                cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                static_cast<int>(PairShape<kTerms>::kSmemBytes)));
         done_device = dev;
     }
 }
 
-// out via `epi` (a tile epilogue): W [n_feat][k] bf16, X = Xhi + Xlo
-// [m_tok][k] bf16 (K-major, row strides 16-byte aligned). One launch, no K
-// split; grids are pairs of 128-feature tiles by 256-token tiles.
+// out via `epi` (a tile epilogue): W [n_feat][k] 16-bit, X = Xhi + Xlo
+// [m_tok][k] 16-bit (K-major, row strides 16-byte aligned; X.lo == nullptr:
+// one activation term). One launch, no K split; grids are pairs of
+// 128-feature tiles by 256-token tiles.
 template <typename Epi>
 inline void gemm_pair_bf16x2(const GemmOperand &W, const GemmOperand &X, int k, cudaStream_t stream, const Epi &epi) {
     static_assert(is_tile_epilogue<Epi>::value, "gemm_pair_bf16x2 runs tile epilogues");
@@ -295,13 +306,19 @@ inline void gemm_pair_bf16x2(const GemmOperand &W, const GemmOperand &X, int k, 
     p.ab_fmt = gemm_ab_format(W, X);
     const CUtensorMap ta = make_tmap_2d(W.hi, true, static_cast<uint64_t>(k), W.rows, W.ld, 64, kUmmaM);
     const CUtensorMap tb = make_tmap_2d(X.hi, true, static_cast<uint64_t>(k), X.rows, X.ld, 64, 128);
-    const CUtensorMap tb_lo = make_tmap_2d(X.lo, true, static_cast<uint64_t>(k), X.rows, X.ld, 64, 128);
-    gemm_pair_prepare_kernel<Epi>();
+    const CUtensorMap tb_lo = X.lo ? make_tmap_2d(X.lo, true, static_cast<uint64_t>(k), X.rows, X.ld, 64, 128) : tb;
     const int ftiles = (W.rows + kUmmaM - 1) / kUmmaM;
-    const dim3 grid((ftiles + 1) / 2 * 2, (X.rows + PairShape::BN - 1) / PairShape::BN, 1);
+    const dim3 grid((ftiles + 1) / 2 * 2, (X.rows + PairShape<2>::BN - 1) / PairShape<2>::BN, 1);
     detail::require(grid.y <= 65535, "gemm_pair_bf16x2: grid exceeds the CUDA limits");
-    launch_ex_cluster(umma_gemm_pair_kernel<Epi>, grid, dim3(2, 1, 1), dim3(192), PairShape::kSmemBytes, stream, ta,
-                      tb, tb_lo, p, epi);
+    if (X.lo) {
+        gemm_pair_prepare_kernel<Epi, 2>();
+        launch_ex_cluster(umma_gemm_pair_kernel<Epi, 2>, grid, dim3(2, 1, 1), dim3(192), PairShape<2>::kSmemBytes,
+                          stream, ta, tb, tb_lo, p, epi);
+    } else {
+        gemm_pair_prepare_kernel<Epi, 1>();
+        launch_ex_cluster(umma_gemm_pair_kernel<Epi, 1>, grid, dim3(2, 1, 1), dim3(192), PairShape<1>::kSmemBytes,
+                          stream, ta, tb, tb_lo, p, epi);
+    }
 }
 
 } // namespace opworks::sm100

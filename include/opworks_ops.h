@@ -143,7 +143,8 @@ OPW_API int opw_gemm_bf16x2_pair(const uint16_t *W, const uint16_t *x_hi, const 
                                  int K, int M, void *stream);
 /* The same two GEMMs with every 16-bit word read as fp16 instead of bf16 (the
  * format the runtime's fast path uses for float32 packs: 11 significant bits
- * at 2 bytes). Extensions of this library (no reference counterpart). */
+ * at 2 bytes). The pair entry points accept x_lo == NULL: one activation term,
+ * one MMA per K step. Extensions of this library (no reference counterpart). */
 OPW_API int opw_gemm_f16x2(const uint16_t *W, const uint16_t *x_hi, const uint16_t *x_lo, float *out, int N, int K,
                            int M, int splits, void *stream);
 OPW_API int opw_gemm_f16x2_pair(const uint16_t *W, const uint16_t *x_hi, const uint16_t *x_lo, float *out, int N,

@@ -390,7 +390,7 @@ int gemm_16x2_pair(const uint16_t *W, const uint16_t *x_hi, const uint16_t *x_lo
                    bool f16, void *stream) {
     return guarded([&] {
         using namespace opworks;
-        detail::require(W && x_hi && x_lo && out && N > 0 && K > 0 && M > 0, "gemm_16x2_pair: bad arguments");
+        detail::require(W && x_hi && out && N > 0 && K > 0 && M > 0, "gemm_16x2_pair: bad arguments");
         detail::require(K % 8 == 0, "gemm_16x2_pair: K must be a multiple of 8 (16-byte rows)");
         sm100::gemm_pair_bf16x2({W, nullptr, N, K, f16}, {x_hi, x_lo, M, K, f16}, K, as_stream(stream),
                                 sm100::StoreTileEpi<sm100::Identity>{out, N, {}});

@@ -205,10 +205,11 @@ def decode(only="all", iters=20):
 
 
 def pair(M=8192, iters=10):
-    """Two-SM bf16 x two-term-bf16 GEMM (the prefill projections' kernel) at
-    the C4 shapes: M token rows against the QKV, O, gate/up and down weights.
-    TFLOP/s counts the useful 2*M*N*K; the tensor cores execute twice that
-    (one MMA per activation term)."""
+    """Two-SM GEMM (the prefill projections' kernel) at the C4 shapes: M
+    token rows against the QKV, O, gate/up and down weights, with two
+    activation terms (16-bit weights x hi + lo; the tensor cores execute
+    twice the useful 2*M*N*K) and with one fp16 term. TFLOP/s counts the
+    useful 2*M*N*K."""
     import torch
 
     import opworks_b200
@@ -225,9 +226,14 @@ def pair(M=8192, iters=10):
         xl = (x - xh.float()).to(torch.bfloat16)
         o = torch.empty(M, N, device="cuda")
         ms = t(lambda: raw(W.view(torch.int16), xh.view(torch.int16), xl.view(torch.int16), o, N, K, M, 0), iters)
+        W16, x16 = W.float().to(torch.float16), x.to(torch.float16)
+        ms1 = t(lambda: ops.raw("gemm_f16x2_pair")(W16.view(torch.int16), x16.view(torch.int16), 0, o, N, K, M, 0),
+                iters)
         f = 2.0 * M * N * K
         res.append({"gemm": name, "M": M, "N": N, "K": K, "us": round(ms * 1e3, 1),
-                    "useful_tflops": round(f / ms / 1e9, 1), "mma_frac_of_bf16_peak": round(2 * f / ms / 1e9 / tc, 3)})
+                    "useful_tflops": round(f / ms / 1e9, 1), "mma_frac_of_bf16_peak": round(2 * f / ms / 1e9 / tc, 3),
+                    "one_term_us": round(ms1 * 1e3, 1), "one_term_tflops": round(f / ms1 / 1e9, 1),
+                    "one_term_frac_of_bf16_peak": round(f / ms1 / 1e9 / tc, 3)})
     return {"peak_source": src, "bf16_tflops": tc, "gemms": res}
 
 

@@ -117,7 +117,13 @@ def round_to_bf16_grid(a):
     return r.view(np.float32)
 
 
-def random_llama_pack(path, cfg=None, seed=1234, std=0.02, norm_value=1.0, eos=None, bf16_grid=True):
+def bf16_bits(a):
+    """fp32 values rounded (nearest-even) to bf16, as raw uint16 bits."""
+    return (round_to_bf16_grid(a).view(np.uint32) >> np.uint32(16)).astype(np.uint16)
+
+
+def random_llama_pack(path, cfg=None, seed=1234, std=0.02, norm_value=1.0, eos=None, bf16_grid=True,
+                      dtype="float32"):
     """Random-init Llama pack: projections/embedding ~ N(0, std) drawn from
     numpy default_rng(seed) in HF order, RMSNorm gains = norm_value (the HF
     init), lm_head.weight aliased to the embedding (tied). With bf16_grid the
@@ -129,16 +135,19 @@ def random_llama_pack(path, cfg=None, seed=1234, std=0.02, norm_value=1.0, eos=N
 
     def produce(name, shape):
         if name.endswith("norm.weight"):
-            return np.full(shape, norm_value, np.float32)
-        a = rng.standard_normal(shape, dtype=np.float32)
-        a *= np.float32(std)
-        return round_to_bf16_grid(a) if bf16_grid else a
+            a = np.full(shape, norm_value, np.float32)
+        else:
+            a = rng.standard_normal(shape, dtype=np.float32)
+            a *= np.float32(std)
+            if bf16_grid:
+                a = round_to_bf16_grid(a)
+        return bf16_bits(a) if dtype == "bfloat16" else a
 
     extra = {"config": cfg, "eos_token_ids": list(eos if eos is not None else LLAMA_EOS),
              "meta": {"init": "random", "seed": seed, "std": std, "norm_value": norm_value,
                       "bf16_grid": bool(bf16_grid)}}
     return write_pack(path, [(n, s) for n, s, _ in specs], produce, extra=extra,
-                      aliases={"lm_head.weight": "model.embed_tokens.weight"})
+                      aliases={"lm_head.weight": "model.embed_tokens.weight"}, dtype=dtype)
 
 
 def read_pack(path, mmap=True):
@@ -166,17 +175,18 @@ def default_pack_dir():
     return os.environ.get("OPWORKS_PACK_DIR", "/tmp/opworks_packs")
 
 
-def ensure_random_llama_pack(cfg=None, seed=1234, name=None, bf16_grid=False):
+def ensure_random_llama_pack(cfg=None, seed=1234, name=None, bf16_grid=False, dtype="float32"):
     """Path of a cached random-init pack, generating it on first use. By
     default the weights keep every fp32 bit of the N(0, 0.02) draw (the fast
     path's 16-bit copy is then a rounding of them); bf16_grid=True rounds them
-    to the bf16 grid first."""
+    to the bf16 grid first. dtype="bfloat16" writes a bf16 pack of the same
+    draw (each weight rounded to nearest even)."""
     cfg = cfg or LLAMA_3_2_1B
     d = default_pack_dir()
     os.makedirs(d, exist_ok=True)
-    grid = "bf16grid" if bf16_grid else "fp32"
+    grid = "bf16pack" if dtype == "bfloat16" else ("bf16grid" if bf16_grid else "fp32")
     tag = name or f"llama_L{cfg['num_hidden_layers']}_H{cfg['hidden_size']}_V{cfg['vocab_size']}_s{seed}_{grid}"
     path = os.path.join(d, tag + ".pack")
     if not os.path.exists(path):
-        random_llama_pack(path, cfg, seed, bf16_grid=bf16_grid)
+        random_llama_pack(path, cfg, seed, bf16_grid=bf16_grid, dtype=dtype)
     return path

@@ -157,7 +157,8 @@ def test_gemm_bf16x2_pair_vs_fp64(ops, M, N, K):
 # wrong format would read every word with the other layout and miss by O(1)
 @pytest.mark.parametrize("kernel,M,N,K", [("gemm_f16x2", 32, 2048, 2048), ("gemm_f16x2", 7, 384, 200),
                                           ("gemm_f16x2", 200, 256, 1024), ("gemm_f16x2_pair", 512, 512, 1024),
-                                          ("gemm_f16x2_pair", 300, 384, 200)])
+                                          ("gemm_f16x2_pair", 300, 384, 200), ("pair_single", 512, 512, 1024),
+                                          ("pair_single", 300, 384, 520)])
 def test_gemm_f16x2_vs_fp64(ops, kernel, M, N, K):
     rng = np.random.default_rng(M + 5 * N + 11 * K)
     w = (rng.standard_normal((N, K)) / math.sqrt(K)).astype(np.float32)
@@ -174,9 +175,12 @@ def test_gemm_f16x2_vs_fp64(ops, kernel, M, N, K):
         got = host(part[:splits]).sum(axis=0)
     else:
         out = torch.full((M, N), float("nan"), device="cuda")
-        assert ops.raw(kernel)(dw, dh, dl, out, N, K, M, 0) == 0
+        single = kernel == "pair_single"  # one activation term: x_lo = NULL
+        assert ops.raw("gemm_f16x2_pair")(dw, dh, 0 if single else dl, out, N, K, M, 0) == 0
         sync(ops)
         got = host(out)
+        if single:
+            xl = torch.zeros_like(xl)
     e = (xh.double() + xl.double()).numpy() @ wh.double().numpy().T
     close(got, e, 2e-5)
 
