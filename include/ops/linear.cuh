@@ -6,7 +6,7 @@
 //
 // B200 paths:
 //   rows == 1  HBM-streaming GEMV: x staged once per block in shared memory,
-//              one warp per output row, 16-byte weight loads four deep per
+//              one warp per output row, 16-byte weight loads eight deep per
 //              lane, warp-shuffle reduction. This is the decode path of the
 //              fp32 (accurate) model.
 //   rows > 1   tcgen05 GEMM. fp32 weights: split-precision TF32 (x3) so the
@@ -46,7 +46,7 @@ template <> struct GemvVec<__nv_bfloat16> {
 
 // y[r][o] = sum_i x[r][i] W[o][i] for R <= 4 rows sharing every weight read.
 // x rows are staged once per block in shared memory; one warp per output
-// row, 16-byte weight loads four deep per lane, warp-shuffle reduction.
+// row, 16-byte weight loads eight deep per lane, warp-shuffle reduction.
 // Requires in % kPer == 0 and 16-byte aligned W and x rows.
 template <typename WT, int R>
 __global__ void __launch_bounds__(kThreads)
@@ -66,20 +66,27 @@ __global__ void __launch_bounds__(kThreads)
     const int warps_total = gridDim.x * (blockDim.x / kWarpSize);
     for (int row = blockIdx.x * (blockDim.x / kWarpSize) + threadIdx.x / kWarpSize; row < out; row += warps_total) {
         const uint4 *w = reinterpret_cast<const uint4 *>(W + static_cast<int64_t>(row) * in);
+        // kDepth 16-byte loads per lane in flight per round trip (a row of
+        // 2048 fp32 weights is two round trips); partial sums alternate
+        // between two accumulators per row
+        constexpr int kDepth = 8;
         float acc[R][2];
 #pragma unroll
         for (int r = 0; r < R; ++r)
             acc[r][0] = acc[r][1] = 0.f;
         int v = lane;
-        for (; v + kWarpSize < nvec; v += 2 * kWarpSize) {
-            const uint4 a = __ldg(w + v), b = __ldg(w + v + kWarpSize);
+        for (; v + (kDepth - 1) * kWarpSize < nvec; v += kDepth * kWarpSize) {
+            uint4 a[kDepth];
 #pragma unroll
-            for (int r = 0; r < R; ++r) {
-                acc[r][0] += GemvVec<WT>::dot(a, xs + r * in + v * kPer);
-                acc[r][1] += GemvVec<WT>::dot(b, xs + r * in + (v + kWarpSize) * kPer);
-            }
+            for (int d = 0; d < kDepth; ++d)
+                a[d] = __ldg(w + v + d * kWarpSize);
+#pragma unroll
+            for (int d = 0; d < kDepth; ++d)
+#pragma unroll
+                for (int r = 0; r < R; ++r)
+                    acc[r][d & 1] += GemvVec<WT>::dot(a[d], xs + r * in + (v + d * kWarpSize) * kPer);
         }
-        if (v < nvec) {
+        for (; v < nvec; v += kWarpSize) {
             const uint4 a = __ldg(w + v);
 #pragma unroll
             for (int r = 0; r < R; ++r)
