@@ -385,7 +385,8 @@ def run_ours(args):
         attn_flop = 4 * model.q_heads * model.head_dim * (8192 * 8193 / 2) * model.layers
         prefill8k = {"tokens": 8192, "ms": round(ms8, 2), "tok_s": round(8192 / (ms8 / 1e3), 1),
                      "tflops_useful": round((gemm_flop + attn_flop) / (ms8 / 1e3) / 1e12, 1),
-                     "frac_of_bf16_peak": round((gemm_flop + attn_flop) / (ms8 / 1e3) / 1e12 / tc_peak, 4)}
+                     "frac_of_bf16_peak": round((gemm_flop + attn_flop) / (ms8 / 1e3) / 1e12 / tc_peak, 4),
+                     "gemm_tflop": round(gemm_flop / 1e12, 2), "attention_tflop": round(attn_flop / 1e12, 2)}
         eng8.close()
 
     # ---- C5: 256-request serving, strong scaling over the ranks (every
@@ -420,6 +421,13 @@ def run_ours(args):
         from opworks_b200 import microbench
 
         c1 = microbench.c1(iters=10)
+        # the TF32 denominator: prefill attention and the split-TF32 mat_mul
+        c1["tf32_peak"] = microbench.tf32_peak()
+        tf = c1["tf32_peak"]["tf32_tflops"]
+        for op in c1.get("ops", []):
+            if "ours_tflops" in op:
+                op["ours_frac_tf32_peak"] = round(op["ours_tflops"] / tf, 4)
+                op["tf32_mma_frac_of_tf32_peak"] = round(3 * op["ours_tflops"] / tf, 4)  # 3 MMAs per K step
 
     cpu = None
     ref_cuda = None

@@ -237,6 +237,45 @@ def pair(M=8192, iters=10):
     return {"peak_source": src, "bf16_tflops": tc, "gemms": res}
 
 
+def tf32_peak(n=8192, burst_iters=10, sustain_s=3.0):
+    """Measured TF32 tensor-core peak (the denominator for this library's
+    TF32 kernels: prefill attention, split-TF32 GEMMs): torch.matmul of n^3
+    fp32 with TF32 allowed (cuBLAS), best of `burst_iters` (burst) and back
+    to back for `sustain_s` seconds (sustained), 2 n^3 flops each."""
+    import torch
+
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = True
+    try:
+        a = torch.randn(n, n, device="cuda")
+        b = torch.randn(n, n, device="cuda")
+        c = torch.empty(n, n, device="cuda")
+        for _ in range(3):
+            torch.matmul(a, b, out=c)
+        torch.cuda.synchronize()
+        best = float("inf")
+        for _ in range(burst_iters):
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            torch.matmul(a, b, out=c)
+            e.record()
+            torch.cuda.synchronize()
+            best = min(best, s.elapsed_time(e))
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = max(1, int(sustain_s * 1e3 / best))
+        s.record()
+        for _ in range(reps):
+            torch.matmul(a, b, out=c)
+        e.record()
+        torch.cuda.synchronize()
+        flop = 2.0 * n ** 3
+        return {"tf32_tflops": round(flop / best / 1e9, 1),
+                "tf32_tflops_sustained": round(flop * reps / s.elapsed_time(e) / 1e9, 1),
+                "how": f"torch.matmul fp32 {n}^3 with allow_tf32 (cuBLAS): best of {burst_iters}, and {reps} back to back"}
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+
+
 def prefill(T=8192, iters=2):
     """BASELINE C4: one T-token prefill of the random-init Llama-3.2-1B on the
     fast path (tensor-core GEMMs and attention), CUDA events on the engine
