@@ -32,6 +32,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdlib>
+#include <cstdio>
 #include <cstring>
 #include <functional>
 #include <map>
@@ -46,6 +47,7 @@
 #include "../ops/attention_kernels.cuh"
 #include "../ops/attention_prefill_tc.cuh"
 #include "../ops/gemm_sm100.cuh"
+#include "../ops/decode_chain.cuh"
 #include "../ops/gemm_sm100_pair.cuh"
 #include "../ops/linear.cuh"
 #include "../ops/llama_kernels.cuh"
@@ -195,6 +197,8 @@ template <typename WT> class LlamaEngineT {
             part = std::max(part, static_cast<int64_t>(plan_splits(*p, rows_max_)) * rows_max_ * p->out);
         part_ = TypedDeviceBuffer<float>(part);
         make_views();
+        if (fast && tp_world_ == 1)
+            alloc_chain();
         if (tp_world_ > 1) {
             tp_y_ = TypedDeviceBuffer<float>(rows_max_ * H);
             tp_comm_ = NcclLite::get().init(tp.nccl_id, tp_world_, tp_rank_);
@@ -784,6 +788,61 @@ template <typename WT> class LlamaEngineT {
         }
     }
 
+    // ---- persistent decode chain (O, gate/up, down, next QKV in one launch)
+    // phase p's (tiles, K blocks) for this model
+    void chain_shape(int ph, int &tiles, int &nk) const {
+        const int H = cfg_.hidden_size, I = cfg_.intermediate_size;
+        const int rows_out[4] = {H, 2 * I, H, cfg_.qkv_width()};
+        const int k[4] = {cfg_.q_width(), H, I, H};
+        tiles = (rows_out[ph] + kUmmaM - 1) / kUmmaM;
+        nk = (k[ph] + 63) / 64;
+    }
+    void alloc_chain() {
+        // CTAs streaming each phase: O and QKV fewer (their weights fit the
+        // rings of the active CTAs; the idle CTAs load the next phase's
+        // weights early), gate/up and down all
+        int want[4] = {64, sm_count_, 128, 96};
+        if (const char *e = std::getenv("OPWORKS_CHAIN_ACTIVE"))
+            std::sscanf(e, "%d,%d,%d,%d", &want[0], &want[1], &want[2], &want[3]);
+        for (int ph = 0; ph < 4; ++ph) {
+            int tiles = 0, nk = 0;
+            chain_shape(ph, tiles, nk);
+            chain_active_[ph] = std::max(1, std::min(want[ph], sm_count_));
+            const int parts = sm100::chain_max_parts(tiles, nk, chain_active_[ph]);
+            if (parts > 1) {
+                chain_part_[ph] = TypedDeviceBuffer<float>(static_cast<int64_t>(tiles) * parts * sm100::kChainBN * kUmmaM);
+                chain_cnt_[ph] = TypedDeviceBuffer<int32_t>(tiles);
+                OPWORKS_CUDA_CHECK(cudaMemset(chain_cnt_[ph].data(), 0, sizeof(int32_t) * tiles));
+            }
+        }
+        chain_sync_ = TypedDeviceBuffer<int32_t>(2);
+        OPWORKS_CUDA_CHECK(cudaMemset(chain_sync_.data(), 0, 2 * sizeof(int32_t)));
+    }
+    bool use_chain(int rows, bool decode) const {
+        return chain_ && fast() && tp_world_ == 1 && decode && rows <= sm100::kChainBN;
+    }
+    template <typename E3>
+    void chain_launch(int l, int rows, const Act &attn, const Act &normed, const Act &act, const detail::ActOut &normed_o,
+                      const detail::ActOut &act_o, const detail::RowSumSq &rs, const float *next_gain, int nphases,
+                      const E3 &e3) {
+        const int H = cfg_.hidden_size, I = cfg_.intermediate_size;
+        auto part = [&](int ph) { return chain_part_[ph].size() ? chain_part_[ph].data() : nullptr; };
+        auto cnt = [&](int ph) {
+            return chain_cnt_[ph].size() ? reinterpret_cast<unsigned *>(chain_cnt_[ph].data()) : nullptr;
+        };
+        sm100::ChainGemm g[4];
+        g[0] = {wop(o_v_[l]), xop(attn, rows, cfg_.q_width()), cfg_.q_width(), chain_active_[0], part(0), cnt(0)};
+        g[1] = {wop(gu_v_[l]), xop(normed, rows, H), H, chain_active_[1], part(1), cnt(1)};
+        g[2] = {wop(down_v_[l]), xop(act, rows, I), I, chain_active_[2], part(2), cnt(2)};
+        if (nphases == 4)
+            g[3] = {wop(qkv_v_[l + 1]), xop(normed, rows, H), H, chain_active_[3], part(3), cnt(3)};
+        const LayerWeights<WT> &L = w_.layers[l];
+        sm100::decode_chain_launch(g, nphases, sm_count_, reinterpret_cast<unsigned *>(chain_sync_.data()), stream_,
+                                   detail::ResidualTileEpi{hidden_.data(), H, L.post_norm.data(), normed_o, rs, false},
+                                   detail::SiluMulTileEpi{act_o, rs},
+                                   detail::ResidualTileEpi{hidden_.data(), H, next_gain, normed_o, rs, false}, e3);
+    }
+
     int plan_splits(const WView &p, int rows, int max_splits = 64) const {
         if (!fast() && rows <= 4)
             return 1;
@@ -1062,7 +1121,10 @@ template <typename WT> class LlamaEngineT {
             const float2 *rope = reinterpret_cast<const float2 *>(w_.rope_table.data());
             int s = 0;
             const detail::RowSumSq rs = row_sumsq();
-            if (fast()) {
+            const bool chain = use_chain(rows, decode);
+            if (fast() && chain && l > 0) {
+                // this layer's QKV ran as the last phase of the previous chain
+            } else if (fast()) {
                 linear_tile(qkv_v_[l], normed, rows,
                             detail::QkvTileEpi{q_.data(), qh, kvh, rope, tm, kv, kv_.k(l), kv_.v(l), rs, narrow_tile(rows)},
                             l2_prefetch_qkv_o_ ? &o_v_[l] : nullptr, 0);
@@ -1111,6 +1173,17 @@ template <typename WT> class LlamaEngineT {
                     linear_tile(down_v_[l], act, rows, sm100::StoreTileEpi<sm100::Identity>{tp_y_.data(), H, {}});
                     tp_residual(rows, next_gain, normed_o, rs);
                     mark("gemm_down_allreduce_residual");
+                } else if (chain) {
+                    if (l + 1 < cfg_.num_layers) {
+                        const detail::PagedKV kv1{kv_.k(l + 1), kv_.v(l + 1), table_dev_.data(), blocks_per_seq_, kvh};
+                        chain_launch(l, rows, attn, normed, act, normed_o, act_o, rs, next_gain, 4,
+                                     detail::QkvTileEpi{q_.data(), qh, kvh, rope, tm, kv1, kv_.k(l + 1), kv_.v(l + 1),
+                                                        rs, false});
+                    } else {
+                        chain_launch(l, rows, attn, normed, act, normed_o, act_o, rs, next_gain, 3,
+                                     sm100::NoTileEpi{});
+                    }
+                    mark("decode_chain");
                 } else {
                     linear_tile(o_v_[l], attn, rows,
                                 detail::ResidualTileEpi{hidden_.data(), H, L.post_norm.data(), normed_o, rs,
@@ -1210,6 +1283,16 @@ template <typename WT> class LlamaEngineT {
     detail::TpPeers tp_peers_{};
     bool tp_p2p_ = false;
     std::string failed_; // set when the engine can take no further step
+    // persistent decode chain (OPWORKS_CHAIN=1): CTAs per phase, split-K
+    // partials and counters per phase, the phase barrier
+    bool chain_ = [] {
+        const char *e = std::getenv("OPWORKS_CHAIN");
+        return e && e[0] == '1';
+    }();
+    int chain_active_[4] = {0, 0, 0, 0};
+    TypedDeviceBuffer<float> chain_part_[4];
+    TypedDeviceBuffer<int32_t> chain_cnt_[4];
+    TypedDeviceBuffer<int32_t> chain_sync_;
     // limit of the cross-rank wait of the peer-store reduction
     unsigned long long tp_wait_ns_ = [] {
         const char *e = std::getenv("OPWORKS_TP_WAIT_MS");

@@ -274,6 +274,301 @@ __global__ void __launch_bounds__(192, 1)
     }
 }
 
+// ------------------------------------------------------------ persistent ---
+//
+// The same pair tile (256 features x 256 tokens, cta_group::2) on a
+// persistent grid: one cluster of 2 per SM pair, each looping over tiles
+// w = cluster, cluster + clusters, ... (tile w: feature pair w / ntt, token
+// tile w % ntt, so the clusters running at one time share a few weight
+// tiles and stream the activations from L2). The K-block ring runs on across
+// tiles, and the accumulator is double-buffered in tensor memory (2 x 256
+// columns): the MMAs of tile i + 1 run while the epilogue warps drain
+// tile i in 32-token chunks through a [32][128] fp32 shared tile.
+//
+// Extra protocol over the one-tile kernel: tmem_empty[b] lives in the
+// leader; each epilogue warp of both CTAs arrives on it (remote arrive for
+// rank 1) once its last TMEM load of buffer b has completed, and the leader's
+// MMA thread waits on it before it reuses buffer b.
+template <int kTerms> struct PairPShape {
+    static constexpr int BN = 256;
+    static constexpr uint32_t kABytes = kUmmaM * kUmmaKBytes;
+    static constexpr uint32_t kBBytes = 128 * kUmmaKBytes;
+    static constexpr uint32_t kStageBytes = kABytes + kTerms * kBBytes;
+    static constexpr int kStages = kTerms == 2 ? 4 : 6;
+    static constexpr int kChunk = 32; // tokens per epilogue chunk
+    static constexpr uint32_t kChunkBytes = kChunk * kUmmaM * 4;
+    static constexpr uint32_t kTmemCols = 2 * BN;
+    static constexpr size_t kEpiScratchBytes = 16u * BN;
+    static constexpr size_t kSmemBytes =
+        1024 + static_cast<size_t>(kStages) * kStageBytes + kChunkBytes + 256 + kEpiScratchBytes;
+    static_assert(kSmemBytes <= 227u * 1024u, "shared memory per CTA");
+};
+
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+}
+
+// mbar_wait with cluster-scope acquire (arrivals come from both CTAs).
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t *bar, uint32_t parity) {
+    const uint64_t start = global_timer_ns();
+    while (true) {
+#pragma unroll 1
+        for (int i = 0; i < 32; ++i) {
+            uint32_t done;
+            asm volatile("{\n\t.reg .pred p;\n\t"
+                         "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+                         "selp.u32 %0, 1, 0, p;\n\t}"
+                         : "=r"(done)
+                         : "r"(smem_u32(bar)), "r"(parity)
+                         : "memory");
+            if (done)
+                return true;
+        }
+        if (global_timer_ns() - start > kWaitTimeoutNs)
+            return false;
+    }
+}
+
+template <typename Epi, int kTerms>
+__global__ void __launch_bounds__(192, 1)
+    umma_gemm_pair_persistent_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                                     const __grid_constant__ CUtensorMap tmB_lo, GemmParams p, int ntt, int ntiles,
+                                     Epi epi) {
+    using S = PairPShape<kTerms>;
+    constexpr int kStages = S::kStages;
+    static_assert(is_tile_epilogue<Epi>::value, "the pair GEMM runs tile epilogues");
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    float *ctile = reinterpret_cast<float *>(smem + kStages * S::kStageBytes);
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + kStages * S::kStageBytes + S::kChunkBytes);
+    uint64_t *empty = full + kStages;
+    uint64_t *accum = empty + kStages;    // [2]
+    uint64_t *tmem_empty = accum + 2;     // [2], the leader's are used
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(tmem_empty + 2);
+    void *epi_scratch = smem + kStages * S::kStageBytes + S::kChunkBytes + 256;
+
+    const int warp = threadIdx.x / kWarpSize;
+    const int lane = threadIdx.x % kWarpSize;
+    const uint32_t rank = cluster_rank();
+    const bool leader = rank == 0;
+    const int cid = static_cast<int>(blockIdx.x) / 2, ncl = static_cast<int>(gridDim.x) / 2;
+
+    if (warp == 0 && lane == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&accum[b], 1);
+            mbar_init(&tmem_empty[b], 8); // 4 epilogue warps x 2 CTAs
+        }
+        fence_mbarrier_init();
+        prefetch_tmap(&tmA);
+        prefetch_tmap(&tmB);
+        if constexpr (kTerms == 2)
+            prefetch_tmap(&tmB_lo);
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(tmem_slot, S::kTmemCols);
+        tmem_relinquish_pair();
+    }
+    pdl_trigger();
+    tc_fence_before();
+    cluster_sync_all();
+    tc_fence_after();
+    const uint32_t tmem_d = *tmem_slot;
+    bool ok = true;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            const uint32_t full0 = map_to_rank(smem_u32(full), 0);
+            auto bar = [&](int s) { return full0 + static_cast<uint32_t>(s) * 8u; };
+            int it = 0, armed = 0;
+            bool first = true;
+            for (int w = cid; w < ntiles && ok; w += ncl) {
+                const int f0 = (2 * (w / ntt) + static_cast<int>(rank)) * kUmmaM;
+                const int tb = (w % ntt) * S::BN + static_cast<int>(rank) * 128;
+                auto load_a = [&](int kb, int s) {
+                    tma_load_2d_pair(smem + s * S::kStageBytes, &tmA, bar(s), kb * 64, f0);
+                };
+                auto load_b = [&](int kb, int s) {
+                    uint8_t *st = smem + s * S::kStageBytes;
+                    tma_load_2d_pair(st + S::kABytes, &tmB, bar(s), kb * 64, tb);
+                    if constexpr (kTerms == 2)
+                        tma_load_2d_pair(st + S::kABytes + S::kBBytes, &tmB_lo, bar(s), kb * 64, tb);
+                };
+                int kb = 0;
+                if (first) {
+                    // weights of the first stages stream before the
+                    // programmatic-launch wait; activations after it
+                    const int pre = min(kStages, p.num_kb);
+                    for (; kb < pre; ++kb, ++it) {
+                        if (leader)
+                            mbar_arrive_expect_tx(&full[it % kStages], 2u * S::kStageBytes);
+                        load_a(kb, it % kStages);
+                        ++armed;
+                    }
+                    pdl_wait();
+                    for (int j = 0; j < pre; ++j)
+                        load_b(j, j % kStages);
+                    first = false;
+                }
+                for (; kb < p.num_kb; ++kb, ++it) {
+                    const int s = it % kStages;
+                    if (!mbar_wait(&empty[s], (static_cast<uint32_t>(it / kStages) & 1u) ^ 1u)) {
+                        ok = false;
+                        break;
+                    }
+                    if (leader)
+                        mbar_arrive_expect_tx(&full[s], 2u * S::kStageBytes);
+                    load_a(kb, s);
+                    load_b(kb, s);
+                    ++armed;
+                }
+            }
+            // no copy in flight at exit, on the error path too: the leader's
+            // full barriers count both CTAs' copies, so the leader waits
+            // (bounded) for the last block armed in every slot, and the
+            // final cluster barrier holds the peer until then
+            if (leader)
+                for (int j = (armed > kStages ? armed - kStages : 0); j < armed; ++j)
+                    if (!mbar_wait(&full[j % kStages], static_cast<uint32_t>(j / kStages) & 1u)) {
+                        ok = false;
+                        break;
+                    }
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && leader) {
+            const uint32_t idesc = idesc_make(p.ab_fmt, 2 * kUmmaM, S::BN);
+            int it = 0, lt = 0;
+            for (int w = cid; w < ntiles && ok; w += ncl, ++lt) {
+                const int buf = lt & 1;
+                if (lt >= 2) { // both CTAs' epilogues drained this buffer's previous tile
+                    if (!mbar_wait_cluster(&tmem_empty[buf], (static_cast<uint32_t>(lt >> 1) - 1u) & 1u)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                }
+                const uint32_t dst = tmem_d + static_cast<uint32_t>(buf * S::BN);
+                for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
+                    const int s = it % kStages;
+                    if (!mbar_wait(&full[s], static_cast<uint32_t>(it / kStages) & 1u)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a = smem_u32(smem + s * S::kStageBytes);
+                    const uint32_t b = a + S::kABytes;
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        const uint64_t ad = sdesc_k128(a + 32 * k);
+                        const uint64_t bd = sdesc_k128(b + 32 * k);
+                        const uint32_t acc = (kb > 0 || k > 0) ? 1u : 0u;
+                        if constexpr (kTerms == 2) {
+                            const uint64_t bd_lo = sdesc_k128(b + S::kBBytes + 32 * k);
+                            umma_bf16_pair(dst, ad, bd_lo, idesc, acc);
+                            umma_bf16_pair(dst, ad, bd, idesc, 1u);
+                        } else {
+                            umma_bf16_pair(dst, ad, bd, idesc, acc);
+                        }
+                    }
+                    umma_commit_pair(&empty[s], 0x3);
+                }
+                // also on the error path: the epilogues of both CTAs wait on it
+                umma_commit_pair(&accum[buf], 0x3);
+            }
+            // every MMA issued has completed before tensor memory is freed
+            if (lt > 0 && !mbar_wait(&accum[(lt - 1) & 1], static_cast<uint32_t>((lt - 1) >> 1) & 1u))
+                ok = false;
+        }
+    } else {
+        pdl_wait(); // the outputs may still be read by an earlier kernel
+        const int et = static_cast<int>(threadIdx.x) - 64;
+        const int q = warp & 3;
+        const int col = q * 32 + lane;
+        const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
+        const uint32_t tmem_empty0 = map_to_rank(smem_u32(tmem_empty), 0);
+        int lt = 0;
+        for (int w = cid; w < ntiles; w += ncl, ++lt) {
+            const int buf = lt & 1;
+            const int f0 = (2 * (w / ntt) + static_cast<int>(rank)) * kUmmaM;
+            const int t0 = (w % ntt) * S::BN;
+            const int nfeat = min(kUmmaM, p.n_feat - f0);
+            if (!ok || !mbar_wait_warp(&accum[buf], static_cast<uint32_t>(lt >> 1) & 1u))
+                ok = false; // after a failed wait, no further wait (warp-uniform)
+            tc_fence_after();
+#pragma unroll 1
+            for (int c = 0; c < S::BN; c += S::kChunk) {
+                uint32_t r[2][16];
+                tmem_ld_32x16(tmem_d + lane_base + static_cast<uint32_t>(buf * S::BN + c), r[0]);
+                tmem_ld_32x16(tmem_d + lane_base + static_cast<uint32_t>(buf * S::BN + c + 16), r[1]);
+                tmem_wait_ld();
+                tmem_reg_fence(r[0]);
+                tmem_reg_fence(r[1]);
+                if (c + S::kChunk == S::BN) { // this warp's last read of the buffer
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0)
+                        mbar_arrive_cluster(tmem_empty0 + static_cast<uint32_t>(buf) * 8u);
+                }
+#pragma unroll
+                for (int i = 0; i < S::kChunk; ++i)
+                    ctile[i * kUmmaM + col] = __uint_as_float(r[i >> 4][i & 15]);
+                const int ntok = max(0, min(S::kChunk, p.m_tok - (t0 + c)));
+                const bool run = nfeat > 0 && ntok > 0; // CTA-uniform
+                if (run) {
+                    if constexpr (has_prepare<Epi>::value)
+                        epi.prepare(t0 + c, ntok, f0, nfeat, et, epi_scratch);
+                }
+                epilogue_bar(); // the chunk (and the scratch) are written
+                if (run)
+                    epi(ctile, t0 + c, ntok, f0, nfeat, et, epi_scratch);
+                epilogue_bar(); // the chunk and the scratch are free again
+            }
+        }
+    }
+    if (!ok)
+        atomicExch(p.err, 1);
+    tc_fence_before();
+    cluster_sync_all();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem_d, S::kTmemCols);
+    }
+}
+
+template <typename Epi, int kTerms> inline int gemm_pair_persistent_prepare() {
+    struct Slot {
+        int device = -1, clusters = 0;
+    };
+    static thread_local Slot slot[16];
+    int dev = 0;
+    OPWORKS_CUDA_CHECK(cudaGetDevice(&dev));
+    Slot &sl = slot[dev % 16];
+    if (sl.device != dev) {
+        auto kernel = umma_gemm_pair_persistent_kernel<Epi, kTerms>;
+        const int smem = static_cast<int>(PairPShape<kTerms>::kSmemBytes);
+        OPWORKS_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = dim3(2 * detail::device_facts().sm_count);
+        cfg.blockDim = dim3(192);
+        cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        int n = 0;
+        OPWORKS_CUDA_CHECK(cudaOccupancyMaxActiveClusters(&n, kernel, &cfg));
+        sl.clusters = n > 0 ? n : detail::device_facts().sm_count / 2;
+        sl.device = dev;
+    }
+    return sl.clusters;
+}
+
 template <typename Epi, int kTerms> inline void gemm_pair_prepare_kernel() {
     static thread_local int done_device = -1;
     int dev = 0;
@@ -284,6 +579,16 @@ template <typename Epi, int kTerms> inline void gemm_pair_prepare_kernel() {
                                                 static_cast<int>(PairShape<kTerms>::kSmemBytes)));
         done_device = dev;
     }
+}
+
+// The persistent form for grids of more than one wave of clusters
+// (OPWORKS_PAIR_PERSISTENT=0: the one-tile kernel for every grid).
+inline bool gemm_pair_persistent_enabled() {
+    static const bool on = [] {
+        const char *e = std::getenv("OPWORKS_PAIR_PERSISTENT");
+        return !(e && e[0] == '0');
+    }();
+    return on;
 }
 
 // out via `epi` (a tile epilogue): W [n_feat][k] 16-bit, X = Xhi + Xlo
@@ -310,6 +615,22 @@ inline void gemm_pair_bf16x2(const GemmOperand &W, const GemmOperand &X, int k, 
     const int ftiles = (W.rows + kUmmaM - 1) / kUmmaM;
     const dim3 grid((ftiles + 1) / 2 * 2, (X.rows + PairShape<2>::BN - 1) / PairShape<2>::BN, 1);
     detail::require(grid.y <= 65535, "gemm_pair_bf16x2: grid exceeds the CUDA limits");
+    const int ntiles = static_cast<int>(grid.x / 2 * grid.y);
+    if (gemm_pair_persistent_enabled()) {
+        // persistent grid: the tiles of more than one wave of clusters
+        const int clusters = X.lo ? gemm_pair_persistent_prepare<Epi, 2>() : gemm_pair_persistent_prepare<Epi, 1>();
+        if (ntiles > clusters) {
+            const dim3 pgrid(2 * clusters);
+            const int ntt = static_cast<int>(grid.y);
+            if (X.lo)
+                launch_ex_cluster(umma_gemm_pair_persistent_kernel<Epi, 2>, pgrid, dim3(2, 1, 1), dim3(192),
+                                  PairPShape<2>::kSmemBytes, stream, ta, tb, tb_lo, p, ntt, ntiles, epi);
+            else
+                launch_ex_cluster(umma_gemm_pair_persistent_kernel<Epi, 1>, pgrid, dim3(2, 1, 1), dim3(192),
+                                  PairPShape<1>::kSmemBytes, stream, ta, tb, tb_lo, p, ntt, ntiles, epi);
+            return;
+        }
+    }
     if (X.lo) {
         gemm_pair_prepare_kernel<Epi, 2>();
         launch_ex_cluster(umma_gemm_pair_kernel<Epi, 2>, grid, dim3(2, 1, 1), dim3(192), PairShape<2>::kSmemBytes,

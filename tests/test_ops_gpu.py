@@ -135,7 +135,10 @@ def test_matmul_builder_launcher(ops, ta, tb, act, bias, M, N, K):
 # two-SM (cta_group::2) GEMM of the prefill projections: even pairs of
 # feature tiles, a padded last pair (384 features), ragged token and K tails,
 # a single K block
-@pytest.mark.parametrize("M,N,K", [(512, 512, 1024), (300, 384, 200), (256, 128, 64), (1024, 2048, 2048)])
+# (2300, 2432, 200): 90 pair tiles, more than one wave of clusters, so the
+# persistent form with its double-buffered accumulator runs them
+@pytest.mark.parametrize("M,N,K", [(512, 512, 1024), (300, 384, 200), (256, 128, 64), (1024, 2048, 2048),
+                                   (2300, 2432, 200)])
 def test_gemm_bf16x2_pair_vs_fp64(ops, M, N, K):
     rng = np.random.default_rng(M + 3 * N + 7 * K)
     w = (rng.standard_normal((N, K)) / math.sqrt(K)).astype(np.float32)
@@ -158,7 +161,12 @@ def test_gemm_bf16x2_pair_vs_fp64(ops, M, N, K):
 @pytest.mark.parametrize("kernel,M,N,K", [("gemm_f16x2", 32, 2048, 2048), ("gemm_f16x2", 7, 384, 200),
                                           ("gemm_f16x2", 200, 256, 1024), ("gemm_f16x2_pair", 512, 512, 1024),
                                           ("gemm_f16x2_pair", 300, 384, 200), ("pair_single", 512, 512, 1024),
-                                          ("pair_single", 300, 384, 520)])
+                                          ("pair_single", 300, 384, 520),
+                                          # persistent pair grids: 190 tiles with an odd feature tile count,
+                                          # 128 tiles, and 512 one-K-block tiles (each cluster reuses both
+                                          # accumulator buffers several times)
+                                          ("gemm_f16x2_pair", 1100, 9600, 256), ("pair_single", 2048, 4096, 520),
+                                          ("pair_single", 4096, 8192, 64)])
 def test_gemm_f16x2_vs_fp64(ops, kernel, M, N, K):
     rng = np.random.default_rng(M + 5 * N + 11 * K)
     w = (rng.standard_normal((N, K)) / math.sqrt(K)).astype(np.float32)
