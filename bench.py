@@ -199,6 +199,67 @@ def load_traffic():
 # ----------------------------------------------------------------- our arm
 
 
+def _kernel_group(name, prev_group):
+    """Kernel group of one launch of a decode step, from its (demangled) name."""
+    if "embed" in name:
+        return "embed_rmsnorm"
+    if "attn" in name:
+        return "attention"
+    if "QkvTile" in name:
+        return "gemm_qkv_rope_kv_write"
+    if "SiluMulTile" in name:
+        return "gemm_gate_up_silu"
+    if "ResidualTile" in name:  # O right after attention, down after gate/up
+        return "gemm_o_residual" if prev_group == "attention" else "gemm_down_residual"
+    if "LogitsTile" in name:
+        return "lm_head"
+    if "sample" in name:
+        return "sample"
+    return name.split("(")[0][-40:]
+
+
+def in_graph_kernel_times(step_fn, steps=3):
+    """Per-group device time of the last of `steps` graph-replayed decode
+    steps, from a CUPTI kernel trace (torch.profiler). With programmatic
+    dependent launch a kernel starts before its predecessor ends and waits
+    inside, so each launch is charged from the later of its own start and the
+    previous launch's end to its own end: the charges add up to the step's
+    span. Returns [{kernel, ms_per_step, launches_per_step}] and the span."""
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(steps):
+            step_fn()
+        torch.cuda.synchronize()
+    ev = sorted((e for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA
+                 and e.name and "Memcpy" not in e.name and "Memset" not in e.name),
+                key=lambda e: e.time_range.start)
+    starts = [i for i, e in enumerate(ev) if "embed" in e.name]
+    if not starts:
+        return None
+    last = ev[starts[-1]:]
+    rows, order, prev_end, prev_group = {}, [], None, None
+    for e in last:
+        g = _kernel_group(e.name, prev_group)
+        t0, t1 = e.time_range.start, e.time_range.end
+        charge = t1 - (max(t0, prev_end) if prev_end is not None else t0)
+        if g not in rows:
+            rows[g] = [0.0, 0]
+            order.append(g)
+        rows[g][0] += max(charge, 0.0) / 1e3
+        rows[g][1] += 1
+        prev_end = t1 if prev_end is None else max(prev_end, t1)
+        prev_group = g
+    span_ms = (prev_end - last[0].time_range.start) / 1e3
+    return {"span_ms": round(span_ms, 4),
+            "timing": "CUPTI kernel trace of the graph-replayed step; each launch charged from max(its start, "
+                      "previous launch end) to its end (programmatic-launch overlap counted once)",
+            "groups": [{"kernel": g, "ms_per_step": round(rows[g][0], 4), "launches_per_step": rows[g][1]}
+                       for g in order]}
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -313,6 +374,11 @@ def run_ours(args):
 
     # ---- per-kernel device time of the last step (roofline)
     kernels = eng.profile(BATCH, args.profile_iters)
+    kernels_in_graph = in_graph_kernel_times(decode_once)
+    if kernels_in_graph is not None:
+        for g in kernels_in_graph["groups"]:
+            b = algorithmic_bytes(g["kernel"], rcfg, BATCH, CTX + W + K)
+            g["gbs"] = round(b / (g["ms_per_step"] / 1e3) / 1e9, 1) if b and g["ms_per_step"] > 0 else None
 
     # ---- host-sync-free multi-step decode (extras): MULTI more steps in
     # chunks of 16 graph replays with device-side token feedback, host clock
@@ -471,7 +537,11 @@ def run_ours(args):
             "clocks": clocks.summary(),
             "prefill": {"c3_tokens": BATCH * CTX, "c3_ms": round(prefill_ms, 1),
                         "c3_tok_s": round(BATCH * CTX * groups / (prefill_ms / 1e3), 1), "c4": prefill8k},
-            "kernels": rows, "load_s": round(t_load, 2),
+            "kernels": rows,
+            "kernels_timing": "CUDA events recorded between kernel groups inside the captured step; the event "
+                              "nodes serialise the programmatic-launch overlap, so the groups add up to more "
+                              "than the step (kernels_in_graph has the overlapped step)",
+            "kernels_in_graph": kernels_in_graph, "load_s": round(t_load, 2),
         }
         if cpu is not None:
             line["cpu_baseline"] = cpu

@@ -114,16 +114,22 @@ struct NoTileEpi {
 
 __device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
 
-// Bounded wait until *cnt >= target (acquire, GPU scope).
+// Bounded wait until *cnt >= target (acquire, GPU scope). One thread per
+// CTA polls, with a short sleep between reads: without it the idle CTAs'
+// reads of the one counter queue up at its L2 slice and slow every access
+// of the working CTAs that maps there.
 __device__ __forceinline__ bool chain_grid_wait(const unsigned *cnt, unsigned target) {
     const uint64_t start = global_timer_ns();
     while (true) {
         unsigned v;
-        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(cnt) : "memory");
-        if (v >= target)
+        asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(cnt) : "memory");
+        if (v >= target) {
+            asm volatile("fence.acq_rel.gpu;" ::: "memory");
             return true;
+        }
         if (global_timer_ns() - start > kWaitTimeoutNs)
             return false;
+        __nanosleep(128);
     }
 }
 
@@ -148,7 +154,8 @@ __global__ void __launch_bounds__(192, 1)
     uint64_t *empty = full + S;
     uint64_t *accum = empty + S;   // [2] TMEM buffer filled
     uint64_t *drained = accum + 2; // [2] TMEM buffer read out
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drained + 2);
+    uint64_t *phase_go = drained + 2; // the producer passed a phase barrier
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(phase_go + 1);
     int *last_flag = reinterpret_cast<int *>(tmem_slot + 1);
     void *scratch = smem + S * kChainStageBytes + kChainTileBytes + 512;
 
@@ -163,6 +170,7 @@ __global__ void __launch_bounds__(192, 1)
             mbar_init(&accum[b], 1);
             mbar_init(&drained[b], 128);
         }
+        mbar_init(phase_go, 1);
         fence_mbarrier_init();
         for (int ph = 0; ph < p.nphases; ++ph) {
             prefetch_tmap(&maps.a[ph]);
@@ -216,10 +224,13 @@ __global__ void __launch_bounds__(192, 1)
                     ++armed;
                 }
                 // activations: the previous kernel (phase 0) or phase ph - 1 of every CTA
-                if (ph == 0)
+                if (ph == 0) {
                     pdl_wait();
-                else if (!chain_grid_wait(p.sync, static_cast<unsigned>(G) * ph))
-                    ok = false;
+                } else {
+                    if (!chain_grid_wait(p.sync, static_cast<unsigned>(G) * ph))
+                        ok = false;
+                    mbar_arrive(phase_go); // the epilogue warps wait on it
+                }
                 fence_proxy_async_global();
                 for (int j = 0; j < issued; ++j)
                     load_b(j);
@@ -302,9 +313,10 @@ __global__ void __launch_bounds__(192, 1)
         for (int ph = 0; ph < p.nphases; ++ph) {
             const ChainPhase &P = p.ph[ph];
             if (ph > 0) { // the other CTAs' writes of the previous phase are visible
-                if (et == 0 && ok && !chain_grid_wait(p.sync, static_cast<unsigned>(G) * ph))
+                // the producer passed the grid barrier of this phase (it
+                // alone polls the counter)
+                if (!ok || !mbar_wait_warp(phase_go, static_cast<uint32_t>(ph - 1) & 1u))
                     ok = false;
-                epilogue_bar();
             }
             int lo, hi;
             chain_range(P.tiles, P.num_kb, P.active, c, lo, hi);

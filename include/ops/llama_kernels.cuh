@@ -44,7 +44,10 @@ struct RowSumSq {
     int cols = 0; // H
     float eps = 0.f;
     __device__ __forceinline__ float inv_rms(int64_t row) const {
+        // unrolled so that the tiles' loads are in flight together (the
+        // additions keep their order)
         float s = 0.f;
+#pragma unroll 16
         for (int t = 0; t < tiles; ++t)
             s += part[t * ld + row];
         return rsqrtf(s / static_cast<float>(cols) + eps);
@@ -244,7 +247,7 @@ struct ResidualTileEpi {
         // reduction. The residual rows of kChunk tokens per warp are loaded
         // together (one memory latency per chunk), from the rows staged in
         // shared memory by prepare() when they fit.
-        constexpr int kChunk = 8;
+        constexpr int kChunk = 2;
         const bool staged = preload && ntok <= kPreTok;
         const float *sg = static_cast<const float *>(scratch) + 4 * kPreTok;
         const float *sh = sg + 128;
@@ -343,7 +346,7 @@ struct SiluMulTileEpi {
         const float *inv = static_cast<const float *>(scratch);
         const int warp = tid >> 5, lane = tid & 31;
         const bool vec = 4 * lane + 3 < nfeat;
-        constexpr int kU = 4;
+        constexpr int kU = 2;
         for (int tb = warp; tb < ntok; tb += 4 * kU) {
             float a0[kU], a1[kU];
 #pragma unroll
@@ -441,7 +444,7 @@ struct QkvTileEpi {
         const float2 *cs = reinterpret_cast<const float2 *>(meta + 4 * kPreTok);
         // kChunk items per thread at a time: their cos/sin loads are issued
         // together (one memory latency per chunk)
-        constexpr int kChunk = 16;
+        constexpr int kChunk = 4;
         const int items = ntok * 64;
         for (int base = 0; base < items; base += kChunk * 128) {
             float2 rv[kChunk];

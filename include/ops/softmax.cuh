@@ -63,6 +63,73 @@ __global__ void __launch_bounds__(kThreads) softmax_rows_kernel(const float *in,
     }
 }
 
+// Warp per row, float4 columns (<= 1024 per row), on a grid of a few warps
+// per SM slot that walk the rows with a stride: each warp loads its next row
+// into a second register tile before it finishes the current one, so the
+// stores of one row overlap the loads of the next (a one-row-per-warp grid
+// runs as a single wave in which every warp loads, then computes, then
+// stores at the same time, and HBM reads and writes do not overlap). The
+// arithmetic is one exponential (SFU) per element and one reciprocal per row.
+template <int kSlots>
+__global__ void __launch_bounds__(kThreads) softmax_rows_pipe_kernel(const float *in, float *out, int64_t rows,
+                                                                     int cols) {
+    const int lane = threadIdx.x % kWarpSize;
+    const int64_t warps = static_cast<int64_t>(gridDim.x) * (kThreads / kWarpSize);
+    int64_t row = static_cast<int64_t>(blockIdx.x) * (kThreads / kWarpSize) + threadIdx.x / kWarpSize;
+    const int nv = cols / 4;
+    float4 x[kSlots], y[kSlots];
+    auto load = [&](int64_t r, float4(&v)[kSlots]) {
+        const float4 *src = reinterpret_cast<const float4 *>(in + r * cols);
+#pragma unroll
+        for (int s = 0; s < kSlots; ++s) {
+            const int idx = lane + s * kWarpSize;
+            v[s] = idx < nv ? src[idx] : make_float4(kNegInf, kNegInf, kNegInf, kNegInf);
+        }
+    };
+    if (row < rows)
+        load(row, x);
+    for (; row < rows; row += warps) {
+        if (row + warps < rows)
+            load(row + warps, y);
+        float m = kNegInf;
+#pragma unroll
+        for (int s = 0; s < kSlots; ++s)
+            m = fmaxf(m, fmaxf(fmaxf(x[s].x, x[s].y), fmaxf(x[s].z, x[s].w)));
+        m = warp_reduce<ReduceMax>(m);
+        float sum = 0.f;
+#pragma unroll
+        for (int s = 0; s < kSlots; ++s) {
+            x[s].x = __expf(x[s].x - m);
+            x[s].y = __expf(x[s].y - m);
+            x[s].z = __expf(x[s].z - m);
+            x[s].w = __expf(x[s].w - m);
+            sum += (x[s].x + x[s].y) + (x[s].z + x[s].w);
+        }
+        const float inv = 1.f / warp_reduce<ReduceSum>(sum);
+        float4 *dst = reinterpret_cast<float4 *>(out + row * cols);
+#pragma unroll
+        for (int s = 0; s < kSlots; ++s) {
+            const int idx = lane + s * kWarpSize;
+            if (idx < nv)
+                dst[idx] = make_float4(x[s].x * inv, x[s].y * inv, x[s].z * inv, x[s].w * inv);
+        }
+#pragma unroll
+        for (int s = 0; s < kSlots; ++s)
+            x[s] = y[s];
+    }
+}
+
+// Warps per SM of the row-walking softmax grid (OPWORKS_SOFTMAX_WARPS_PER_SM
+// overrides it).
+inline int softmax_warps_per_sm() {
+    static const int v = [] {
+        const char *e = std::getenv("OPWORKS_SOFTMAX_WARPS_PER_SM");
+        const int w = e ? std::atoi(e) : 16;
+        return w >= 8 && w <= 64 ? w : 16;
+    }();
+    return v;
+}
+
 // Rows longer than the register tile: one online (max, sum) pass, one write pass.
 static __global__ void __launch_bounds__(kThreads) softmax_rows_stream_kernel(const float *in, float *out, int cols) {
     const float *src = in + static_cast<int64_t>(blockIdx.x) * cols;
@@ -115,7 +182,19 @@ inline void softmax(const float *in, float *out, int rows, int cols, cudaStream_
     const detail::RowPlan p = detail::plan_rows(cols, detail::aligned16(in) && detail::aligned16(out));
     if (p.slots == 0)
         launch_async(stream, detail::softmax_rows_stream_kernel, rows, kThreads, in, out, cols);
-    else if (p.group == 32)
+    else if (p.group == 32 && p.vec) {
+        const int per_block = kThreads / kWarpSize;
+        const int64_t cap = static_cast<int64_t>(detail::device_facts().sm_count) * detail::softmax_warps_per_sm() /
+                            per_block;
+        const int64_t need = (static_cast<int64_t>(rows) + per_block - 1) / per_block;
+        const int grid = static_cast<int>(need < cap ? need : cap);
+        switch (p.slots) {
+        case 1: launch_async(stream, detail::softmax_rows_pipe_kernel<1>, grid, kThreads, in, out, int64_t(rows), cols); break;
+        case 2: launch_async(stream, detail::softmax_rows_pipe_kernel<2>, grid, kThreads, in, out, int64_t(rows), cols); break;
+        case 4: launch_async(stream, detail::softmax_rows_pipe_kernel<4>, grid, kThreads, in, out, int64_t(rows), cols); break;
+        default: launch_async(stream, detail::softmax_rows_pipe_kernel<8>, grid, kThreads, in, out, int64_t(rows), cols); break;
+        }
+    } else if (p.group == 32)
         detail::softmax_dispatch<32>(p, in, out, rows, cols, stream);
     else
         detail::softmax_dispatch<kThreads>(p, in, out, rows, cols, stream);
