@@ -58,20 +58,7 @@ struct PrefillTcSmem {
     static constexpr size_t kBytes = kQBytes + kPfStages * kStageBytes + 256 + 4 * 128 * 4;
 };
 
-// Shared-memory descriptor of an MN-major tf32 operand: MN-major 32-bit
-// operands take the 128-byte swizzle with 32-byte atomicity (layout type 1,
-// SWIZZLE_128B_BASE32B; atoms of 4 K-rows x 128 bytes along MN, as a TMA load
-// with CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B writes them): `lbo` = bytes between
-// atoms adjacent along MN, `sbo` = bytes between 4-row groups along K.
-__device__ __forceinline__ uint64_t sdesc_mn128_32b(uint32_t smem_addr, uint32_t lbo, uint32_t sbo) {
-    uint64_t d = 0;
-    d |= static_cast<uint64_t>((smem_addr & 0x3FFFFu) >> 4);
-    d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
-    d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
-    d |= static_cast<uint64_t>(1u) << 46;
-    d |= static_cast<uint64_t>(1u) << 61;
-    return d;
-}
+using sm100::sdesc_mn128_32b;
 
 // D[tmem] (+)= A[tmem] * B[smem desc], tf32 (A from tensor memory, K-major).
 __device__ __forceinline__ void umma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,

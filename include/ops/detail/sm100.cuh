@@ -215,6 +215,21 @@ __device__ __forceinline__ uint64_t sdesc_k128(uint32_t smem_addr) {
 
 // Instruction descriptor: D fp32, A/B format (kind::f16: 0 = fp16, 1 = bf16;
 // kind::tf32: 2), both K-major, N >> 3 at [17,23), M >> 4 at [24,29).
+// Shared-memory descriptor of an MN-major tf32 operand: MN-major 32-bit
+// operands take the 128-byte swizzle with 32-byte atomicity (layout type 1,
+// SWIZZLE_128B_BASE32B; atoms of 4 K-rows x 128 bytes along MN, as a TMA load
+// with CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B writes them): `lbo` = bytes between
+// atoms adjacent along MN, `sbo` = bytes between 4-row groups along K.
+__device__ __forceinline__ uint64_t sdesc_mn128_32b(uint32_t smem_addr, uint32_t lbo, uint32_t sbo) {
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((smem_addr & 0x3FFFFu) >> 4);
+    d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+    d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
+    d |= static_cast<uint64_t>(1u) << 46;
+    d |= static_cast<uint64_t>(1u) << 61;
+    return d;
+}
+
 __host__ __device__ constexpr uint32_t idesc_make(uint32_t ab_format, int m, int n) {
     return (1u << 4) | (ab_format << 7) | (ab_format << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
            (static_cast<uint32_t>(m >> 4) << 24);
@@ -243,8 +258,11 @@ inline PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 // 2-D tiled map of 16-bit (word16) or 32-bit elements. Tiled copies move
 // bytes without conversion, so 16-bit words of either format (bf16 or fp16)
 // use the one 16-bit map type.
+// swz: CU_TENSOR_MAP_SWIZZLE_128B for K-major operands; MN-major 32-bit
+// operands take CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B (sdesc_mn128_32b)
 inline CUtensorMap make_tmap_2d(const void *base, bool word16, uint64_t cols, uint64_t rows, uint64_t ld,
-                                uint32_t box_cols, uint32_t box_rows) {
+                                uint32_t box_cols, uint32_t box_rows,
+                                CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B) {
     const size_t elem = word16 ? 2 : 4;
     detail::require(reinterpret_cast<uintptr_t>(base) % 16 == 0, "TMA base must be 16-byte aligned");
     detail::require((ld * elem) % 16 == 0, "TMA row stride must be a multiple of 16 bytes");
@@ -257,8 +275,8 @@ inline CUtensorMap make_tmap_2d(const void *base, bool word16, uint64_t cols, ui
     const cuuint32_t estr[2] = {1, 1};
     const CUresult r = tensor_map_encoder()(
         &tm, word16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void *>(base),
-        dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     detail::require(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed");
     return tm;
 }

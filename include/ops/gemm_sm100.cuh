@@ -36,11 +36,16 @@
 #include <cooperative_groups.h>
 #include <cuda_bf16.h>
 
+#include "detail/operand_prep.cuh"
 #include "detail/sm100.cuh"
 
 namespace opworks::sm100 {
 
-enum class GemmKind { kBF16, kTF32x3, kBF16x2 };
+// kTF32x3S: the split-precision GEMM on raw fp32 operands — the A (feature)
+// operand MN-major straight from a row-major [contraction][features] matrix,
+// the B (token) operand K-major — split into tf32 hi / lo in shared memory by
+// four converter warps (no pre-pass, no scratch).
+enum class GemmKind { kBF16, kTF32x3, kBF16x2, kTF32x3S };
 
 struct GemmParams {
     float *out;           // [splits][m_tok][ldo]
@@ -124,13 +129,63 @@ __device__ __forceinline__ float apply_epilogue(const Epi &epi, float v, int tok
         return epi(v);
 }
 
+// Split-K reduction of a cluster's partial tiles [tokens][128] through
+// distributed shared memory: this CTA's token slice [tl0, tl1) summed over
+// the kN CTAs in rank order (0 + p0 + p1 + ..., the order of the generic
+// loop) into rtile. Clusters of 2 and 4: several items per thread are
+// loaded together so that eight remote loads are in flight (clusters of 8
+// already have eight per item; the batched form measured slower there).
+template <int kN, typename Cluster>
+__device__ __forceinline__ void cluster_reduce_slice(Cluster &cluster, const float *ptile, float *rtile, int tl0,
+                                                     int tl1, int et) {
+    constexpr int kItems = kN >= 8 ? 1 : 8 / kN;
+    constexpr int kF4 = kUmmaM / 4; // float4 per token row
+    const int n = (tl1 - tl0) * kF4;
+    const float4 *src[kN];
+#pragma unroll
+    for (int r = 0; r < kN; ++r)
+        src[r] = reinterpret_cast<const float4 *>(cluster.map_shared_rank(ptile, r));
+    for (int i0 = et; i0 < n; i0 += 128 * kItems) {
+        float4 v[kItems][kN];
+#pragma unroll
+        for (int i = 0; i < kItems; ++i) {
+            const int idx = i0 + i * 128;
+            const int t = tl0 + idx / kF4, c4 = idx % kF4;
+#pragma unroll
+            for (int r = 0; r < kN; ++r)
+                if (idx < n)
+                    v[i][r] = src[r][t * kF4 + c4];
+        }
+#pragma unroll
+        for (int i = 0; i < kItems; ++i) {
+            const int idx = i0 + i * 128;
+            if (idx < n) {
+                float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                for (int r = 0; r < kN; ++r) {
+                    acc.x += v[i][r].x;
+                    acc.y += v[i][r].y;
+                    acc.z += v[i][r].z;
+                    acc.w += v[i][r].w;
+                }
+                reinterpret_cast<float4 *>(rtile)[idx] = acc;
+            }
+        }
+    }
+}
+
 template <GemmKind kKind, int BN> struct GemmShape {
-    static constexpr bool kSplit3 = kKind == GemmKind::kTF32x3;
+    static constexpr bool kSplit3 = kKind == GemmKind::kTF32x3 || kKind == GemmKind::kTF32x3S;
+    // hi / lo halves made in shared memory by warps 6-9 (kTF32x3S)
+    static constexpr bool kConvert = kKind == GemmKind::kTF32x3S;
+    static constexpr int kThreads = kConvert ? 320 : 192;
     static constexpr bool kSplitB = kKind == GemmKind::kBF16x2; // B_lo tile, A shared
     static constexpr uint32_t kABytes = kUmmaM * kUmmaKBytes;
     static constexpr uint32_t kBBytes = BN * kUmmaKBytes;
     static constexpr uint32_t kStageBytes =
         kSplit3 ? 2u * (kABytes + kBBytes) : (kSplitB ? kABytes + 2u * kBBytes : kABytes + kBBytes);
+    // bytes the TMA brings per stage (kConvert: the hi halves only)
+    static constexpr uint32_t kLoadBytes = kConvert ? kABytes + kBBytes : kStageBytes;
     // narrow token tiles (decode) run two CTAs per SM: the hardware keeps two
     // tensor-memory CTAs of this size resident (the occupancy calculator
     // reports one for any kernel that allocates tensor memory), and a second
@@ -151,11 +206,11 @@ template <GemmKind kKind, int BN> struct GemmShape {
     static constexpr size_t kEpiScratchBytes = BN <= 64 ? kEpiScratchNarrow : (16u * BN > 2048u ? 16u * BN : 2048u);
     static constexpr size_t kSmemBytes = 1024 + static_cast<size_t>(kStages) * kStageBytes + 256 + kEpiScratchBytes;
     static_assert(kStages >= 2, "GEMM tile does not fit two pipeline stages");
-    static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N must be a multiple of 16 in [16, 256]");
+    static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "token tiles are multiples of 32 in [32, 256] (UMMA N)");
 };
 
 template <GemmKind kKind, int BN, typename Epi>
-__global__ void __launch_bounds__(192, GemmShape<kKind, BN>::kCtasPerSm)
+__global__ void __launch_bounds__(GemmShape<kKind, BN>::kThreads, GemmShape<kKind, BN>::kCtasPerSm)
     umma_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmA_lo, const __grid_constant__ CUtensorMap tmB_lo,
                      GemmParams p, Epi epi) {
@@ -174,7 +229,9 @@ __global__ void __launch_bounds__(192, GemmShape<kKind, BN>::kCtasPerSm)
     uint64_t *accum = empty + kStages;
     uint64_t *ready = accum + 1;   // [2] promotion buffers filled (split path)
     uint64_t *drained = ready + 2; // [2] promotion buffers read (split path)
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drained + 2);
+    uint64_t *conv = drained + 2;  // [kStages] stage split into hi / lo (kConvert)
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(conv + kStages);
+    static_assert((3 * kStages + 5) * 8 + 4 <= 256, "barriers fit their 256-byte slot");
     void *epi_scratch = smem + kStages * S::kStageBytes + 256;
 
     const int warp = threadIdx.x / kWarpSize;
@@ -195,6 +252,9 @@ __global__ void __launch_bounds__(192, GemmShape<kKind, BN>::kCtasPerSm)
         mbar_init(&ready[1], 1);
         mbar_init(&drained[0], 128);
         mbar_init(&drained[1], 128);
+        if constexpr (S::kConvert)
+            for (int s = 0; s < kStages; ++s)
+                mbar_init(&conv[s], 4); // one arrival per converter warp
         fence_mbarrier_init();
         prefetch_tmap(&tmA);
         prefetch_tmap(&tmB);
@@ -224,22 +284,30 @@ __global__ void __launch_bounds__(192, GemmShape<kKind, BN>::kCtasPerSm)
             auto load_a = [&](int kb, int s) {
                 uint8_t *st = smem + s * S::kStageBytes;
                 const int kc = kb * S::kKElems;
-                tma_load_2d(st, &tmA, &full[s], kc, f0);
-                if constexpr (S::kSplit3)
-                    tma_load_2d(st + S::kABytes + S::kBBytes, &tmA_lo, &full[s], kc, f0);
+                if constexpr (S::kConvert) {
+                    // MN-major: four 32-feature x 32-contraction boxes
+                    // ([32 contraction rows][32 features] each, 4 KB apart)
+#pragma unroll
+                    for (int j = 0; j < 4; ++j)
+                        tma_load_2d(st + j * 4096, &tmA, &full[s], f0 + 32 * j, kc);
+                } else {
+                    tma_load_2d(st, &tmA, &full[s], kc, f0);
+                    if constexpr (S::kSplit3)
+                        tma_load_2d(st + S::kABytes + S::kBBytes, &tmA_lo, &full[s], kc, f0);
+                }
             };
             auto load_b = [&](int kb, int s) {
                 uint8_t *st = smem + s * S::kStageBytes;
                 const int kc = kb * S::kKElems;
                 tma_load_2d(st + S::kABytes, &tmB, &full[s], kc, t0);
-                if constexpr (S::kSplit3)
+                if constexpr (S::kSplit3 && !S::kConvert)
                     tma_load_2d(st + 2 * S::kABytes + S::kBBytes, &tmB_lo, &full[s], kc, t0);
                 if constexpr (S::kSplitB)
                     tma_load_2d(st + S::kABytes + S::kBBytes, &tmB_lo, &full[s], kc, t0);
             };
             const int pre = min(kStages, kb_end - kb_begin);
             for (int j = 0; j < pre; ++j) {
-                mbar_arrive_expect_tx(&full[j], S::kStageBytes);
+                mbar_arrive_expect_tx(&full[j], S::kLoadBytes);
                 load_a(kb_begin + j, j);
             }
             // this CTA's share of the next kernel's stream, in 16-byte
@@ -266,7 +334,7 @@ __global__ void __launch_bounds__(192, GemmShape<kKind, BN>::kCtasPerSm)
                     ok = false;
                     break;
                 }
-                mbar_arrive_expect_tx(&full[s], S::kStageBytes);
+                mbar_arrive_expect_tx(&full[s], S::kLoadBytes);
                 load_a(kb, s);
                 load_b(kb, s);
             }
@@ -281,7 +349,9 @@ __global__ void __launch_bounds__(192, GemmShape<kKind, BN>::kCtasPerSm)
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            const uint32_t idesc = idesc_make(S::kSplit3 ? kFmtTF32 : p.ab_fmt, kUmmaM, BN);
+            // kConvert: A (features) MN-major (instruction descriptor bit 15)
+            const uint32_t idesc =
+                idesc_make(S::kSplit3 ? kFmtTF32 : p.ab_fmt, kUmmaM, BN) | (S::kConvert ? (1u << 15) : 0u);
             int it = 0;
             for (int kb = kb_begin; kb < kb_end; ++kb, ++it) {
                 const int s = it % kStages;
@@ -297,20 +367,27 @@ __global__ void __launch_bounds__(192, GemmShape<kKind, BN>::kCtasPerSm)
                     }
                     tc_fence_after();
                 }
-                if (!mbar_wait(&full[s], ph)) {
+                // kConvert: the stage is also split into hi / lo
+                if (!mbar_wait(S::kConvert ? &conv[s] : &full[s], ph)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
                 const uint32_t a = smem_u32(smem + s * S::kStageBytes);
                 const uint32_t b = a + S::kABytes;
+                // MN-major A: a K step is 8 contraction rows (1 KB) of the four
+                // 4 KB feature boxes; atoms 4 rows x 128 bytes
+                auto a_desc = [&](uint32_t base, int k) {
+                    return S::kConvert ? sdesc_mn128_32b(base + 1024u * static_cast<uint32_t>(k), 4096u, 512u)
+                                       : sdesc_k128(base + 32u * static_cast<uint32_t>(k));
+                };
 #pragma unroll
                 for (int k = 0; k < 4; ++k) { // four 32-byte K steps per 128-byte block
-                    const uint64_t ad = sdesc_k128(a + 32 * k);
+                    const uint64_t ad = a_desc(a, k);
                     const uint64_t bd = sdesc_k128(b + 32 * k);
                     if constexpr (S::kSplit3) {
                         const uint32_t acc = (first_in_group && k == 0) ? 0u : 1u;
-                        const uint64_t ad_lo = sdesc_k128(a + S::kABytes + S::kBBytes + 32 * k);
+                        const uint64_t ad_lo = a_desc(a + S::kABytes + S::kBBytes, k);
                         const uint64_t bd_lo = sdesc_k128(a + 2 * S::kABytes + S::kBBytes + 32 * k);
                         umma_tf32(dst, ad, bd_lo, idesc, acc);
                         umma_tf32(dst, ad_lo, bd, idesc, 1u);
@@ -332,7 +409,7 @@ __global__ void __launch_bounds__(192, GemmShape<kKind, BN>::kCtasPerSm)
             if (!S::kSplit3)
                 umma_commit(accum);
         }
-    } else {
+    } else if (warp < 6) {
         pdl_wait(); // the output may still be read by an earlier kernel
         const int q = warp & 3; // TMEM lane quarter this warp may access
         const int feat = f0 + q * 32 + lane;
@@ -391,21 +468,54 @@ __global__ void __launch_bounds__(192, GemmShape<kKind, BN>::kCtasPerSm)
             ok = false;
         }
         tc_fence_after();
+        // two 16-column loads per wait (BN is a multiple of 32)
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 16) {
-            uint32_t r[16];
-            tmem_ld_32x16(tmem_d + lane_base + static_cast<uint32_t>(c), r);
+        for (int c = 0; c < BN; c += 32) {
+            uint32_t r[2][16];
+            tmem_ld_32x16(tmem_d + lane_base + static_cast<uint32_t>(c), r[0]);
+            tmem_ld_32x16(tmem_d + lane_base + static_cast<uint32_t>(c + 16), r[1]);
             tmem_wait_ld();
+            tmem_reg_fence(r[0]);
+            tmem_reg_fence(r[1]);
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
+            for (int i = 0; i < 32; ++i) {
                 const int tok = t0 + c + i;
+                const float v = __uint_as_float(r[i >> 4][i & 15]);
                 if constexpr (kTileEpi)
-                    ptile[(c + i) * kUmmaM + col] = __uint_as_float(r[i]);
+                    ptile[(c + i) * kUmmaM + col] = v;
                 else if (feat_ok && tok < p.m_tok)
-                    out[static_cast<int64_t>(tok) * p.ldo + feat] =
-                        apply_epilogue(epi, __uint_as_float(r[i]), tok, feat);
+                    out[static_cast<int64_t>(tok) * p.ldo + feat] = apply_epilogue(epi, v, tok, feat);
             }
         }
+        }
+    } else if constexpr (S::kConvert) {
+        // warps 6-9: each landed stage's fp32 values x stay in place as the
+        // hi halves (the tensor cores read a 32-bit operand as tf32 by
+        // dropping its 13 low mantissa bits) and lo = x - that truncation
+        // (exact in fp32) goes to the lo half of the stage; the layout does
+        // not matter (the same element-wise map over both swizzled tiles).
+        // Infinities and NaNs give a NaN lo, as in the pre-pass split.
+        const int ct = threadIdx.x - 192;
+        int it = 0;
+        for (int kb = kb_begin; kb < kb_end; ++kb, ++it) {
+            const int s = it % kStages;
+            if (!mbar_wait_warp(&full[s], static_cast<uint32_t>(it / kStages) & 1u)) {
+                ok = false;
+                break;
+            }
+            const float4 *hi = reinterpret_cast<const float4 *>(smem + s * S::kStageBytes);
+            float4 *lo = reinterpret_cast<float4 *>(smem + s * S::kStageBytes + S::kABytes + S::kBBytes);
+            constexpr int kVecs = static_cast<int>((S::kABytes + S::kBBytes) / 16);
+            auto low = [](float x) { return x - __uint_as_float(__float_as_uint(x) & 0xffffe000u); };
+#pragma unroll 4
+            for (int i = ct; i < kVecs; i += 128) {
+                const float4 x = hi[i];
+                lo[i] = make_float4(low(x.x), low(x.y), low(x.z), low(x.w));
+            }
+            fence_proxy_async_smem(); // generic writes, read next by the tensor cores
+            __syncwarp();
+            if (lane == 0)
+                mbar_arrive(&conv[s]);
         }
     }
     if constexpr (kTileEpi) {
@@ -430,31 +540,37 @@ __global__ void __launch_bounds__(192, GemmShape<kKind, BN>::kCtasPerSm)
         }
         const float *src = ptile;
         if (nsplit > 1) {
-            if (warp >= 2) {
+            if (warp >= 2 && warp < 6) {
                 const int et = threadIdx.x - 64;
                 cg::cluster_group cluster = cg::this_cluster();
-                for (int idx = et; idx < (tl1 - tl0) * (kUmmaM / 4); idx += 128) {
-                    const int t = tl0 + idx / (kUmmaM / 4), c4 = idx % (kUmmaM / 4);
-                    // eight remote loads in flight at a time, summed in rank
-                    // order
-                    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-                    for (int r0 = 0; r0 < nsplit; r0 += 8) {
-                        float4 v[8];
+                switch (nsplit) {
+                case 2: cluster_reduce_slice<2>(cluster, ptile, rtile, tl0, tl1, et); break;
+                case 4: cluster_reduce_slice<4>(cluster, ptile, rtile, tl0, tl1, et); break;
+                default:
+                    // other cluster sizes: one item at a time, eight remote
+                    // loads in flight, summed in rank order
+                    for (int idx = et; idx < (tl1 - tl0) * (kUmmaM / 4); idx += 128) {
+                        const int t = tl0 + idx / (kUmmaM / 4), c4 = idx % (kUmmaM / 4);
+                        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+                        for (int r0 = 0; r0 < nsplit; r0 += 8) {
+                            float4 v[8];
 #pragma unroll
-                        for (int j = 0; j < 8; ++j)
-                            if (r0 + j < nsplit)
-                                v[j] = reinterpret_cast<const float4 *>(
-                                    cluster.map_shared_rank(ptile, r0 + j))[t * (kUmmaM / 4) + c4];
+                            for (int j = 0; j < 8; ++j)
+                                if (r0 + j < nsplit)
+                                    v[j] = reinterpret_cast<const float4 *>(
+                                        cluster.map_shared_rank(ptile, r0 + j))[t * (kUmmaM / 4) + c4];
 #pragma unroll
-                        for (int j = 0; j < 8; ++j)
-                            if (r0 + j < nsplit) {
-                                acc.x += v[j].x;
-                                acc.y += v[j].y;
-                                acc.z += v[j].z;
-                                acc.w += v[j].w;
-                            }
+                            for (int j = 0; j < 8; ++j)
+                                if (r0 + j < nsplit) {
+                                    acc.x += v[j].x;
+                                    acc.y += v[j].y;
+                                    acc.z += v[j].z;
+                                    acc.w += v[j].w;
+                                }
+                        }
+                        reinterpret_cast<float4 *>(rtile)[idx] = acc;
                     }
-                    reinterpret_cast<float4 *>(rtile)[(t - tl0) * (kUmmaM / 4) + c4] = acc;
+                    break;
                 }
                 epilogue_bar();
                 if (groups > 1) {
@@ -498,7 +614,7 @@ __global__ void __launch_bounds__(192, GemmShape<kKind, BN>::kCtasPerSm)
             src = rtile;
             cluster_arrive(); // done reading the peers' tiles; the epilogue runs under the barrier
         }
-        if (warp >= 2 && (groups == 1 || run_epilogue)) {
+        if (warp >= 2 && warp < 6 && (groups == 1 || run_epilogue)) {
             const int tb = nsplit > 1 ? tl0 : 0;
             const int ntok = max(0, min(nsplit > 1 ? tl1 - tl0 : BN, p.m_tok - (t0 + tb)));
             epi(src, t0 + tb, ntok, f0, min(kUmmaM, p.n_feat - f0), static_cast<int>(threadIdx.x) - 64, epi_scratch);
@@ -545,10 +661,11 @@ inline void gemm_launch(const CUtensorMap &a, const CUtensorMap &b, const CUtens
                         "tile epilogue: at most 16 K splits per cluster, splits a multiple of the cluster");
         detail::require(p.splits == csz || (p.red_ws != nullptr && p.red_cnt != nullptr),
                         "tile epilogue: grouped split K needs a workspace");
-        launch_ex_cluster(umma_gemm_kernel<kKind, BN, Epi>, grid, dim3(1, 1, csz), dim3(192), S::kSmemBytes,
-                          stream, a, b, a_lo, b_lo, p, epi);
+        launch_ex_cluster(umma_gemm_kernel<kKind, BN, Epi>, grid, dim3(1, 1, csz), dim3(S::kThreads),
+                          S::kSmemBytes, stream, a, b, a_lo, b_lo, p, epi);
     } else {
-        launch_ex(umma_gemm_kernel<kKind, BN, Epi>, grid, dim3(192), S::kSmemBytes, stream, a, b, a_lo, b_lo, p, epi);
+        launch_ex(umma_gemm_kernel<kKind, BN, Epi>, grid, dim3(S::kThreads), S::kSmemBytes, stream, a, b, a_lo, b_lo,
+                  p, epi);
     }
 }
 
@@ -707,6 +824,58 @@ inline void gemm_tf32x3(const GemmOperand &A, const GemmOperand &B, int k, float
         }
     }
     gemm_tn<GemmKind::kTF32x3, Epi>(A, B, k, C, ldc, 1, 0, stream, epi);
+}
+
+// C[m][k] = epi(sum_n A[m][n] * B[n][k]) on raw row-major fp32 matrices
+// (A [M][N] row stride lda, B [N][K] row stride ldb): kTF32x3S, the
+// split-precision GEMM that splits both operands into tf32 hi / lo in shared
+// memory, with B's rows read as the MN-major feature operand (no transpose,
+// no scratch). A, B 16-byte aligned and lda, ldb multiples of 4; grids of
+// fewer tiles than half the SMs split K over a cluster as gemm_tf32x3 does.
+template <typename Epi>
+inline void gemm_tf32x3s(const float *A, int64_t lda, const float *B, int64_t ldb, int M, int N, int K, float *C,
+                         int64_t ldc, cudaStream_t stream, const Epi &epi = {}) {
+    detail::require(M > 0 && N > 0 && K > 0, "gemm_tf32x3s: empty operand");
+    GemmParams p;
+    p.out = C;
+    p.ldo = ldc;
+    p.split_stride = 0;
+    p.n_feat = K;
+    p.m_tok = M;
+    p.num_kb = (N + 31) / 32;
+    p.splits = 1;
+    p.err = device_error_word();
+    const int sms = detail::device_facts().sm_count;
+    const int ftiles = (K + kUmmaM - 1) / kUmmaM;
+    int bn = gemm_pick_bn(GemmKind::kTF32x3S, M);
+    int splits = 1;
+    if (M > 64 && ftiles * ((M + 127) / 128) < sms / 2) {
+        splits = sms / (ftiles * ((M + 127) / 128));
+        splits = splits > kMaxClusterSplits ? kMaxClusterSplits : splits;
+        splits = splits > p.num_kb / 8 ? p.num_kb / 8 : splits;
+        splits = splits < 1 ? 1 : splits;
+    }
+    if (splits == 1)
+        while (bn > 32 && ftiles * ((M + bn - 1) / bn) < sms)
+            bn /= 2;
+    else
+        bn = 128;
+    const CUtensorMap ta = make_tmap_2d(B, false, static_cast<uint64_t>(K), static_cast<uint64_t>(N),
+                                        static_cast<uint64_t>(ldb), 32, 32, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
+    const CUtensorMap tb = make_tmap_2d(A, false, static_cast<uint64_t>(N), static_cast<uint64_t>(M),
+                                        static_cast<uint64_t>(lda), 32, static_cast<uint32_t>(bn));
+    if (splits > 1) {
+        p.splits = splits;
+        p.out = nullptr;
+        gemm_launch<GemmKind::kTF32x3S, 128, StoreTileEpi<Epi>>(ta, tb, ta, tb, p, StoreTileEpi<Epi>{C, ldc, epi},
+                                                                 stream);
+        return;
+    }
+    switch (bn) {
+    case 32: gemm_launch<GemmKind::kTF32x3S, 32, Epi>(ta, tb, ta, tb, p, epi, stream); break;
+    case 64: gemm_launch<GemmKind::kTF32x3S, 64, Epi>(ta, tb, ta, tb, p, epi, stream); break;
+    default: gemm_launch<GemmKind::kTF32x3S, 128, Epi>(ta, tb, ta, tb, p, epi, stream); break;
+    }
 }
 
 } // namespace opworks::sm100

@@ -231,14 +231,18 @@ struct ResidualTileEpi {
         const bool col_ok = c < nfeat;
         sg[c] = (gain && col_ok) ? gain[f0 + c] : 0.f;
         const float *col = hidden + static_cast<int64_t>(tok0) * ld + f0 + c;
-        float hv[kPreTok];
+        // four rows in flight per step (a decode slice is one step): short
+        // code, few instruction-cache lines on a cold SM
+        for (int j0 = 0; j0 < ntok; j0 += 4) {
+            float hv[4];
 #pragma unroll
-        for (int j = 0; j < kPreTok; ++j)
-            hv[j] = (col_ok && j < ntok) ? col[static_cast<int64_t>(j) * ld] : 0.f;
+            for (int u = 0; u < 4; ++u)
+                hv[u] = (col_ok && j0 + u < ntok) ? col[static_cast<int64_t>(j0 + u) * ld] : 0.f;
 #pragma unroll
-        for (int j = 0; j < kPreTok; ++j)
-            if (j < ntok)
-                sh[j * 128 + c] = hv[j];
+            for (int u = 0; u < 4; ++u)
+                if (j0 + u < ntok)
+                    sh[(j0 + u) * 128 + c] = hv[u];
+        }
     }
     __device__ __forceinline__ void operator()(const float *tile, int tok0, int ntok, int f0, int nfeat, int tid,
                                                void *scratch) const {

@@ -7,11 +7,15 @@
 //
 // B200 path: split-precision TF32 on the tcgen05 tensor cores (three
 // kind::tf32 MMAs per K step on hi/lo operand halves), so the fp32 API keeps
-// fp32-class accuracy (~1e-6 relative) instead of plain TF32's ~1e-3. A
-// pre-pass writes the hi/lo halves of A and of B^T (B is N-major; the GEMM
-// wants both operands K-major) into stream-ordered scratch; the GEMM then
-// streams them through TMA into a 128 x BN TMEM accumulator and applies the
-// epilogue functor on the way out. Grids of few 128 x 128 tiles (e.g. 1024 x
+// fp32-class accuracy (~1e-6 relative) instead of plain TF32's ~1e-3. When
+// the rows of A and B are 16-byte aligned (N and K multiples of 4) the GEMM
+// (sm100::gemm_tf32x3s) loads both matrices as they are — B's rows as an
+// MN-major operand — and four converter warps split each staged tile into
+// hi/lo in shared memory: asynchronous, allocation-free, one launch.
+// Otherwise a pre-pass writes aligned hi/lo halves of A and of B^T into
+// stream-ordered scratch for the K-major kernel. Either way the GEMM streams
+// through TMA into a 128 x BN TMEM accumulator and applies the epilogue
+// functor on the way out. Grids of few 128 x 128 tiles (e.g. 1024 x
 // 1024 outputs) split K across a thread-block cluster and reduce the partial
 // tiles on chip before the epilogue (sm100::gemm_tf32x3).
 
@@ -40,6 +44,15 @@ inline void mat_mul(const float *A, const float *B, float *C, int M, int N, int 
                      out_elems, epilogue);
         return;
     }
+    if (N % 4 == 0 && K % 4 == 0 && reinterpret_cast<uintptr_t>(A) % 16 == 0 &&
+        reinterpret_cast<uintptr_t>(B) % 16 == 0) {
+        // rows of A and B are 16-byte aligned: the GEMM reads both as they
+        // are and splits them into tf32 hi / lo in shared memory (no
+        // pre-pass, no scratch, nothing allocated)
+        sm100::gemm_tf32x3s<Epilogue>(A, N, B, K, M, N, K, C, K, stream, epilogue);
+        return;
+    }
+    // unaligned rows: a pre-pass writes 16-byte-aligned hi / lo copies
     const int64_t ld = detail::round_up(N, 4); // 16-byte row stride for TMA
     const size_t a_bytes = sizeof(float) * static_cast<size_t>(M) * ld;
     const size_t b_bytes = sizeof(float) * static_cast<size_t>(K) * ld;

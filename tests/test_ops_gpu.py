@@ -99,6 +99,28 @@ def test_mat_mul_3xtf32_vs_oracle(ops, M, N, K):
     close(host(dc), oracle.mat_mul(a, b, epilogue=1))
 
 
+# Rows of A and B 16-byte aligned (N, K multiples of 4): the kTF32x3S kernel
+# reads both matrices as they are and splits them into tf32 hi / lo in shared
+# memory. Ragged feature and token tiles, a contraction tail shorter than one
+# 32-element block (1028), a tiny grid with narrowed token tiles, and a
+# cluster split-K plan (200 x 4096 x 300: 6 tiles, 8 splits). B is unscaled,
+# so the products are O(1) and a single tf32 pass (no lo terms) would miss
+# the 1e-5 tolerance by two orders of magnitude.
+@pytest.mark.parametrize("M,N,K", [(4, 8, 4), (100, 36, 44), (513, 1028, 260), (200, 4096, 300), (2000, 512, 2052)])
+def test_mat_mul_in_kernel_split(ops, M, N, K):
+    rng = np.random.default_rng(M * 3 + N * 5 + K)
+    a = (rng.standard_normal((M, N)) / math.sqrt(N)).astype(np.float32)
+    b = rng.standard_normal((N, K)).astype(np.float32)
+    da, db, dc = dev(a), dev(b), torch.full((M, K), float("nan"), device="cuda")
+    ops.mat_mul(da, db, dc, M, N, K, 1, 0.0, 0)  # ReLU epilogue
+    sync(ops)
+    close(host(dc), oracle.mat_mul(a, b, epilogue=1))
+    # the identity epilogue on the same data
+    ops.mat_mul(da, db, dc, M, N, K, 0, 0.0, 0)
+    sync(ops)
+    close(host(dc), a.astype(np.float64) @ b)
+
+
 def test_mat_mul_framework_cases(ops):
     a = np.array([i % 7 - 3 for i in range(15)], np.float32).reshape(3, 5)
     b = np.array([i % 5 - 2 for i in range(35)], np.float32).reshape(5, 7)
