@@ -56,6 +56,9 @@ class Timer:
         times = []
         for _ in range(iters):
             torch.sum(self.flush_buf, dim=0, keepdim=True, out=self.flush_out)
+            # a ~50 us device spin after the flush keeps the host's launch of
+            # fn ahead of the GPU, so the events bracket device time only
+            torch.cuda._sleep(100_000)
             s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             s.record()
             fn()
@@ -71,11 +74,13 @@ def _ref_ops():
     lib = ctypes.CDLL(REF_OPS)
     P, I, F = ctypes.c_void_p, ctypes.c_int, ctypes.c_float
     sigs = {"ref_softmax": [P, P, I, I], "ref_layer_norm": [P, P, P, P, I, I, F], "ref_mat_mul_relu": [P, P, P, I, I, I],
-            "ref_reduce_sum": [P, P, I], "ref_sync": []}
+            "ref_reduce_sum": [P, P, I], "ref_reduce_sum_ws": [P, P, I, P, I], "ref_sync": []}
     for name, args in sigs.items():
         fn = getattr(lib, name)
         fn.argtypes = args
         fn.restype = None
+    lib.ref_reduction_workspace_size.argtypes = [I]
+    lib.ref_reduction_workspace_size.restype = I
     return lib
 
 
@@ -140,7 +145,12 @@ def c1(iters=20):
     o = torch.empty(1, device="cuda")
     ws = torch.empty(max(1, ops.lib.opw_reduction_workspace_size(n)), device="cuda")
     ours = t(lambda: ops.reduce(0, x, o, n, ws, ws.numel(), 0), iters)
-    theirs = t(lambda: ref.ref_reduce_sum(x.data_ptr(), o.data_ptr(), n), iters) if ref else None
+    # the reference's allocation-free overload with its own workspace size
+    # (its convenience overload allocates and frees scratch on every call)
+    theirs = None
+    if ref:
+        rws = torch.empty(max(1, ref.ref_reduction_workspace_size(n)), device="cuda")
+        theirs = t(lambda: ref.ref_reduce_sum_ws(x.data_ptr(), o.data_ptr(), n, rws.data_ptr(), rws.numel()), iters)
     row("reduce sum 2^24", bytes_=n * 4, ours=ours, theirs=theirs)
     return {"peak_source": src, "hbm_gbs": hbm, "bf16_tflops": tc, "ops": out}
 

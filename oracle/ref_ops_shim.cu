@@ -30,6 +30,11 @@ struct RefAdd {
 extern "C" {
 void ref_map_add(const float *a, const float *b, float *out, int n) { opworks::ops::map(a, b, out, n, RefAdd{}); }
 void ref_reduce_sum(const float *in, float *out, int n) { opworks::ops::reduce<RefSum>(in, out, n); }
+// the allocation-free overload (caller's workspace of reduction_workspace_size(n) floats)
+int ref_reduction_workspace_size(int n) { return opworks::ops::reduction_workspace_size(n); }
+void ref_reduce_sum_ws(const float *in, float *out, int n, float *ws, int ws_floats) {
+    opworks::ops::reduce<RefSum>(in, out, n, opworks::DeviceSpan<float>(ws, ws_floats));
+}
 void ref_softmax(const float *in, float *out, int rows, int cols) { opworks::ops::softmax(in, out, rows, cols); }
 void ref_layer_norm(const float *in, float *out, const float *g, const float *b, int rows, int cols, float eps) {
     opworks::ops::layer_norm(in, out, g, b, rows, cols, eps);
