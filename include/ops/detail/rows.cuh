@@ -102,4 +102,34 @@ inline int row_grid(int rows, int group) {
 
 inline bool aligned16(const void *p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; }
 
+// Warps per SM of the row-walking (warp per row, next row prefetched) grid
+// of softmax; OPWORKS_ROW_WARPS_PER_SM overrides the measured default.
+inline int row_walk_warps_per_sm() {
+    static const int v = [] {
+        const char *e = std::getenv("OPWORKS_ROW_WARPS_PER_SM");
+        const int w = e ? std::atoi(e) : 16;
+        return w >= 8 && w <= 64 ? w : 16;
+    }();
+    return v;
+}
+
+// Blocks of kThreads in a row-walking grid of `rows` rows (one warp per row):
+// at most one resident wave, at most row_walk_warps_per_sm() warps per SM
+// (the kernel's occupancy, queried once per device, may allow fewer).
+template <auto Kernel> inline int row_walk_grid(int64_t rows) {
+    static thread_local int per_sm[16] = {0};
+    const DeviceFacts &f = device_facts();
+    int &slot = per_sm[f.device % 16];
+    if (slot == 0) {
+        int occ = 0;
+        OPWORKS_CUDA_CHECK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, Kernel, kThreads, 0));
+        const int want = row_walk_warps_per_sm() / (kThreads / kWarpSize);
+        slot = occ < want ? (occ > 0 ? occ : 1) : (want > 0 ? want : 1);
+    }
+    const int per_block = kThreads / kWarpSize;
+    const int64_t need = (rows + per_block - 1) / per_block;
+    const int64_t cap = static_cast<int64_t>(f.sm_count) * slot;
+    return static_cast<int>(need < cap ? need : cap);
+}
+
 } // namespace opworks::detail

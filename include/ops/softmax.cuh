@@ -119,15 +119,9 @@ __global__ void __launch_bounds__(kThreads) softmax_rows_pipe_kernel(const float
     }
 }
 
-// Warps per SM of the row-walking softmax grid (OPWORKS_SOFTMAX_WARPS_PER_SM
-// overrides it).
-inline int softmax_warps_per_sm() {
-    static const int v = [] {
-        const char *e = std::getenv("OPWORKS_SOFTMAX_WARPS_PER_SM");
-        const int w = e ? std::atoi(e) : 16;
-        return w >= 8 && w <= 64 ? w : 16;
-    }();
-    return v;
+template <int kSlots> inline void softmax_pipe_launch(const float *in, float *out, int rows, int cols, cudaStream_t stream) {
+    constexpr auto kernel = softmax_rows_pipe_kernel<kSlots>;
+    launch_async(stream, kernel, row_walk_grid<kernel>(rows), kThreads, in, out, int64_t(rows), cols);
 }
 
 // Rows longer than the register tile: one online (max, sum) pass, one write pass.
@@ -183,16 +177,11 @@ inline void softmax(const float *in, float *out, int rows, int cols, cudaStream_
     if (p.slots == 0)
         launch_async(stream, detail::softmax_rows_stream_kernel, rows, kThreads, in, out, cols);
     else if (p.group == 32 && p.vec) {
-        const int per_block = kThreads / kWarpSize;
-        const int64_t cap = static_cast<int64_t>(detail::device_facts().sm_count) * detail::softmax_warps_per_sm() /
-                            per_block;
-        const int64_t need = (static_cast<int64_t>(rows) + per_block - 1) / per_block;
-        const int grid = static_cast<int>(need < cap ? need : cap);
         switch (p.slots) {
-        case 1: launch_async(stream, detail::softmax_rows_pipe_kernel<1>, grid, kThreads, in, out, int64_t(rows), cols); break;
-        case 2: launch_async(stream, detail::softmax_rows_pipe_kernel<2>, grid, kThreads, in, out, int64_t(rows), cols); break;
-        case 4: launch_async(stream, detail::softmax_rows_pipe_kernel<4>, grid, kThreads, in, out, int64_t(rows), cols); break;
-        default: launch_async(stream, detail::softmax_rows_pipe_kernel<8>, grid, kThreads, in, out, int64_t(rows), cols); break;
+        case 1: detail::softmax_pipe_launch<1>(in, out, rows, cols, stream); break;
+        case 2: detail::softmax_pipe_launch<2>(in, out, rows, cols, stream); break;
+        case 4: detail::softmax_pipe_launch<4>(in, out, rows, cols, stream); break;
+        default: detail::softmax_pipe_launch<8>(in, out, rows, cols, stream); break;
         }
     } else if (p.group == 32)
         detail::softmax_dispatch<32>(p, in, out, rows, cols, stream);
