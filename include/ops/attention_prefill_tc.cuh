@@ -19,7 +19,7 @@
 //               query row (64 of the 128 keys), the pair exchanges half-row
 //               maxima; scores in log2 units (one FFMA + exp2 on the SFU per
 //               score), causal mask on diagonal tiles only, running max /
-//               sum; P rounded to tf32
+//               sum; P truncated to tf32 as the MMA reads it
 //   O += P V    tcgen05.mma kind::tf32, A = P (TMEM, written back over S),
 //               B = V (MN-major smem: the same [token][dim] rows), D in TMEM
 //               (128 x 64, double-buffered); the softmax warps fold tile n-1's
@@ -59,6 +59,32 @@ struct PrefillTcSmem {
 };
 
 using sm100::sdesc_mn128_32b;
+
+// sm_100 packed fp32 pairs (one instruction for two lanes' worth of work)
+// and the three-input max: the softmax's per-score instruction count.
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+        "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+    return d;
+}
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+        "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
 
 // D[tmem] (+)= A[tmem] * B[smem desc], tf32 (A from tensor memory, K-major).
 __device__ __forceinline__ void umma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
@@ -352,12 +378,17 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 sm100::tmem_ld_32x16(tmem + lane_addr + 256u + static_cast<uint32_t>((k & 1) * 64 + 32 * half + cc * 16),
                                      rr[cc]);
             sm100::tmem_wait_ld();
+            const float2 a2 = make_float2(alpha, alpha);
 #pragma unroll
             for (int cc = 0; cc < 2; ++cc) {
                 sm100::tmem_reg_fence(rr[cc]);
 #pragma unroll
-                for (int i = 0; i < 16; ++i)
-                    o[cc * 16 + i] = o[cc * 16 + i] * alpha + __uint_as_float(rr[cc][i]);
+                for (int i = 0; i < 16; i += 2) {
+                    const float2 r = ffma2(make_float2(o[cc * 16 + i], o[cc * 16 + i + 1]), a2,
+                                           make_float2(__uint_as_float(rr[cc][i]), __uint_as_float(rr[cc][i + 1])));
+                    o[cc * 16 + i] = r.x;
+                    o[cc * 16 + i + 1] = r.y;
+                }
             }
             sm100::tc_fence_before();
             sm100::mbar_arrive(&o_free[k & 1]);
@@ -393,8 +424,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                     }
                 } else {
 #pragma unroll
-                    for (int i = 0; i < 16; ++i)
-                        mg[cc] = fmaxf(mg[cc], __uint_as_float(v[cc][i]));
+                    for (int i = 0; i < 16; i += 2)
+                        mg[cc] = fmax3(mg[cc], __uint_as_float(v[cc][i]), __uint_as_float(v[cc][i + 1]));
                 }
             }
             float mt = fmaxf(fmaxf(mg[0], mg[1]), fmaxf(mg[2], mg[3]));
@@ -409,26 +440,31 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             const float m_new = fmaxf(m_run, mt);
             const float alpha = m_run == kNegInf ? 0.f : exp2_approx((m_run - m_new) * c);
             const float mc = m_new == kNegInf ? 0.f : m_new * c;
-            float lg[4];
+            float2 lg[4];
+            const float2 c2 = make_float2(c, c), nmc2 = make_float2(-mc, -mc);
 #pragma unroll
             for (int cc = 0; cc < 4; ++cc) {
-                lg[cc] = 0.f;
+                lg[cc] = make_float2(0.f, 0.f);
 #pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    // masked scores are -inf: 2^-inf = 0. P is rounded to
-                    // the nearest tf32 here (the MMA would truncate it), and
-                    // the row sum adds the rounded values, so the weights the
-                    // P V product uses are exactly the ones normalised
-                    const float pv = exp2_approx(fmaf(__uint_as_float(v[cc][i]), c, -mc));
-                    uint32_t u = __float_as_uint(pv);
-                    u = (u + 0xfffu + ((u >> 13) & 1u)) & 0xffffe000u;
-                    lg[cc] += __uint_as_float(u);
-                    v[cc][i] = u;
+                for (int i = 0; i < 16; i += 2) {
+                    // masked scores are -inf: 2^-inf = 0. The MMA reads P as
+                    // tf32 by dropping the 13 low mantissa bits, so the row
+                    // sum adds P truncated the same way: the weights the P V
+                    // product uses are exactly the ones normalised. Pairs of
+                    // scores go through the packed fp32x2 FMA and add.
+                    const float2 t =
+                        ffma2(make_float2(__uint_as_float(v[cc][i]), __uint_as_float(v[cc][i + 1])), c2, nmc2);
+                    const uint32_t u0 = __float_as_uint(exp2_approx(t.x)), u1 = __float_as_uint(exp2_approx(t.y));
+                    lg[cc] = fadd2(lg[cc], make_float2(__uint_as_float(u0 & 0xffffe000u),
+                                                       __uint_as_float(u1 & 0xffffe000u)));
+                    v[cc][i] = u0;
+                    v[cc][i + 1] = u1;
                 }
                 tmem_st_32x16(sb + static_cast<uint32_t>(cc * 16), v[cc]);
             }
             tmem_wait_st();
-            l_run = l_run * alpha + ((lg[0] + lg[1]) + (lg[2] + lg[3]));
+            l_run = l_run * alpha + (((lg[0].x + lg[0].y) + (lg[1].x + lg[1].y)) +
+                                     ((lg[2].x + lg[2].y) + (lg[3].x + lg[3].y)));
             m_run = m_new;
             sm100::tc_fence_before();
             sm100::mbar_arrive(&p_ready[n & 1]);
