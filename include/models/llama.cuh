@@ -197,7 +197,7 @@ template <typename WT> class LlamaEngineT {
             part = std::max(part, static_cast<int64_t>(plan_splits(*p, rows_max_)) * rows_max_ * p->out);
         part_ = TypedDeviceBuffer<float>(part);
         make_views();
-        if (fast && tp_world_ == 1)
+        if (fast && tp_world_ == 1 && chain_)
             alloc_chain();
         if (tp_world_ > 1) {
             tp_y_ = TypedDeviceBuffer<float>(rows_max_ * H);

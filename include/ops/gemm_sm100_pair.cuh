@@ -289,15 +289,21 @@ __global__ void __launch_bounds__(192, 1)
 // leader; each epilogue warp of both CTAs arrives on it (remote arrive for
 // rank 1) once its last TMEM load of buffer b has completed, and the leader's
 // MMA thread waits on it before it reuses buffer b.
-template <int kTerms> struct PairPShape {
-    static constexpr int BN = 256;
+// kBN: tokens per pair tile (256, or 192 where it leaves a smaller last
+// wave); each CTA stages half of them.
+template <int kTerms, int kBN = 256> struct PairPShape {
+    static constexpr int BN = kBN;
+    static constexpr int kHalf = kBN / 2; // token rows staged per CTA
     static constexpr uint32_t kABytes = kUmmaM * kUmmaKBytes;
-    static constexpr uint32_t kBBytes = 128 * kUmmaKBytes;
+    static constexpr uint32_t kBBytes = kHalf * kUmmaKBytes;
     static constexpr uint32_t kStageBytes = kABytes + kTerms * kBBytes;
-    static constexpr int kStages = kTerms == 2 ? 4 : 6;
+    static constexpr int kStages = kTerms == 2 ? 4 : (kBN == 256 ? 6 : 7);
     static constexpr int kChunk = 32; // tokens per epilogue chunk
     static constexpr uint32_t kChunkBytes = kChunk * kUmmaM * 4;
-    static constexpr uint32_t kTmemCols = 2 * BN;
+    // two accumulator buffers 256 columns apart
+    static constexpr uint32_t kBufCols = 256;
+    static constexpr uint32_t kTmemCols = 2 * kBufCols;
+    static_assert(kBN % 32 == 0 && kBN <= 256 && kHalf % 8 == 0, "pair tile width");
     static constexpr size_t kEpiScratchBytes = 16u * BN;
     static constexpr size_t kSmemBytes =
         1024 + static_cast<size_t>(kStages) * kStageBytes + kChunkBytes + 256 + kEpiScratchBytes;
@@ -329,12 +335,12 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t *bar, uint32_t parity
     }
 }
 
-template <typename Epi, int kTerms>
+template <typename Epi, int kTerms, int kBN>
 __global__ void __launch_bounds__(192, 1)
     umma_gemm_pair_persistent_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                                      const __grid_constant__ CUtensorMap tmB_lo, GemmParams p, int ntt, int ntiles,
                                      Epi epi) {
-    using S = PairPShape<kTerms>;
+    using S = PairPShape<kTerms, kBN>;
     constexpr int kStages = S::kStages;
     static_assert(is_tile_epilogue<Epi>::value, "the pair GEMM runs tile epilogues");
     extern __shared__ uint8_t smem_raw[];
@@ -387,7 +393,7 @@ __global__ void __launch_bounds__(192, 1)
             bool first = true;
             for (int w = cid; w < ntiles && ok; w += ncl) {
                 const int f0 = (2 * (w / ntt) + static_cast<int>(rank)) * kUmmaM;
-                const int tb = (w % ntt) * S::BN + static_cast<int>(rank) * 128;
+                const int tb = (w % ntt) * S::BN + static_cast<int>(rank) * S::kHalf;
                 auto load_a = [&](int kb, int s) {
                     tma_load_2d_pair(smem + s * S::kStageBytes, &tmA, bar(s), kb * 64, f0);
                 };
@@ -450,7 +456,7 @@ __global__ void __launch_bounds__(192, 1)
                     }
                     tc_fence_after();
                 }
-                const uint32_t dst = tmem_d + static_cast<uint32_t>(buf * S::BN);
+                const uint32_t dst = tmem_d + static_cast<uint32_t>(buf) * S::kBufCols;
                 for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
                     const int s = it % kStages;
                     if (!mbar_wait(&full[s], static_cast<uint32_t>(it / kStages) & 1u)) {
@@ -501,8 +507,11 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll 1
             for (int c = 0; c < S::BN; c += S::kChunk) {
                 uint32_t r[2][16];
-                tmem_ld_32x16(tmem_d + lane_base + static_cast<uint32_t>(buf * S::BN + c), r[0]);
-                tmem_ld_32x16(tmem_d + lane_base + static_cast<uint32_t>(buf * S::BN + c + 16), r[1]);
+                tmem_ld_32x16(tmem_d + lane_base + static_cast<uint32_t>(buf) * S::kBufCols + static_cast<uint32_t>(c),
+                              r[0]);
+                tmem_ld_32x16(tmem_d + lane_base + static_cast<uint32_t>(buf) * S::kBufCols +
+                                  static_cast<uint32_t>(c + 16),
+                              r[1]);
                 tmem_wait_ld();
                 tmem_reg_fence(r[0]);
                 tmem_reg_fence(r[1]);
@@ -538,7 +547,7 @@ __global__ void __launch_bounds__(192, 1)
     }
 }
 
-template <typename Epi, int kTerms> inline int gemm_pair_persistent_prepare() {
+template <typename Epi, int kTerms, int kBN> inline int gemm_pair_persistent_prepare() {
     struct Slot {
         int device = -1, clusters = 0;
     };
@@ -547,8 +556,8 @@ template <typename Epi, int kTerms> inline int gemm_pair_persistent_prepare() {
     OPWORKS_CUDA_CHECK(cudaGetDevice(&dev));
     Slot &sl = slot[dev % 16];
     if (sl.device != dev) {
-        auto kernel = umma_gemm_pair_persistent_kernel<Epi, kTerms>;
-        const int smem = static_cast<int>(PairPShape<kTerms>::kSmemBytes);
+        auto kernel = umma_gemm_pair_persistent_kernel<Epi, kTerms, kBN>;
+        const int smem = static_cast<int>(PairPShape<kTerms, kBN>::kSmemBytes);
         OPWORKS_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
         cudaLaunchConfig_t cfg{};
         cfg.gridDim = dim3(2 * detail::device_facts().sm_count);
@@ -617,17 +626,40 @@ inline void gemm_pair_bf16x2(const GemmOperand &W, const GemmOperand &X, int k, 
     detail::require(grid.y <= 65535, "gemm_pair_bf16x2: grid exceeds the CUDA limits");
     const int ntiles = static_cast<int>(grid.x / 2 * grid.y);
     if (gemm_pair_persistent_enabled()) {
-        // persistent grid: the tiles of more than one wave of clusters
-        const int clusters = X.lo ? gemm_pair_persistent_prepare<Epi, 2>() : gemm_pair_persistent_prepare<Epi, 1>();
+        // persistent grid: the tiles of more than one wave of clusters, with
+        // the token tile (256 or 192) that needs fewer token rows of rounds:
+        // rounds x width, rounds = ceil(tiles / clusters). One-term tiles
+        // of 192 must win by 10%: they move a third more weight bytes per
+        // flop (measured at M = 8192: QKV 7% faster, O even, down 13%
+        // slower); two-term tiles carry twice the MMA work per byte.
+        const int clusters = X.lo ? gemm_pair_persistent_prepare<Epi, 2, 256>()
+                                  : gemm_pair_persistent_prepare<Epi, 1, 256>();
         if (ntiles > clusters) {
-            const dim3 pgrid(2 * clusters);
-            const int ntt = static_cast<int>(grid.y);
+            const int pairs = static_cast<int>(grid.x / 2);
+            auto cost = [&](int bn) {
+                const int64_t tiles = static_cast<int64_t>(pairs) * ((X.rows + bn - 1) / bn);
+                return ((tiles + clusters - 1) / clusters) * bn;
+            };
+            const int bn = (X.lo ? cost(192) < cost(256) : 10 * cost(192) < 9 * cost(256)) ? 192 : 256;
+            const int ntt = (X.rows + bn - 1) / bn;
+            const int nt = pairs * ntt;
+            const CUtensorMap pb = make_tmap_2d(X.hi, true, static_cast<uint64_t>(k), X.rows, X.ld, 64, bn / 2);
+            const CUtensorMap pb_lo = X.lo ? make_tmap_2d(X.lo, true, static_cast<uint64_t>(k), X.rows, X.ld, 64, bn / 2)
+                                           : pb;
+            auto go = [&](auto terms, auto width) {
+                constexpr int kT = decltype(terms)::value, kW = decltype(width)::value;
+                const int cl = gemm_pair_persistent_prepare<Epi, kT, kW>();
+                launch_ex_cluster(umma_gemm_pair_persistent_kernel<Epi, kT, kW>, dim3(2 * cl), dim3(2, 1, 1),
+                                  dim3(192), PairPShape<kT, kW>::kSmemBytes, stream, ta, pb, pb_lo, p, ntt, nt, epi);
+            };
+            using I1 = std::integral_constant<int, 1>;
+            using I2 = std::integral_constant<int, 2>;
+            using W192 = std::integral_constant<int, 192>;
+            using W256 = std::integral_constant<int, 256>;
             if (X.lo)
-                launch_ex_cluster(umma_gemm_pair_persistent_kernel<Epi, 2>, pgrid, dim3(2, 1, 1), dim3(192),
-                                  PairPShape<2>::kSmemBytes, stream, ta, tb, tb_lo, p, ntt, ntiles, epi);
+                bn == 192 ? go(I2{}, W192{}) : go(I2{}, W256{});
             else
-                launch_ex_cluster(umma_gemm_pair_persistent_kernel<Epi, 1>, pgrid, dim3(2, 1, 1), dim3(192),
-                                  PairPShape<1>::kSmemBytes, stream, ta, tb, tb_lo, p, ntt, ntiles, epi);
+                bn == 192 ? go(I1{}, W192{}) : go(I1{}, W256{});
             return;
         }
     }

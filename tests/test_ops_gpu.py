@@ -188,7 +188,10 @@ def test_gemm_bf16x2_pair_vs_fp64(ops, M, N, K):
                                           # 128 tiles, and 512 one-K-block tiles (each cluster reuses both
                                           # accumulator buffers several times)
                                           ("gemm_f16x2_pair", 1100, 9600, 256), ("pair_single", 2048, 4096, 520),
-                                          ("pair_single", 4096, 8192, 64)])
+                                          ("pair_single", 4096, 8192, 64),
+                                          # 12 feature pairs x 2000 tokens: 192-token tiles (132 tiles in
+                                          # 2 rounds) beat 256 (96 tiles, 2 rounds); ragged M and K
+                                          ("pair_single", 2000, 3072, 256), ("gemm_f16x2_pair", 2000, 3072, 200)])
 def test_gemm_f16x2_vs_fp64(ops, kernel, M, N, K):
     rng = np.random.default_rng(M + 5 * N + 11 * K)
     w = (rng.standard_normal((N, K)) / math.sqrt(K)).astype(np.float32)
