@@ -769,6 +769,11 @@ def cpu_measure(pack_path, steps, warmup):
     oracle after `warmup` untimed ones, each step the sample of
     cpu_sample_batch at context 2048; value = sequences per step / seconds per
     step (tok/s)."""
+    import oracle
+
+    # every host thread this process may use: torchrun sets OMP_NUM_THREADS=1
+    # for its ranks, and rank 0 runs this alone
+    oracle.lib().orc_set_threads(len(os.sched_getaffinity(0)))
     batch, probe = cpu_sample_batch(pack_path)
     sec, threads = cpu_decode_steps(pack_path, batch, steps, warmup=warmup)
     return {"value": round(batch / sec, 3), "unit": UNIT, "cores": threads, "kind": "port",
