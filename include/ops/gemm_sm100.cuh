@@ -116,7 +116,16 @@ constexpr size_t kEpiScratchNarrow = 8192; // epilogue scratch bytes of BN <= 64
 constexpr int kMaxClusterSplits = 8;           // portable cluster size
 constexpr int kMaxClusterSplitsNonPortable = 16; // with the non-portable opt-in
 
-__device__ __forceinline__ void epilogue_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// Named barrier of the 128 threads of one epilogue group: warps 2-5 are group
+// 0 (barrier 1), warps 6-9 group 1 (barrier 2; the persistent two-SM GEMM
+// runs two epilogue groups on alternating chunks). Constant barrier ids (a
+// warp-uniform branch), so kernels reserve only the barriers they name.
+__device__ __forceinline__ void epilogue_bar() {
+    if (threadIdx.x < 192)
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+    else
+        asm volatile("bar.sync 2, 128;" ::: "memory");
+}
 // split cluster barrier: arrive (release this CTA's shared-memory writes) and
 // wait (acquire the peers'); every thread of every CTA takes both
 __device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }

@@ -282,8 +282,10 @@ __global__ void __launch_bounds__(192, 1)
 // tile w % ntt, so the clusters running at one time share a few weight
 // tiles and stream the activations from L2). The K-block ring runs on across
 // tiles, and the accumulator is double-buffered in tensor memory (2 x 256
-// columns): the MMAs of tile i + 1 run while the epilogue warps drain
-// tile i in 32-token chunks through a [32][128] fp32 shared tile.
+// columns): the MMAs of tile i + 1 run while two groups of four epilogue
+// warps drain tile i in alternate 32-token chunks, each through its own
+// [32][128] fp32 shared tile (one group alone took ~1.8x the MMA time of a
+// K = 2048 tile and set the kernel's pace).
 //
 // Extra protocol over the one-tile kernel: tmem_empty[b] lives in the
 // leader; each epilogue warp of both CTAs arrives on it (remote arrive for
@@ -297,17 +299,22 @@ template <int kTerms, int kBN = 256> struct PairPShape {
     static constexpr uint32_t kABytes = kUmmaM * kUmmaKBytes;
     static constexpr uint32_t kBBytes = kHalf * kUmmaKBytes;
     static constexpr uint32_t kStageBytes = kABytes + kTerms * kBBytes;
-    static constexpr int kStages = kTerms == 2 ? 4 : (kBN == 256 ? 6 : 7);
+    static constexpr int kStages = kTerms == 2 ? (kBN == 256 ? 3 : 4) : (kBN == 256 ? 5 : 6);
     static constexpr int kChunk = 32; // tokens per epilogue chunk
     static constexpr uint32_t kChunkBytes = kChunk * kUmmaM * 4;
+    // two epilogue groups of four warps (warps 2-5 and 6-9) drain alternate
+    // chunks, each through its own chunk tile and scratch
+    static constexpr int kEpiGroups = 2;
+    static constexpr int kThreads = 64 + 128 * kEpiGroups;
     // two accumulator buffers 256 columns apart
     static constexpr uint32_t kBufCols = 256;
     static constexpr uint32_t kTmemCols = 2 * kBufCols;
     static_assert(kBN % 32 == 0 && kBN <= 256 && kHalf % 8 == 0, "pair tile width");
-    static constexpr size_t kEpiScratchBytes = 16u * BN;
-    static constexpr size_t kSmemBytes =
-        1024 + static_cast<size_t>(kStages) * kStageBytes + kChunkBytes + 256 + kEpiScratchBytes;
+    static constexpr size_t kEpiScratchBytes = 16u * BN; // per group
+    static constexpr size_t kSmemBytes = 1024 + static_cast<size_t>(kStages) * kStageBytes +
+                                         kEpiGroups * kChunkBytes + 256 + kEpiGroups * kEpiScratchBytes;
     static_assert(kSmemBytes <= 227u * 1024u, "shared memory per CTA");
+    static_assert(kBN >= kEpiGroups * kChunk, "every epilogue group drains a chunk of every tile");
 };
 
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
@@ -336,7 +343,7 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t *bar, uint32_t parity
 }
 
 template <typename Epi, int kTerms, int kBN>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(PairPShape<kTerms, kBN>::kThreads, 1)
     umma_gemm_pair_persistent_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                                      const __grid_constant__ CUtensorMap tmB_lo, GemmParams p, int ntt, int ntiles,
                                      Epi epi) {
@@ -345,13 +352,14 @@ __global__ void __launch_bounds__(192, 1)
     static_assert(is_tile_epilogue<Epi>::value, "the pair GEMM runs tile epilogues");
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    float *ctile = reinterpret_cast<float *>(smem + kStages * S::kStageBytes);
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem + kStages * S::kStageBytes + S::kChunkBytes);
+    // [stages][chunk tile per epilogue group][barriers][scratch per group]
+    float *ctile_all = reinterpret_cast<float *>(smem + kStages * S::kStageBytes);
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + kStages * S::kStageBytes + S::kEpiGroups * S::kChunkBytes);
     uint64_t *empty = full + kStages;
     uint64_t *accum = empty + kStages;    // [2]
     uint64_t *tmem_empty = accum + 2;     // [2], the leader's are used
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(tmem_empty + 2);
-    void *epi_scratch = smem + kStages * S::kStageBytes + S::kChunkBytes + 256;
+    uint8_t *scratch_all = smem + kStages * S::kStageBytes + S::kEpiGroups * S::kChunkBytes + 256;
 
     const int warp = threadIdx.x / kWarpSize;
     const int lane = threadIdx.x % kWarpSize;
@@ -366,7 +374,7 @@ __global__ void __launch_bounds__(192, 1)
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&accum[b], 1);
-            mbar_init(&tmem_empty[b], 8); // 4 epilogue warps x 2 CTAs
+            mbar_init(&tmem_empty[b], 8 * S::kEpiGroups); // every epilogue warp of both CTAs
         }
         fence_mbarrier_init();
         prefetch_tmap(&tmA);
@@ -490,7 +498,13 @@ __global__ void __launch_bounds__(192, 1)
         }
     } else {
         pdl_wait(); // the outputs may still be read by an earlier kernel
-        const int et = static_cast<int>(threadIdx.x) - 64;
+        // epilogue group g (warps 2-5: 0, 6-9: 1) drains chunks g, g + 2, ...
+        // of every tile through its own chunk tile and scratch; its named
+        // barrier (epilogue_bar) is 1 + g
+        const int eg = (warp - 2) >> 2;
+        const int et = (static_cast<int>(threadIdx.x) - 64) & 127; // thread of the group
+        float *ctile = ctile_all + eg * (S::kChunk * kUmmaM);
+        void *epi_scratch = scratch_all + eg * S::kEpiScratchBytes;
         const int q = warp & 3;
         const int col = q * 32 + lane;
         const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
@@ -505,7 +519,7 @@ __global__ void __launch_bounds__(192, 1)
                 ok = false; // after a failed wait, no further wait (warp-uniform)
             tc_fence_after();
 #pragma unroll 1
-            for (int c = 0; c < S::BN; c += S::kChunk) {
+            for (int c = eg * S::kChunk; c < S::BN; c += S::kEpiGroups * S::kChunk) {
                 uint32_t r[2][16];
                 tmem_ld_32x16(tmem_d + lane_base + static_cast<uint32_t>(buf) * S::kBufCols + static_cast<uint32_t>(c),
                               r[0]);
@@ -515,7 +529,7 @@ __global__ void __launch_bounds__(192, 1)
                 tmem_wait_ld();
                 tmem_reg_fence(r[0]);
                 tmem_reg_fence(r[1]);
-                if (c + S::kChunk == S::BN) { // this warp's last read of the buffer
+                if (c + S::kEpiGroups * S::kChunk >= S::BN) { // this warp's last read of the buffer
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0)
@@ -525,7 +539,7 @@ __global__ void __launch_bounds__(192, 1)
                 for (int i = 0; i < S::kChunk; ++i)
                     ctile[i * kUmmaM + col] = __uint_as_float(r[i >> 4][i & 15]);
                 const int ntok = max(0, min(S::kChunk, p.m_tok - (t0 + c)));
-                const bool run = nfeat > 0 && ntok > 0; // CTA-uniform
+                const bool run = nfeat > 0 && ntok > 0; // uniform over the group
                 if (run) {
                     if constexpr (has_prepare<Epi>::value)
                         epi.prepare(t0 + c, ntok, f0, nfeat, et, epi_scratch);
@@ -561,7 +575,7 @@ template <typename Epi, int kTerms, int kBN> inline int gemm_pair_persistent_pre
         OPWORKS_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
         cudaLaunchConfig_t cfg{};
         cfg.gridDim = dim3(2 * detail::device_facts().sm_count);
-        cfg.blockDim = dim3(192);
+        cfg.blockDim = dim3(PairPShape<kTerms, kBN>::kThreads);
         cfg.dynamicSmemBytes = static_cast<size_t>(smem);
         cudaLaunchAttribute attr[1];
         attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -650,7 +664,8 @@ inline void gemm_pair_bf16x2(const GemmOperand &W, const GemmOperand &X, int k, 
                 constexpr int kT = decltype(terms)::value, kW = decltype(width)::value;
                 const int cl = gemm_pair_persistent_prepare<Epi, kT, kW>();
                 launch_ex_cluster(umma_gemm_pair_persistent_kernel<Epi, kT, kW>, dim3(2 * cl), dim3(2, 1, 1),
-                                  dim3(192), PairPShape<kT, kW>::kSmemBytes, stream, ta, pb, pb_lo, p, ntt, nt, epi);
+                                  dim3(PairPShape<kT, kW>::kThreads), PairPShape<kT, kW>::kSmemBytes, stream, ta, pb,
+                                  pb_lo, p, ntt, nt, epi);
             };
             using I1 = std::integral_constant<int, 1>;
             using I2 = std::integral_constant<int, 2>;
