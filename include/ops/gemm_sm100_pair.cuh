@@ -28,6 +28,8 @@
 //     [256][128] fp32 tile in shared memory and run the tile epilogue.
 // Loads carry no cluster multicast: each CTA fetches its own operands.
 
+#include <algorithm>
+
 #include "gemm_sm100.cuh"
 
 namespace opworks::sm100 {
@@ -604,8 +606,8 @@ template <typename Epi, int kTerms> inline void gemm_pair_prepare_kernel() {
     }
 }
 
-// The persistent form for grids of more than one wave of clusters
-// (OPWORKS_PAIR_PERSISTENT=0: the one-tile kernel for every grid).
+// The persistent form for every grid (OPWORKS_PAIR_PERSISTENT=0: the one-tile
+// kernel instead).
 inline bool gemm_pair_persistent_enabled() {
     static const bool on = [] {
         const char *e = std::getenv("OPWORKS_PAIR_PERSISTENT");
@@ -640,15 +642,16 @@ inline void gemm_pair_bf16x2(const GemmOperand &W, const GemmOperand &X, int k, 
     detail::require(grid.y <= 65535, "gemm_pair_bf16x2: grid exceeds the CUDA limits");
     const int ntiles = static_cast<int>(grid.x / 2 * grid.y);
     if (gemm_pair_persistent_enabled()) {
-        // persistent grid: the tiles of more than one wave of clusters, with
-        // the token tile (256 or 192) that needs fewer token rows of rounds:
+        // persistent grid (at most one cluster per tile; a grid of one
+        // wave still drains with both epilogue groups), with the token tile
+        // (256 or 192) that needs fewer token rows of rounds:
         // rounds x width, rounds = ceil(tiles / clusters). One-term tiles
         // of 192 must win by 10%: they move a third more weight bytes per
         // flop (measured at M = 8192: QKV 7% faster, O even, down 13%
         // slower); two-term tiles carry twice the MMA work per byte.
         const int clusters = X.lo ? gemm_pair_persistent_prepare<Epi, 2, 256>()
                                   : gemm_pair_persistent_prepare<Epi, 1, 256>();
-        if (ntiles > clusters) {
+        {
             const int pairs = static_cast<int>(grid.x / 2);
             auto cost = [&](int bn) {
                 const int64_t tiles = static_cast<int64_t>(pairs) * ((X.rows + bn - 1) / bn);
@@ -662,7 +665,7 @@ inline void gemm_pair_bf16x2(const GemmOperand &W, const GemmOperand &X, int k, 
                                            : pb;
             auto go = [&](auto terms, auto width) {
                 constexpr int kT = decltype(terms)::value, kW = decltype(width)::value;
-                const int cl = gemm_pair_persistent_prepare<Epi, kT, kW>();
+                const int cl = std::min(gemm_pair_persistent_prepare<Epi, kT, kW>(), nt);
                 launch_ex_cluster(umma_gemm_pair_persistent_kernel<Epi, kT, kW>, dim3(2 * cl), dim3(2, 1, 1),
                                   dim3(PairPShape<kT, kW>::kThreads), PairPShape<kT, kW>::kSmemBytes, stream, ta, pb,
                                   pb_lo, p, ntt, nt, epi);
