@@ -25,7 +25,7 @@ Reported (one JSON line from rank 0):
   cpu_baseline  the C++ oracle's batched decode step on the host cores
              (bounded sample: a few steps), rank 0 at N = 1
   prefill    C3 prefill (32 x 2048 tokens) and C4 (one 8192-token prompt)
-  c5         BASELINE C5 serving at this N: 256 requests partitioned over the
+  c5         config C5 serving at this N: 256 requests partitioned over the
              ranks (strong scaling: total generated tok/s, per-rank busy time)
   c2_session C2 through the 11-symbol session ABI (our library and the
              reference's, float32 and bfloat16 packs)
@@ -783,7 +783,7 @@ def cpu_measure(pack_path, steps, warmup):
 
 
 def cpu_extras(pack_path):
-    """The CPU numbers BASELINE.md promises beside the C3 one, on the host
+    """The CPU numbers reported beside the C3 one, on the host
     cores (the C++/OpenMP oracle, double accumulation): C1 operators timed in
     full; C2 = a 128-token prefill timed in full and 8 greedy decode steps
     (per token); C4 (8192-token prefill) extrapolated from the measured
@@ -870,7 +870,7 @@ def run_reference(args):
 
 
 def c5_serve(model, args, rank, world, device_id):
-    """BASELINE C5 on an already loaded model: 256 requests (prompt lengths
+    """Config C5 on an already loaded model: 256 requests (prompt lengths
     U[256, 1024], 256 sampled tokens each, T=0.7 top-p 0.9) split over the
     ranks by the deterministic LPT partition (opworks_b200/serving.py); every
     rank serves its share with continuous batching on its GPU, no collective

@@ -2,7 +2,7 @@
 stream, warm-up first, L2 flushed (a 256 MB read) before every timed launch,
 median over the timed launches.
 
-    python -m opworks_b200.microbench c1        # BASELINE C1 operator configs
+    python -m opworks_b200.microbench c1        # config C1 operator shapes
     python -m opworks_b200.microbench decode    # decode-step kernels (C3 shapes)
     python -m opworks_b200.microbench prefill   # one 8192-token prefill (C4)
     python -m opworks_b200.microbench pair      # two-SM prefill GEMMs at the C4 shapes
@@ -85,7 +85,7 @@ def _ref_ops():
 
 
 def c1(iters=20):
-    """BASELINE C1: softmax 4096x1024, layer_norm 4096x2048, mat_mul
+    """Config C1: softmax 4096x1024, layer_norm 4096x2048, mat_mul
     1024x2048 @ 2048x1024 + ReLU, Sum over 2^24 floats (seeded inputs)."""
     import torch
 
@@ -287,7 +287,7 @@ def tf32_peak(n=8192, burst_iters=10, sustain_s=3.0):
 
 
 def prefill(T=8192, iters=2):
-    """BASELINE C4: one T-token prefill of the random-init Llama-3.2-1B on the
+    """Config C4: one T-token prefill of the random-init Llama-3.2-1B on the
     fast path (tensor-core GEMMs and attention), CUDA events on the engine
     stream; returns ms and tokens/s."""
     import torch

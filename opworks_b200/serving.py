@@ -1,4 +1,4 @@
-"""Request-partitioned serving (BASELINE C5): requests are independent, so N
+"""Request-partitioned serving (benchmark config C5): requests are independent, so N
 GPUs serve disjoint subsets of them, one process per GPU, with no collective
 on the data path. Each process runs continuous batching over one LlamaBatch
 (paged KV cache, CUDA-graph decode steps, device sampling); results are
@@ -129,7 +129,7 @@ def serve_partitioned(requests: Sequence[Request], rank: int, world: int,
 
 
 def c5_requests(n=256, lo=256, hi=1024, new_tokens=256, vocab=128256, temperature=0.7, top_p=0.9, seed=9):
-    """BASELINE C5: `n` requests, prompt lengths uniform in [lo, hi], uniform
+    """Config C5: `n` requests, prompt lengths uniform in [lo, hi], uniform
     random ids, `new_tokens` sampled tokens each."""
     rng = np.random.default_rng(seed)
     lens = rng.integers(lo, hi + 1, n)

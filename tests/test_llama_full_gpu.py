@@ -1,11 +1,11 @@
 """Full-size random-init Llama-3.2-1B (OPWPACK1 float32 pack, N(0, 0.02)
-weights, seed 1234, generated once per box) — BASELINE config C2 parity:
+weights, seed 1234, generated once per box) — benchmark config C2 parity:
 
 * the accurate (fp32) session path gives the same first 32 greedy tokens
   after a 128-token random prompt as the CPU oracle and as the reference's own
   CUDA library (oracle/_ref/libopworks_llama_ref.so, built from the reference
   sources) on the same pack;
-* the fast (bf16) path's logits stay within the BASELINE GEMM tolerance of the
+* the fast (bf16) path's logits stay within the GEMM tolerance of the
   fp32 path (max-abs <= 2e-2 on the logits);
 * a bs32 decode step of the batch engine equals 32 single-sequence steps.
 """
@@ -144,9 +144,9 @@ def test_batched_decode_equals_single(pack_path):
 
 
 def test_fast_path_long_prompt_logits_within_gemm_tolerance(pack_path):
-    """A 1024-token prompt: the fast path's prefill runs the two-SM bf16 x
-    two-term-bf16 GEMMs (at least 512 token rows) and tensor-core TF32
-    attention; its last-row logits stay within the BASELINE GEMM tolerance of
+    """A 1024-token prompt: the fast path's prefill runs the two-SM GEMMs
+    (16-bit weights x one fp16 activation term, from 256 token rows on) and tensor-core TF32
+    attention; its last-row logits stay within the GEMM tolerance of
     the accurate path (fp32 weights, split-TF32 GEMMs, fp32 attention)."""
     from opworks_b200.llama import LlamaBatch, Model
 

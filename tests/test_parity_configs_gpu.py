@@ -1,4 +1,4 @@
-"""Parity at the sizes the benchmark runs (BASELINE configs C2-C4), on the
+"""Parity at the sizes the benchmark runs (benchmark configs C2-C5), on the
 full-size random-init Llama-3.2-1B pack.
 
 * C3: 32 sequences prefilled to 2048 random ids, then 8 sampled decode steps
@@ -9,6 +9,9 @@ full-size random-init Llama-3.2-1B pack.
   row 17 (prefill and last step) are within 1e-3 of the CPU oracle.
 * C4: one 8192-token prefill; last-row logits of the fast path (two-SM GEMMs,
   tensor-core attention) within 2e-2 of the accurate path, same greedy token.
+* C5 prompt lengths (255, 256, 300, 511, 1000 tokens: both sides of the
+  two-SM threshold, ragged last tiles): prefill logits and one decode step
+  within 2e-2 of the accurate path, same greedy token.
 * Weights off the bf16 grid: the C2 check (128-token prompt, 32 greedy steps)
   on a pack whose fp32 weights are a plain N(0, 0.02) draw, so the fast path's
   bf16 weights are a rounding of the accurate path's.
@@ -29,7 +32,7 @@ import oracle
 pytestmark = pytest.mark.gpu
 torch = pytest.importorskip("torch")
 
-TOL_GEMM = 2e-2  # BASELINE: logits of the bf16/TF32 tensor-core path, max-abs
+TOL_GEMM = 2e-2  # logits of the bf16/TF32 tensor-core path, max-abs
 TOL_ORACLE = 1e-3  # accurate (fp32 / split-TF32) path against the double-accumulated oracle
 V = 128256
 ALL_SETS = 7  # bf16 + fp32 + split-TF32 weights
@@ -124,9 +127,35 @@ def test_c4_8192_prefill_fast_vs_accurate(model):
     assert t_fast == t_acc
 
 
+@pytest.mark.parametrize("n", [255, 256, 300, 511, 1000])
+def test_c5_prompt_lengths_fast_vs_accurate(model, n):
+    """C5 prompts (U[256, 1024] tokens) on both sides of the two-SM threshold
+    (256 rows): from 256 rows on the projections run the persistent pair kernel
+    with one fp16 activation term (192- or 256-token tiles, ragged last tile);
+    the prefill logits and one decode step after it stay within the GEMM
+    tolerance of the accurate path."""
+    from opworks_b200.llama import LlamaBatch
+
+    prompt = np.random.default_rng(60 + n).integers(0, V, n).astype(np.int32)
+    out = {}
+    for precision in ("fast", "accurate"):
+        with LlamaBatch(model, 1, 1024 + 8, precision, prefill_rows=1024) as b:
+            t0 = b.prefill(0, prompt)
+            pre = b.logits(0)
+            t1 = b.decode([0], [t0])[0]
+            out[precision] = (t0, pre, t1, b.logits(0))
+    (f0, fpre, f1, fdec), (a0, apre, a1, adec) = out["fast"], out["accurate"]
+    err_pre = float(np.max(np.abs(fpre - apre)))
+    err_dec = float(np.max(np.abs(fdec - adec)))
+    print(f"PARITY c5 prompt={n} fast_vs_accurate prefill={err_pre:.3e} decode={err_dec:.3e}")
+    assert f0 == a0  # the decode step below starts from the same token on both sides
+    assert err_pre <= TOL_GEMM, err_pre
+    assert err_dec <= TOL_GEMM, err_dec
+
+
 def test_unrounded_weights_c2_fast_vs_accurate():
     """The fast path reads bf16 copies of fp32 weights that are not on the
-    bf16 grid (BASELINE's plain N(0, 0.02) weights)."""
+    bf16 grid (plain N(0, 0.02) weights)."""
     from opworks_b200 import pack
     from opworks_b200.llama import LlamaBatch, Model
 

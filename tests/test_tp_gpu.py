@@ -3,7 +3,7 @@ reductions of the o and down projections: the NCCL all-reduce, then the
 fused peer-to-peer one (GEMM epilogue stores into every rank's receive
 buffer over CUDA IPC mappings, rank-order sum in the residual kernel). Both
 ranks return the same tokens, and they equal the single-GPU fast engine's
-greedy tokens on the same prompts, with last-step logits within the BASELINE
+greedy tokens on the same prompts, with last-step logits within the
 GEMM tolerance (2e-2 max-abs; the ranks' partial sums only reorder fp32
 additions). Skipped on fewer than 2 GPUs."""
 
