@@ -294,7 +294,9 @@ def run_ours(args):
 
     K, W = args.steps, args.warmup
     MULTI = 64  # extra steps of the host-sync-free multi-step decode (extras)
-    max_seq = ((CTX + W + K + 1 + MULTI + 15) // 16) * 16
+    # positions: W warm-up steps, K (warm multi-step), K (timed), K (e2e),
+    # 3 (in-graph trace), MULTI (extras), 1 spare
+    max_seq = ((CTX + W + 3 * K + 3 + MULTI + 1 + 15) // 16) * 16
     t_load = time.perf_counter()
     model = Model(pack_path, weight_sets=1, max_positions=max(8192, max_seq), device=local)
     t_load = time.perf_counter() - t_load
@@ -344,8 +346,22 @@ def run_ours(args):
         prev = eng.decode(slots, prev, temperature=TEMPERATURE, top_p=TOP_P, seeds=seeds, steps=step)
         step += 1
 
+    # `value`: K steps with every step's sampled tokens fed back on the device
+    # (one opw_llama_batch_decode_multi call: K replays of the step graph plus
+    # the token-advance kernel, inputs resident, one D2H of the K x 32 tokens
+    # at the end). Tensor-parallel runs keep the per-step call.
+    multi_value = not tp
+
+    def decode_k():
+        nonlocal prev, step
+        toks, _ = eng.decode_multi(slots, prev, K, temperature=TEMPERATURE, top_p=TOP_P, seeds=seeds, steps0=step)
+        prev = toks[-1]
+        step += K
+
     for _ in range(W):
         decode_once()
+    if multi_value:
+        decode_k()  # warm: the K-step graph is captured here
     torch.cuda.synchronize()
 
     clocks = ClockSampler(local if "CUDA_VISIBLE_DEVICES" not in os.environ else local)
@@ -354,19 +370,36 @@ def run_ours(args):
     barrier()
     torch.cuda.synchronize()
     s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    t0 = time.perf_counter()
+    ctx0 = step - 1  # positions decoded after the prefill so far
+    if multi_value:
+        # a ~0.5 ms device spin ahead of the start event: the host's enqueue
+        # of the timed call (input staging, K graph launches) lands before
+        # the GPU reaches it, so the events bracket device work only
+        with torch.cuda.stream(stream):
+            torch.cuda._sleep(1_000_000)
     s0.record(stream)
+    if multi_value:
+        decode_k()
+    else:
+        for _ in range(K):
+            decode_once()
+    s1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    dev_ms = allmax(s0.elapsed_time(s1))
+    # e2e: the public per-step call (H2D of the step's tokens and sampling
+    # inputs, graph replay, D2H of the sampled tokens, blocking), host clock
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
     for _ in range(K):
         decode_once()
-    s1.record(stream)
     torch.cuda.synchronize()
     wall = time.perf_counter() - t0
     clocks.stop()
     barrier()
-    dev_ms = allmax(s0.elapsed_time(s1))
     wall = allmax(wall)
 
-    ctx_mean = CTX + W + K / 2.0
+    ctx_mean = CTX + ctx0 + K / 2.0
     groups = 1 if tp else world  # independent sequence groups across the ranks
     value = BATCH * K * groups / (dev_ms / 1e3)
     e2e_value = BATCH * K * groups / wall
@@ -374,10 +407,11 @@ def run_ours(args):
 
     # ---- per-kernel device time of the last step (roofline)
     kernels = eng.profile(BATCH, args.profile_iters)
+    ctx_prof = CTX + step - 1  # context of the profiled step
     kernels_in_graph = in_graph_kernel_times(decode_once)
     if kernels_in_graph is not None:
         for g in kernels_in_graph["groups"]:
-            b = algorithmic_bytes(g["kernel"], rcfg, BATCH, CTX + W + K)
+            b = algorithmic_bytes(g["kernel"], rcfg, BATCH, CTX + step - 1)  # after the traced steps
             g["gbs"] = round(b / (g["ms_per_step"] / 1e3) / 1e9, 1) if b and g["ms_per_step"] > 0 else None
 
     # ---- host-sync-free multi-step decode (extras): MULTI more steps in
@@ -404,7 +438,7 @@ def run_ours(args):
                  "timing": "host wall clock around opw_llama_batch_decode_multi calls (one H2D before and one "
                            "D2H after each chunk)"}
     hbm_peak, tc_peak, peak_src = measured_peaks()
-    ctx_now = CTX + W + K
+    ctx_now = ctx_prof
     traffic = load_traffic()
     rows = []
     for label, ms, launches in kernels:
@@ -520,7 +554,7 @@ def run_ours(args):
                                    f"prefilled to {CTX} random ids, T=0.7 top-p=0.9 device sampling, fp32 paged KV "
                                    "(16-token blocks)",
                        "model": "Llama-3.2-1B (16 layers, 2048 hidden, 32/8 heads, 128256 vocab)",
-                       "global_batch": BATCH * groups, "seq_len": CTX, "ctx_range": [CTX + W, CTX + W + K],
+                       "global_batch": BATCH * groups, "seq_len": CTX, "ctx_range": [CTX + ctx0, CTX + ctx0 + K],
                        "parallelism": (f"tp{world}: tensor-parallel heads / MLP columns, "
                                        + ("NCCL all-reduce" if args.tp_reduce == "nccl" else
                                           "peer stores from the GEMM epilogue + rank-order sum")
@@ -529,11 +563,17 @@ def run_ours(args):
                        "precision": "fp16 weights (rounded from the fp32 pack) and two-term fp16 GEMM operands, "
                                     "fp32 accumulation / residual / KV cache / attention / softmax, sampling fp64",
                        "l2": "inputs larger than L2: every step streams 2.47 GB of weights + ~4.5 GB of KV",
-                       "cuda_graph": True},
+                       "cuda_graph": True,
+                       "timed_step": ("K replays of the step graph in one decode_multi call, sampled tokens fed "
+                                      "back on the device (token-advance kernel), CUDA events on the engine stream"
+                                      if multi_value else "K blocking per-step decode calls, CUDA events"),
+                       "e2e_step": "K blocking opw_llama_batch_decode calls (H2D of the step's inputs, graph "
+                                   "replay, D2H of the sampled tokens), host wall clock"},
             "roofline": roofline, "step_roofline": step_roofline,
             "e2e": {"value": round(e2e_value, 1), "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
-            "gpu_launches": gpu_launches_per_step * K, "gpu_launches_per_step": gpu_launches_per_step,
+            "gpu_launches": (gpu_launches_per_step + (1 if multi_value else 0)) * K,
+            "gpu_launches_per_step": gpu_launches_per_step + (1 if multi_value else 0),
             "clocks": clocks.summary(),
             "prefill": {"c3_tokens": BATCH * CTX, "c3_ms": round(prefill_ms, 1),
                         "c3_tok_s": round(BATCH * CTX * groups / (prefill_ms / 1e3), 1), "c4": prefill8k},

@@ -700,12 +700,13 @@ template <typename WT> class LlamaEngineT {
         forward(n, /*decode=*/true, 0, 0, nullptr);
         sample(n);
         int32_t *st = multi_state_.data(); // done[max_batch] | count[max_batch] | step counter
-        detail::decode_advance_kernel<<<1, 1024, 0, stream_>>>(
-            n, multi_steps_, tokens_.data(), dev_at<int32_t>(layout_.ids), dev_at<int32_t>(layout_.pos),
-            dev_at<int32_t>(layout_.lens), dev_at<int32_t>(layout_.step), dev_at<double>(layout_.uniform),
-            multi_has_uni_ ? reinterpret_cast<const double *>(multi_uni_.data()) : nullptr, multi_eos_, st,
-            st + max_batch_, multi_out_.data(), st + 2 * max_batch_);
-        OPWORKS_CUDA_CHECK(cudaGetLastError());
+        // programmatic launch: resident while the sampler runs, it waits
+        // for the sampler's tokens on the device
+        launch_ex(detail::decode_advance_kernel, dim3(1), dim3(1024), 0, stream_, n, multi_steps_,
+                  static_cast<const int32_t *>(tokens_.data()), dev_at<int32_t>(layout_.ids), dev_at<int32_t>(layout_.pos),
+                  dev_at<int32_t>(layout_.lens), dev_at<int32_t>(layout_.step), dev_at<double>(layout_.uniform),
+                  multi_has_uni_ ? reinterpret_cast<const double *>(multi_uni_.data()) : nullptr, multi_eos_, st,
+                  st + max_batch_, multi_out_.data(), st + 2 * max_batch_);
     }
 
     void fetch_tokens(int n) {
