@@ -379,7 +379,7 @@ template <typename WT> class LlamaEngineT {
 
     // `steps` decode tokens for each of n slots without a host round trip per
     // step: the step's CUDA graph is replayed `steps` times with the sampled
-    // tokens fed back on the device (decode_advance_kernel); KV blocks for all
+    // tokens fed back on the device (by the sampler, SampleAdvance); KV blocks for all
     // steps are reserved up front. out[k * n + i] is row i's token of step k,
     // or -1 after the row emitted `eos` (eos < 0: none); count[i] is the
     // number of tokens row i produced up to and including its eos. uniforms
@@ -416,7 +416,7 @@ template <typename WT> class LlamaEngineT {
             multi_uni_ = TypedDeviceBuffer<uint8_t>(8 * multi_cap_);
         }
         if (multi_state_.size() == 0)
-            multi_state_ = TypedDeviceBuffer<int32_t>(2 * static_cast<int64_t>(max_batch_) + 1);
+            multi_state_ = TypedDeviceBuffer<int32_t>(3 * static_cast<int64_t>(max_batch_));
         multi_steps_ = steps;
         multi_eos_ = eos;
         multi_has_uni_ = uniforms != nullptr;
@@ -424,7 +424,7 @@ template <typename WT> class LlamaEngineT {
         if (uniforms)
             OPWORKS_CUDA_CHECK(cudaMemcpyAsync(multi_uni_.data(), uniforms, sizeof(double) * steps * n,
                                                cudaMemcpyHostToDevice, stream_));
-        OPWORKS_CUDA_CHECK(cudaMemsetAsync(multi_state_.data(), 0, sizeof(int32_t) * (2 * max_batch_ + 1), stream_));
+        OPWORKS_CUDA_CHECK(cudaMemsetAsync(multi_state_.data(), 0, sizeof(int32_t) * 3 * max_batch_, stream_));
         // the step graph bakes in steps, eos and whether uniforms are given
         const MultiKey key{n, steps, eos, multi_has_uni_};
         auto it = multi_graphs_.find(key);
@@ -436,7 +436,7 @@ template <typename WT> class LlamaEngineT {
                 // undo that eager step: same inputs again, counter to 0
                 OPWORKS_CUDA_CHECK(cudaMemcpyAsync(in_dev_.data(), in_host_, dec_.bytes, cudaMemcpyHostToDevice,
                                                    stream_));
-                OPWORKS_CUDA_CHECK(cudaMemsetAsync(multi_state_.data(), 0, sizeof(int32_t) * (2 * max_batch_ + 1),
+                OPWORKS_CUDA_CHECK(cudaMemsetAsync(multi_state_.data(), 0, sizeof(int32_t) * 3 * max_batch_,
                                                    stream_));
             }
             cudaGraph_t graph = nullptr;
@@ -698,15 +698,22 @@ template <typename WT> class LlamaEngineT {
     // one step of a multi-step decode: forward, sample, feed the tokens back
     void multi_body(int n) {
         forward(n, /*decode=*/true, 0, 0, nullptr);
-        sample(n);
-        int32_t *st = multi_state_.data(); // done[max_batch] | count[max_batch] | step counter
-        // programmatic launch: resident while the sampler runs, it waits
-        // for the sampler's tokens on the device
-        launch_ex(detail::decode_advance_kernel, dim3(1), dim3(1024), 0, stream_, n, multi_steps_,
-                  static_cast<const int32_t *>(tokens_.data()), dev_at<int32_t>(layout_.ids), dev_at<int32_t>(layout_.pos),
-                  dev_at<int32_t>(layout_.lens), dev_at<int32_t>(layout_.step), dev_at<double>(layout_.uniform),
-                  multi_has_uni_ ? reinterpret_cast<const double *>(multi_uni_.data()) : nullptr, multi_eos_, st,
-                  st + max_batch_, multi_out_.data(), st + 2 * max_batch_);
+        int32_t *st = multi_state_.data(); // done[max_batch] | count[max_batch] | steps taken[max_batch]
+        detail::SampleAdvance adv;
+        adv.ids = dev_at<int32_t>(layout_.ids);
+        adv.pos = dev_at<int32_t>(layout_.pos);
+        adv.lens = dev_at<int32_t>(layout_.lens);
+        adv.step = dev_at<int32_t>(layout_.step);
+        adv.uniform = dev_at<double>(layout_.uniform);
+        adv.uniforms = multi_has_uni_ ? reinterpret_cast<const double *>(multi_uni_.data()) : nullptr;
+        adv.done = st;
+        adv.count = st + max_batch_;
+        adv.taken = st + 2 * max_batch_;
+        adv.out = multi_out_.data();
+        adv.n = n;
+        adv.steps = multi_steps_;
+        adv.eos = multi_eos_;
+        sample(n, adv);
     }
 
     void fetch_tokens(int n) {
@@ -1250,7 +1257,7 @@ template <typename WT> class LlamaEngineT {
         mark("lm_head");
     }
 
-    void sample(int rows) {
+    void sample(int rows, const detail::SampleAdvance &adv = {}) {
         const PdlScope pdl(pdl_);
         detail::SampleParams sp;
         sp.temperature = dev_at<float>(layout_.temp);
@@ -1258,7 +1265,7 @@ template <typename WT> class LlamaEngineT {
         sp.uniform = dev_at<double>(layout_.uniform);
         sp.seed = dev_at<uint64_t>(layout_.seed);
         sp.step = dev_at<int32_t>(layout_.step);
-        detail::sample_launch(logits_.data(), cfg_.vocab_size, rows, cfg_.vocab_size, sp, tokens_.data(), stream_);
+        detail::sample_launch(logits_.data(), cfg_.vocab_size, rows, cfg_.vocab_size, sp, tokens_.data(), stream_, adv);
     }
 
     ModelConfig cfg_;

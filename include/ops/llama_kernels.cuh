@@ -672,39 +672,6 @@ static __global__ void __launch_bounds__(128)
     }
 }
 
-// Device-side step feedback of a multi-step decode (one block, n <= 1024
-// rows): step k = *counter. Row i's sampled token goes to out[k][i] (-1 once
-// the row has emitted `eos`, which ends its count) and becomes the row's next
-// input; position, length and the sampling step advance; the next step's
-// uniform comes from uniforms[k + 1][i] when given. The counter advances last.
-static __global__ void __launch_bounds__(1024)
-    decode_advance_kernel(int n, int steps, const int32_t *__restrict__ sampled, int32_t *ids, int32_t *pos,
-                          int32_t *lens, int32_t *step, double *uniform, const double *__restrict__ uniforms, int eos,
-                          int32_t *done, int32_t *count, int32_t *out, int32_t *counter) {
-    pdl_wait(); // launched while the sampler runs; its tokens are visible from here on
-    const int k = *counter;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
-        const int32_t tok = sampled[i];
-        int32_t emitted = -1;
-        if (!done[i]) {
-            emitted = tok;
-            count[i] = k + 1;
-            if (tok == eos)
-                done[i] = 1;
-        }
-        out[static_cast<int64_t>(k) * n + i] = emitted;
-        ids[i] = tok;
-        pos[i] += 1;
-        lens[i] += 1;
-        step[i] += 1;
-        if (uniforms != nullptr && k + 1 < steps)
-            uniform[i] = uniforms[static_cast<int64_t>(k + 1) * n + i];
-    }
-    __syncthreads();
-    if (threadIdx.x == 0)
-        *counter = k + 1;
-}
-
 // cos/sin table of RoPE: table[pos][i] = (cosf(a), sinf(a)), a = fp32(pos) *
 // inv_freq[i], the same fp32 expression as ops::rope.
 static __global__ void rope_table_kernel(const float *__restrict__ inv_freq, int max_pos, int half, float2 *__restrict__ out) {
@@ -774,6 +741,64 @@ struct SampleParams {
     const uint64_t *seed;     // [rows] counter-based uniforms when uniform == nullptr
     const int *step;          // [rows]
 };
+
+// Device-side step feedback of a multi-step decode, done by the thread that
+// writes a row's token (ids == nullptr: plain sampling). Row i's token of
+// step k = taken[i] goes to out[k][i] (-1 once the row has emitted `eos`,
+// which ends its count) and becomes the row's next input; position, length
+// and the sampling step advance; the next step's uniform comes from
+// uniforms[k + 1][i] when given.
+struct SampleAdvance {
+    int32_t *ids = nullptr, *pos = nullptr, *lens = nullptr, *step = nullptr; // the next step's inputs
+    double *uniform = nullptr;                                                 // the next step's uniform
+    const double *uniforms = nullptr;                                          // [steps][n], or nullptr
+    int32_t *done = nullptr, *count = nullptr, *taken = nullptr;               // per row
+    int32_t *out = nullptr;                                                    // [steps][n]
+    int n = 0, steps = 0, eos = -1;
+};
+
+// A row's advance state as read at kernel start (every CTA of the row reads
+// it while the row is being sampled, so the one writer only stores).
+struct SampleAdvanceIn {
+    int taken, done, pos, lens, step;
+    double next_uniform; // valid when has_uniform
+    bool has_uniform;
+};
+
+__device__ __forceinline__ void sample_advance_load(const SampleAdvance &adv, int row, SampleAdvanceIn &in) {
+    in.taken = adv.taken[row];
+    in.done = adv.done[row];
+    in.pos = adv.pos[row];
+    in.lens = adv.lens[row];
+    in.step = adv.step[row];
+    in.has_uniform = adv.uniforms != nullptr && in.taken + 1 < adv.steps;
+    in.next_uniform = in.has_uniform ? adv.uniforms[static_cast<int64_t>(in.taken + 1) * adv.n + row] : 0.0;
+}
+
+// Every CTA of a row has read the row's sampling inputs (uniform, step)
+// before the one writer gets here (after the row's last cluster barrier).
+__device__ __forceinline__ void sample_emit(int *out, int row, int tok, const SampleAdvance &adv,
+                                            const SampleAdvanceIn &in) {
+    out[row] = tok;
+    if (adv.ids == nullptr)
+        return;
+    const int k = in.taken;
+    int32_t emitted = -1;
+    if (!in.done) {
+        emitted = tok;
+        adv.count[row] = k + 1;
+        if (tok == adv.eos)
+            adv.done[row] = 1;
+    }
+    adv.out[static_cast<int64_t>(k) * adv.n + row] = emitted;
+    adv.ids[row] = tok;
+    adv.pos[row] = in.pos + 1;
+    adv.lens[row] = in.lens + 1;
+    adv.step[row] = in.step + 1;
+    if (in.has_uniform)
+        adv.uniform[row] = in.next_uniform;
+    adv.taken[row] = k + 1;
+}
 
 __device__ __forceinline__ uint64_t splitmix64(uint64_t x) {
     x += 0x9e3779b97f4a7c15ull;
@@ -855,6 +880,7 @@ struct SampleShared {
     int best_i;
     unsigned long long part_mass; // final pass: kept mass of this CTA
     int part_ties;                // final pass: boundary ties of this CTA
+    SampleAdvanceIn adv_in;       // the row's multi-step state (thread 0 reads it)
     int res_bucket;               // crossing bucket of the current level
     unsigned long long res_above; // mass above it
 };
@@ -936,7 +962,8 @@ __device__ __forceinline__ void sample_hist_add(uint32_t (*h)[kSampleBuckets], i
 // memory (256 x 8 loads) and finds the crossing bucket itself (identical
 // integer arithmetic everywhere), so one barrier per level suffices.
 static __global__ void __cluster_dims__(kSampleCluster, 1, 1) __launch_bounds__(kSampleThreads, 2)
-    sample_kernel(const float *__restrict__ logits, int64_t ld, int vocab, SampleParams sp, int *__restrict__ out) {
+    sample_kernel(const float *__restrict__ logits, int64_t ld, int vocab, SampleParams sp, int *__restrict__ out,
+                  SampleAdvance adv) {
     namespace cg = cooperative_groups;
     cg::cluster_group cluster = cg::this_cluster();
     extern __shared__ __align__(16) uint8_t smem_raw[];
@@ -951,6 +978,8 @@ static __global__ void __cluster_dims__(kSampleCluster, 1, 1) __launch_bounds__(
     const float *src = logits + static_cast<int64_t>(row) * ld + lo;
     pdl_trigger();
     pdl_wait();
+    if (adv.ids != nullptr && tid == 0)
+        sample_advance_load(adv, row, sh.adv_in);
 
     // pass 0: stage the slice, local (max, first index)
     float bv = kNegInf;
@@ -1020,9 +1049,9 @@ static __global__ void __cluster_dims__(kSampleCluster, 1, 1) __launch_bounds__(
     }
     const float temp = sp.temperature ? sp.temperature[row] : 0.f;
     if (!(temp > 0.f)) {
-        if (rank == 0 && tid == 0)
-            out[row] = garg;
         cluster.sync(); // peers finished reading this CTA's shared memory
+        if (rank == 0 && tid == 0)
+            sample_emit(out, row, garg, adv, sh.adv_in);
         return;
     }
     const float inv_t = 1.f / fmaxf(temp, 1e-6f);
@@ -1302,7 +1331,7 @@ static __global__ void __cluster_dims__(kSampleCluster, 1, 1) __launch_bounds__(
                 }
             }
         }
-        out[row] = pick;
+        sample_emit(out, row, pick, adv, sh.adv_in);
     }
     // u -> 1 rounding: the goal lands past the last kept token
     if (rank == kSampleCluster - 1 && tid == 0 && !(goal < static_cast<double>(all))) {
@@ -1313,7 +1342,7 @@ static __global__ void __cluster_dims__(kSampleCluster, 1, 1) __launch_bounds__(
                 last = i;
                 break;
             }
-        out[row] = last;
+        sample_emit(out, row, last, adv, sh.adv_in);
     }
     cluster.sync(); // keep shared memory alive until every peer is done with it
 }
@@ -1321,7 +1350,7 @@ static __global__ void __cluster_dims__(kSampleCluster, 1, 1) __launch_bounds__(
 inline size_t sample_smem_bytes() { return sizeof(SampleShared); }
 
 inline void sample_launch(const float *logits, int64_t ld, int rows, int vocab, const SampleParams &sp, int *out,
-                          cudaStream_t stream) {
+                          cudaStream_t stream, const SampleAdvance &adv = {}) {
     require((vocab + kSampleCluster - 1) / kSampleCluster <= kSampleChunkMax, "vocabulary too large for the sampler");
     static thread_local int done = -1;
     int dev = 0;
@@ -1332,7 +1361,7 @@ inline void sample_launch(const float *logits, int64_t ld, int rows, int vocab, 
         done = dev;
     }
     launch_ex(sample_kernel, dim3(rows * kSampleCluster), dim3(kSampleThreads), sample_smem_bytes(), stream, logits, ld,
-              vocab, sp, out);
+              vocab, sp, out, adv);
 }
 
 } // namespace opworks::detail
