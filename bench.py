@@ -294,8 +294,8 @@ def run_ours(args):
 
     K, W = args.steps, args.warmup
     MULTI = 64  # extra steps of the host-sync-free multi-step decode (extras)
-    # positions: W warm-up steps, K (warm multi-step), K (timed), K (e2e),
-    # 3 (in-graph trace), MULTI (extras), 1 spare
+    # positions: W warm-up steps, 1 or K (warm multi-step), K (timed), K
+    # (e2e), 3 (in-graph trace), MULTI (extras), 1 spare
     max_seq = ((CTX + W + 3 * K + 3 + MULTI + 1 + 15) // 16) * 16
     t_load = time.perf_counter()
     model = Model(pack_path, weight_sets=1, max_positions=max(8192, max_seq), device=local)
@@ -352,16 +352,18 @@ def run_ours(args):
     # at the end). Tensor-parallel runs keep the per-step call.
     multi_value = not tp
 
-    def decode_k():
+    def decode_k(k=K):
         nonlocal prev, step
-        toks, _ = eng.decode_multi(slots, prev, K, temperature=TEMPERATURE, top_p=TOP_P, seeds=seeds, steps0=step)
+        toks, _ = eng.decode_multi(slots, prev, k, temperature=TEMPERATURE, top_p=TOP_P, seeds=seeds, steps0=step)
         prev = toks[-1]
-        step += K
+        step += k
 
     for _ in range(W):
         decode_once()
     if multi_value:
-        decode_k()  # warm: the K-step graph is captured here
+        # warm: the multi-step graph is captured here (one graph serves calls
+        # of up to 256 steps; longer calls regrow its buffers once)
+        decode_k(1 if K <= 256 else K)
     torch.cuda.synchronize()
 
     clocks = ClockSampler(local if "CUDA_VISIBLE_DEVICES" not in os.environ else local)

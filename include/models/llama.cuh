@@ -410,14 +410,22 @@ template <typename WT> class LlamaEngineT {
             stage_sampling(i, sa ? sa[i] : SampleArgs{});
         }
         flush_table();
-        if (multi_cap_ < static_cast<int64_t>(steps) * n) {
-            multi_cap_ = static_cast<int64_t>(steps) * n;
-            multi_out_ = TypedDeviceBuffer<int32_t>(multi_cap_);
-            multi_uni_ = TypedDeviceBuffer<uint8_t>(8 * multi_cap_);
+        // step rows of the token and uniform buffers: steps + 1 (each step
+        // reads the next row's uniforms; after the last step that value is
+        // never used), at least 257 so that calls of up to 256 steps share
+        // one captured graph. The graphs hold these pointers: a regrowth
+        // recaptures them.
+        if (multi_rows_ < steps + 1) {
+            OPWORKS_CUDA_CHECK(cudaStreamSynchronize(stream_));
+            for (auto &g : multi_graphs_)
+                cudaGraphExecDestroy(g.second);
+            multi_graphs_.clear();
+            multi_rows_ = std::max(steps + 1, 257);
+            multi_out_ = TypedDeviceBuffer<int32_t>(static_cast<int64_t>(multi_rows_) * max_batch_);
+            multi_uni_ = TypedDeviceBuffer<uint8_t>(8 * static_cast<int64_t>(multi_rows_) * max_batch_);
         }
         if (multi_state_.size() == 0)
             multi_state_ = TypedDeviceBuffer<int32_t>(3 * static_cast<int64_t>(max_batch_));
-        multi_steps_ = steps;
         multi_eos_ = eos;
         multi_has_uni_ = uniforms != nullptr;
         OPWORKS_CUDA_CHECK(cudaMemcpyAsync(in_dev_.data(), in_host_, dec_.bytes, cudaMemcpyHostToDevice, stream_));
@@ -425,8 +433,8 @@ template <typename WT> class LlamaEngineT {
             OPWORKS_CUDA_CHECK(cudaMemcpyAsync(multi_uni_.data(), uniforms, sizeof(double) * steps * n,
                                                cudaMemcpyHostToDevice, stream_));
         OPWORKS_CUDA_CHECK(cudaMemsetAsync(multi_state_.data(), 0, sizeof(int32_t) * 3 * max_batch_, stream_));
-        // the step graph bakes in steps, eos and whether uniforms are given
-        const MultiKey key{n, steps, eos, multi_has_uni_};
+        // the step graph bakes in the rows, eos and whether uniforms are given
+        const MultiKey key{n, eos, multi_has_uni_};
         auto it = multi_graphs_.find(key);
         if (it == multi_graphs_.end()) {
             if (graphs_.count(n) == 0) {
@@ -711,7 +719,6 @@ template <typename WT> class LlamaEngineT {
         adv.taken = st + 2 * max_batch_;
         adv.out = multi_out_.data();
         adv.n = n;
-        adv.steps = multi_steps_;
         adv.eos = multi_eos_;
         sample(n, adv);
     }
@@ -1331,19 +1338,17 @@ template <typename WT> class LlamaEngineT {
     void *in_host_ = nullptr;
     int32_t *out_host_ = nullptr;
     std::map<int, cudaGraphExec_t> graphs_;
-    // multi-step decode: graphs keyed by (rows, steps, eos, uniforms given)
+    // multi-step decode: graphs keyed by (rows, eos, uniforms given); the
+    // step count is the number of replays
     struct MultiKey {
-        int n, steps, eos;
+        int n, eos;
         bool uni;
-        bool operator<(const MultiKey &o) const {
-            return std::tie(n, steps, eos, uni) < std::tie(o.n, o.steps, o.eos, o.uni);
-        }
+        bool operator<(const MultiKey &o) const { return std::tie(n, eos, uni) < std::tie(o.n, o.eos, o.uni); }
     };
     std::map<MultiKey, cudaGraphExec_t> multi_graphs_;
     TypedDeviceBuffer<int32_t> multi_out_, multi_state_;
     TypedDeviceBuffer<uint8_t> multi_uni_;
-    int64_t multi_cap_ = 0;
-    int multi_steps_ = 0, multi_eos_ = -1;
+    int multi_rows_ = 0, multi_eos_ = -1;
     bool multi_has_uni_ = false;
     bool marks_enabled_ = false;
     // fast-path GEMMs with more token rows than this use single-term 16-bit

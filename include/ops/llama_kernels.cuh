@@ -747,14 +747,15 @@ struct SampleParams {
 // step k = taken[i] goes to out[k][i] (-1 once the row has emitted `eos`,
 // which ends its count) and becomes the row's next input; position, length
 // and the sampling step advance; the next step's uniform comes from
-// uniforms[k + 1][i] when given.
+// uniforms[k + 1][i] when given (uniforms holds one row more than the
+// steps of a call).
 struct SampleAdvance {
     int32_t *ids = nullptr, *pos = nullptr, *lens = nullptr, *step = nullptr; // the next step's inputs
     double *uniform = nullptr;                                                 // the next step's uniform
-    const double *uniforms = nullptr;                                          // [steps][n], or nullptr
+    const double *uniforms = nullptr;                                          // [steps + 1][n], or nullptr
     int32_t *done = nullptr, *count = nullptr, *taken = nullptr;               // per row
     int32_t *out = nullptr;                                                    // [steps][n]
-    int n = 0, steps = 0, eos = -1;
+    int n = 0, eos = -1;
 };
 
 // A row's advance state as read at kernel start (every CTA of the row reads
@@ -771,7 +772,7 @@ __device__ __forceinline__ void sample_advance_load(const SampleAdvance &adv, in
     in.pos = adv.pos[row];
     in.lens = adv.lens[row];
     in.step = adv.step[row];
-    in.has_uniform = adv.uniforms != nullptr && in.taken + 1 < adv.steps;
+    in.has_uniform = adv.uniforms != nullptr;
     in.next_uniform = in.has_uniform ? adv.uniforms[static_cast<int64_t>(in.taken + 1) * adv.n + row] : 0.0;
 }
 

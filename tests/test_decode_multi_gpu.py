@@ -82,3 +82,38 @@ def test_multi_step_eos_stops_count(model):
             assert counts[i] == stop
             assert np.array_equal(got[:stop, i], ref[:stop, i])
             assert np.all(got[stop:, i] == -1)
+
+
+def test_multi_step_call_lengths_share_and_regrow_graphs(model):
+    """Calls of 4, 300 and again 4 steps (explicit uniforms): the 300-step
+    call outgrows the token and uniform buffers (257 step rows), which
+    recaptures the multi-step graph; every call still gives the tokens of
+    single-step calls with the same uniforms."""
+    from opworks_b200.llama import LlamaBatch
+
+    n = 2
+    lengths = (4, 300, 4)
+    total = sum(lengths)
+    rng = np.random.default_rng(33)
+    prompts = [rng.integers(0, model.vocab, 20).tolist() for _ in range(n)]
+    uni = rng.random((total, n))
+    seeds = (900 + np.arange(n)).astype(np.uint64)
+    slots = np.arange(n, dtype=np.int32)
+    with LlamaBatch(model, n, 20 + total + 8, "fast", prefill_rows=32) as b:
+        prev = prefill_all(b, prompts, 0.7, seeds)
+        multi, k = [], 0
+        for length in lengths:
+            toks, counts = b.decode_multi(slots, prev, length, temperature=0.7, top_p=0.9, uniforms=uni[k:k + length],
+                                          seeds=seeds, steps0=1 + k)
+            assert np.all(counts == length)
+            multi.append(toks)
+            prev = toks[-1]
+            k += length
+        multi = np.concatenate(multi)
+    with LlamaBatch(model, n, 20 + total + 8, "fast", prefill_rows=32) as b:
+        t = prefill_all(b, prompts, 0.7, seeds)
+        single = []
+        for k in range(total):
+            t = b.decode(slots, t, temperature=0.7, top_p=0.9, uniforms=uni[k], seeds=seeds, steps=k + 1)
+            single.append(t)
+    assert np.array_equal(multi, np.array(single))
