@@ -347,9 +347,9 @@ def run_ours(args):
         step += 1
 
     # `value`: K steps with every step's sampled tokens fed back on the device
-    # (one opw_llama_batch_decode_multi call: K replays of the step graph plus
-    # the token-advance kernel, inputs resident, one D2H of the K x 32 tokens
-    # at the end). Tensor-parallel runs keep the per-step call.
+    # (one opw_llama_batch_decode_multi call: K replays of the step graph, the
+    # sampler writing each row's next inputs, inputs resident, one D2H of the
+    # K x 32 tokens at the end). Tensor-parallel runs keep the per-step call.
     multi_value = not tp
 
     def decode_k(k=K):
@@ -567,15 +567,14 @@ def run_ours(args):
                        "l2": "inputs larger than L2: every step streams 2.47 GB of weights + ~4.5 GB of KV",
                        "cuda_graph": True,
                        "timed_step": ("K replays of the step graph in one decode_multi call, sampled tokens fed "
-                                      "back on the device (token-advance kernel), CUDA events on the engine stream"
+                                      "back on the device by the sampler, CUDA events on the engine stream"
                                       if multi_value else "K blocking per-step decode calls, CUDA events"),
                        "e2e_step": "K blocking opw_llama_batch_decode calls (H2D of the step's inputs, graph "
                                    "replay, D2H of the sampled tokens), host wall clock"},
             "roofline": roofline, "step_roofline": step_roofline,
             "e2e": {"value": round(e2e_value, 1), "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
-            "gpu_launches": (gpu_launches_per_step + (1 if multi_value else 0)) * K,
-            "gpu_launches_per_step": gpu_launches_per_step + (1 if multi_value else 0),
+            "gpu_launches": gpu_launches_per_step * K, "gpu_launches_per_step": gpu_launches_per_step,
             "clocks": clocks.summary(),
             "prefill": {"c3_tokens": BATCH * CTX, "c3_ms": round(prefill_ms, 1),
                         "c3_tok_s": round(BATCH * CTX * groups / (prefill_ms / 1e3), 1), "c4": prefill8k},
